@@ -1,0 +1,188 @@
+/*
+ * q27_b200.h -- C ABI of the B200 (sm_100a) attention engine that slots in behind the
+ * kernel-launch surface of signalnine/q27's full-attention layers.
+ *
+ * Every entry point takes plain pointers and sizes, returns an int status (0 = ok) and
+ * never exits the process or throws. Pointers named d_* / tables / Q / out / scratch are
+ * DEVICE pointers owned by the caller; small descriptor structs are HOST memory read
+ * during the call. All work is enqueued on the caller's stream; nothing is allocated and
+ * nothing synchronises, so every entry point may be called under stream capture (the
+ * reference captures its rounds into CUDA graphs, src/engine.cuh:2515).
+ *
+ * Fixed geometry of the path (src/engine.cuh:45, docs/SPEC.md:17): head_dim 256,
+ * n_q_heads = 6 * n_kv_heads (24 / 4), 64-row KV pages (src/cuda_common.h:70-105).
+ */
+#ifndef Q27_B200_H
+#define Q27_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------------------ */
+enum {
+    Q27_OK = 0,
+    Q27_ERR_INVALID_ARG = 1,      /* null pointer, bad stride, misaligned page, ... */
+    Q27_ERR_UNSUPPORTED_KIND = 2, /* a KvKind this engine does not read (refused, never
+                                     mis-read: src/spec3.cu:1109-1122) */
+    Q27_ERR_UNSUPPORTED_WIDTH = 3,/* ntok / geometry outside the instantiated range
+                                     (the reference's `bool false`, src/fdmma.cuh:497) */
+    Q27_ERR_CUDA = 4,             /* a CUDA call failed; see q27_last_cuda_error() */
+    Q27_ERR_TOO_LARGE = 5         /* exceeds a fixed capacity (no-allocation entry) */
+};
+
+/* KvKind, src/cuda_common.h:53. Kinds 3..5 (turbo3v, turbo5k, int8-g64) are refused. */
+enum { Q27_KV_F16 = 0, Q27_KV_FP8 = 1, Q27_KV_T3 = 2 };
+
+#define Q27_KV_PAGE 64        /* rows per page, src/cuda_common.h:70 */
+#define Q27_HEAD_DIM 256
+#define Q27_GQA 6
+#define Q27_MAX_LANES 16      /* lane-pointer bundles carry p[16], src/kernels.cuh:67-68 */
+#define Q27_MAX_SPLITS 128    /* FD_MAXNS, src/spec3.cuh:126 */
+#define Q27_PART_STRIDE 258   /* {m, l, acc[256]}: FD_ST src/spec3.cuh:127, PF_PART_STRIDE */
+#define Q27_PF_SPLIT_MAX 8    /* src/prefill.cuh:88 */
+#define Q27_T3_BLOCK_BYTES 50 /* sizeof(block_turbo3), src/turbo3.cuh:26-32 */
+#define Q27_MAX_SLOTS 8       /* slots per batched launch */
+
+/* Lane pointer bundles: P3 / CP3 (src/kernels.cuh:67-68) and IP3 (src/spec3.cuh:13).
+ * Slots >= ntok may hold garbage and are never dereferenced. */
+typedef struct { float* p[Q27_MAX_LANES]; } q27_P3;
+typedef struct { const float* p[Q27_MAX_LANES]; } q27_CP3;
+typedef struct { const int* p[Q27_MAX_LANES]; } q27_IP3;
+
+const char* q27_status_string(int status);
+/* cudaError_t of the most recent failing CUDA call made by this library on this thread */
+int q27_last_cuda_error(void);
+/* compiled-for architecture, e.g. 1000 for sm_100a; 0 if the image cannot run here */
+int q27_device_arch(void);
+
+/* bytes per cache row: fp16 n_kv*512, fp8 n_kv*256, turbo3 n_kv*100; -1 = refused kind */
+int64_t q27_kv_row_bytes(int kvk, int n_kv_heads);
+/* floats the caller must provide as `scratch` for ntok lanes:
+ * ntok * n_q_heads * Q27_MAX_SPLITS * Q27_PART_STRIDE (src/spec3.cuh:109-111) */
+int64_t q27_decode_scratch_floats(int ntok, int n_q_heads);
+/* floats for `part` of q27_attn_prefill_T: n_q_heads * round_up(SB,16) * 8 * 258
+ * (src/prefill.cuh:86-88) */
+int64_t q27_prefill_part_floats(int SB, int n_q_heads);
+
+/* ---- decode / verify --------------------------------------------------------------- */
+
+/* Replaces q27k::attn_decode (src/blocks.cuh:39-42, src/spec3.cu:1291-1299): one query
+ * token attends cache rows [0, *d_pos]. q: head h at q + h*q_stride (first 256 floats of
+ * each head; the gate half is not touched). out: [n_q_heads][256] fp32. For Q27_KV_T3, q
+ * is already WHT-rotated and out is left in the rotated basis. max_ctx is unused, as in
+ * the reference. */
+int q27_attn_decode(const float* q, int q_stride, const void* const* ktab,
+                    const void* const* vtab, float* out, float* scratch, const int* d_pos,
+                    int max_ctx, int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                    void* stream, int kvk);
+
+/* Replaces q27k::attn_decode3 and attn_decode3_fd2 (src/spec3.cuh:139-147,
+ * src/spec3.cu:1066-1288): ntok lanes (1..16) against ONE pass over the cache; lane t
+ * attends rows [0, *pos->p[t]], which makes draft lanes causal among themselves
+ * (src/engine.cuh:2124-2125). This is also the shared-KV verify step that the reference
+ * reaches through fdmma::launch_fdmma / launch_fdmma_h16 (src/fdmma.cuh:460,808). */
+int q27_attn_decode3(const q27_CP3* q, int q_stride, const void* const* ktab,
+                     const void* const* vtab, const q27_P3* out, float* scratch,
+                     const q27_IP3* pos, int max_ctx, int n_q_heads, int n_kv_heads,
+                     int head_dim, float scale, void* stream, int ntok, int kvk);
+
+/* One slot of a batched launch. The reference runs one attn_decode3 per slot on its own
+ * stream (src/conductor.h:681-694); here all slots ride one launch.
+ * row_base / row_count describe which logical rows the tables hold (KV-sequence
+ * sharding): table row r is logical row row_base + r, for 0 <= r < row_count. An
+ * unsharded cache passes row_base = 0, row_count = INT32_MAX. */
+typedef struct {
+    const void* const* ktab;
+    const void* const* vtab;
+    q27_CP3 q;
+    q27_IP3 pos;
+    q27_P3 out;       /* normalised output rows; used by q27_attn_decode_batched */
+    float* scratch;   /* ntok * n_q_heads * 128 * 258 floats, private to the slot */
+    int ntok;
+    int row_base;
+    int row_count;
+    int reserved;
+} q27_slot;
+
+/* Additive (no reference counterpart as a single call): nslots (1..8) independent slots
+ * in one launch, same per-slot semantics as q27_attn_decode3. */
+int q27_attn_decode_batched(const q27_slot* slots, int nslots, int q_stride, int n_q_heads,
+                            int n_kv_heads, int head_dim, float scale, void* stream, int kvk);
+
+/* Additive: the fp32-scalar ("exact") kernel family behind the same arguments, the
+ * counterpart of the reference's explicit attn_decode3_fd2 entry (src/spec3.cuh:144-147),
+ * which its unit gate compares the default dispatch against. */
+int q27_attn_decode_batched_exact(const q27_slot* slots, int nslots, int q_stride,
+                                  int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                                  void* stream, int kvk);
+
+/* Additive, for KV-sequence sharding across GPUs: like q27_attn_decode_batched but each
+ * lane's rows are clipped to the slot's [row_base, row_base+row_count) window and the
+ * result is left UN-normalised: partial_out receives, per (slot, lane, head), the
+ * merged {m, l, acc[256]} (258 floats) at ((slot*lanes_stride + lane)*n_q_heads + h)*258.
+ * A lane whose window is empty gets {-FLT_MAX, 0, 0...} (src/prefill.cu:1353-1362). */
+int q27_attn_decode_partial(const q27_slot* slots, int nslots, int lanes_stride, int q_stride,
+                            int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                            float* partial_out, void* stream, int kvk);
+
+/* Additive: log-sum-exp merge of nparts partial sets (k_attn_fd_combine,
+ * src/spec3.cu:706-739, applied across GPUs instead of across splits).
+ * parts: [nparts][npairs][258]; out: [npairs][256] normalised. */
+int q27_attn_merge_partials(const float* parts, int nparts, int64_t npairs, float* out,
+                            void* stream);
+
+/* ---- prefill ----------------------------------------------------------------------- */
+
+/* Replaces q27k::attn_prefill_T (src/prefill.cuh:95-98, src/prefill.cu:2620-2655):
+ * causal GQA attention for SB tokens t0..t0+SB-1 of a chunk whose first token sits at
+ * cache row base_pos; token t attends rows [0, base_pos + t + 1) -- the reused prefix
+ * fully, the chunk causally. qT: [T][q_row] fp32, head h at h*q_stride; outT:
+ * [T][out_row], head h at h*256. part: caller scratch (may be NULL). */
+int q27_attn_prefill_T(const float* qT, int q_stride, int q_row, const void* const* ktab,
+                       const void* const* vtab, float* outT, int out_row, float* part,
+                       int base_pos, int t0, int SB, int n_q_heads, int n_kv_heads,
+                       int head_dim, float scale, void* stream, int kvk);
+
+/* The scalar fp32 prefill (the reference's "lite" k_attn_prefill_T, src/prefill.cu:2293-2388,
+ * its in-repo exact GPU reference), same arguments. */
+int q27_attn_prefill_T_exact(const float* qT, int q_stride, int q_row,
+                             const void* const* ktab, const void* const* vtab, float* outT,
+                             int out_row, float* part, int base_pos, int t0, int SB,
+                             int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                             void* stream, int kvk);
+
+/* ---- KV formats -------------------------------------------------------------------- */
+
+/* Bit-exact dequantisation of cache rows [row0, row0+nrows) through a page table to fp32
+ * [nrows][n_kv_heads][256]: half2float / float(e4m3) / CENTROIDS[idx]*half2float(norm)
+ * (kv2f src/cuda_common.h:113-114, turbo3_deq_elem src/turbo3.cuh:134-137). */
+int q27_kv_dequant(const void* const* tab, int kvk, int row0, int nrows, int n_kv_heads,
+                   float* out, void* stream);
+
+/* mk_tab (src/test_kernels.cu:27-36): fill a DEVICE table of ceil(rows/64) entries with
+ * identity page pointers over a contiguous buffer. d_tab is caller-allocated. */
+int q27_mk_tab(const void* base, size_t row_bytes, int rows, void** d_tab, void* stream);
+
+/* ---- KvPool (src/kv_pool.h:24-72) ---------------------------------------------------
+ * Two device allocations (K side, V side) carved into 64-row pages, LIFO free lists,
+ * page address = base + idx*page_bytes. No lock of its own (caller's mutex), allocation
+ * happens once at creation. */
+typedef struct q27_kvpool q27_kvpool;
+/* returns NULL if either side would get zero pages (pool disabled) or allocation fails */
+q27_kvpool* q27_kvpool_create(size_t k_bytes, size_t v_bytes, size_t k_row, size_t v_row);
+void q27_kvpool_destroy(q27_kvpool* pool);
+int q27_kvpool_npages(const q27_kvpool* pool, int side);
+int q27_kvpool_free_pages(const q27_kvpool* pool, int side);
+size_t q27_kvpool_page_bytes(const q27_kvpool* pool, int side);
+void* q27_kvpool_page_ptr(const q27_kvpool* pool, int side, int idx);
+/* pops n page indices into out_idx; returns 0 (and pops nothing) if fewer are free */
+int q27_kvpool_reserve(q27_kvpool* pool, int side, int n, int* out_idx);
+void q27_kvpool_release(q27_kvpool* pool, int side, const int* idx, int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,14 @@
+"""q27_b200 -- a B200 (sm_100a) attention engine behind the kernel-launch surface of
+signalnine/q27's full-attention layers: split-KV flash-decode, shared-KV MTP verify,
+causal GQA prefill over a reused prefix, all over fp16 / fp8-e4m3 / turbo3 paged KV.
+
+The compute path is hand-written CUDA reached through a C ABI (include/q27_b200.h);
+this package is the thin host-side mirror of the reference's launch functions."""
+from . import _lib
+from .kv import (KV_F16, KV_FP8, KV_T3, KV_PAGE, KvPool, PagedSide, kv_k_rotated, mk_tab,
+                 paged_from_rows, row_bytes)
+from .attn import (SlotArgs, attn_decode, attn_decode3, attn_decode_batched,
+                   attn_decode_partial, attn_merge_partials, attn_prefill_T,
+                   decode_scratch_floats, kv_dequant, prefill_part_floats)
+
+__all__ = [n for n in dir() if not n.startswith("_")]

@@ -1,0 +1,129 @@
+"""Host-side mirror of the reference's attention launch surface (same names, argument
+meaning and error behaviour), over the C ABI:
+
+* ``attn_decode``     <- q27k::attn_decode     (src/blocks.cuh:39-42)
+* ``attn_decode3``    <- q27k::attn_decode3    (src/spec3.cuh:139-143)
+* ``attn_prefill_T``  <- q27k::attn_prefill_T  (src/prefill.cuh:95-98)
+
+plus the additive batched / sharded entries. Tensors are torch CUDA tensors owned by the
+caller; nothing here allocates on the hot path except where a docstring says so.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib as L
+from .kv import stream_ptr
+
+INT_MAX = 2**31 - 1
+FD_ST = L.PART_STRIDE
+
+
+def decode_scratch_floats(ntok: int, n_q_heads: int = 24) -> int:
+    return int(L.lib().q27_decode_scratch_floats(ntok, n_q_heads))
+
+
+def prefill_part_floats(SB: int, n_q_heads: int = 24) -> int:
+    return int(L.lib().q27_prefill_part_floats(SB, n_q_heads))
+
+
+def _p3(tensors) -> L.P3:
+    p = L.P3()
+    for i, t in enumerate(tensors):
+        p.p[i] = t.data_ptr() if isinstance(t, torch.Tensor) else int(t)
+    return p
+
+
+def attn_decode(q, q_stride, ktab, vtab, out, scratch, d_pos, max_ctx, n_q_heads, n_kv_heads,
+                head_dim, scale, st=None, kvk=0):
+    """Causal decode attention for one new token; seq_len = *d_pos + 1 read on device."""
+    L.check(L.lib().q27_attn_decode(q.data_ptr(), q_stride, ktab.data_ptr(), vtab.data_ptr(),
+                                    out.data_ptr(), scratch.data_ptr(), d_pos.data_ptr(), max_ctx,
+                                    n_q_heads, n_kv_heads, head_dim, scale, stream_ptr(st), kvk),
+            "q27_attn_decode")
+
+
+def attn_decode3(q_lanes, q_stride, ktab, vtab, out_lanes, scratch, pos_lanes, max_ctx,
+                 n_q_heads, n_kv_heads, head_dim, scale, st=None, ntok=3, kvk=0):
+    """ntok lanes against one pass over the cache; lane t attends cache[0 .. *pos_lanes[t]].
+
+    q_lanes / out_lanes / pos_lanes: sequences of per-lane tensors (the reference's CP3 /
+    P3 / IP3 bundles); entries beyond ntok are ignored."""
+    q = _p3(q_lanes[:ntok])
+    o = _p3(out_lanes[:ntok])
+    p = _p3(pos_lanes[:ntok])
+    L.check(L.lib().q27_attn_decode3(C.byref(q), q_stride, ktab.data_ptr(), vtab.data_ptr(),
+                                     C.byref(o), scratch.data_ptr(), C.byref(p), max_ctx,
+                                     n_q_heads, n_kv_heads, head_dim, scale, stream_ptr(st),
+                                     ntok, kvk),
+            "q27_attn_decode3")
+
+
+@dataclass
+class SlotArgs:
+    """One slot of a batched launch (q27_slot)."""
+    ktab: torch.Tensor
+    vtab: torch.Tensor
+    q_lanes: list
+    pos_lanes: list
+    out_lanes: list = field(default_factory=list)
+    scratch: torch.Tensor | None = None
+    row_base: int = 0
+    row_count: int = INT_MAX
+
+
+def _slots(slots) -> C.Array:
+    arr = (L.Slot * len(slots))()
+    for i, s in enumerate(slots):
+        arr[i].ktab = s.ktab.data_ptr()
+        arr[i].vtab = s.vtab.data_ptr()
+        arr[i].q = _p3(s.q_lanes)
+        arr[i].pos = _p3(s.pos_lanes)
+        arr[i].out = _p3(s.out_lanes)
+        arr[i].scratch = s.scratch.data_ptr()
+        arr[i].ntok = len(s.q_lanes)
+        arr[i].row_base = s.row_base
+        arr[i].row_count = s.row_count
+    return arr
+
+
+def attn_decode_batched(slots, q_stride, n_q_heads, n_kv_heads, head_dim, scale, st=None, kvk=0,
+                        exact=False):
+    """All slots in one launch; per-slot semantics of attn_decode3."""
+    arr = _slots(slots)
+    fn = L.lib().q27_attn_decode_batched_exact if exact else L.lib().q27_attn_decode_batched
+    L.check(fn(arr, len(slots), q_stride, n_q_heads, n_kv_heads, head_dim, scale, stream_ptr(st),
+               kvk), "q27_attn_decode_batched")
+
+
+def attn_decode_partial(slots, lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim, scale,
+                        partial_out, st=None, kvk=0):
+    """Un-normalised {m, l, acc} per (slot, lane, head) over each slot's row window."""
+    arr = _slots(slots)
+    L.check(L.lib().q27_attn_decode_partial(arr, len(slots), lanes_stride, q_stride, n_q_heads,
+                                            n_kv_heads, head_dim, scale, partial_out.data_ptr(),
+                                            stream_ptr(st), kvk), "q27_attn_decode_partial")
+
+
+def attn_merge_partials(parts, nparts, npairs, out, st=None):
+    """LSE merge of ``nparts`` partial sets [nparts][npairs][258] -> out [npairs][256]."""
+    L.check(L.lib().q27_attn_merge_partials(parts.data_ptr(), nparts, npairs, out.data_ptr(),
+                                            stream_ptr(st)), "q27_attn_merge_partials")
+
+
+def attn_prefill_T(qT, q_stride, q_row, ktab, vtab, outT, out_row, part, base_pos, t0, SB,
+                   n_q_heads, n_kv_heads, head_dim, scale, st=None, kvk=0, exact=False):
+    """Causal GQA prefill attention for SB tokens starting at base_pos + t0."""
+    fn = L.lib().q27_attn_prefill_T_exact if exact else L.lib().q27_attn_prefill_T
+    L.check(fn(qT.data_ptr(), q_stride, q_row, ktab.data_ptr(), vtab.data_ptr(), outT.data_ptr(),
+               out_row, part.data_ptr() if part is not None else None, base_pos, t0, SB,
+               n_q_heads, n_kv_heads, head_dim, scale, stream_ptr(st), kvk), "q27_attn_prefill_T")
+
+
+def kv_dequant(tab, kvk, row0, nrows, n_kv_heads, out, st=None):
+    """Bit-exact dequantisation of cache rows to fp32 [nrows][n_kv_heads][256]."""
+    L.check(L.lib().q27_kv_dequant(tab.data_ptr(), kvk, row0, nrows, n_kv_heads, out.data_ptr(),
+                                   stream_ptr(st)), "q27_kv_dequant")

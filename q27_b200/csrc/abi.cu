@@ -1,0 +1,255 @@
+// The extern "C" surface: argument validation, split planning and dispatch. Nothing here
+// allocates or synchronises; every call only enqueues kernels on the caller's stream.
+#include <limits.h>
+
+#include "common.cuh"
+#include "decode_mma.cuh"
+
+namespace q27b {
+thread_local int g_last_cuda_error = 0;
+
+namespace {
+
+int sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cached[dev] == 0) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+            v = 148;
+        cached[dev] = v;
+    }
+    return cached[dev];
+}
+
+int check_geometry(int q_stride, int n_q, int n_kv, int head_dim, int kvk) {
+    if (kvk != Q27_KV_F16 && kvk != Q27_KV_FP8 && kvk != Q27_KV_T3) return Q27_ERR_UNSUPPORTED_KIND;
+    if (head_dim != HD || n_kv < 1 || n_kv > 8 || n_q != GQA * n_kv) return Q27_ERR_UNSUPPORTED_WIDTH;
+    if (q_stride < HD) return Q27_ERR_INVALID_ARG;
+    return Q27_OK;
+}
+
+// Copy and validate the caller's slot descriptors into the by-value kernel bundle.
+int build_batch(const q27_slot* slots, int nslots, int q_stride, int n_q, int n_kv, int head_dim,
+                float scale, int kvk, bool need_out, DevBatch& b) {
+    int rc = check_geometry(q_stride, n_q, n_kv, head_dim, kvk);
+    if (rc) return rc;
+    if (!slots || nslots < 1) return Q27_ERR_INVALID_ARG;
+    if (nslots > Q27_MAX_SLOTS) return Q27_ERR_UNSUPPORTED_WIDTH;
+    b.nslots = nslots;
+    b.max_ntok = 0;
+    int total_lanes = 0;
+    for (int i = 0; i < nslots; i++) {
+        const q27_slot& s = slots[i];
+        if (s.ntok < 1 || s.ntok > Q27_MAX_LANES) return Q27_ERR_UNSUPPORTED_WIDTH;
+        if (!s.ktab || !s.vtab || !s.scratch || s.row_base < 0 || s.row_count < 0)
+            return Q27_ERR_INVALID_ARG;
+        DevSlot& d = b.s[i];
+        d.ktab = s.ktab;
+        d.vtab = s.vtab;
+        d.scratch = s.scratch;
+        d.ntok = s.ntok;
+        d.row_base = s.row_base;
+        d.row_count = s.row_count;
+        d.pad = 0;
+        for (int t = 0; t < Q27_MAX_LANES; t++) {
+            const bool live = t < s.ntok;
+            if (live && (!s.q.p[t] || !s.pos.p[t] || (need_out && !s.out.p[t])))
+                return Q27_ERR_INVALID_ARG;
+            d.q[t] = live ? s.q.p[t] : nullptr; // dead slots may hold garbage: never forwarded
+            d.pos[t] = live ? s.pos.p[t] : nullptr;
+            d.out[t] = live ? s.out.p[t] : nullptr;
+        }
+        b.max_ntok = s.ntok > b.max_ntok ? s.ntok : b.max_ntok;
+        total_lanes += s.ntok;
+    }
+    for (int i = nslots; i < Q27_MAX_SLOTS; i++) b.s[i] = DevSlot{};
+    b.q_stride = q_stride;
+    b.n_q = n_q;
+    b.n_kv = n_kv;
+    b.scale = scale;
+    b.unit = 32;
+    (void)total_lanes;
+    return Q27_OK;
+}
+
+enum Family { FAM_AUTO = 0, FAM_EXACT = 1 };
+
+int run_decode(const q27_slot* slots, int nslots, int lanes_stride, int q_stride, int n_q, int n_kv,
+               int head_dim, float scale, float* partial_out, void* stream, int kvk, Family fam) {
+    DevBatch b;
+    int rc = build_batch(slots, nslots, q_stride, n_q, n_kv, head_dim, scale, kvk,
+                         partial_out == nullptr, b);
+    if (rc) return rc;
+    if (partial_out && (lanes_stride < b.max_ntok || lanes_stride > Q27_MAX_LANES))
+        return Q27_ERR_INVALID_ARG;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int sms = sm_count();
+    bool done = false;
+    if (fam == FAM_AUTO) {
+        rc = launch_decode_mma(b, kvk, sms, st, &done);
+        if (rc) return rc;
+    }
+    if (!done) {
+        // exact family: one CTA per (split, kv head, lane)
+        int lanes = b.nslots * b.max_ntok;
+        int ns = (16 * sms) / (n_kv * lanes);
+        b.nsplit = ns < 8 ? 8 : ns > Q27_MAX_SPLITS ? Q27_MAX_SPLITS : ns;
+        b.unit = 32;
+        rc = launch_exact_partials(b, kvk, st);
+        if (rc) return rc;
+    }
+    return launch_combine(b, partial_out, partial_out ? lanes_stride : b.max_ntok, st);
+}
+
+q27_slot single_slot(const q27_CP3* q, const void* const* ktab, const void* const* vtab,
+                     const q27_P3* out, float* scratch, const q27_IP3* pos, int ntok) {
+    q27_slot s{};
+    s.ktab = ktab;
+    s.vtab = vtab;
+    if (q) s.q = *q;
+    if (pos) s.pos = *pos;
+    if (out) s.out = *out;
+    s.scratch = scratch;
+    s.ntok = ntok;
+    s.row_base = 0;
+    s.row_count = INT_MAX;
+    return s;
+}
+
+} // namespace
+} // namespace q27b
+
+using namespace q27b;
+
+extern "C" {
+
+const char* q27_status_string(int status) {
+    switch (status) {
+    case Q27_OK: return "ok";
+    case Q27_ERR_INVALID_ARG: return "invalid argument";
+    case Q27_ERR_UNSUPPORTED_KIND: return "unsupported KV kind (refused, not mis-read)";
+    case Q27_ERR_UNSUPPORTED_WIDTH: return "unsupported width or geometry";
+    case Q27_ERR_CUDA: return "CUDA error (see q27_last_cuda_error)";
+    case Q27_ERR_TOO_LARGE: return "size exceeds a fixed capacity";
+    default: return "unknown status";
+    }
+}
+
+int q27_last_cuda_error(void) { return g_last_cuda_error; }
+
+int q27_device_arch(void) {
+    int dev = 0, mj = 0, mn = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (cudaDeviceGetAttribute(&mj, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return 0;
+    if (cudaDeviceGetAttribute(&mn, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) return 0;
+    return (mj == 10 && mn == 0) ? 1000 : 0; // the image holds sm_100a code only
+}
+
+int64_t q27_kv_row_bytes(int kvk, int n_kv_heads) {
+    if (kvk != Q27_KV_F16 && kvk != Q27_KV_FP8 && kvk != Q27_KV_T3) return -1;
+    return row_bytes_of(kvk, n_kv_heads);
+}
+
+int64_t q27_decode_scratch_floats(int ntok, int n_q_heads) {
+    return (int64_t)ntok * n_q_heads * Q27_MAX_SPLITS * Q27_PART_STRIDE;
+}
+
+int64_t q27_prefill_part_floats(int SB, int n_q_heads) {
+    return (int64_t)n_q_heads * ((SB + 15) / 16 * 16) * Q27_PF_SPLIT_MAX * Q27_PART_STRIDE;
+}
+
+int q27_attn_decode3(const q27_CP3* q, int q_stride, const void* const* ktab,
+                     const void* const* vtab, const q27_P3* out, float* scratch,
+                     const q27_IP3* pos, int max_ctx, int n_q_heads, int n_kv_heads,
+                     int head_dim, float scale, void* stream, int ntok, int kvk) {
+    (void)max_ctx;
+    if (!q || !out || !pos) return Q27_ERR_INVALID_ARG;
+    if (ntok < 1 || ntok > Q27_MAX_LANES) return Q27_ERR_UNSUPPORTED_WIDTH;
+    q27_slot s = single_slot(q, ktab, vtab, out, scratch, pos, ntok);
+    return run_decode(&s, 1, 0, q_stride, n_q_heads, n_kv_heads, head_dim, scale, nullptr, stream,
+                      kvk, FAM_AUTO);
+}
+
+int q27_attn_decode(const float* q, int q_stride, const void* const* ktab,
+                    const void* const* vtab, float* out, float* scratch, const int* d_pos,
+                    int max_ctx, int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                    void* stream, int kvk) {
+    q27_CP3 qp{};
+    q27_P3 op{};
+    q27_IP3 pp{};
+    qp.p[0] = q;
+    op.p[0] = out;
+    pp.p[0] = d_pos;
+    return q27_attn_decode3(&qp, q_stride, ktab, vtab, &op, scratch, &pp, max_ctx, n_q_heads,
+                            n_kv_heads, head_dim, scale, stream, 1, kvk);
+}
+
+int q27_attn_decode_batched(const q27_slot* slots, int nslots, int q_stride, int n_q_heads,
+                            int n_kv_heads, int head_dim, float scale, void* stream, int kvk) {
+    return run_decode(slots, nslots, 0, q_stride, n_q_heads, n_kv_heads, head_dim, scale, nullptr,
+                      stream, kvk, FAM_AUTO);
+}
+
+int q27_attn_decode_batched_exact(const q27_slot* slots, int nslots, int q_stride, int n_q_heads,
+                                  int n_kv_heads, int head_dim, float scale, void* stream,
+                                  int kvk) {
+    return run_decode(slots, nslots, 0, q_stride, n_q_heads, n_kv_heads, head_dim, scale, nullptr,
+                      stream, kvk, FAM_EXACT);
+}
+
+int q27_attn_decode_partial(const q27_slot* slots, int nslots, int lanes_stride, int q_stride,
+                            int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                            float* partial_out, void* stream, int kvk) {
+    if (!partial_out) return Q27_ERR_INVALID_ARG;
+    return run_decode(slots, nslots, lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim, scale,
+                      partial_out, stream, kvk, FAM_AUTO);
+}
+
+int q27_attn_merge_partials(const float* parts, int nparts, int64_t npairs, float* out,
+                            void* stream) {
+    if (!parts || !out || nparts < 1 || npairs < 0) return Q27_ERR_INVALID_ARG;
+    if (npairs == 0) return Q27_OK;
+    if (npairs > INT_MAX) return Q27_ERR_TOO_LARGE;
+    return launch_merge(parts, nparts, npairs, out, static_cast<cudaStream_t>(stream));
+}
+
+int q27_attn_prefill_T_exact(const float* qT, int q_stride, int q_row, const void* const* ktab,
+                             const void* const* vtab, float* outT, int out_row, float* part,
+                             int base_pos, int t0, int SB, int n_q_heads, int n_kv_heads,
+                             int head_dim, float scale, void* stream, int kvk) {
+    (void)part;
+    int rc = check_geometry(q_stride, n_q_heads, n_kv_heads, head_dim, kvk);
+    if (rc) return rc;
+    if (!qT || !ktab || !vtab || !outT || base_pos < 0 || t0 < 0 || SB < 0 ||
+        q_row < n_q_heads * HD || out_row < n_q_heads * HD)
+        return Q27_ERR_INVALID_ARG;
+    if (SB == 0) return Q27_OK;
+    return launch_prefill_exact(qT, q_stride, q_row, ktab, vtab, outT, out_row, base_pos, t0, SB,
+                                n_q_heads, n_kv_heads, scale, static_cast<cudaStream_t>(stream),
+                                kvk);
+}
+
+int q27_attn_prefill_T(const float* qT, int q_stride, int q_row, const void* const* ktab,
+                       const void* const* vtab, float* outT, int out_row, float* part,
+                       int base_pos, int t0, int SB, int n_q_heads, int n_kv_heads,
+                       int head_dim, float scale, void* stream, int kvk) {
+    return q27_attn_prefill_T_exact(qT, q_stride, q_row, ktab, vtab, outT, out_row, part, base_pos,
+                                    t0, SB, n_q_heads, n_kv_heads, head_dim, scale, stream, kvk);
+}
+
+int q27_kv_dequant(const void* const* tab, int kvk, int row0, int nrows, int n_kv_heads,
+                   float* out, void* stream) {
+    if (kvk != Q27_KV_F16 && kvk != Q27_KV_FP8 && kvk != Q27_KV_T3) return Q27_ERR_UNSUPPORTED_KIND;
+    if (!tab || !out || row0 < 0 || nrows < 0 || n_kv_heads < 1) return Q27_ERR_INVALID_ARG;
+    return launch_kv_dequant(tab, kvk, row0, nrows, n_kv_heads, out,
+                             static_cast<cudaStream_t>(stream));
+}
+
+int q27_mk_tab(const void* base, size_t row_bytes, int rows, void** d_tab, void* stream) {
+    if (!base || !d_tab || row_bytes == 0 || rows < 0) return Q27_ERR_INVALID_ARG;
+    return launch_mk_tab(base, row_bytes, rows, d_tab, static_cast<cudaStream_t>(stream));
+}
+
+} // extern "C"

@@ -1,0 +1,312 @@
+// Exact (fp32 scalar) attention family: split-KV partials, the log-sum-exp combine / merge
+// kernels, and a scalar causal prefill. These kernels decode every cache element with the
+// bit-exact decoders of common.cuh and do all arithmetic in fp32 with expf, so they are the
+// engine's tight-tolerance path (the class of the reference's k_attn_fd2, src/spec3.cu:804-921,
+// and k_attn_prefill_T, src/prefill.cu:2293-2388). The tensor-core kernels are checked
+// against them on the GPU and against the CPU oracle.
+#include "common.cuh"
+
+namespace q27b {
+
+namespace {
+
+constexpr int EX_WARPS = 4;
+
+// Partial over one (split, kv head, slot-lane). Warp w walks rows lo+w, lo+w+4, ...; lane
+// owns dims [8*lane, 8*lane+8); the six query heads of the KV head share every row read.
+template <int KVK>
+__global__ void __launch_bounds__(EX_WARPS * 32)
+k_exact_partial(const __grid_constant__ DevBatch b) {
+    const int sp = blockIdx.x, kvh = blockIdx.y;
+    const int slot = blockIdx.z / b.max_ntok, t = blockIdx.z % b.max_ntok;
+    const DevSlot& S = b.s[slot];
+    if (t >= S.ntok) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // slot-wide chunking from the longest lane (all lanes share split boundaries)
+    int max_len = 0;
+    for (int u = 0; u < S.ntok; u++)
+        max_len = max(max_len, local_len(__ldg(S.pos[u]), S.row_base, S.row_count));
+    const int my_len = local_len(__ldg(S.pos[t]), S.row_base, S.row_count);
+    const int chunk = split_chunk(max_len, b.nsplit, b.unit);
+    const int lo = sp * chunk, hi = min(my_len, lo + chunk);
+
+    float* dst0 = S.scratch + (((size_t)t * b.n_q + kvh * GQA) * b.nsplit + sp) * PART;
+    if (lo >= hi) { // empty window: stamp the sentinel so the combine can skip it
+        if (threadIdx.x < GQA) {
+            float* d = dst0 + (size_t)threadIdx.x * b.nsplit * PART;
+            d[0] = NEG_SENTINEL;
+            d[1] = 0.f;
+        }
+        return;
+    }
+
+    __shared__ float s_q[GQA][HD];
+    __shared__ float s_acc[GQA][HD];
+    __shared__ float s_ml[EX_WARPS][GQA][2];
+    for (int i = threadIdx.x; i < GQA * HD; i += blockDim.x) {
+        s_q[i / HD][i % HD] = S.q[t][(size_t)(kvh * GQA + i / HD) * b.q_stride + (i % HD)];
+        s_acc[i / HD][i % HD] = 0.f;
+    }
+    __syncthreads();
+
+    float qr[GQA][8];
+#pragma unroll
+    for (int j = 0; j < GQA; j++)
+#pragma unroll
+        for (int i = 0; i < 8; i++) qr[j][i] = s_q[j][8 * lane + i];
+
+    float m[GQA], l[GQA], acc[GQA][8];
+#pragma unroll
+    for (int j = 0; j < GQA; j++) {
+        m[j] = NEG_SENTINEL;
+        l[j] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) acc[j][i] = 0.f;
+    }
+
+    for (int p = lo + warp; p < hi;) {
+        const int pg = p >> PAGE_SHIFT;
+        const int pend = min(hi, (pg + 1) << PAGE_SHIFT);
+        const uint8_t* kpage = static_cast<const uint8_t*>(S.ktab[pg]);
+        const uint8_t* vpage = static_cast<const uint8_t*>(S.vtab[pg]);
+        for (; p < pend; p += EX_WARPS) {
+            float kv[8], vv[8];
+            load8_exact<KVK>(kpage, p & (PAGE - 1), b.n_kv, kvh, 8 * lane, kv);
+            load8_exact<KVK>(vpage, p & (PAGE - 1), b.n_kv, kvh, 8 * lane, vv);
+#pragma unroll
+            for (int j = 0; j < GQA; j++) {
+                float d = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; i++) d = fmaf(qr[j][i], kv[i], d);
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+                d *= b.scale;
+                const float mn = fmaxf(m[j], d);
+                const float so = expf(m[j] - mn), w = expf(d - mn);
+                l[j] = l[j] * so + w;
+                m[j] = mn;
+#pragma unroll
+                for (int i = 0; i < 8; i++) acc[j][i] = acc[j][i] * so + w * vv[i];
+            }
+        }
+    }
+
+    if (lane == 0)
+#pragma unroll
+        for (int j = 0; j < GQA; j++) { s_ml[warp][j][0] = m[j]; s_ml[warp][j][1] = l[j]; }
+    __syncthreads();
+    // warps add their rescaled accumulators in warp order: run-to-run bitwise stable
+    for (int w = 0; w < EX_WARPS; w++) {
+        if (warp == w) {
+#pragma unroll
+            for (int j = 0; j < GQA; j++) {
+                float mb = NEG_SENTINEL;
+#pragma unroll
+                for (int u = 0; u < EX_WARPS; u++) mb = fmaxf(mb, s_ml[u][j][0]);
+                const float sc = m[j] == NEG_SENTINEL ? 0.f : expf(m[j] - mb);
+#pragma unroll
+                for (int i = 0; i < 8; i++) s_acc[j][8 * lane + i] += acc[j][i] * sc;
+            }
+        }
+        __syncthreads();
+    }
+    for (int j = warp; j < GQA; j += EX_WARPS) {
+        float mb = NEG_SENTINEL;
+        for (int u = 0; u < EX_WARPS; u++) mb = fmaxf(mb, s_ml[u][j][0]);
+        float lb = 0.f;
+        for (int u = 0; u < EX_WARPS; u++)
+            lb += s_ml[u][j][0] == NEG_SENTINEL ? 0.f : s_ml[u][j][1] * expf(s_ml[u][j][0] - mb);
+        float* d = dst0 + (size_t)j * b.nsplit * PART;
+        if (lane == 0) { d[0] = mb; d[1] = lb; }
+        for (int i = lane; i < HD; i += 32) d[2 + i] = s_acc[j][i];
+    }
+}
+
+// Merge the nsplit partials of one (slot, lane, head). NORMALISE: write out = acc / l to the
+// lane's output row; otherwise write the merged {m, l, acc} for a cross-GPU merge.
+template <bool NORMALISE>
+__global__ void __launch_bounds__(256)
+k_combine(const __grid_constant__ DevBatch b, float* __restrict__ partial_out, int lanes_stride) {
+    const int h = blockIdx.x, t = blockIdx.y, slot = blockIdx.z;
+    const DevSlot& S = b.s[slot];
+    if (t >= S.ntok) {
+        if (!NORMALISE && t < lanes_stride) { // keep padded lanes well-defined for collectives
+            float* d = partial_out + (((size_t)slot * lanes_stride + t) * b.n_q + h) * PART;
+            for (int i = threadIdx.x; i < PART; i += blockDim.x)
+                d[i] = i == 0 ? NEG_SENTINEL : 0.f;
+        }
+        return;
+    }
+    const float* pp = S.scratch + ((size_t)t * b.n_q + h) * b.nsplit * PART;
+    __shared__ float s_m, s_l;
+    __shared__ float s_w[Q27_MAX_SPLITS];
+    if (threadIdx.x < 32) {
+        float mg = NEG_SENTINEL;
+        for (int sp = threadIdx.x; sp < b.nsplit; sp += 32) mg = fmaxf(mg, pp[(size_t)sp * PART]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, off));
+        float lg = 0.f;
+        for (int sp = threadIdx.x; sp < b.nsplit; sp += 32) {
+            const float ms = pp[(size_t)sp * PART];
+            const float w = ms == NEG_SENTINEL ? 0.f : expf(ms - mg);
+            s_w[sp] = w;
+            lg += pp[(size_t)sp * PART + 1] * w;
+        }
+        // fixed-shape tree: the same order every run
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) lg += __shfl_xor_sync(0xffffffffu, lg, off);
+        if (threadIdx.x == 0) { s_m = mg; s_l = lg; }
+    }
+    __syncthreads();
+    const float lg = s_l;
+    const float inv = lg > 0.f ? 1.0f / lg : 0.f;
+    for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+        float a = 0.f;
+        for (int sp = 0; sp < b.nsplit; sp++) {
+            const float w = s_w[sp];
+            if (w != 0.f) a += pp[(size_t)sp * PART + 2 + d] * w;
+        }
+        if (NORMALISE) S.out[t][(size_t)h * HD + d] = a * inv;
+        else partial_out[(((size_t)slot * lanes_stride + t) * b.n_q + h) * PART + 2 + d] = a;
+    }
+    if (!NORMALISE && threadIdx.x == 0) {
+        float* d = partial_out + (((size_t)slot * lanes_stride + t) * b.n_q + h) * PART;
+        d[0] = s_m;
+        d[1] = lg;
+    }
+}
+
+// parts: [nparts][npairs][258] -> out [npairs][256] normalised
+__global__ void __launch_bounds__(256)
+k_merge(const float* __restrict__ parts, int nparts, int64_t npairs, float* __restrict__ out) {
+    const int64_t w = blockIdx.x;
+    float mg = NEG_SENTINEL;
+    for (int s = 0; s < nparts; s++) mg = fmaxf(mg, parts[((size_t)s * npairs + w) * PART]);
+    float lg = 0.f;
+    for (int s = 0; s < nparts; s++) {
+        const float* pp = parts + ((size_t)s * npairs + w) * PART;
+        if (pp[0] != NEG_SENTINEL) lg += pp[1] * expf(pp[0] - mg);
+    }
+    const float inv = lg > 0.f ? 1.0f / lg : 0.f;
+    for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+        float a = 0.f;
+        for (int s = 0; s < nparts; s++) {
+            const float* pp = parts + ((size_t)s * npairs + w) * PART;
+            if (pp[0] != NEG_SENTINEL) a += pp[2 + d] * expf(pp[0] - mg);
+        }
+        out[(size_t)w * HD + d] = a * inv;
+    }
+}
+
+// Scalar causal prefill: one warp per (token, kv head), six heads per warp, rows read
+// straight from the paged cache (neighbouring tokens share them through L1/L2).
+constexpr int PFX_WARPS = 8;
+template <int KVK>
+__global__ void __launch_bounds__(PFX_WARPS * 32)
+k_prefill_exact(const float* __restrict__ qT, int q_stride, int q_row,
+                const void* const* __restrict__ ktab, const void* const* __restrict__ vtab,
+                float* __restrict__ outT, int out_row, int base_pos, int t0, int t_end, int n_kv,
+                float scale) {
+    const int kvh = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = t0 + blockIdx.y * PFX_WARPS + warp;
+    if (t >= t_end) return;
+    const int bound = base_pos + t + 1;
+    float qr[GQA][8], m[GQA], l[GQA], acc[GQA][8];
+#pragma unroll
+    for (int j = 0; j < GQA; j++) {
+        m[j] = NEG_SENTINEL;
+        l[j] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            acc[j][i] = 0.f;
+            qr[j][i] = qT[(size_t)t * q_row + (size_t)(kvh * GQA + j) * q_stride + 8 * lane + i];
+        }
+    }
+    for (int p = 0; p < bound;) {
+        const int pg = p >> PAGE_SHIFT;
+        const int pend = min(bound, (pg + 1) << PAGE_SHIFT);
+        const uint8_t* kpage = static_cast<const uint8_t*>(ktab[pg]);
+        const uint8_t* vpage = static_cast<const uint8_t*>(vtab[pg]);
+        for (; p < pend; p++) {
+            float kv[8], vv[8];
+            load8_exact<KVK>(kpage, p & (PAGE - 1), n_kv, kvh, 8 * lane, kv);
+            load8_exact<KVK>(vpage, p & (PAGE - 1), n_kv, kvh, 8 * lane, vv);
+#pragma unroll
+            for (int j = 0; j < GQA; j++) {
+                float d = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; i++) d = fmaf(qr[j][i], kv[i], d);
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+                d *= scale;
+                const float mn = fmaxf(m[j], d);
+                const float so = expf(m[j] - mn), w = expf(d - mn);
+                l[j] = l[j] * so + w;
+                m[j] = mn;
+#pragma unroll
+                for (int i = 0; i < 8; i++) acc[j][i] = acc[j][i] * so + w * vv[i];
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < GQA; j++) {
+        const float inv = 1.0f / l[j];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            outT[(size_t)t * out_row + (size_t)(kvh * GQA + j) * HD + 8 * lane + i] = acc[j][i] * inv;
+    }
+}
+
+} // namespace
+
+int launch_exact_partials(const DevBatch& b, int kvk, cudaStream_t st) {
+    dim3 grid(b.nsplit, b.n_kv, b.nslots * b.max_ntok);
+    if (kvk == Q27_KV_F16) k_exact_partial<Q27_KV_F16><<<grid, EX_WARPS * 32, 0, st>>>(b);
+    else if (kvk == Q27_KV_FP8) k_exact_partial<Q27_KV_FP8><<<grid, EX_WARPS * 32, 0, st>>>(b);
+    else if (kvk == Q27_KV_T3) k_exact_partial<Q27_KV_T3><<<grid, EX_WARPS * 32, 0, st>>>(b);
+    else return Q27_ERR_UNSUPPORTED_KIND;
+    Q27_CUDA_TRY(cudaGetLastError());
+    return Q27_OK;
+}
+
+int launch_combine(const DevBatch& b, float* partial_out, int lanes_stride, cudaStream_t st) {
+    if (partial_out) {
+        dim3 grid(b.n_q, lanes_stride, b.nslots);
+        k_combine<false><<<grid, 256, 0, st>>>(b, partial_out, lanes_stride);
+    } else {
+        dim3 grid(b.n_q, b.max_ntok, b.nslots);
+        k_combine<true><<<grid, 256, 0, st>>>(b, nullptr, b.max_ntok);
+    }
+    Q27_CUDA_TRY(cudaGetLastError());
+    return Q27_OK;
+}
+
+int launch_merge(const float* parts, int nparts, int64_t npairs, float* out, cudaStream_t st) {
+    k_merge<<<(unsigned)npairs, 256, 0, st>>>(parts, nparts, npairs, out);
+    Q27_CUDA_TRY(cudaGetLastError());
+    return Q27_OK;
+}
+
+int launch_prefill_exact(const float* qT, int q_stride, int q_row, const void* const* ktab,
+                         const void* const* vtab, float* outT, int out_row, int base_pos, int t0,
+                         int SB, int n_q, int n_kv, float scale, cudaStream_t st, int kvk) {
+    (void)n_q;
+    dim3 grid(n_kv, (SB + PFX_WARPS - 1) / PFX_WARPS);
+    const int te = t0 + SB;
+    if (kvk == Q27_KV_F16)
+        k_prefill_exact<Q27_KV_F16><<<grid, PFX_WARPS * 32, 0, st>>>(
+            qT, q_stride, q_row, ktab, vtab, outT, out_row, base_pos, t0, te, n_kv, scale);
+    else if (kvk == Q27_KV_FP8)
+        k_prefill_exact<Q27_KV_FP8><<<grid, PFX_WARPS * 32, 0, st>>>(
+            qT, q_stride, q_row, ktab, vtab, outT, out_row, base_pos, t0, te, n_kv, scale);
+    else if (kvk == Q27_KV_T3)
+        k_prefill_exact<Q27_KV_T3><<<grid, PFX_WARPS * 32, 0, st>>>(
+            qT, q_stride, q_row, ktab, vtab, outT, out_row, base_pos, t0, te, n_kv, scale);
+    else return Q27_ERR_UNSUPPORTED_KIND;
+    Q27_CUDA_TRY(cudaGetLastError());
+    return Q27_OK;
+}
+
+} // namespace q27b

@@ -1,0 +1,142 @@
+// Shared definitions of the sm_100a attention engine: geometry, status plumbing, KV-format
+// element decoders (bit-exact to the reference codec) and the per-launch argument bundles.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <float.h>
+#include <stdint.h>
+
+#include "../../include/q27_b200.h"
+
+namespace q27b {
+
+constexpr int HD = Q27_HEAD_DIM;       // 256
+constexpr int GQA = Q27_GQA;           // 6 query heads per KV head
+constexpr int PAGE = Q27_KV_PAGE;      // 64 rows per page (src/cuda_common.h:70)
+constexpr int PAGE_SHIFT = 6;
+constexpr int PART = Q27_PART_STRIDE;  // 258 floats: m, l, acc[256]
+constexpr int T3_BLK = Q27_T3_BLOCK_BYTES;
+constexpr float NEG_SENTINEL = -FLT_MAX; // "empty partial" marker (src/prefill.cu:1353-1362)
+
+// Per-thread record of the last failing CUDA call (read by q27_last_cuda_error()).
+extern thread_local int g_last_cuda_error;
+
+#define Q27_CUDA_TRY(expr)                                  \
+    do {                                                    \
+        cudaError_t e__ = (expr);                           \
+        if (e__ != cudaSuccess) {                           \
+            q27b::g_last_cuda_error = (int)e__;             \
+            return Q27_ERR_CUDA;                            \
+        }                                                   \
+    } while (0)
+
+// One slot as the kernels see it (device-visible copy of q27_slot, passed by value as a
+// __grid_constant__ parameter so no descriptor memory has to be allocated or copied).
+struct DevSlot {
+    const void* const* ktab;
+    const void* const* vtab;
+    const float* q[Q27_MAX_LANES];
+    const int* pos[Q27_MAX_LANES];
+    float* out[Q27_MAX_LANES];
+    float* scratch;  // partials: [lane][head][nsplit][258]
+    int ntok;
+    int row_base;
+    int row_count;
+    int pad;
+};
+struct DevBatch {
+    DevSlot s[Q27_MAX_SLOTS];
+    int nslots;
+    int nsplit;     // position splits per slot
+    int max_ntok;   // widest slot (grid extent of the lane axis)
+    int q_stride;
+    int n_q;
+    int n_kv;
+    float scale;
+    int unit;       // split granularity in rows (chunk is a multiple of it)
+};
+static_assert(sizeof(DevBatch) <= 4000, "DevBatch must fit the kernel parameter space");
+
+// Rows of the slot's tables a lane may read: [0, local_len). Lane t attends logical rows
+// [0, pos_t]; the tables hold logical rows [row_base, row_base + row_count).
+__host__ __device__ __forceinline__ int local_len(int pos, int row_base, int row_count) {
+    long long n = (long long)pos + 1 - row_base;
+    if (n < 0) n = 0;
+    if (n > row_count) n = row_count;
+    return (int)n;
+}
+
+// Split geometry shared by the partial kernels and the combine: the slot's longest lane
+// decides the chunk; every lane uses the same chunk boundaries (one KV pass serves all).
+__host__ __device__ __forceinline__ int split_chunk(int max_len, int nsplit, int unit) {
+    int c = (max_len + nsplit - 1) / nsplit;
+    c = (c + unit - 1) / unit * unit;
+    return c < unit ? unit : c;
+}
+
+// ---- element decoders ---------------------------------------------------------------
+
+// fp32 turbo3 centroids (src/turbo3.cuh:38-40); idx = low2 | hi << 2
+static __device__ __constant__ float kT3Centroid[8] = {-0.190207f, -0.118786f, -0.066822f,
+                                                      -0.021663f, 0.021663f,  0.066822f,
+                                                      0.118786f,  0.190207f};
+
+__device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
+    __half_raw hr = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3);
+    return __half2float(__half(hr));
+}
+
+// 8 consecutive elements (d0 multiple of 8) of one (row, kv head) slice as fp32.
+// Bit-exact to kv2f (src/cuda_common.h:113-114) and turbo3_deq_elem (src/turbo3.cuh:134).
+template <int KVK>
+__device__ __forceinline__ void load8_exact(const uint8_t* __restrict__ page, int r, int n_kv,
+                                            int kvh, int d0, float* o) {
+    if constexpr (KVK == Q27_KV_F16) {
+        const uint4 v = *reinterpret_cast<const uint4*>(
+            page + ((size_t)(r * n_kv + kvh) * HD + d0) * 2);
+        const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float2 f = __half22float2(h[i]);
+            o[2 * i] = f.x;
+            o[2 * i + 1] = f.y;
+        }
+    } else if constexpr (KVK == Q27_KV_FP8) {
+        const uint2 v =
+            *reinterpret_cast<const uint2*>(page + (size_t)(r * n_kv + kvh) * HD + d0);
+        const uint8_t* b = reinterpret_cast<const uint8_t*>(&v);
+#pragma unroll
+        for (int i = 0; i < 8; i++) o[i] = e4m3_to_f32(b[i]);
+    } else {
+        // block = 50 B: fp16 norm @0, qs[32] @2 (2 bits/elem), signs[16] @34 (1 bit/elem)
+        const uint8_t* blk = page + ((size_t)(r * n_kv + kvh) * 2 + (d0 >> 7)) * T3_BLK;
+        const int j0 = d0 & 127;
+        const float norm = __half2float(*reinterpret_cast<const __half*>(blk));
+        const uint32_t qs = *reinterpret_cast<const uint16_t*>(blk + 2 + (j0 >> 2));
+        const uint32_t sg = blk[34 + (j0 >> 3)];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            int idx = ((qs >> (2 * i)) & 3) | (((sg >> i) & 1) << 2);
+            o[i] = kT3Centroid[idx] * norm;
+        }
+    }
+}
+
+__host__ __device__ __forceinline__ int row_bytes_of(int kvk, int n_kv) {
+    return kvk == Q27_KV_F16 ? n_kv * HD * 2 : kvk == Q27_KV_FP8 ? n_kv * HD : n_kv * 2 * T3_BLK;
+}
+
+// ---- launch entry points implemented per translation unit -----------------------------
+// exact (fp32 scalar) family
+int launch_exact_partials(const DevBatch& b, int kvk, cudaStream_t st);
+int launch_combine(const DevBatch& b, float* partial_out, int lanes_stride, cudaStream_t st);
+int launch_merge(const float* parts, int nparts, int64_t npairs, float* out, cudaStream_t st);
+int launch_prefill_exact(const float* qT, int q_stride, int q_row, const void* const* ktab,
+                         const void* const* vtab, float* outT, int out_row, int base_pos, int t0,
+                         int SB, int n_q, int n_kv, float scale, cudaStream_t st, int kvk);
+int launch_kv_dequant(const void* const* tab, int kvk, int row0, int nrows, int n_kv, float* out,
+                      cudaStream_t st);
+int launch_mk_tab(const void* base, size_t row_bytes, int rows, void** d_tab, cudaStream_t st);
+
+} // namespace q27b

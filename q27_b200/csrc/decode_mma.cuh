@@ -1,0 +1,10 @@
+// Tensor-core decode family (split-KV partials through an mbarrier-guarded shared-memory
+// ring fed by bulk async copies). launch_decode_mma sets *done = true when it has written
+// the partials for the batch (and the split geometry in `b`); false means the shape is not
+// covered and the caller must run the exact family.
+#pragma once
+#include "common.cuh"
+
+namespace q27b {
+int launch_decode_mma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool* done);
+}

@@ -1,0 +1,55 @@
+"""Generates tests/golden/turbo3_codec.npz from the REFERENCE's own code: the CPU turbo3
+codec in tools/turbo3_test.cu and the CUDA toolkit's host fp16/e4m3 converters, both built
+from the reference tree into oracle/_ref/libq27ref_codec.so by oracle/Makefile.
+
+Run in a container that has the reference tree:  make -C oracle ref && python tests/golden/make_golden.py
+The inputs come from an LCG of the kind the reference's tools use
+(tools/turbo3_test.cu:95-96); no oracle code is involved in producing the fixture."""
+import ctypes as C
+import sys
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent.parent.parent
+sys.path.insert(0, str(ROOT))
+from tests.oracle_lib import RefCodec  # noqa: E402
+
+_fp = C.POINTER(C.c_float)
+
+
+def lcg_floats(n, seed, scale):
+    s = np.uint32(seed)
+    out = np.empty(n, np.float32)
+    with np.errstate(over="ignore"):
+        for i in range(n):
+            s = np.uint32(s * np.uint32(1664525) + np.uint32(1013904223))
+            out[i] = (float((int(s) >> 8) & 0xFFFF) / 65536.0 - 0.5) * scale
+    return out
+
+
+def main():
+    ref = RefCodec()
+    ngroups = 128  # 16 rows x 4 kv heads x 2 blocks
+    x = lcg_floats(ngroups * 128, 1234567, 2.0).reshape(ngroups, 128)
+    x[::7] *= 8.0
+    x[5] = 0.0
+    blocks = np.zeros((ngroups, 50), np.uint8)
+    deq = np.zeros((ngroups, 128), np.float32)
+    fw = x.copy()
+    for i in range(ngroups):
+        ref.lib.q27ref_cpu_quant(x[i].ctypes.data_as(_fp), blocks[i].ctypes.data_as(C.c_void_p))
+        ref.lib.q27ref_cpu_dequant(blocks[i].ctypes.data_as(C.c_void_p), deq[i].ctypes.data_as(_fp))
+        ref.lib.q27ref_cpu_fwht(fw[i].ctypes.data_as(_fp))
+    conv_in = np.concatenate([lcg_floats(2048, 99, s) for s in (1e-6, 1e-3, 1.0, 40.0, 1000.0, 2e5)])
+    half_bits = np.array([ref.lib.q27ref_float_to_half(float(v)) for v in conv_in], np.uint16)
+    e4m3_bits = np.array([ref.lib.q27ref_float_to_e4m3(float(v)) for v in conv_in], np.uint8)
+    e4m3_table = np.array([ref.lib.q27ref_e4m3_to_float(b) for b in range(256)], np.float32)
+    np.savez_compressed(Path(__file__).parent / "turbo3_codec.npz", x=x, blocks=blocks, dequant=deq,
+                        fwht=fw, conv_in=conv_in, half_bits=half_bits, e4m3_bits=e4m3_bits,
+                        e4m3_table=e4m3_table)
+    print("wrote turbo3_codec.npz", blocks.shape, conv_in.shape)
+
+
+if __name__ == "__main__":
+    main()

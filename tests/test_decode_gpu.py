@@ -1,0 +1,190 @@
+"""GPU parity tests of decode / verify attention through the C ABI, against the CPU oracle
+(and, when oracle/_ref was built, against the reference's own fd2 kernels on this GPU).
+
+Matrix follows the reference's test_attn_fd2 (src/test_kernels.cu:843-1049): sequence
+lengths {1, 47, 1024, 16384, 61440} x ntok {1, 5} x formats, NaN-poisoned scratch,
+run-to-run bitwise repeat, and the scattered page table proof (Q27_KV_SCATTER)."""
+import numpy as np
+import pytest
+import torch
+
+import q27_b200 as Q
+from tests import synth
+from tests.gpu_util import SCALE, DeviceCase, RefGpu
+from tests.oracle_lib import KV_F16, KV_FP8, KV_T3, REF_GPU_SO
+
+pytestmark = pytest.mark.gpu
+KINDS = [KV_F16, KV_FP8, KV_T3]
+
+# tight bar for the fp32 "exact" family: max-abs/RMS, the reference's own gate for fd2
+# (1e-4 fp16/fp8, 2e-4 turbo3: src/test_kernels.cu:981,1521)
+EXACT_TOL = {KV_F16: 1e-4, KV_FP8: 1e-4, KV_T3: 2e-4}
+
+
+def lanes_for(seq, ntok):
+    # verify lanes sit at P+1+t (src/spec3.cu:1319-1326): the last lane sees the whole cache
+    return [max(seq - ntok + t, 0) for t in range(ntok)]
+
+
+@pytest.mark.parametrize("kvk", KINDS)
+def test_dequant_is_bit_exact(oracle, cuda, kvk):
+    c = synth.make_case(oracle, kvk, rows=200, pos=[199], seed=5, outlier_frac=0.02)
+    dc = DeviceCase(c, cuda, scatter_seed=3)
+    for side, raw in ((dc.kside, c.k), (dc.vside, c.v)):
+        out = torch.empty((150, 4, 256), device=cuda)
+        Q.kv_dequant(side.tab, kvk, 37, 150, 4, out)
+        ref = oracle.kv_dequant(raw[37:187], kvk, 150)
+        assert (out.cpu().numpy().view(np.uint32) == ref.view(np.uint32)).all()
+
+
+@pytest.mark.parametrize("kvk", KINDS)
+@pytest.mark.parametrize("ntok", [1, 5])
+@pytest.mark.parametrize("seq", [1, 47, 1024, 16384, 61440])
+def test_decode_vs_oracle(oracle, cuda, kvk, ntok, seq):
+    c = synth.make_case(oracle, kvk, rows=seq, pos=lanes_for(seq, ntok), seed=100 + seq % 97)
+    ref = oracle.attn_decode(c.q, c.k, c.v, kvk, c.pos)
+    dc = DeviceCase(c, cuda)
+    exact = dc.run3(exact=True)
+    rms = np.sqrt((ref.astype(np.float64) ** 2).mean()) + 1e-12
+    assert np.abs(exact - ref).max() / rms < EXACT_TOL[kvk]
+    got = dc.run3()
+    ok, excess, rel = synth.tolerance_ok(got, ref)   # 2e-3 abs + 1e-3 rel (BASELINE)
+    assert ok, (excess, rel)
+    assert rel < 1e-2                                 # the reference's fp16-MMA class bar
+    again = dc.run3()
+    assert (again.view(np.uint32) == got.view(np.uint32)).all()   # run-to-run bitwise
+
+
+@pytest.mark.parametrize("kvk", KINDS)
+def test_scattered_pages_and_untouched_gate(oracle, cuda, kvk):
+    c = synth.make_case(oracle, kvk, rows=1500, pos=[1499, 700, 64], seed=77, outlier_frac=0.02)
+    c.q[:, :, 256:] = np.nan                      # the gate half must never be read
+    ref = oracle.attn_decode(c.q, c.k, c.v, kvk, c.pos)
+    dc = DeviceCase(c, cuda, scatter_seed=11)
+    qcopy = [t.clone() for t in dc.q]
+    for exact in (True, False):
+        got = dc.run3(exact=exact)
+        ok, excess, rel = synth.tolerance_ok(got, ref)
+        assert ok and np.isfinite(got).all(), (exact, excess, rel)
+    for a, b in zip(dc.q, qcopy):
+        assert torch.equal(a.view(torch.int32), b.view(torch.int32))  # q||gate left as is
+
+
+def test_attn_decode_single_token_entry(oracle, cuda):
+    c = synth.make_case(oracle, KV_F16, rows=4096, pos=[4095], seed=1)
+    ref = oracle.attn_decode(c.q, c.k, c.v, KV_F16, c.pos)
+    dc = DeviceCase(c, cuda)
+    Q.attn_decode(dc.q[0], synth.Q_STRIDE, dc.kside.tab, dc.vside.tab, dc.out[0], dc.scratch,
+                  dc.pos[0], 4096, 24, 4, 256, SCALE, kvk=KV_F16)
+    torch.cuda.synchronize()
+    ok, excess, rel = synth.tolerance_ok(dc.out[0].cpu().numpy(), ref[0])
+    assert ok, (excess, rel)
+
+
+def test_positions_are_read_on_device(oracle, cuda):
+    # the same launch arguments, new *pos contents: graph-stable control (src/spec3.cu:628)
+    c = synth.make_case(oracle, KV_FP8, rows=900, pos=[899, 500], seed=9)
+    dc = DeviceCase(c, cuda)
+    dc.run3()
+    for newpos in ([10, 899], [0, 0]):
+        for t, p in enumerate(newpos):
+            dc.pos[t].fill_(p)
+        got = dc.run3()
+        ref = oracle.attn_decode(c.q, c.k, c.v, KV_FP8, newpos)
+        assert synth.tolerance_ok(got, ref)[0]
+
+
+@pytest.mark.parametrize("kvk", KINDS)
+def test_batched_slots(oracle, cuda, kvk):
+    cases = [synth.make_case(oracle, kvk, rows=r, pos=p, seed=s, outlier_frac=0.02)
+             for r, p, s in ((700, [699], 1), (2300, [2299, 2298, 100], 2), (64, [63, 62], 3))]
+    dcs = [DeviceCase(c, cuda, scatter_seed=i) for i, c in enumerate(cases)]
+    for exact in (True, False):
+        Q.attn_decode_batched([d.slot() for d in dcs], synth.Q_STRIDE, 24, 4, 256, SCALE, kvk=kvk,
+                              exact=exact)
+        torch.cuda.synchronize()
+        for d, c in zip(dcs, cases):
+            got = np.stack([o.cpu().numpy() for o in d.out])
+            ref = oracle.attn_decode(c.q, c.k, c.v, kvk, c.pos)
+            assert synth.tolerance_ok(got, ref)[0]
+
+
+@pytest.mark.parametrize("kvk", KINDS)
+@pytest.mark.parametrize("nshards", [2, 4])
+def test_kv_split_partials_merge(oracle, cuda, kvk, nshards):
+    """KV-sequence sharding emulated on one GPU: every shard holds a page-aligned row range
+    behind its own tables, emits un-normalised partials, and the LSE merge of the shards
+    equals attention over the whole cache (and the oracle's partials, shard by shard)."""
+    rows = 64 * 4 * nshards
+    pos = [rows - 1, rows - 2, rows // 2 + 3, 70, 0]
+    c = synth.make_case(oracle, kvk, rows=rows, pos=pos, seed=55, outlier_frac=0.02)
+    full = oracle.attn_decode(c.q, c.k, c.v, kvk, c.pos)
+    per = rows // nshards
+    lanes_stride = 6
+    parts = torch.empty((nshards, 1, lanes_stride, 24, 258), device=cuda)
+    for g in range(nshards):
+        dc = DeviceCase(c, cuda, row_lo=g * per, row_hi=(g + 1) * per)
+        Q.attn_decode_partial([dc.slot()], lanes_stride, synth.Q_STRIDE, 24, 4, 256, SCALE,
+                              parts[g], kvk=kvk)
+        torch.cuda.synchronize()
+        mine = parts[g, 0, : len(pos)].cpu().numpy()
+        want = oracle.attn_partial(c.q, c.k, c.v, kvk, c.pos, g * per, (g + 1) * per)
+        # partials agree after normalising each by its own l (m conventions may differ)
+        live = want[:, :, 0] > -1e38
+        assert ((mine[:, :, 0] > -1e38) == live).all()
+        assert (mine[:, :, 1][~live] == 0).all()
+        a = mine[live][:, 2:] / mine[live][:, 1:2]
+        b = want[live][:, 2:] / want[live][:, 1:2]
+        assert synth.tolerance_ok(a, b)[0]
+        # padded lane (index 5) is a well-formed empty partial
+        assert (parts[g, 0, 5, :, 0].cpu().numpy() < -1e38).all()
+    out = torch.empty((lanes_stride * 24, 256), device=cuda)
+    Q.attn_merge_partials(parts, nshards, lanes_stride * 24, out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().reshape(lanes_stride, -1)[: len(pos)]
+    assert synth.tolerance_ok(got, full)[0]
+
+
+@pytest.mark.skipif(not REF_GPU_SO.exists(), reason="oracle/_ref not built")
+@pytest.mark.parametrize("kvk", KINDS)
+def test_against_reference_kernels_on_this_gpu(oracle, cuda, kvk):
+    """The reference's own k_attn_fd2 + combine, recompiled for sm_100a from the reference
+    tree, on the identical buffers: pins the oracle to the reference itself (<= 1e-4 / 2e-4
+    max-abs/RMS, its own gate) and the engine to the reference within the BASELINE bar."""
+    ref_gpu = RefGpu()
+    for seq, ntok in ((47, 1), (1024, 5), (16384, 5)):
+        c = synth.make_case(oracle, kvk, rows=seq, pos=lanes_for(seq, ntok), seed=300 + seq % 89)
+        oracle_out = oracle.attn_decode(c.q, c.k, c.v, kvk, c.pos)
+        dc = DeviceCase(c, cuda)
+        theirs = ref_gpu.decode3(dc).copy()
+        rms = np.sqrt((oracle_out.astype(np.float64) ** 2).mean()) + 1e-12
+        assert np.abs(theirs - oracle_out).max() / rms < EXACT_TOL[kvk]
+        mine = dc.run3()
+        assert synth.tolerance_ok(mine, theirs)[0]
+
+
+def test_errors_are_status_codes(cuda, oracle):
+    c = synth.make_case(oracle, KV_F16, rows=64, pos=[63], seed=2)
+    dc = DeviceCase(c, cuda)
+    with pytest.raises(Q._lib.Q27Error) as e:
+        Q.attn_decode3(dc.q, synth.Q_STRIDE, dc.kside.tab, dc.vside.tab, dc.out, dc.scratch,
+                       dc.pos, 0, 24, 4, 256, SCALE, ntok=1, kvk=4)     # turbo5k: refused
+    assert e.value.status == Q._lib.ERR_UNSUPPORTED_KIND
+    assert torch.isnan(dc.out[0]).all()                                  # nothing was written
+
+
+def test_kvpool_on_device(cuda):
+    # src/kv_pool.h:24-72: sides rounded DOWN to whole pages, LIFO with low indices first
+    rb = Q.row_bytes(KV_T3)
+    pool = Q.KvPool(10 * 64 * rb + 17, 7 * 64 * rb, rb, rb)
+    assert pool.enabled() and pool.npages(0) == 10 and pool.npages(1) == 7
+    assert pool.page_bytes(0) == 64 * rb
+    got = []
+    assert pool.reserve(0, 3, got) and got == [0, 1, 2]
+    assert pool.page_ptr(0, 2) - pool.page_ptr(0, 0) == 2 * 64 * rb
+    assert not pool.reserve(1, 8, got) and pool.free_pages(1) == 7     # pops nothing
+    pool.release(0, got)
+    assert pool.free_pages(0) == 10 and got == []
+    again = []
+    assert pool.reserve(0, 1, again) and again == [2]                   # LIFO
+    pool.close()
