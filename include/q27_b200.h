@@ -58,6 +58,11 @@ int q27_last_cuda_error(void);
 /* compiled-for architecture, e.g. 1000 for sm_100a; 0 if the image cannot run here */
 int q27_device_arch(void);
 
+/* Diagnostics: every device-side wait in this library is bounded; a kernel whose wait ran
+ * out sets a device flag and returns early. This reads the flag (synchronous copy; do
+ * not call under stream capture). 0 = no wait has ever timed out in this process. */
+int q27_wait_timeout_flag(int* out);
+
 /* bytes per cache row: fp16 n_kv*512, fp8 n_kv*256, turbo3 n_kv*100; -1 = refused kind */
 int64_t q27_kv_row_bytes(int kvk, int n_kv_heads);
 /* floats the caller must provide as `scratch` for ntok lanes:
@@ -161,6 +166,27 @@ int q27_attn_prefill_T_exact(const float* qT, int q_stride, int q_row,
  * (kv2f src/cuda_common.h:113-114, turbo3_deq_elem src/turbo3.cuh:134-137). */
 int q27_kv_dequant(const void* const* tab, int kvk, int row0, int nrows, int n_kv_heads,
                    float* out, void* stream);
+
+/* Replaces q27k::kv_store_T (src/blocks.cuh:56-57, src/prefill.cu:1221-1243): store T
+ * tokens' K and V rows (fp32 [T][rowlen], rowlen = n_kv_heads*256) into cache rows
+ * base_pos .. base_pos+T-1 as fp16 (round to nearest even) or saturating e4m3. */
+int q27_kv_store_T(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
+                   int base_pos, int rowlen, int T, void* stream, int fp8);
+
+/* Replaces q27k::kv_store_T_t3 (src/blocks.cuh:63-65, src/prefill.cu:2556-2596) for
+ * Q27_KV_T3: per 128-element group L2 norm -> forward WHT -> nearest of 8 centroids -> pack
+ * -> corrected fp16 norm, written block-addressed. Byte-identical to the reference's
+ * serial CPU codec (t3_quant, src/test_kernels.cu:1089-1103). K must already be rope'd. */
+int q27_kv_store_T_t3(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
+                      int base_pos, int n_kv_heads, int head_dim, int T, void* stream, int kvk);
+
+/* Replaces q27k::wht_T (src/blocks.cuh:76-81, src/prefill.cu:2598-2618): per-128-group
+ * signed Walsh-Hadamard rotation in place over a flat [T][row_stride] buffer; forward on Q
+ * after rope (inv = 0), inverse on the attention output (inv = 1). Only the first 256
+ * floats of each head are touched (head_stride = 512 for the q||gate layout). T = ntok
+ * rows cover the decode-time wht3 (src/spec3.cuh:103-105) when lanes are contiguous. */
+int q27_wht_T(float* x, int n_heads, int head_dim, int head_stride, int row_stride, int T, int inv,
+              void* stream);
 
 /* mk_tab (src/test_kernels.cu:27-36): fill a DEVICE table of ceil(rows/64) entries with
  * identity page pointers over a contiguous buffer. d_tab is caller-allocated. */

@@ -48,6 +48,7 @@ SIGNATURES = {
     "q27_status_string": (C.c_char_p, [_i]),
     "q27_last_cuda_error": (_i, []),
     "q27_device_arch": (_i, []),
+    "q27_wait_timeout_flag": (_i, [C.POINTER(_i)]),
     "q27_kv_row_bytes": (_i64, [_i, _i]),
     "q27_decode_scratch_floats": (_i64, [_i, _i]),
     "q27_prefill_part_floats": (_i64, [_i, _i]),
@@ -63,6 +64,9 @@ SIGNATURES = {
     "q27_attn_prefill_T_exact": (_i, [_vp, _i, _i, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i,
                                       _f, _vp, _i]),
     "q27_kv_dequant": (_i, [_vp, _i, _i, _i, _i, _vp, _vp]),
+    "q27_kv_store_T": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _i]),
+    "q27_kv_store_T_t3": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _i]),
+    "q27_wht_T": (_i, [_vp, _i, _i, _i, _i, _i, _i, _vp]),
     "q27_mk_tab": (_i, [_vp, _sz, _i, _vp, _vp]),
     "q27_kvpool_create": (_vp, [_sz, _sz, _sz, _sz]),
     "q27_kvpool_destroy": (None, [_vp]),

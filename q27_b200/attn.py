@@ -127,3 +127,22 @@ def kv_dequant(tab, kvk, row0, nrows, n_kv_heads, out, st=None):
     """Bit-exact dequantisation of cache rows to fp32 [nrows][n_kv_heads][256]."""
     L.check(L.lib().q27_kv_dequant(tab.data_ptr(), kvk, row0, nrows, n_kv_heads, out.data_ptr(),
                                    stream_ptr(st)), "q27_kv_dequant")
+
+
+def kv_store_T(kT, vT, ktab, vtab, base_pos, rowlen, T, st=None, fp8=False):
+    """Store T tokens' K/V rows (fp32 [T][rowlen]) at cache rows base_pos.. as fp16 / e4m3."""
+    L.check(L.lib().q27_kv_store_T(kT.data_ptr(), vT.data_ptr(), ktab.data_ptr(), vtab.data_ptr(),
+                                   base_pos, rowlen, T, stream_ptr(st), int(fp8)), "q27_kv_store_T")
+
+
+def kv_store_T_t3(kT, vT, ktab, vtab, base_pos, n_kv_heads, head_dim, T, st=None, kvk=2):
+    """turbo3 prefill store: cooperative per-128-group quantise of T tokens' K and V rows."""
+    L.check(L.lib().q27_kv_store_T_t3(kT.data_ptr(), vT.data_ptr(), ktab.data_ptr(),
+                                      vtab.data_ptr(), base_pos, n_kv_heads, head_dim, T,
+                                      stream_ptr(st), kvk), "q27_kv_store_T_t3")
+
+
+def wht_T(x, n_heads, head_dim, head_stride, row_stride, T, inv, st=None):
+    """Per-128-group WHT rotate in place over a flat [T][row_stride] buffer."""
+    L.check(L.lib().q27_wht_T(x.data_ptr(), n_heads, head_dim, head_stride, row_stride, T,
+                              int(inv), stream_ptr(st)), "q27_wht_T")

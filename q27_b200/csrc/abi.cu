@@ -239,12 +239,42 @@ int q27_attn_prefill_T(const float* qT, int q_stride, int q_row, const void* con
                                     t0, SB, n_q_heads, n_kv_heads, head_dim, scale, stream, kvk);
 }
 
+int q27_wait_timeout_flag(int* out) {
+    if (!out) return Q27_ERR_INVALID_ARG;
+    return read_wait_timeout_flag(out);
+}
+
 int q27_kv_dequant(const void* const* tab, int kvk, int row0, int nrows, int n_kv_heads,
                    float* out, void* stream) {
     if (kvk != Q27_KV_F16 && kvk != Q27_KV_FP8 && kvk != Q27_KV_T3) return Q27_ERR_UNSUPPORTED_KIND;
     if (!tab || !out || row0 < 0 || nrows < 0 || n_kv_heads < 1) return Q27_ERR_INVALID_ARG;
     return launch_kv_dequant(tab, kvk, row0, nrows, n_kv_heads, out,
                              static_cast<cudaStream_t>(stream));
+}
+
+int q27_kv_store_T(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
+                   int base_pos, int rowlen, int T, void* stream, int fp8) {
+    if (!kT || !vT || !ktab || !vtab || base_pos < 0 || T < 0 || rowlen <= 0 || rowlen % HD)
+        return Q27_ERR_INVALID_ARG;
+    return launch_kv_store_T(kT, vT, ktab, vtab, base_pos, rowlen / HD, T,
+                             static_cast<cudaStream_t>(stream), fp8 ? Q27_KV_FP8 : Q27_KV_F16);
+}
+
+int q27_kv_store_T_t3(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
+                      int base_pos, int n_kv_heads, int head_dim, int T, void* stream, int kvk) {
+    if (kvk != Q27_KV_T3) return Q27_ERR_UNSUPPORTED_KIND; // turbo3v / turbo5k K legs: refused
+    if (head_dim != HD || n_kv_heads < 1) return Q27_ERR_UNSUPPORTED_WIDTH;
+    if (!kT || !vT || !ktab || !vtab || base_pos < 0 || T < 0) return Q27_ERR_INVALID_ARG;
+    return launch_kv_store_T(kT, vT, ktab, vtab, base_pos, n_kv_heads, T,
+                             static_cast<cudaStream_t>(stream), Q27_KV_T3);
+}
+
+int q27_wht_T(float* x, int n_heads, int head_dim, int head_stride, int row_stride, int T, int inv,
+              void* stream) {
+    if (head_dim != HD) return Q27_ERR_UNSUPPORTED_WIDTH;
+    if (!x || n_heads < 0 || T < 0 || head_stride < HD) return Q27_ERR_INVALID_ARG;
+    return launch_wht_T(x, n_heads, head_stride, row_stride, T, inv != 0,
+                        static_cast<cudaStream_t>(stream));
 }
 
 int q27_mk_tab(const void* base, size_t row_bytes, int rows, void** d_tab, void* stream) {

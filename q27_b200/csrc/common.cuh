@@ -137,6 +137,10 @@ int launch_prefill_exact(const float* qT, int q_stride, int q_row, const void* c
                          int SB, int n_q, int n_kv, float scale, cudaStream_t st, int kvk);
 int launch_kv_dequant(const void* const* tab, int kvk, int row0, int nrows, int n_kv, float* out,
                       cudaStream_t st);
+int launch_kv_store_T(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
+                      int base_pos, int n_kv, int T, cudaStream_t st, int kvk);
+int launch_wht_T(float* x, int n_heads, int head_stride, int row_stride, int T, bool inv,
+                 cudaStream_t st);
 int launch_mk_tab(const void* base, size_t row_bytes, int rows, void** d_tab, cudaStream_t st);
 
 } // namespace q27b

@@ -1,9 +1,659 @@
+// Tensor-core split-KV decode for sm_100a.
+//
+// One CTA = (slot, lane, position split [, kv head]). A producer warp streams the split's
+// K and V rows into a shared-memory ring with bulk async copies (cp.async.bulk, completion
+// on an mbarrier); eight consumer warps turn ring rows straight into mma.sync fragments in
+// registers -- no dequantised tile is ever written back to shared memory -- and run
+//     S^T = K . Q^T        (16 keys x 8 query columns per MMA, fp16 operands, fp32 accum)
+//     O^T += V^T . P^T     (16 dims x 8 query columns, contraction over 16 keys)
+// with an online softmax per query column. The six GQA heads of a KV head are the columns
+// (8 with padding), so one read of a row serves all of them.
+//
+// turbo3 rows are never multiplied out to centroid*norm per element: the per-block fp16
+// norm is factored out of the dot product (two accumulators per tile, one per 128-dim
+// block, recombined as nK0*D0 + nK1*D1) and folded into P for the V side, so the MMA
+// operands are the eight centroid constants, looked up 4 elements per PRMT. The bit-exact
+// centroid*norm product lives in the exact family and q27_kv_dequant.
+//
+// Dimension and key indices inside a tile are permuted per format so that every thread's
+// fragment registers come from contiguous packed bytes; Q^T fragments and the output rows
+// use the same maps (kdim_* / vdim_* below), so the permutation cancels.
 #include "decode_mma.cuh"
 
 namespace q27b {
-int launch_decode_mma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool* done) {
-    (void)b; (void)kvk; (void)sm_count; (void)st;
-    *done = false;
+
+__device__ int g_wait_timeout_flag = 0; // set when a bounded mbarrier wait ran out
+
+namespace {
+
+constexpr int NCW = 8;            // consumer warps
+constexpr int STAGE_ROWS = 32;    // rows per ring stage (= 2 key tiles; never crosses a page)
+constexpr int TILE = 16;          // keys per MMA tile
+constexpr float LOG2E = 1.4426950408889634f;
+
+template <int KVK> struct Fmt;
+template <> struct Fmt<Q27_KV_F16> {
+    static constexpr int KVH = 1;               // kv heads per CTA
+    static constexpr int PITCH = 512 + 16;      // one (row, head) slice + pad: conflict-free ldmatrix
+    static constexpr int SLICE = 512;
+    static constexpr int STAGES = 5;
+};
+template <> struct Fmt<Q27_KV_FP8> {
+    static constexpr int KVH = 1;
+    static constexpr int PITCH = 256 + 16;
+    static constexpr int SLICE = 256;
+    static constexpr int STAGES = 8;
+};
+template <> struct Fmt<Q27_KV_T3> {
+    static constexpr int KVH = 4;               // whole 400-byte rows: all four kv heads
+    static constexpr int PITCH = 400;
+    static constexpr int SLICE = 400;
+    static constexpr int STAGES = 5;
+};
+template <int KVK> constexpr int stage_bytes() { return 2 * STAGE_ROWS * Fmt<KVK>::PITCH; }
+template <int KVK> constexpr int ring_bytes() { return stage_bytes<KVK>() * Fmt<KVK>::STAGES; }
+constexpr int MERGE_BYTES = NCW * GQA * PART * 4; // per-warp partials for the final merge
+template <int KVK> constexpr int smem_bytes() {
+    return 256 + (ring_bytes<KVK>() > MERGE_BYTES ? ring_bytes<KVK>() : MERGE_BYTES);
+}
+
+// ---- PTX helpers ----------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)),
+                 "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok) : "r"(smem_u32(b)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait: gives up after ~1M polls, records it, and lets the caller bail out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+    for (int i = 0; i < (1 << 20); i++) {
+        if (mbar_try_wait(b, parity)) return true;
+        if (i > 4096) __nanosleep(128);
+    }
+    atomicExch(&g_wait_timeout_flag, 1);
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+    uint32_t d;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(x));
+    return d;
+}
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) {
+    return *reinterpret_cast<const uint32_t*>(p);
+}
+__device__ __forceinline__ uint32_t lds16(const uint8_t* p) {
+    return *reinterpret_cast<const uint16_t*>(p);
+}
+// 32 bits starting at a 2-byte-aligned shared address
+__device__ __forceinline__ uint32_t lds32_a2(const uint8_t* p, bool aligned4) {
+    if (aligned4) return lds32(p);
+    const uint32_t lo = lds32(p - 2), hi = lds32(p + 2);
+    return __funnelshift_r(lo, hi, 16);
+}
+
+// ---- index maps: (MMA-logical index) -> (actual dimension / key) -------------------------
+// K side: contraction step s (0..15), thread column c (0..3), register r (0: logical k
+// 2c,2c+1; 1: logical k 2c+8,2c+9), element e (0/1) -> dimension of the head.
+template <int KVK>
+__host__ __device__ __forceinline__ int kdim(int s, int c, int r, int e) {
+    if (KVK == Q27_KV_F16) return 16 * s + 2 * c + 8 * r + e;
+    if (KVK == Q27_KV_FP8) return 16 * (c + 4 * (s >> 2)) + 4 * (s & 3) + 2 * r + e;
+    // turbo3: s = 8*block + 4*group + i; the thread owns dims [32c, 32c+32) of the block
+    const int b = s >> 3, w = (s >> 2) & 1, i = s & 3;
+    const int e16 = (i & 1) * 8 + (i >> 1) + 4 * r + 2 * e;
+    return 128 * b + 32 * c + 16 * w + e16;
+}
+// V side: output tile mt (0..15), row rr (0..15) of O^T -> dimension of the head.
+__host__ __device__ __forceinline__ int t3_vorder(int i) {
+    // order in which the interleaved selectors yield a thread's 16 dims of a block
+    return ((i >> 2) == 0 ? 0 : (i >> 2) == 1 ? 2 : (i >> 2) == 2 ? 1 : 3) + 4 * (i & 3);
+}
+template <int KVK>
+__host__ __device__ __forceinline__ int vdim(int mt, int rr) {
+    if (KVK == Q27_KV_F16) return 16 * mt + rr;
+    if (KVK == Q27_KV_FP8) {
+        const int g = rr & 7;
+        return 16 * (4 * (g & 1) + (g >> 1) + 8 * (mt >> 3)) + 2 * (mt & 7) + (rr >> 3);
+    }
+    const int b = mt >> 3, j = mt & 7;
+    return 128 * b + 16 * (rr & 7) + t3_vorder(2 * j + (rr >> 3));
+}
+// logical key index (row of S^T / contraction index of PV) -> key within the 16-key tile
+template <int KVK>
+__host__ __device__ __forceinline__ int keyperm(int k) {
+    if (KVK == Q27_KV_FP8) return ((k >> 1) & 3) + 4 * (k & 1) + 8 * (k >> 3);
+    return k;
+}
+
+// ---- turbo3 selector / lookup machinery ----------------------------------------------
+// fp16 bit patterns of the centroids (src/turbo3.cuh:38-40), split into low and high bytes
+// and packed as PRMT pools: pool byte i (0..7) = byte of centroid i.
+struct T3Tab {
+    uint32_t lo_a, lo_b, hi_a, hi_b;
+};
+__device__ __forceinline__ T3Tab t3_tables() {
+    uint32_t lo[2] = {0, 0}, hi[2] = {0, 0};
+    const float c[8] = {-0.190207f, -0.118786f, -0.066822f, -0.021663f,
+                        0.021663f,  0.066822f,  0.118786f,  0.190207f};
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint32_t bits = __half_as_ushort(__float2half_rn(c[i]));
+        lo[i >> 2] |= (bits & 0xffu) << (8 * (i & 3));
+        hi[i >> 2] |= (bits >> 8) << (8 * (i & 3));
+    }
+    return T3Tab{lo[0], lo[1], hi[0], hi[1]};
+}
+// 16 elements: qs word Q (2 bits each) + 16 sign bits -> selectors with one nibble
+// (hi<<2 | low2) per element; ze holds elements 0,2,..,14 and zo elements 1,3,..,15.
+__device__ __forceinline__ void t3_selectors(uint32_t Q, uint32_t S16, uint32_t& ze, uint32_t& zo) {
+    // byte LUT spreading sign bits (b0, b2 of a nibble) to bit 2 of two output nibbles
+    const uint32_t he = prmt(0x04000400u, 0x44404440u, S16 & 0x7777u);
+    const uint32_t ho = prmt(0x04000400u, 0x44404440u, (S16 >> 1) & 0x7777u);
+    ze = (Q & 0x33333333u) | he;
+    zo = ((Q >> 2) & 0x33333333u) | ho;
+}
+// 8 selector nibbles -> 4 half2 registers (nibbles 2i, 2i+1 -> h[i])
+__device__ __forceinline__ void t3_lookup(const T3Tab& t, uint32_t z, uint32_t* h) {
+    const uint32_t zh = z >> 16;
+    const uint32_t l0 = prmt(t.lo_a, t.lo_b, z), h0 = prmt(t.hi_a, t.hi_b, z);
+    const uint32_t l1 = prmt(t.lo_a, t.lo_b, zh), h1 = prmt(t.hi_a, t.hi_b, zh);
+    h[0] = prmt(l0, h0, 0x5140u);
+    h[1] = prmt(l0, h0, 0x7362u);
+    h[2] = prmt(l1, h1, 0x5140u);
+    h[3] = prmt(l1, h1, 0x7362u);
+}
+
+// ---- per-warp state -----------------------------------------------------------------------
+struct WarpAcc {
+    float o[16][4];   // O^T: tile mt, regs {(row g, col 2c), (g, 2c+1), (g+8, 2c), (g+8, 2c+1)}
+    float m[2];       // running max (log2 domain) of columns 2c, 2c+1
+    float l[2];       // this thread's share of the running sum
+};
+
+// Online-softmax update for one 16-key tile. s[4] = scores (already scaled to log2 domain)
+// for rows g, g+8 and columns 2c, 2c+1; valid rows carry real scores, masked rows -inf.
+// Returns P as two half2 registers (rows g / g+8), columns (2c, 2c+1).
+__device__ __forceinline__ void softmax_tile(WarpAcc& A, const float (&s)[4], float (&p)[4]) {
+    float mx0 = fmaxf(s[0], s[2]), mx1 = fmaxf(s[1], s[3]);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float mn0 = fmaxf(A.m[0], mx0), mn1 = fmaxf(A.m[1], mx1);
+    if (mn0 > A.m[0] || mn1 > A.m[1]) { // rescale (every thread of a column group agrees)
+        const float a0 = ex2(A.m[0] - mn0), a1 = ex2(A.m[1] - mn1);
+        A.l[0] *= a0;
+        A.l[1] *= a1;
+#pragma unroll
+        for (int mt = 0; mt < 16; mt++) {
+            A.o[mt][0] *= a0; A.o[mt][1] *= a1; A.o[mt][2] *= a0; A.o[mt][3] *= a1;
+        }
+        A.m[0] = mn0;
+        A.m[1] = mn1;
+    }
+    p[0] = ex2(s[0] - A.m[0]);
+    p[1] = ex2(s[1] - A.m[1]);
+    p[2] = ex2(s[2] - A.m[0]);
+    p[3] = ex2(s[3] - A.m[1]);
+    A.l[0] += p[0] + p[2];
+    A.l[1] += p[1] + p[3];
+}
+
+// ---- tile processors ------------------------------------------------------------------
+// Each consumes one 16-key tile of one kv head from the ring stage. `valid` = number of
+// real keys in the tile (rows >= valid are masked). qf = Q^T fragments, 2 regs per step.
+
+template <int KVK>
+__device__ __forceinline__ void tile_f16(WarpAcc& A, const uint8_t* ks, const uint8_t* vs,
+                                         const uint32_t (&qf)[16][2], int valid, float sc2,
+                                         int lane) {
+    constexpr int P = Fmt<Q27_KV_F16>::PITCH;
+    const int g = lane >> 2;
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+        const int row = (lane & 7) + ((lane >> 3) & 1) * 8, col = (lane >> 4) * 8;
+        const uint32_t base = smem_u32(ks) + row * P + col * 2;
+#pragma unroll
+        for (int s = 0; s < 16; s++) {
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(base + s * 32, a0, a1, a2, a3);
+            mma16816(d, a0, a1, a2, a3, qf[s][0], qf[s][1]);
+        }
+    }
+    float sv[4], p[4];
+    sv[0] = g < valid ? d[0] * sc2 : -INFINITY;
+    sv[1] = g < valid ? d[1] * sc2 : -INFINITY;
+    sv[2] = g + 8 < valid ? d[2] * sc2 : -INFINITY;
+    sv[3] = g + 8 < valid ? d[3] * sc2 : -INFINITY;
+    softmax_tile(A, sv, p);
+    const uint32_t b0 = movmatrix_t(pack_h2(p[0], p[1]));
+    const uint32_t b1 = movmatrix_t(pack_h2(p[2], p[3]));
+    {
+        const int row = (lane & 7) + (lane >> 4) * 8, col = ((lane >> 3) & 1) * 8;
+        const uint32_t base = smem_u32(vs) + row * P + col * 2;
+#pragma unroll
+        for (int mt = 0; mt < 16; mt++) {
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4_t(base + mt * 32, a0, a1, a2, a3);
+            mma16816(A.o[mt], a0, a1, a2, a3, b0, b1);
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t two_bytes) {
+    __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two_bytes, __NV_E4M3);
+    return (uint32_t)h.x | ((uint32_t)h.y << 16);
+}
+
+__device__ __forceinline__ void tile_fp8(WarpAcc& A, const uint8_t* ks, const uint8_t* vs,
+                                         const uint32_t (&qf)[16][2], int valid, float sc2,
+                                         int lane) {
+    constexpr int P = Fmt<Q27_KV_FP8>::PITCH;
+    const int g = lane >> 2, c = lane & 3;
+    const int r0 = keyperm<Q27_KV_FP8>(g), r1 = keyperm<Q27_KV_FP8>(g + 8);
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint4 x = *reinterpret_cast<const uint4*>(ks + r0 * P + 16 * (c + 4 * j));
+        const uint4 y = *reinterpret_cast<const uint4*>(ks + r1 * P + 16 * (c + 4 * j));
+        const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, yw[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int s = 4 * j + i;
+            mma16816(d, e4m3x2_to_h2(xw[i] & 0xffffu), e4m3x2_to_h2(yw[i] & 0xffffu),
+                     e4m3x2_to_h2(xw[i] >> 16), e4m3x2_to_h2(yw[i] >> 16), qf[s][0], qf[s][1]);
+        }
+    }
+    float sv[4], p[4];
+    sv[0] = r0 < valid ? d[0] * sc2 : -INFINITY;
+    sv[1] = r0 < valid ? d[1] * sc2 : -INFINITY;
+    sv[2] = r1 < valid ? d[2] * sc2 : -INFINITY;
+    sv[3] = r1 < valid ? d[3] * sc2 : -INFINITY;
+    softmax_tile(A, sv, p);
+    const uint32_t b0 = movmatrix_t(pack_h2(p[0], p[1]));
+    const uint32_t b1 = movmatrix_t(pack_h2(p[2], p[3]));
+    // V: this thread's four keys are c, c+4, c+8, c+12; dims: two 16-byte chunks by g
+#pragma unroll
+    for (int hh = 0; hh < 2; hh++) {
+        const int ch = 4 * (g & 1) + (g >> 1) + 8 * hh;
+        const uint4 k0 = *reinterpret_cast<const uint4*>(vs + (c) * P + 16 * ch);
+        const uint4 k1 = *reinterpret_cast<const uint4*>(vs + (c + 4) * P + 16 * ch);
+        const uint4 k2 = *reinterpret_cast<const uint4*>(vs + (c + 8) * P + 16 * ch);
+        const uint4 k3 = *reinterpret_cast<const uint4*>(vs + (c + 12) * P + 16 * ch);
+        const uint32_t w0[4] = {k0.x, k0.y, k0.z, k0.w}, w1[4] = {k1.x, k1.y, k1.z, k1.w};
+        const uint32_t w2[4] = {k2.x, k2.y, k2.z, k2.w}, w3[4] = {k3.x, k3.y, k3.z, k3.w};
+#pragma unroll
+        for (int m8 = 0; m8 < 8; m8++) {
+            // dims u = 2*m8, 2*m8+1 of this chunk: bytes (2*m8 & 3), +1 of word m8 >> 1
+            const uint32_t sel = (m8 & 1) ? 0x7362u : 0x5140u;
+            const uint32_t x01 = prmt(w0[m8 >> 1], w1[m8 >> 1], sel); // (k0[u],k1[u],k0[u+1],k1[u+1])
+            const uint32_t x23 = prmt(w2[m8 >> 1], w3[m8 >> 1], sel);
+            mma16816(A.o[8 * hh + m8], e4m3x2_to_h2(x01 & 0xffffu), e4m3x2_to_h2(x01 >> 16),
+                     e4m3x2_to_h2(x23 & 0xffffu), e4m3x2_to_h2(x23 >> 16), b0, b1);
+        }
+    }
+}
+
+__device__ __forceinline__ void tile_t3(WarpAcc& A, const uint8_t* ks, const uint8_t* vs, int kvh,
+                                        const uint32_t (&qf)[16][2], int valid, float sc2,
+                                        int lane, const T3Tab& tab) {
+    constexpr int P = Fmt<Q27_KV_T3>::PITCH;
+    const int g = lane >> 2, c = lane & 3;
+    // ---- scores: per 128-dim block an accumulator of centroid dot products ----
+    float dk[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    const uint8_t* kr0 = ks + g * P + kvh * 100;
+    const uint8_t* kr1 = ks + (g + 8) * P + kvh * 100;
+#pragma unroll
+    for (int b = 0; b < 2; b++) {
+        // block b starts at +50b: 4-byte aligned for b == 1, 2 mod 4 for b == 0; qs at +2,
+        // signs at +34
+        const bool al = (b == 1);
+        const uint8_t* q0 = kr0 + 50 * b + 2 + 8 * c;
+        const uint8_t* q1 = kr1 + 50 * b + 2 + 8 * c;
+        const uint32_t s0 = lds32_a2(kr0 + 50 * b + 34 + 4 * c, al);
+        const uint32_t s1 = lds32_a2(kr1 + 50 * b + 34 + 4 * c, al);
+#pragma unroll
+        for (int w = 0; w < 2; w++) {
+            uint32_t ze0, zo0, ze1, zo1, h0[8], h1[8];
+            t3_selectors(lds32_a2(q0 + 4 * w, al), w ? s0 >> 16 : s0 & 0xffffu, ze0, zo0);
+            t3_selectors(lds32_a2(q1 + 4 * w, al), w ? s1 >> 16 : s1 & 0xffffu, ze1, zo1);
+            t3_lookup(tab, ze0, h0);
+            t3_lookup(tab, zo0, h0 + 4);
+            t3_lookup(tab, ze1, h1);
+            t3_lookup(tab, zo1, h1 + 4);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int s = 8 * b + 4 * w + i;
+                mma16816(dk[b], h0[2 * i], h1[2 * i], h0[2 * i + 1], h1[2 * i + 1], qf[s][0],
+                         qf[s][1]);
+            }
+        }
+    }
+    // norms: K for the score recombination, V folded into P
+    const float nk00 = __half2float(*reinterpret_cast<const __half*>(kr0));
+    const float nk01 = __half2float(*reinterpret_cast<const __half*>(kr0 + 50));
+    const float nk10 = __half2float(*reinterpret_cast<const __half*>(kr1));
+    const float nk11 = __half2float(*reinterpret_cast<const __half*>(kr1 + 50));
+    float sv[4], p[4];
+    sv[0] = g < valid ? (dk[0][0] * nk00 + dk[1][0] * nk01) * sc2 : -INFINITY;
+    sv[1] = g < valid ? (dk[0][1] * nk00 + dk[1][1] * nk01) * sc2 : -INFINITY;
+    sv[2] = g + 8 < valid ? (dk[0][2] * nk10 + dk[1][2] * nk11) * sc2 : -INFINITY;
+    sv[3] = g + 8 < valid ? (dk[0][3] * nk10 + dk[1][3] * nk11) * sc2 : -INFINITY;
+    softmax_tile(A, sv, p);
+    const uint8_t* vr0 = vs + g * P + kvh * 100;
+    const uint8_t* vr1 = vs + (g + 8) * P + kvh * 100;
+    uint32_t pb[2][2]; // [block][key half] P^T fragments with the V norm folded in
+#pragma unroll
+    for (int b = 0; b < 2; b++) {
+        // masked rows may hold stale bytes: keep their weight an exact zero
+        const float n0 = g < valid ? __half2float(*reinterpret_cast<const __half*>(vr0 + 50 * b)) : 0.f;
+        const float n1 = g + 8 < valid ? __half2float(*reinterpret_cast<const __half*>(vr1 + 50 * b)) : 0.f;
+        pb[b][0] = movmatrix_t(pack_h2(p[0] * n0, p[1] * n0));
+        pb[b][1] = movmatrix_t(pack_h2(p[2] * n1, p[3] * n1));
+    }
+    // ---- V: this thread's keys are 2c, 2c+1 (pair 0) and 2c+8, 2c+9 (pair 1); its dims
+    // are [16g, 16g+16) of each block: one qs word + 16 sign bits per (key, block) ----
+#pragma unroll
+    for (int b = 0; b < 2; b++) {
+        const bool al = (b == 1);
+        uint32_t ze[4], zo[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int key = 2 * c + (k & 1) + 8 * (k >> 1);
+            const uint8_t* blk = vs + key * P + kvh * 100 + 50 * b;
+            t3_selectors(lds32_a2(blk + 2 + 4 * g, al), lds16(blk + 34 + 2 * g), ze[k], zo[k]);
+        }
+        uint32_t hp[2][16]; // [pair][dim order] half2 = (key A, key B) of one dim
+#pragma unroll
+        for (int pr = 0; pr < 2; pr++) {
+            const uint32_t ea = ze[2 * pr], eb = ze[2 * pr + 1], oa = zo[2 * pr], ob = zo[2 * pr + 1];
+            const uint32_t ze_lo = (ea & 0x0F0F0F0Fu) | ((eb << 4) & 0xF0F0F0F0u);
+            const uint32_t ze_hi = ((ea >> 4) & 0x0F0F0F0Fu) | (eb & 0xF0F0F0F0u);
+            const uint32_t zo_lo = (oa & 0x0F0F0F0Fu) | ((ob << 4) & 0xF0F0F0F0u);
+            const uint32_t zo_hi = ((oa >> 4) & 0x0F0F0F0Fu) | (ob & 0xF0F0F0F0u);
+            t3_lookup(tab, ze_lo, hp[pr]);       // dims e16 = 0, 4, 8, 12
+            t3_lookup(tab, ze_hi, hp[pr] + 4);   // 2, 6, 10, 14
+            t3_lookup(tab, zo_lo, hp[pr] + 8);   // 1, 5, 9, 13
+            t3_lookup(tab, zo_hi, hp[pr] + 12);  // 3, 7, 11, 15
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            mma16816(A.o[8 * b + j], hp[0][2 * j], hp[0][2 * j + 1], hp[1][2 * j],
+                     hp[1][2 * j + 1], pb[b][0], pb[b][1]);
+    }
+}
+
+// ---- the kernel -------------------------------------------------------------------------
+template <int KVK>
+__global__ void __launch_bounds__((NCW + 1) * 32, 1)
+k_decode_mma(const __grid_constant__ DevBatch b) {
+    using F = Fmt<KVK>;
+    constexpr int WAYS = NCW / F::KVH;             // consumer warps per kv head
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + 16;
+    uint8_t* ring = smem + 256;
+
+    const int t = blockIdx.x, sp = blockIdx.y;
+    const int slot = blockIdx.z / (b.n_kv / F::KVH), kvg = blockIdx.z % (b.n_kv / F::KVH);
+    const DevSlot& S = b.s[slot];
+    if (t >= S.ntok) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    int max_len = 0;
+    for (int u = 0; u < S.ntok; u++)
+        max_len = max(max_len, local_len(__ldg(S.pos[u]), S.row_base, S.row_count));
+    const int my_len = local_len(__ldg(S.pos[t]), S.row_base, S.row_count);
+    const int chunk = split_chunk(max_len, b.nsplit, b.unit);
+    const int lo = sp * chunk, hi = min(my_len, lo + chunk);
+    const int kvh0 = kvg * F::KVH;
+    float* dst0 = S.scratch + (((size_t)t * b.n_q + kvh0 * GQA) * b.nsplit + sp) * PART;
+    if (lo >= hi) {
+        if (threadIdx.x < F::KVH * GQA) {
+            float* d = dst0 + (size_t)threadIdx.x * b.nsplit * PART;
+            d[0] = NEG_SENTINEL;
+            d[1] = 0.f;
+        }
+        return;
+    }
+    const int nstages = (hi - lo + STAGE_ROWS - 1) / STAGE_ROWS;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < F::STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 2 * F::KVH); // the warps owning the stage's two tiles
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // stale ring bytes must at least be finite numbers: zero the ring once
+    for (int i = threadIdx.x; i < ring_bytes<KVK>() / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(ring)[i] = make_uint4(0, 0, 0, 0);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+
+    if (warp == NCW) {
+        // ---------------- producer ----------------
+        for (int i = 0; i < nstages; i++) {
+            const int s = i % F::STAGES;
+            const uint32_t ph = (uint32_t)((i / F::STAGES) & 1);
+            if (i >= F::STAGES && !mbar_wait(&empty[s], ph ^ 1)) break;
+            const int row0 = lo + i * STAGE_ROWS;
+            const int nrows = min(STAGE_ROWS, hi - row0);
+            uint8_t* kdst = ring + (size_t)s * stage_bytes<KVK>();
+            uint8_t* vdst = kdst + STAGE_ROWS * F::PITCH;
+            if (KVK == Q27_KV_T3) {
+                if (lane == 0) {
+                    const uint32_t bytes = (uint32_t)nrows * F::SLICE;
+                    const size_t off = (size_t)(row0 & (PAGE - 1)) * F::SLICE;
+                    mbar_expect_tx(&full[s], 2 * bytes);
+                    bulk_g2s(kdst, static_cast<const uint8_t*>(S.ktab[row0 >> PAGE_SHIFT]) + off,
+                             bytes, &full[s]);
+                    bulk_g2s(vdst, static_cast<const uint8_t*>(S.vtab[row0 >> PAGE_SHIFT]) + off,
+                             bytes, &full[s]);
+                }
+            } else {
+                if (lane == 0) mbar_expect_tx(&full[s], (uint32_t)nrows * 2 * F::SLICE);
+                __syncwarp();
+                if (lane < nrows) {
+                    const int r = row0 + lane;
+                    const size_t off = ((size_t)(r & (PAGE - 1)) * b.n_kv + kvh0) * F::SLICE;
+                    bulk_g2s(kdst + lane * F::PITCH,
+                             static_cast<const uint8_t*>(S.ktab[r >> PAGE_SHIFT]) + off, F::SLICE,
+                             &full[s]);
+                    bulk_g2s(vdst + lane * F::PITCH,
+                             static_cast<const uint8_t*>(S.vtab[r >> PAGE_SHIFT]) + off, F::SLICE,
+                             &full[s]);
+                }
+            }
+        }
+    } else {
+        // ---------------- consumers ----------------
+        const int hq = warp % F::KVH, way = warp / F::KVH;
+        const int kvh = kvh0 + hq;
+        const int g = lane >> 2, c = lane & 3;
+        // Q^T fragments: column n = g is head kvh*6 + g (columns 6, 7 are zero padding)
+        uint32_t qf[16][2];
+        {
+            const float* qh = S.q[t] + (size_t)(kvh * GQA + (g < GQA ? g : 0)) * b.q_stride;
+#pragma unroll
+            for (int s = 0; s < 16; s++)
+#pragma unroll
+                for (int r = 0; r < 2; r++) {
+                    const float x0 = g < GQA ? __ldg(qh + kdim<KVK>(s, c, r, 0)) : 0.f;
+                    const float x1 = g < GQA ? __ldg(qh + kdim<KVK>(s, c, r, 1)) : 0.f;
+                    qf[s][r] = pack_h2(x0, x1);
+                }
+        }
+        WarpAcc A;
+#pragma unroll
+        for (int mt = 0; mt < 16; mt++) A.o[mt][0] = A.o[mt][1] = A.o[mt][2] = A.o[mt][3] = 0.f;
+        A.m[0] = A.m[1] = -INFINITY;
+        A.l[0] = A.l[1] = 0.f;
+        const float sc2 = b.scale * LOG2E;
+        T3Tab tab = t3_tables();
+        (void)tab;
+
+        const int ntiles = (hi - lo + TILE - 1) / TILE;
+        bool alive = true;
+        for (int tile = way; tile < 2 * nstages && alive; tile += WAYS) {
+            const int i = tile >> 1, s = i % F::STAGES;
+            const uint32_t ph = (uint32_t)((i / F::STAGES) & 1);
+            alive = mbar_wait(&full[s], ph);
+            if (!alive) break;
+            if (tile < ntiles) {
+                const int valid = min(TILE, hi - lo - tile * TILE);
+                const uint8_t* ks = ring + (size_t)s * stage_bytes<KVK>() + (tile & 1) * TILE * F::PITCH;
+                const uint8_t* vs = ks + STAGE_ROWS * F::PITCH;
+                if (KVK == Q27_KV_F16) tile_f16<KVK>(A, ks, vs, qf, valid, sc2, lane);
+                else if (KVK == Q27_KV_FP8) tile_fp8(A, ks, vs, qf, valid, sc2, lane);
+                else tile_t3(A, ks, vs, hq, qf, valid, sc2, lane, tab);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+
+        // every consumer is past its last ring read once all of them reach this barrier
+        asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32));
+        // column sums: add the shares of the 8 threads of a column group
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            A.l[0] += __shfl_xor_sync(0xffffffffu, A.l[0], off);
+            A.l[1] += __shfl_xor_sync(0xffffffffu, A.l[1], off);
+        }
+        // per-warp partial [head j][258] into the (now idle) ring; natural-log domain for m
+        float* wp = reinterpret_cast<float*>(ring) + (size_t)warp * GQA * PART;
+        const float LN2 = 0.6931471805599453f;
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const int j = 2 * c + e;
+            if (j < GQA) {
+                if (g == 0) {
+                    wp[j * PART] = A.m[e] == -INFINITY ? NEG_SENTINEL : A.m[e] * LN2;
+                    wp[j * PART + 1] = A.l[e];
+                }
+#pragma unroll
+                for (int mt = 0; mt < 16; mt++) {
+                    wp[j * PART + 2 + vdim<KVK>(mt, g)] = A.o[mt][e];
+                    wp[j * PART + 2 + vdim<KVK>(mt, g + 8)] = A.o[mt][2 + e];
+                }
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32));
+        // merge the WAYS warps of each kv head in a fixed order and write the CTA partial
+        const int tid = threadIdx.x; // 0..255
+        for (int hj = 0; hj < F::KVH * GQA; hj++) {
+            const int h = hj / GQA, j = hj % GQA;
+            const float* src = reinterpret_cast<float*>(ring) + (size_t)h * GQA * PART + j * PART;
+            float mb = NEG_SENTINEL;
+#pragma unroll
+            for (int w = 0; w < WAYS; w++) mb = fmaxf(mb, src[(size_t)w * F::KVH * GQA * PART]);
+            float lb = 0.f, acc = 0.f;
+#pragma unroll
+            for (int w = 0; w < WAYS; w++) {
+                const float* pw = src + (size_t)w * F::KVH * GQA * PART;
+                const float e = pw[0] == NEG_SENTINEL ? 0.f : expf(pw[0] - mb);
+                lb += pw[1] * e;
+                acc += pw[2 + tid] * e;
+            }
+            float* d = dst0 + (size_t)hj * b.nsplit * PART;
+            if (tid == 0) { d[0] = mb; d[1] = lb; }
+            d[2 + tid] = acc;
+        }
+    }
+}
+
+template <int KVK>
+int launch_one(DevBatch& b, int sm_count, cudaStream_t st) {
+    using F = Fmt<KVK>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        Q27_CUDA_TRY(cudaFuncSetAttribute(k_decode_mma<KVK>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          smem_bytes<KVK>()));
+        attr_set = true;
+    }
+    const int groups = b.n_kv / F::KVH;
+    const int per_split = b.nslots * b.max_ntok * groups;
+    int ns = sm_count / per_split;
+    b.nsplit = ns < 1 ? 1 : ns > Q27_MAX_SPLITS ? Q27_MAX_SPLITS : ns;
+    b.unit = STAGE_ROWS;
+    dim3 grid(b.max_ntok, b.nsplit, b.nslots * groups);
+    k_decode_mma<KVK><<<grid, (NCW + 1) * 32, smem_bytes<KVK>(), st>>>(b);
+    Q27_CUDA_TRY(cudaGetLastError());
     return Q27_OK;
 }
+
+} // namespace
+
+int launch_decode_mma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool* done) {
+    *done = false;
+    if (b.n_kv != 4) return Q27_OK; // the ring layouts assume 4 kv heads per row
+    int rc;
+    if (kvk == Q27_KV_F16) rc = launch_one<Q27_KV_F16>(b, sm_count, st);
+    else if (kvk == Q27_KV_FP8) rc = launch_one<Q27_KV_FP8>(b, sm_count, st);
+    else if (kvk == Q27_KV_T3) rc = launch_one<Q27_KV_T3>(b, sm_count, st);
+    else return Q27_ERR_UNSUPPORTED_KIND;
+    if (rc == Q27_OK) *done = true;
+    return rc;
 }
+
+int read_wait_timeout_flag(int* out) {
+    Q27_CUDA_TRY(cudaMemcpyFromSymbol(out, g_wait_timeout_flag, sizeof(int)));
+    return Q27_OK;
+}
+
+} // namespace q27b

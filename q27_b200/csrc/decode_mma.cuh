@@ -7,4 +7,6 @@
 
 namespace q27b {
 int launch_decode_mma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool* done);
+// Reads (synchronously) the flag a kernel sets when one of its bounded waits ran out.
+int read_wait_timeout_flag(int* out);
 }

@@ -1,0 +1,220 @@
+// KV row stores and the per-128-group Walsh-Hadamard rotation: the steps either side of
+// attention in every call stack of the reference (kv_store_T / kv_store_T_t3 / wht_T,
+// src/prefill.cu:1221-1243,2556-2618; kv_store3 / kv_store_t3 / wht3, src/spec3.cu:512-614).
+//
+// The turbo3 encoder follows the reference's serial CPU codec (t3_quant,
+// src/test_kernels.cu:1089-1103) operation for operation -- serial fp32 sums in element
+// order, separate multiply and add -- so its blocks are byte-identical to that codec. (The
+// reference's own device encoder reduces in a tree and is allowed <= 0.2 % index ties
+// against the same CPU codec, src/test_kernels.cu:1150-1316.)
+#include "common.cuh"
+
+namespace q27b {
+namespace {
+
+constexpr float INV_SQRT_128 = 0.08838834764831845f;
+// WHT sign diagonals as bit masks: bit j set <=> element j is -1 (src/turbo3.cuh:42-43)
+__device__ __constant__ uint32_t kS1Neg[4] = {0xE46A0359u, 0x42F85949u, 0xA4C63BBBu, 0x49F250A9u};
+__device__ __constant__ uint32_t kS2Neg[4] = {0x16ACEE90u, 0x3F628FDCu, 0xB7A5357Au, 0xBEA56562u};
+
+__device__ __forceinline__ float sgn(const uint32_t* m, int j) {
+    return (m[j >> 5] >> (j & 31)) & 1u ? -1.f : 1.f;
+}
+
+__device__ __forceinline__ int t3_nearest(float v) { // src/turbo3.cuh:57-66
+    if (v < -0.154496f) return 0;
+    if (v < -0.092804f) return 1;
+    if (v < -0.044243f) return 2;
+    if (v < 0.000000f) return 3;
+    if (v < 0.044243f) return 4;
+    if (v < 0.092804f) return 5;
+    if (v < 0.154496f) return 6;
+    return 7;
+}
+
+// 128-point butterfly over a warp's shared buffer: element pairs (j, j^h), lo+hi / lo-hi.
+// Every output is one add or subtract of two fixed inputs, so the result does not depend
+// on how the work is distributed: bitwise equal to the serial loop.
+__device__ __forceinline__ void butterfly128(float* x, int lane) {
+#pragma unroll
+    for (int h = 1; h < 128; h <<= 1) {
+        __syncwarp();
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int j = lane + 32 * i;
+            const float a = x[j], b = x[j ^ h];
+            v[i] = (j & h) ? __fsub_rn(b, a) : __fadd_rn(a, b);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 4; i++) x[lane + 32 * i] = v[i];
+    }
+    __syncwarp();
+}
+
+// forward rotation of one group in place: x *= s1; butterfly; x *= inv_sqrt*s2 (t3_fwht)
+template <bool INV>
+__device__ __forceinline__ void wht_group(float* x, int lane) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int j = lane + 32 * i;
+        x[j] = __fmul_rn(x[j], sgn(INV ? kS2Neg : kS1Neg, j));
+    }
+    butterfly128(x, lane);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int j = lane + 32 * i;
+        x[j] = __fmul_rn(x[j], __fmul_rn(INV_SQRT_128, sgn(INV ? kS1Neg : kS2Neg, j)));
+    }
+    __syncwarp();
+}
+
+constexpr int ST_WARPS = 8;
+
+// One warp encodes one 128-element group into a 50-byte block.
+__device__ __forceinline__ void t3_encode_group(const float* __restrict__ src, uint8_t* blk,
+                                                float* xs, int lane) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) xs[lane + 32 * i] = src[lane + 32 * i];
+    __syncwarp();
+    float gn = 0.f;
+    if (lane == 0) { // serial sum in element order, as the CPU codec does
+        float nsq = 0.f;
+        for (int j = 0; j < 128; j++) nsq = __fadd_rn(nsq, __fmul_rn(xs[j], xs[j]));
+        gn = sqrtf(nsq);
+    }
+    gn = __shfl_sync(0xffffffffu, gn, 0);
+    const float inv = gn > 1e-10f ? __fdiv_rn(1.f, gn) : 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; i++) xs[lane + 32 * i] = __fmul_rn(xs[lane + 32 * i], inv);
+    __syncwarp();
+    wht_group<false>(xs, lane);
+    // lane owns elements 4*lane .. 4*lane+3: one qs byte, half a signs byte
+    int idx[4];
+    uint32_t qs = 0, hb = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        idx[i] = t3_nearest(xs[4 * lane + i]);
+        qs |= (uint32_t)(idx[i] & 3) << (2 * i);
+        hb |= (uint32_t)((idx[i] >> 2) & 1) << i;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float cv = kT3Centroid[idx[i]];
+        xs[4 * lane + i] = __fmul_rn(cv, cv);
+    }
+    __syncwarp();
+    const uint32_t hb_hi = __shfl_down_sync(0xffffffffu, hb, 1);
+    blk[2 + lane] = (uint8_t)qs;
+    if ((lane & 1) == 0) blk[34 + (lane >> 1)] = (uint8_t)(hb | (hb_hi << 4));
+    if (lane == 0) {
+        float rsq = 0.f;
+        for (int j = 0; j < 128; j++) rsq = __fadd_rn(rsq, xs[j]);
+        const float rn = sqrtf(rsq);
+        const float corr = rn > 1e-10f ? __fdiv_rn(gn, rn) : gn;
+        *reinterpret_cast<__half*>(blk) = __float2half_rn(corr);
+    }
+    __syncwarp();
+}
+
+// rows base_pos .. base_pos+T-1; kT/vT: [T][n_kv*256] fp32
+__global__ void __launch_bounds__(ST_WARPS * 32)
+k_kv_store_T_t3(const float* __restrict__ kT, const float* __restrict__ vT, void* const* ktab,
+                void* const* vtab, int base_pos, int n_kv, int T) {
+    __shared__ float xs[ST_WARPS][128];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gpr = n_kv * 2; // groups per row per side
+    const int64_t total = (int64_t)T * gpr * 2;
+    for (int64_t w = (int64_t)blockIdx.x * ST_WARPS + warp; w < total;
+         w += (int64_t)gridDim.x * ST_WARPS) {
+        const int side = (int)(w & 1);
+        const int64_t gidx = w >> 1;
+        const int t = (int)(gidx / gpr), gi = (int)(gidx % gpr);
+        const int p = base_pos + t;
+        uint8_t* page = static_cast<uint8_t*>((side ? vtab : ktab)[p >> PAGE_SHIFT]);
+        uint8_t* blk = page + ((size_t)(p & (PAGE - 1)) * gpr + gi) * T3_BLK;
+        t3_encode_group((side ? vT : kT) + (size_t)t * gpr * 128 + (size_t)gi * 128, blk, xs[warp],
+                        lane);
+    }
+}
+
+template <bool FP8>
+__global__ void __launch_bounds__(256)
+k_kv_store_T(const float* __restrict__ kT, const float* __restrict__ vT, void* const* ktab,
+             void* const* vtab, int base_pos, int rowlen, int T) {
+    const int64_t total = (int64_t)T * rowlen;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / rowlen), e = (int)(i % rowlen);
+        const int p = base_pos + t;
+        const size_t off = (size_t)(p & (PAGE - 1)) * rowlen + e;
+        if (FP8) {
+            static_cast<__nv_fp8_e4m3*>(ktab[p >> PAGE_SHIFT])[off] = __nv_fp8_e4m3(kT[i]);
+            static_cast<__nv_fp8_e4m3*>(vtab[p >> PAGE_SHIFT])[off] = __nv_fp8_e4m3(vT[i]);
+        } else {
+            static_cast<__half*>(ktab[p >> PAGE_SHIFT])[off] = __float2half_rn(kT[i]);
+            static_cast<__half*>(vtab[p >> PAGE_SHIFT])[off] = __float2half_rn(vT[i]);
+        }
+    }
+}
+
+// In-place rotation of the first head_dim floats of every head of T rows.
+template <bool INV>
+__global__ void __launch_bounds__(ST_WARPS * 32)
+k_wht_T(float* __restrict__ x, int n_heads, int head_stride, int row_stride, int T) {
+    __shared__ float xs[ST_WARPS][128];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t total = (int64_t)T * n_heads * 2;
+    for (int64_t w = (int64_t)blockIdx.x * ST_WARPS + warp; w < total;
+         w += (int64_t)gridDim.x * ST_WARPS) {
+        const int half = (int)(w & 1), h = (int)((w >> 1) % n_heads), t = (int)((w >> 1) / n_heads);
+        float* g = x + (size_t)t * row_stride + (size_t)h * head_stride + half * 128;
+#pragma unroll
+        for (int i = 0; i < 4; i++) xs[warp][lane + 32 * i] = g[lane + 32 * i];
+        __syncwarp();
+        wht_group<INV>(xs[warp], lane);
+#pragma unroll
+        for (int i = 0; i < 4; i++) g[lane + 32 * i] = xs[warp][lane + 32 * i];
+        __syncwarp();
+    }
+}
+
+unsigned blocks_for(int64_t units, int per_block) {
+    int64_t b = (units + per_block - 1) / per_block;
+    return (unsigned)(b < 1 ? 1 : b > 148 * 16 ? 148 * 16 : b);
+}
+
+} // namespace
+
+int launch_kv_store_T(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
+                      int base_pos, int n_kv, int T, cudaStream_t st, int kvk) {
+    if (T == 0) return Q27_OK;
+    if (kvk == Q27_KV_T3) {
+        k_kv_store_T_t3<<<blocks_for((int64_t)T * n_kv * 4, ST_WARPS), ST_WARPS * 32, 0, st>>>(
+            kT, vT, ktab, vtab, base_pos, n_kv, T);
+    } else if (kvk == Q27_KV_FP8) {
+        k_kv_store_T<true><<<blocks_for((int64_t)T * n_kv * HD, 256), 256, 0, st>>>(
+            kT, vT, ktab, vtab, base_pos, n_kv * HD, T);
+    } else if (kvk == Q27_KV_F16) {
+        k_kv_store_T<false><<<blocks_for((int64_t)T * n_kv * HD, 256), 256, 0, st>>>(
+            kT, vT, ktab, vtab, base_pos, n_kv * HD, T);
+    } else {
+        return Q27_ERR_UNSUPPORTED_KIND;
+    }
+    Q27_CUDA_TRY(cudaGetLastError());
+    return Q27_OK;
+}
+
+int launch_wht_T(float* x, int n_heads, int head_stride, int row_stride, int T, bool inv,
+                 cudaStream_t st) {
+    if (T == 0 || n_heads == 0) return Q27_OK;
+    const unsigned blocks = blocks_for((int64_t)T * n_heads * 2, ST_WARPS);
+    if (inv) k_wht_T<true><<<blocks, ST_WARPS * 32, 0, st>>>(x, n_heads, head_stride, row_stride, T);
+    else k_wht_T<false><<<blocks, ST_WARPS * 32, 0, st>>>(x, n_heads, head_stride, row_stride, T);
+    Q27_CUDA_TRY(cudaGetLastError());
+    return Q27_OK;
+}
+
+} // namespace q27b

@@ -70,7 +70,21 @@ def make_case(o: Oracle, kvk: int, rows: int, pos: list, seed: int,
     q = q_raw.copy()
     if kvk == KV_T3:  # the engine receives Q already rotated (src/engine.cuh:1485-1488)
         q[:, :, :HD] = o.wht(np.ascontiguousarray(q_raw[:, :, :HD]))
+    if kvk == KV_FP8:
+        # the reference's fp8 cache is scale-free (src/cuda_common.h:110-121): the per-head
+        # absmax scale of the K side is folded into Q by the caller, the V side's into the
+        # output (Case.scale_out)
+        q[:, :, :HD] *= np.repeat(ks, GQA)[None, :, None]
     return Case(kvk, rows, q, q_raw, k, v, list(pos), ks, vs, kf, vf)
+
+
+def scale_out(case: Case, out: np.ndarray) -> np.ndarray:
+    """Apply the V-side dequant scale (fp8 absmax) to [lanes, N_Q*HD] outputs; identity for
+    the other kinds. Parity is judged on these real-valued outputs."""
+    if case.v_scale is None:
+        return out
+    o3 = np.asarray(out).reshape(out.shape[0], N_Q, HD)
+    return (o3 * np.repeat(case.v_scale, GQA)[None, :, None]).reshape(out.shape)
 
 
 def tolerance_ok(got: np.ndarray, ref: np.ndarray, atol=2e-3, rtol=1e-3):

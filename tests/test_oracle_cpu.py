@@ -158,16 +158,12 @@ def test_prefill_matches_decode_row_by_row(oracle):
 def test_fp8_scale_folding_identity(oracle):
     # C2's per-head absmax scale folds outside the scale-free entry points: scaling Q by
     # s_K and the output by s_V reproduces attention over the scaled dequantised cache
-    c = synth.make_case(oracle, KV_FP8, rows=128, pos=[127], seed=41)
-    qs = c.q.copy()
-    for h in range(24):
-        qs[:, h, :HD] *= c.k_scale[h // 6]
-    out = oracle.attn_decode(qs, c.k, c.v, KV_FP8, c.pos).reshape(1, 24, HD)
-    out = out * np.repeat(c.v_scale, 6)[None, :, None]
+    c = synth.make_case(oracle, KV_FP8, rows=128, pos=[127], seed=41)   # c.q = q_raw * s_K
+    out = synth.scale_out(c, oracle.attn_decode(c.q, c.k, c.v, KV_FP8, c.pos)).reshape(1, 24, HD)
     kd = oracle.kv_dequant(c.k, KV_FP8, 128).astype(np.float64) * c.k_scale[None, :, None]
     vd = oracle.kv_dequant(c.v, KV_FP8, 128).astype(np.float64) * c.v_scale[None, :, None]
     for h in (0, 7, 23):
-        s = kd[:, h // 6] @ c.q[0, h, :HD].astype(np.float64) / 16.0
+        s = kd[:, h // 6] @ c.q_raw[0, h, :HD].astype(np.float64) / 16.0
         w = np.exp(s - s.max())
         ref = (w[:, None] * vd[:, h // 6]).sum(0) / w.sum()
         assert np.abs(out[0, h] - ref).max() < 1e-5

@@ -17,7 +17,7 @@ def run_prefill(oracle, cuda, kvk, base, T, t0=0, SB=None, seed=1, exact=False, 
                 bf16=False):
     SB = T - t0 if SB is None else SB
     c = synth.make_case(oracle, kvk, rows=base + T, pos=[0] * T, seed=seed, bf16=bf16)
-    ref = oracle.attn_prefill(c.q, c.k, c.v, kvk, base, t0, SB)
+    ref = synth.scale_out(c, oracle.attn_prefill(c.q, c.k, c.v, kvk, base, t0, SB))
     perm = None
     if scatter is not None:
         perm = torch.from_numpy(np.random.default_rng(scatter).permutation((base + T + 63) // 64))
@@ -29,7 +29,7 @@ def run_prefill(oracle, cuda, kvk, base, T, t0=0, SB=None, seed=1, exact=False, 
     Q.attn_prefill_T(qT, synth.Q_STRIDE, synth.Q_ROW, ks.tab, vs.tab, outT, synth.OUT_ROW, part,
                      base, t0, SB, 24, 4, 256, SCALE, kvk=kvk, exact=exact)
     torch.cuda.synchronize()
-    return outT.cpu().numpy(), ref
+    return synth.scale_out(c, outT.cpu().numpy()), ref
 
 
 @pytest.mark.parametrize("kvk", [KV_F16, KV_FP8, KV_T3])
