@@ -1,0 +1,457 @@
+#!/usr/bin/env python
+"""Benchmark of the attention hot path on synthetic data.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c3] [--impl reference]
+
+Default workload (N=1) is the 131K-context turbo3 decode the headline metric is quoted on:
+2 slots x 1 query token, GQA 24/4, head_dim 256, 131072 turbo3 rows per slot (K/V drawn
+N(0,1) with 2 % of the (kv head, dim) channels scaled x8, encoded by the engine's turbo3
+store). With N > 1 ranks the KV sequence is split: every rank holds one 131072-row shard of
+each slot (context N x 131072), computes partials over it, and the {m, l, acc} partials
+are all-gathered over NCCL and merged (weak scaling: per-GPU work fixed).
+
+One "step" = one pass of decode attention over one set of resident KV caches. The step
+rotates over several distinct cache copies whose total exceeds twice the L2, so every
+timed read comes from HBM.
+
+Prints ONE JSON line (rank 0). `--impl reference` times the CPU restatement of the
+reference's scalar host attention (oracle/) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+N_Q, N_KV, HD, GQA = 24, 4, 256, 6
+Q_STRIDE = 2 * HD
+SCALE = 1.0 / 16.0
+KV_F16, KV_FP8, KV_T3 = 0, 1, 2
+ROW_BYTES = {KV_F16: 2048, KV_FP8: 1024, KV_T3: 400}
+KIND_NAME = {KV_F16: "fp16", KV_FP8: "fp8-e4m3", KV_T3: "turbo3"}
+
+# name -> (kvk, slots, lanes, rows per slot per rank, outlier fraction)
+WORKLOADS = {
+    "c1": (KV_F16, 1, 1, 4096, 0.0),
+    "c2": (KV_FP8, 1, 6, 32768, 0.0),
+    "c3": (KV_T3, 2, 1, 131072, 0.02),     # BASELINE config 3 (the headline, default)
+    "c5": (KV_T3, 8, 6, 262144, 0.02),     # rows are split over ranks
+}
+METRIC = "decode/verify attn KV GB/s (frac of HBM peak) @131K ctx"
+L2_BYTES = 126 * 2**20
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from the
+# ncu captures summarised under profiles/ (None until a capture exists for the workload)
+NCU_TRAFFIC = {}
+
+
+def measured_peak_gbs() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        clocks, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in self.samples:
+            f = [x.strip() for x in s.split(",")]
+            if len(f) < 6:
+                continue
+            try:
+                clocks.append(float(f[0]))
+                maxes.append(float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[2:6]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        clocks.sort()
+        # under load = the upper half of the samples (idle samples sit at the floor clock)
+        load = clocks[len(clocks) // 2:] if clocks else []
+        med = load[len(load) // 2] if load else None
+        return {"sm_mhz": med, "sm_max_mhz": max(maxes) if maxes else None,
+                "reasons": sorted(reasons), "samples": len(clocks)}
+
+
+def make_turbo3_or_scalar_cache(torch, Q, kvk, rows, seed, outlier_frac, device):
+    """One slot's K and V caches, generated and encoded on the device in row chunks."""
+    rb = ROW_BYTES[kvk]
+    npages = (rows + 63) // 64
+    sides = []
+    for _ in range(2):
+        store = torch.empty(npages * 64 * rb, dtype=torch.uint8, device=device)
+        sides.append((store, Q.mk_tab(store, rb, rows)))
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    cg = torch.Generator(device="cpu")
+    cg.manual_seed(seed + 7)
+    mult = []
+    for _ in range(2):
+        m = torch.ones(N_KV * HD, device=device)
+        if outlier_frac > 0:
+            n = max(1, int(round(outlier_frac * N_KV * HD)))
+            m[torch.randperm(N_KV * HD, generator=cg)[:n].to(device)] = 8.0
+        mult.append(m)
+    chunk = 8192
+    for r0 in range(0, rows, chunk):
+        t = min(chunk, rows - r0)
+        k = torch.randn((t, N_KV * HD), generator=g, device=device) * mult[0]
+        v = torch.randn((t, N_KV * HD), generator=g, device=device) * mult[1]
+        # values pass through fp16 first, as the BASELINE generator states
+        k, v = k.half().float(), v.half().float()
+        if kvk == KV_T3:
+            Q.kv_store_T_t3(k, v, sides[0][1], sides[1][1], r0, N_KV, HD, t)
+        elif kvk == KV_FP8:
+            # per-(side, head) absmax scale to +-448; the scale folds into Q / the output
+            Q.kv_store_T(k * (448.0 / 6.0), v * (448.0 / 6.0), sides[0][1], sides[1][1], r0,
+                         N_KV * HD, t, fp8=True)
+        else:
+            Q.kv_store_T(k, v, sides[0][1], sides[1][1], r0, N_KV * HD, t, fp8=False)
+    torch.cuda.synchronize()
+    return sides
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import q27_b200 as Q
+    from q27_b200 import dist as qd
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            raise SystemExit("launch N>1 with torch.distributed.run (one rank per GPU)")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    if Q._lib.lib().q27_device_arch() != 1000:
+        raise SystemExit("the engine is built for sm_100a only")
+
+    kvk, nslots, lanes, rows, outl = WORKLOADS[args.workload]
+    if args.workload == "c5":                # strong scaling: 262144 rows split over the ranks
+        rows_total = rows
+        lo, hi = qd.shard_ranges(rows_total, world)[rank]
+        scaling = "strong"
+    else:                                    # weak scaling: every rank holds `rows` rows
+        rows_total = rows * world
+        lo, hi = rank * rows, (rank + 1) * rows
+        scaling = "weak"
+    local_rows = hi - lo
+    bytes_per_slot = local_rows * ROW_BYTES[kvk] * 2
+    step_bytes_rank = nslots * bytes_per_slot          # algorithmic: K+V rows, counted once
+    copies = max(2, -(-2 * L2_BYTES // step_bytes_rank) + 1) if step_bytes_rank < 4 * L2_BYTES else 2
+    copies = min(copies, 24)
+
+    # ---- resident state: `copies` distinct cache sets per slot --------------------------
+    caches = [[make_turbo3_or_scalar_cache(torch, Q, kvk, local_rows, 1000 * rank + 10 * c + s,
+                                           outl, dev) for s in range(nslots)]
+              for c in range(copies)]
+    g = torch.Generator(device="cpu")
+    g.manual_seed(4242)
+    q_host = torch.randn((nslots, lanes, N_Q * Q_STRIDE), generator=g).pin_memory()
+    pos_host = torch.tensor([[rows_total - lanes + t for t in range(lanes)] for _ in range(nslots)],
+                            dtype=torch.int32).pin_memory()
+    q_dev = q_host.to(dev)
+    pos_dev = pos_host.to(dev)
+    out_dev = torch.zeros((nslots, lanes, N_Q * HD), device=dev)
+    out_host = torch.zeros((nslots, lanes, N_Q * HD)).pin_memory()
+    scratch = [torch.empty(Q.decode_scratch_floats(lanes), device=dev) for _ in range(nslots)]
+    ex = qd.PartialExchange.create(nslots, lanes, N_Q, world, dev) if world > 1 else None
+    merged = torch.zeros((nslots * lanes * N_Q, HD), device=dev)
+
+    def slots_for(c):
+        return [Q.SlotArgs(caches[c][s][0][1], caches[c][s][1][1],
+                           [q_dev[s, t] for t in range(lanes)],
+                           [pos_dev[s, t:t + 1] for t in range(lanes)],
+                           [out_dev[s, t] for t in range(lanes)], scratch[s],
+                           row_base=lo if world > 1 else 0,
+                           row_count=local_rows if world > 1 else 2**31 - 1)
+                for s in range(nslots)]
+
+    slot_sets = [slots_for(c) for c in range(copies)]
+
+    def step(i):
+        sl = slot_sets[i % copies]
+        if world > 1:
+            qd.sharded_decode(sl, ex, merged, Q_STRIDE, N_KV, SCALE, kvk)
+        else:
+            Q.attn_decode_batched(sl, Q_STRIDE, N_Q, N_KV, HD, SCALE, kvk=kvk)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+            torch.cuda.synchronize()
+
+    # ---- device-resident timing ---------------------------------------------------------
+    for i in range(args.warmup):
+        step(i)
+    barrier()
+    sampler = ClockSampler(local_rank)
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.15)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    e1.record()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # ---- dominant kernel alone (events recorded by the library around the partial kernel)
+    k0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    k1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        k0[i].record()
+        k1[i].record()                          # materialise the handles; re-recorded below
+        Q._lib.lib().q27_set_kernel_events(k0[i].cuda_event, k1[i].cuda_event)
+        step(args.warmup + i)
+    Q._lib.lib().q27_set_kernel_events(None, None)
+    barrier()
+    kms = sorted(a.elapsed_time(b) for a, b in zip(k0, k1))
+    kernel_ms = sum(kms) / len(kms)
+
+    # ---- end to end through the public call with host buffers ---------------------------
+    def e2e_step(i):
+        q_dev.copy_(q_host, non_blocking=True)
+        pos_dev.copy_(pos_host, non_blocking=True)
+        step(i)
+        src = merged.view(nslots, lanes, N_Q * HD) if world > 1 else out_dev
+        out_host.copy_(src, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        e2e_step(args.warmup + i)
+    barrier()
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    clocks = sampler.stop() if rank == 0 else None
+
+    flag = __import__("ctypes").c_int(0)
+    Q._lib.lib().q27_wait_timeout_flag(__import__("ctypes").byref(flag))
+    if flag.value:
+        raise SystemExit("a bounded device wait timed out during the run: numbers are invalid")
+
+    total_bytes = step_bytes_rank * world
+    value = total_bytes * args.steps / (ms * 1e-3) / 1e9
+    e2e_value = total_bytes * args.steps / e2e_s / 1e9
+    peak, which = measured_peak_gbs()
+    achieved = step_bytes_rank / (kernel_ms * 1e-3) / 1e9
+    launches_per_step = 2 + (1 if world > 1 else 0)
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+        "dtype": "u8" if kvk != KV_F16 else "f16", "data": "synthetic",
+        "config": {"workload": args.workload, "kv_kind": KIND_NAME[kvk], "slots": nslots,
+                   "lanes": lanes, "context_rows_per_slot": rows_total,
+                   "rows_per_gpu_per_slot": local_rows, "heads": "24q/4kv", "head_dim": HD,
+                   "parallelism": f"kv-split x{world}" if world > 1 else "single gpu",
+                   "l2_policy": f"inputs rotate over {copies} cache copies "
+                                f"({copies * step_bytes_rank / 2**20:.0f} MiB > 2 x L2)"},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": int(q_host.numel() * 4 + pos_host.numel() * 4),
+                "d2h_bytes_per_step": int(out_host.numel() * 4),
+                "note": "Q lanes + positions in from pinned host memory, outputs back, one "
+                        "stream sync per step; the KV cache is engine state resident in HBM"},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": NCU_TRAFFIC.get(args.workload),
+                     "peak_source": f"{which} copy bandwidth (MEASURED_PEAKS.json)",
+                     "kernel": "k_decode_mma (split-KV partials)", "kernel_ms": round(kernel_ms, 5),
+                     "algorithmic_bytes_per_launch": step_bytes_rank,
+                     "frac_of_nominal_8TBps": round(achieved / 8000.0, 4)},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(args, caches[0], q_host, pos_host, kvk, nslots, lanes,
+                                            local_rows, out_dev_check=(slot_sets[0], out_dev, Q))
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def cpu_baseline(args, cache_set, q_host, pos_host, kvk, nslots, lanes, rows, out_dev_check=None,
+                 budget_s=20.0):
+    """Times the CPU oracle (a port of the reference's scalar host attention) on the host
+    cores over a bounded sample of the same workload, and cross-checks the GPU output."""
+    import numpy as np
+    import torch
+
+    from tests.oracle_lib import Oracle
+    o = Oracle()
+    cores = os.cpu_count() or 1
+    rb = ROW_BYTES[kvk]
+    # sample: all slots and lanes, the first `srows` rows (the oracle's cost is linear in rows)
+    srows = rows
+    k0 = cache_set[0][0][0][: 4096 * rb].cpu().numpy().reshape(4096, rb)
+    v0 = cache_set[0][1][0][: 4096 * rb].cpu().numpy().reshape(4096, rb)
+    q = q_host[0].numpy().reshape(lanes, N_Q, Q_STRIDE)
+    t0 = time.perf_counter()
+    o.attn_decode(q, k0, v0, kvk, [4095] * lanes)
+    per_row = (time.perf_counter() - t0) / 4096
+    srows = int(min(rows, max(4096, budget_s / max(per_row, 1e-9) / nslots)))
+    secs = 0.0
+    for s in range(nslots):
+        k = cache_set[s][0][0][: srows * rb].cpu().numpy().reshape(srows, rb)
+        v = cache_set[s][1][0][: srows * rb].cpu().numpy().reshape(srows, rb)
+        qs = q_host[s].numpy().reshape(lanes, N_Q, Q_STRIDE)
+        pos = [srows - lanes + t for t in range(lanes)]
+        t0 = time.perf_counter()
+        ref = o.attn_decode(qs, k, v, kvk, pos)
+        secs += time.perf_counter() - t0
+        if out_dev_check is not None and srows == rows and s == 0:
+            slot_set, out_dev, Q = out_dev_check
+            Q.attn_decode_batched(slot_set, Q_STRIDE, N_Q, N_KV, HD, SCALE, kvk=kvk)
+            torch.cuda.synchronize()
+            got = out_dev[0].cpu().numpy()
+            err = np.abs(got - ref)
+            assert (err <= 2e-3 + 1e-3 * np.abs(ref)).all(), "GPU result disagrees with the oracle"
+    sample_bytes = nslots * srows * rb * 2
+    return {"value": round(sample_bytes / secs / 1e9, 4), "unit": "GB/s", "cores": cores,
+            "kind": "port",
+            "sample": f"{nslots} slots x {lanes} lanes x first {srows} of {rows} rows, one pass, "
+                      f"{secs:.2f} s (OpenMP over lane x head)"}
+
+
+def run_reference(args):
+    """The reference arm: the CPU restatement of the reference's scalar host attention
+    (its own host_ref lives inside a test binary and cannot be built apart), all host
+    threads, same config; each step is a bounded row sample of the workload."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    from tests.oracle_lib import Oracle
+    o = Oracle()
+    kvk, nslots, lanes, rows, outl = WORKLOADS[args.workload]
+    world = args.gpus
+    rows_total = rows if args.workload == "c5" else rows * world
+    rb = ROW_BYTES[kvk]
+    cores = os.cpu_count() or 1
+    srows = min(rows_total, 16384)
+    kf = o.randn(srows * N_KV * HD, 1).reshape(srows, N_KV * HD)
+    vf = o.randn(srows * N_KV * HD, 2).reshape(srows, N_KV * HD)
+    if kvk == KV_T3:
+        k, v = o.t3_quant(kf).reshape(srows, rb), o.t3_quant(vf).reshape(srows, rb)
+    elif kvk == KV_FP8:
+        k, v = o.to_e4m3(kf * 74.0), o.to_e4m3(vf * 74.0)
+    else:
+        k, v = o.to_half_bits(kf).view(np.uint8).reshape(srows, rb), \
+            o.to_half_bits(vf).view(np.uint8).reshape(srows, rb)
+    q = o.randn(lanes * N_Q * Q_STRIDE, 3).reshape(lanes, N_Q, Q_STRIDE)
+    pos = [srows - lanes + t for t in range(lanes)]
+    for _ in range(max(1, min(args.warmup, 1))):
+        o.attn_decode(q, k, v, kvk, pos)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for _s in range(nslots):
+            o.attn_decode(q, k, v, kvk, pos)
+    secs = time.perf_counter() - t0
+    sample_bytes = nslots * srows * rb * 2
+    value = sample_bytes * args.steps / secs / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(secs / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong" if args.workload == "c5" else "weak", "vs_baseline": None,
+        "dtype": "f64", "data": "synthetic",
+        "config": {"workload": args.workload, "kv_kind": KIND_NAME[kvk], "slots": nslots,
+                   "lanes": lanes, "context_rows_per_slot": rows_total, "heads": "24q/4kv",
+                   "head_dim": HD},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"each step = {nslots} slots x {lanes} lanes x {srows} of "
+                                   f"{rows_total} rows (cost is linear in rows)"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="c3", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

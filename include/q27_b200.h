@@ -63,6 +63,12 @@ int q27_device_arch(void);
  * not call under stream capture). 0 = no wait has ever timed out in this process. */
 int q27_wait_timeout_flag(int* out);
 
+/* Measurement hook: when both events (cudaEvent_t) are non-NULL, every decode / verify
+ * call made by this thread records ev_start before and ev_stop after its split-KV partial
+ * kernel, on the call's stream, so that the dominant kernel can be timed apart from the
+ * combine. Pass NULLs to switch it off. Not for use under stream capture. */
+int q27_set_kernel_events(void* ev_start, void* ev_stop);
+
 /* bytes per cache row: fp16 n_kv*512, fp8 n_kv*256, turbo3 n_kv*100; -1 = refused kind */
 int64_t q27_kv_row_bytes(int kvk, int n_kv_heads);
 /* floats the caller must provide as `scratch` for ntok lanes:

@@ -49,6 +49,7 @@ SIGNATURES = {
     "q27_last_cuda_error": (_i, []),
     "q27_device_arch": (_i, []),
     "q27_wait_timeout_flag": (_i, [C.POINTER(_i)]),
+    "q27_set_kernel_events": (_i, [_vp, _vp]),
     "q27_kv_row_bytes": (_i64, [_i, _i]),
     "q27_decode_scratch_floats": (_i64, [_i, _i]),
     "q27_prefill_part_floats": (_i64, [_i, _i]),

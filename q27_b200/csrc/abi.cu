@@ -76,6 +76,10 @@ int build_batch(const q27_slot* slots, int nslots, int q_stride, int n_q, int n_
 
 enum Family { FAM_AUTO = 0, FAM_EXACT = 1 };
 
+// Optional measurement hook: when set, the split-KV partial kernel of every decode call
+// made by this thread is bracketed by these two events on the launch stream.
+thread_local cudaEvent_t g_ev_start = nullptr, g_ev_stop = nullptr;
+
 int run_decode(const q27_slot* slots, int nslots, int lanes_stride, int q_stride, int n_q, int n_kv,
                int head_dim, float scale, float* partial_out, void* stream, int kvk, Family fam) {
     DevBatch b;
@@ -87,6 +91,7 @@ int run_decode(const q27_slot* slots, int nslots, int lanes_stride, int q_stride
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int sms = sm_count();
     bool done = false;
+    if (g_ev_start) Q27_CUDA_TRY(cudaEventRecord(g_ev_start, st));
     if (fam == FAM_AUTO) {
         rc = launch_decode_mma(b, kvk, sms, st, &done);
         if (rc) return rc;
@@ -100,6 +105,7 @@ int run_decode(const q27_slot* slots, int nslots, int lanes_stride, int q_stride
         rc = launch_exact_partials(b, kvk, st);
         if (rc) return rc;
     }
+    if (g_ev_stop) Q27_CUDA_TRY(cudaEventRecord(g_ev_stop, st));
     return launch_combine(b, partial_out, partial_out ? lanes_stride : b.max_ntok, st);
 }
 
@@ -237,6 +243,12 @@ int q27_attn_prefill_T(const float* qT, int q_stride, int q_row, const void* con
                        int head_dim, float scale, void* stream, int kvk) {
     return q27_attn_prefill_T_exact(qT, q_stride, q_row, ktab, vtab, outT, out_row, part, base_pos,
                                     t0, SB, n_q_heads, n_kv_heads, head_dim, scale, stream, kvk);
+}
+
+int q27_set_kernel_events(void* ev_start, void* ev_stop) {
+    g_ev_start = static_cast<cudaEvent_t>(ev_start);
+    g_ev_stop = static_cast<cudaEvent_t>(ev_stop);
+    return Q27_OK;
 }
 
 int q27_wait_timeout_flag(int* out) {
