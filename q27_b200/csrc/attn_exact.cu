@@ -163,9 +163,12 @@ k_combine(const __grid_constant__ DevBatch b, float* __restrict__ partial_out, i
     const float inv = lg > 0.f ? 1.0f / lg : 0.f;
     for (int d = threadIdx.x; d < HD; d += blockDim.x) {
         float a = 0.f;
+        // splits with weight 0 (sentinels) hold undefined accumulators: select, never multiply
+#pragma unroll 8
         for (int sp = 0; sp < b.nsplit; sp++) {
             const float w = s_w[sp];
-            if (w != 0.f) a += pp[(size_t)sp * PART + 2 + d] * w;
+            const float v = pp[(size_t)sp * PART + 2 + d];
+            a += w != 0.f ? v * w : 0.f;
         }
         if (NORMALISE) S.out[t][(size_t)h * HD + d] = a * inv;
         else partial_out[(((size_t)slot * lanes_stride + t) * b.n_q + h) * PART + 2 + d] = a;

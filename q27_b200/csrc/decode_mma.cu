@@ -30,6 +30,9 @@ constexpr int NCW = 8;            // consumer warps
 constexpr int STAGE_ROWS = 32;    // rows per ring stage (= 2 key tiles; never crosses a page)
 constexpr int TILE = 16;          // keys per MMA tile
 constexpr float LOG2E = 1.4426950408889634f;
+#ifndef Q27_ABLATE
+#define Q27_ABLATE 0   // timing experiments only: 1 skip K lookups, 2 skip V lookups, 4 skip MMAs
+#endif
 
 template <int KVK> struct Fmt;
 template <> struct Fmt<Q27_KV_F16> {
@@ -101,6 +104,11 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 }
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+    if (Q27_ABLATE & 4) {
+        c[0] += __uint_as_float(a0 ^ b0); c[1] += __uint_as_float(a1 ^ b1);
+        c[2] += __uint_as_float(a2); c[3] += __uint_as_float(a3);
+        return;
+    }
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%0,%1,%2,%3};"
@@ -131,17 +139,31 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
 }
-__device__ __forceinline__ uint32_t lds32(const uint8_t* p) {
-    return *reinterpret_cast<const uint32_t*>(p);
+// shared-space loads on 32-bit shared addresses (no generic-pointer arithmetic)
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
 }
-__device__ __forceinline__ uint32_t lds16(const uint8_t* p) {
-    return *reinterpret_cast<const uint16_t*>(p);
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
 }
 // 32 bits starting at a 2-byte-aligned shared address
-__device__ __forceinline__ uint32_t lds32_a2(const uint8_t* p, bool aligned4) {
-    if (aligned4) return lds32(p);
-    const uint32_t lo = lds32(p - 2), hi = lds32(p + 2);
+__device__ __forceinline__ uint32_t lds32_a2(uint32_t a, bool aligned4) {
+    if (aligned4) return lds32(a);
+    const uint32_t lo = lds32(a - 2), hi = lds32(a + 2);
     return __funnelshift_r(lo, hi, 16);
+}
+__device__ __forceinline__ float lds_half(uint32_t a) {
+    return __half2float(__ushort_as_half((unsigned short)lds16(a)));
 }
 
 // ---- index maps: (MMA-logical index) -> (actual dimension / key) -------------------------
@@ -258,7 +280,7 @@ __device__ __forceinline__ void softmax_tile(WarpAcc& A, const float (&s)[4], fl
 // real keys in the tile (rows >= valid are masked). qf = Q^T fragments, 2 regs per step.
 
 template <int KVK>
-__device__ __forceinline__ void tile_f16(WarpAcc& A, const uint8_t* ks, const uint8_t* vs,
+__device__ __forceinline__ void tile_f16(WarpAcc& A, uint32_t ks, uint32_t vs,
                                          const uint32_t (&qf)[16][2], int valid, float sc2,
                                          int lane) {
     constexpr int P = Fmt<Q27_KV_F16>::PITCH;
@@ -266,7 +288,7 @@ __device__ __forceinline__ void tile_f16(WarpAcc& A, const uint8_t* ks, const ui
     float d[4] = {0.f, 0.f, 0.f, 0.f};
     {
         const int row = (lane & 7) + ((lane >> 3) & 1) * 8, col = (lane >> 4) * 8;
-        const uint32_t base = smem_u32(ks) + row * P + col * 2;
+        const uint32_t base = ks + row * P + col * 2;
 #pragma unroll
         for (int s = 0; s < 16; s++) {
             uint32_t a0, a1, a2, a3;
@@ -284,7 +306,7 @@ __device__ __forceinline__ void tile_f16(WarpAcc& A, const uint8_t* ks, const ui
     const uint32_t b1 = movmatrix_t(pack_h2(p[2], p[3]));
     {
         const int row = (lane & 7) + (lane >> 4) * 8, col = ((lane >> 3) & 1) * 8;
-        const uint32_t base = smem_u32(vs) + row * P + col * 2;
+        const uint32_t base = vs + row * P + col * 2;
 #pragma unroll
         for (int mt = 0; mt < 16; mt++) {
             uint32_t a0, a1, a2, a3;
@@ -299,7 +321,7 @@ __device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t two_bytes) {
     return (uint32_t)h.x | ((uint32_t)h.y << 16);
 }
 
-__device__ __forceinline__ void tile_fp8(WarpAcc& A, const uint8_t* ks, const uint8_t* vs,
+__device__ __forceinline__ void tile_fp8(WarpAcc& A, uint32_t ks, uint32_t vs,
                                          const uint32_t (&qf)[16][2], int valid, float sc2,
                                          int lane) {
     constexpr int P = Fmt<Q27_KV_FP8>::PITCH;
@@ -308,8 +330,8 @@ __device__ __forceinline__ void tile_fp8(WarpAcc& A, const uint8_t* ks, const ui
     float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-        const uint4 x = *reinterpret_cast<const uint4*>(ks + r0 * P + 16 * (c + 4 * j));
-        const uint4 y = *reinterpret_cast<const uint4*>(ks + r1 * P + 16 * (c + 4 * j));
+        const uint4 x = lds128(ks + r0 * P + 16 * (c + 4 * j));
+        const uint4 y = lds128(ks + r1 * P + 16 * (c + 4 * j));
         const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, yw[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -330,10 +352,10 @@ __device__ __forceinline__ void tile_fp8(WarpAcc& A, const uint8_t* ks, const ui
 #pragma unroll
     for (int hh = 0; hh < 2; hh++) {
         const int ch = 4 * (g & 1) + (g >> 1) + 8 * hh;
-        const uint4 k0 = *reinterpret_cast<const uint4*>(vs + (c) * P + 16 * ch);
-        const uint4 k1 = *reinterpret_cast<const uint4*>(vs + (c + 4) * P + 16 * ch);
-        const uint4 k2 = *reinterpret_cast<const uint4*>(vs + (c + 8) * P + 16 * ch);
-        const uint4 k3 = *reinterpret_cast<const uint4*>(vs + (c + 12) * P + 16 * ch);
+        const uint4 k0 = lds128(vs + (c) * P + 16 * ch);
+        const uint4 k1 = lds128(vs + (c + 4) * P + 16 * ch);
+        const uint4 k2 = lds128(vs + (c + 8) * P + 16 * ch);
+        const uint4 k3 = lds128(vs + (c + 12) * P + 16 * ch);
         const uint32_t w0[4] = {k0.x, k0.y, k0.z, k0.w}, w1[4] = {k1.x, k1.y, k1.z, k1.w};
         const uint32_t w2[4] = {k2.x, k2.y, k2.z, k2.w}, w3[4] = {k3.x, k3.y, k3.z, k3.w};
 #pragma unroll
@@ -348,22 +370,22 @@ __device__ __forceinline__ void tile_fp8(WarpAcc& A, const uint8_t* ks, const ui
     }
 }
 
-__device__ __forceinline__ void tile_t3(WarpAcc& A, const uint8_t* ks, const uint8_t* vs, int kvh,
+__device__ __forceinline__ void tile_t3(WarpAcc& A, uint32_t ks, uint32_t vs, int kvh,
                                         const uint32_t (&qf)[16][2], int valid, float sc2,
                                         int lane, const T3Tab& tab) {
     constexpr int P = Fmt<Q27_KV_T3>::PITCH;
     const int g = lane >> 2, c = lane & 3;
     // ---- scores: per 128-dim block an accumulator of centroid dot products ----
     float dk[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    const uint8_t* kr0 = ks + g * P + kvh * 100;
-    const uint8_t* kr1 = ks + (g + 8) * P + kvh * 100;
+    const uint32_t kr0 = ks + g * P + kvh * 100;
+    const uint32_t kr1 = kr0 + 8 * P;
 #pragma unroll
     for (int b = 0; b < 2; b++) {
         // block b starts at +50b: 4-byte aligned for b == 1, 2 mod 4 for b == 0; qs at +2,
         // signs at +34
         const bool al = (b == 1);
-        const uint8_t* q0 = kr0 + 50 * b + 2 + 8 * c;
-        const uint8_t* q1 = kr1 + 50 * b + 2 + 8 * c;
+        const uint32_t q0 = kr0 + 50 * b + 2 + 8 * c;
+        const uint32_t q1 = kr1 + 50 * b + 2 + 8 * c;
         const uint32_t s0 = lds32_a2(kr0 + 50 * b + 34 + 4 * c, al);
         const uint32_t s1 = lds32_a2(kr1 + 50 * b + 34 + 4 * c, al);
 #pragma unroll
@@ -371,10 +393,15 @@ __device__ __forceinline__ void tile_t3(WarpAcc& A, const uint8_t* ks, const uin
             uint32_t ze0, zo0, ze1, zo1, h0[8], h1[8];
             t3_selectors(lds32_a2(q0 + 4 * w, al), w ? s0 >> 16 : s0 & 0xffffu, ze0, zo0);
             t3_selectors(lds32_a2(q1 + 4 * w, al), w ? s1 >> 16 : s1 & 0xffffu, ze1, zo1);
-            t3_lookup(tab, ze0, h0);
-            t3_lookup(tab, zo0, h0 + 4);
-            t3_lookup(tab, ze1, h1);
-            t3_lookup(tab, zo1, h1 + 4);
+            if (Q27_ABLATE & 1) {
+#pragma unroll
+                for (int x = 0; x < 8; x++) { h0[x] = ze0 + x; h1[x] = zo1 ^ x; }
+            } else {
+                t3_lookup(tab, ze0, h0);
+                t3_lookup(tab, zo0, h0 + 4);
+                t3_lookup(tab, ze1, h1);
+                t3_lookup(tab, zo1, h1 + 4);
+            }
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 const int s = 8 * b + 4 * w + i;
@@ -384,24 +411,22 @@ __device__ __forceinline__ void tile_t3(WarpAcc& A, const uint8_t* ks, const uin
         }
     }
     // norms: K for the score recombination, V folded into P
-    const float nk00 = __half2float(*reinterpret_cast<const __half*>(kr0));
-    const float nk01 = __half2float(*reinterpret_cast<const __half*>(kr0 + 50));
-    const float nk10 = __half2float(*reinterpret_cast<const __half*>(kr1));
-    const float nk11 = __half2float(*reinterpret_cast<const __half*>(kr1 + 50));
+    const float nk00 = lds_half(kr0), nk01 = lds_half(kr0 + 50);
+    const float nk10 = lds_half(kr1), nk11 = lds_half(kr1 + 50);
     float sv[4], p[4];
     sv[0] = g < valid ? (dk[0][0] * nk00 + dk[1][0] * nk01) * sc2 : -INFINITY;
     sv[1] = g < valid ? (dk[0][1] * nk00 + dk[1][1] * nk01) * sc2 : -INFINITY;
     sv[2] = g + 8 < valid ? (dk[0][2] * nk10 + dk[1][2] * nk11) * sc2 : -INFINITY;
     sv[3] = g + 8 < valid ? (dk[0][3] * nk10 + dk[1][3] * nk11) * sc2 : -INFINITY;
     softmax_tile(A, sv, p);
-    const uint8_t* vr0 = vs + g * P + kvh * 100;
-    const uint8_t* vr1 = vs + (g + 8) * P + kvh * 100;
+    const uint32_t vr0 = vs + g * P + kvh * 100;
+    const uint32_t vr1 = vr0 + 8 * P;
     uint32_t pb[2][2]; // [block][key half] P^T fragments with the V norm folded in
 #pragma unroll
     for (int b = 0; b < 2; b++) {
         // masked rows may hold stale bytes: keep their weight an exact zero
-        const float n0 = g < valid ? __half2float(*reinterpret_cast<const __half*>(vr0 + 50 * b)) : 0.f;
-        const float n1 = g + 8 < valid ? __half2float(*reinterpret_cast<const __half*>(vr1 + 50 * b)) : 0.f;
+        const float n0 = g < valid ? lds_half(vr0 + 50 * b) : 0.f;
+        const float n1 = g + 8 < valid ? lds_half(vr1 + 50 * b) : 0.f;
         pb[b][0] = movmatrix_t(pack_h2(p[0] * n0, p[1] * n0));
         pb[b][1] = movmatrix_t(pack_h2(p[2] * n1, p[3] * n1));
     }
@@ -414,7 +439,7 @@ __device__ __forceinline__ void tile_t3(WarpAcc& A, const uint8_t* ks, const uin
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             const int key = 2 * c + (k & 1) + 8 * (k >> 1);
-            const uint8_t* blk = vs + key * P + kvh * 100 + 50 * b;
+            const uint32_t blk = vs + key * P + kvh * 100 + 50 * b;
             t3_selectors(lds32_a2(blk + 2 + 4 * g, al), lds16(blk + 34 + 2 * g), ze[k], zo[k]);
         }
         uint32_t hp[2][16]; // [pair][dim order] half2 = (key A, key B) of one dim
@@ -425,10 +450,15 @@ __device__ __forceinline__ void tile_t3(WarpAcc& A, const uint8_t* ks, const uin
             const uint32_t ze_hi = ((ea >> 4) & 0x0F0F0F0Fu) | (eb & 0xF0F0F0F0u);
             const uint32_t zo_lo = (oa & 0x0F0F0F0Fu) | ((ob << 4) & 0xF0F0F0F0u);
             const uint32_t zo_hi = ((oa >> 4) & 0x0F0F0F0Fu) | (ob & 0xF0F0F0F0u);
-            t3_lookup(tab, ze_lo, hp[pr]);       // dims e16 = 0, 4, 8, 12
-            t3_lookup(tab, ze_hi, hp[pr] + 4);   // 2, 6, 10, 14
-            t3_lookup(tab, zo_lo, hp[pr] + 8);   // 1, 5, 9, 13
-            t3_lookup(tab, zo_hi, hp[pr] + 12);  // 3, 7, 11, 15
+            if (Q27_ABLATE & 2) {
+#pragma unroll
+                for (int x = 0; x < 16; x++) hp[pr][x] = (ze_lo + x) ^ zo_hi ^ (ze_hi + zo_lo);
+            } else {
+                t3_lookup(tab, ze_lo, hp[pr]);       // dims e16 = 0, 4, 8, 12
+                t3_lookup(tab, ze_hi, hp[pr] + 4);   // 2, 6, 10, 14
+                t3_lookup(tab, zo_lo, hp[pr] + 8);   // 1, 5, 9, 13
+                t3_lookup(tab, zo_hi, hp[pr] + 12);  // 3, 7, 11, 15
+            }
         }
 #pragma unroll
         for (int j = 0; j < 8; j++)
@@ -475,14 +505,19 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < F::STAGES; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 2 * F::KVH); // the warps owning the stage's two tiles
+            mbar_init(&empty[s], NCW);        // every consumer warp releases every stage
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    // stale ring bytes must at least be finite numbers: zero the ring once
-    for (int i = threadIdx.x; i < ring_bytes<KVK>() / 16; i += blockDim.x)
-        reinterpret_cast<uint4*>(ring)[i] = make_uint4(0, 0, 0, 0);
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    // Rows past the end of a ragged last stage are never copied; their weights are exact
+    // zeros, so the stale bytes only have to decode to finite numbers. Any turbo3 byte
+    // pattern decodes to a centroid (its norms are masked); fp16 / fp8 patterns may be
+    // NaN or Inf, so those rings are cleared once.
+    if (KVK != Q27_KV_T3) {
+        for (int i = threadIdx.x; i < ring_bytes<KVK>() / 16; i += blockDim.x)
+            reinterpret_cast<uint4*>(ring)[i] = make_uint4(0, 0, 0, 0);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
     __syncthreads();
 
     if (warp == NCW) {
@@ -548,19 +583,25 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
         (void)tab;
 
         const int ntiles = (hi - lo + TILE - 1) / TILE;
-        bool alive = true;
-        for (int tile = way; tile < 2 * nstages && alive; tile += WAYS) {
-            const int i = tile >> 1, s = i % F::STAGES;
+        const uint32_t ring_s = smem_u32(ring);
+        // Every consumer warp observes every phase of every ring slot, in order (waits on
+        // `full`, arrives on `empty`), whether or not it owns a tile of that stage: a warp
+        // that skipped phases could not tell them apart by parity.
+        for (int i = 0; i < nstages; i++) {
+            const int s = i % F::STAGES;
             const uint32_t ph = (uint32_t)((i / F::STAGES) & 1);
-            alive = mbar_wait(&full[s], ph);
-            if (!alive) break;
-            if (tile < ntiles) {
-                const int valid = min(TILE, hi - lo - tile * TILE);
-                const uint8_t* ks = ring + (size_t)s * stage_bytes<KVK>() + (tile & 1) * TILE * F::PITCH;
-                const uint8_t* vs = ks + STAGE_ROWS * F::PITCH;
-                if (KVK == Q27_KV_F16) tile_f16<KVK>(A, ks, vs, qf, valid, sc2, lane);
-                else if (KVK == Q27_KV_FP8) tile_fp8(A, ks, vs, qf, valid, sc2, lane);
-                else tile_t3(A, ks, vs, hq, qf, valid, sc2, lane, tab);
+            if (!mbar_wait(&full[s], ph)) break;
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                const int tile = 2 * i + half;
+                if (i % WAYS == way && tile < ntiles) {
+                    const int valid = min(TILE, hi - lo - tile * TILE);
+                    const uint32_t ks = ring_s + s * stage_bytes<KVK>() + half * TILE * F::PITCH;
+                    const uint32_t vs = ks + STAGE_ROWS * F::PITCH;
+                    if (KVK == Q27_KV_F16) tile_f16<KVK>(A, ks, vs, qf, valid, sc2, lane);
+                    else if (KVK == Q27_KV_FP8) tile_fp8(A, ks, vs, qf, valid, sc2, lane);
+                    else tile_t3(A, ks, vs, hq, qf, valid, sc2, lane, tab);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
@@ -594,8 +635,8 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
         }
         asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32));
         // merge the WAYS warps of each kv head in a fixed order and write the CTA partial
-        const int tid = threadIdx.x; // 0..255
-        for (int hj = 0; hj < F::KVH * GQA; hj++) {
+        const int tid = threadIdx.x;
+        for (int hj = 0; tid < HD && hj < F::KVH * GQA; hj++) {
             const int h = hj / GQA, j = hj % GQA;
             const float* src = reinterpret_cast<float*>(ring) + (size_t)h * GQA * PART + j * PART;
             float mb = NEG_SENTINEL;
