@@ -1,0 +1,120 @@
+// q27k_shim.cuh -- the reference's own launch functions, by name and signature, over the C
+// ABI of q27_b200. A translation unit of the reference that includes this header instead of
+// the attention declarations of blocks.cuh / spec3.cuh / prefill.cuh (and links
+// libq27_b200.so) calls the B200 engine unchanged:
+//
+//   q27k::attn_decode      src/blocks.cuh:39-42     -> q27_attn_decode
+//   q27k::attn_decode3     src/spec3.cuh:139-143    -> q27_attn_decode3
+//   q27k::attn_decode3_fd2 src/spec3.cuh:144-147    -> q27_attn_decode_batched_exact
+//   q27k::attn_prefill_T   src/prefill.cuh:95-98    -> q27_attn_prefill_T
+//   q27k::kv_store_T       src/blocks.cuh:56-57     -> q27_kv_store_T
+//   q27k::kv_store_T_t3    src/blocks.cuh:63-65     -> q27_kv_store_T_t3
+//   q27k::wht_T            src/blocks.cuh:76-81     -> q27_wht_T
+//
+// Error behaviour is the reference's: these functions return void and a failure is fatal
+// (message + exit(1), CUDA_CHECK in src/cuda_common.h:8-16). Kinds the engine does not read
+// (turbo3v, turbo5k, int8-g64) are therefore fatal here rather than silently mis-read.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+
+#include "q27_b200.h"
+
+#ifndef Q27K_SHIM_NO_TYPES
+// The reference's lane bundles (src/kernels.cuh:67-68, src/spec3.cuh:13) and KvKind
+// (src/cuda_common.h:53). Define Q27K_SHIM_NO_TYPES when the reference's own headers are
+// included before this one.
+enum KvKind : int { KV_F16 = 0, KV_FP8 = 1, KV_T3 = 2, KV_T3V = 3, KV_T5K = 4, KV_I8G64 = 5 };
+namespace q27k {
+struct P3 { float* p[16]; };
+struct CP3 { const float* p[16]; };
+struct IP3 { const int* p[16]; };
+} // namespace q27k
+#endif
+
+namespace q27k {
+
+static_assert(sizeof(P3) == sizeof(q27_P3) && sizeof(CP3) == sizeof(q27_CP3) &&
+                  sizeof(IP3) == sizeof(q27_IP3),
+              "lane bundles must stay layout-compatible with the C ABI");
+
+inline void q27_shim_check(int rc, const char* what) {
+    if (rc != Q27_OK) {
+        std::fprintf(stderr, "q27_b200: %s failed: %s (cudaError %d)\n", what,
+                     q27_status_string(rc), q27_last_cuda_error());
+        std::exit(1);
+    }
+}
+
+inline void attn_decode(const float* q, int q_stride, const void* const* ktab,
+                        const void* const* vtab, float* out, float* scratch, const int* d_pos,
+                        int max_ctx, int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                        cudaStream_t st = 0, int kvk = KV_F16) {
+    q27_shim_check(q27_attn_decode(q, q_stride, ktab, vtab, out, scratch, d_pos, max_ctx,
+                                   n_q_heads, n_kv_heads, head_dim, scale, st, kvk),
+                   "attn_decode");
+}
+
+inline void attn_decode3(CP3 q, int q_stride, const void* const* ktab, const void* const* vtab,
+                         P3 out, float* scratch, IP3 pos, int max_ctx, int n_q_heads,
+                         int n_kv_heads, int head_dim, float scale, cudaStream_t st = 0,
+                         int ntok = 3, int kvk = KV_F16) {
+    q27_shim_check(q27_attn_decode3(reinterpret_cast<const q27_CP3*>(&q), q_stride, ktab, vtab,
+                                    reinterpret_cast<const q27_P3*>(&out), scratch,
+                                    reinterpret_cast<const q27_IP3*>(&pos), max_ctx, n_q_heads,
+                                    n_kv_heads, head_dim, scale, st, ntok, kvk),
+                   "attn_decode3");
+}
+
+// the explicit fp32 entry the reference's unit gate compares the default dispatch against
+inline void attn_decode3_fd2(CP3 q, int q_stride, const void* const* ktab,
+                             const void* const* vtab, P3 out, float* scratch, IP3 pos,
+                             int max_ctx, int n_q_heads, int n_kv_heads, int head_dim,
+                             float scale, cudaStream_t st = 0, int ntok = 3, int kvk = KV_F16) {
+    (void)max_ctx;
+    q27_slot s{};
+    s.ktab = ktab;
+    s.vtab = vtab;
+    s.scratch = scratch;
+    s.ntok = ntok;
+    s.row_base = 0;
+    s.row_count = 0x7fffffff;
+    for (int t = 0; t < ntok && t < 16; t++) { s.q.p[t] = q.p[t]; s.pos.p[t] = pos.p[t]; s.out.p[t] = out.p[t]; }
+    q27_shim_check(q27_attn_decode_batched_exact(&s, 1, q_stride, n_q_heads, n_kv_heads, head_dim,
+                                                 scale, st, kvk),
+                   "attn_decode3_fd2");
+}
+
+inline void attn_prefill_T(const float* qT, int q_stride, int q_row, const void* const* ktab,
+                           const void* const* vtab, float* outT, int out_row, float* part,
+                           int base_pos, int t0, int SB, int n_q_heads, int n_kv_heads,
+                           int head_dim, float scale, cudaStream_t st, int kvk = KV_F16) {
+    q27_shim_check(q27_attn_prefill_T(qT, q_stride, q_row, ktab, vtab, outT, out_row, part,
+                                      base_pos, t0, SB, n_q_heads, n_kv_heads, head_dim, scale, st,
+                                      kvk),
+                   "attn_prefill_T");
+}
+
+inline void kv_store_T(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
+                       int base_pos, int rowlen, int T, cudaStream_t st, bool fp8 = false) {
+    q27_shim_check(q27_kv_store_T(kT, vT, ktab, vtab, base_pos, rowlen, T, st, fp8 ? 1 : 0),
+                   "kv_store_T");
+}
+
+inline void kv_store_T_t3(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
+                          int base_pos, int n_kv_heads, int head_dim, int T, cudaStream_t st,
+                          int kvk = KV_T3) {
+    q27_shim_check(q27_kv_store_T_t3(kT, vT, ktab, vtab, base_pos, n_kv_heads, head_dim, T, st,
+                                     kvk),
+                   "kv_store_T_t3");
+}
+
+inline void wht_T(float* x, int n_heads, int head_dim, int head_stride, int row_stride, int T,
+                  bool inv, cudaStream_t st) {
+    q27_shim_check(q27_wht_T(x, n_heads, head_dim, head_stride, row_stride, T, inv ? 1 : 0, st),
+                   "wht_T");
+}
+
+} // namespace q27k
