@@ -100,6 +100,27 @@ int q27_attn_decode3(const q27_CP3* q, int q_stride, const void* const* ktab,
                      const q27_IP3* pos, int max_ctx, int n_q_heads, int n_kv_heads,
                      int head_dim, float scale, void* stream, int ntok, int kvk);
 
+/* Has no counterpart in the reference. For callers that are not able to hand over scratch
+ * memory: code running where device allocation is off limits (a CUDA graph being captured in
+ * global mode forbids cudaMalloc from every thread, which is why the reference allocates
+ * everything before serving, src/kv_pool.h:8-10), plugin hosts that own no allocator, or a
+ * thin binding that only forwards the tensors it was given. Same semantics as
+ * q27_attn_decode3 without the `scratch` argument: the split partials go to an array that
+ * is part of the library image, sized for Q27_NOALLOC_MAX_LANES lanes (4 lanes x 24 heads
+ * x 128 splits x 258 floats = 12.1 MiB, held by every GPU that loads the library until the
+ * process exits). ntok above that limit (or more than 24 query heads) is refused with
+ * Q27_ERR_TOO_LARGE. The call itself allocates nothing and frees nothing.
+ *   - The first call on each device looks the array's device address up; make that first
+ *     call outside any stream capture.
+ *   - All calls share the one array. Nothing in it has to be cleared between calls (every
+ *     cell that is read was written by the same call), but two calls that overlap on the
+ *     GPU -- different streams, or graph branches that run side by side -- race on it. */
+#define Q27_NOALLOC_MAX_LANES 4
+int q27_attn_decode3_noalloc(const q27_CP3* q, int q_stride, const void* const* ktab,
+                             const void* const* vtab, const q27_P3* out, const q27_IP3* pos,
+                             int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                             void* stream, int ntok, int kvk);
+
 /* One slot of a batched launch. The reference runs one attn_decode3 per slot on its own
  * stream (src/conductor.h:681-694); here all slots ride one launch.
  * row_base / row_count describe which logical rows the tables hold (KV-sequence

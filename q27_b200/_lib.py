@@ -14,6 +14,7 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libq27_b200.so"
 MAX_LANES = 16
 MAX_SLOTS = 8
 MAX_SPLITS = 128
+NOALLOC_MAX_LANES = 4
 PART_STRIDE = 258
 KV_PAGE = 64
 HEAD_DIM = 256
@@ -56,6 +57,8 @@ SIGNATURES = {
     "q27_attn_decode": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp, _i]),
     "q27_attn_decode3": (_i, [C.POINTER(P3), _i, _vp, _vp, C.POINTER(P3), _vp, C.POINTER(P3),
                               _i, _i, _i, _i, _f, _vp, _i, _i]),
+    "q27_attn_decode3_noalloc": (_i, [C.POINTER(P3), _i, _vp, _vp, C.POINTER(P3), C.POINTER(P3),
+                                      _i, _i, _i, _f, _vp, _i, _i]),
     "q27_attn_decode_batched": (_i, [C.POINTER(Slot), _i, _i, _i, _i, _i, _f, _vp, _i]),
     "q27_attn_decode_batched_exact": (_i, [C.POINTER(Slot), _i, _i, _i, _i, _i, _f, _vp, _i]),
     "q27_attn_decode_partial": (_i, [C.POINTER(Slot), _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _i]),

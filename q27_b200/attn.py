@@ -62,6 +62,22 @@ def attn_decode3(q_lanes, q_stride, ktab, vtab, out_lanes, scratch, pos_lanes, m
             "q27_attn_decode3")
 
 
+def attn_decode3_noalloc(q_lanes, q_stride, ktab, vtab, out_lanes, pos_lanes, n_q_heads,
+                         n_kv_heads, head_dim, scale, st=None, ntok=1, kvk=0):
+    """attn_decode3 for callers with no scratch buffer to give (no device allocator at
+    hand, or allocation forbidden where they run): the split partials live in an array
+    inside the library, sized for at most ``_lib.NOALLOC_MAX_LANES`` lanes. Calls share
+    that array, so calls that overlap on the GPU race; the first call on a device should
+    come before any stream capture."""
+    q = _p3(q_lanes[:ntok])
+    o = _p3(out_lanes[:ntok])
+    p = _p3(pos_lanes[:ntok])
+    L.check(L.lib().q27_attn_decode3_noalloc(C.byref(q), q_stride, ktab.data_ptr(),
+                                             vtab.data_ptr(), C.byref(o), C.byref(p), n_q_heads,
+                                             n_kv_heads, head_dim, scale, stream_ptr(st), ntok,
+                                             kvk), "q27_attn_decode3_noalloc")
+
+
 @dataclass
 class SlotArgs:
     """One slot of a batched launch (q27_slot)."""

@@ -124,6 +124,30 @@ q27_slot single_slot(const q27_CP3* q, const void* const* ktab, const void* cons
     return s;
 }
 
+// ---- scratch that nobody has to allocate ---------------------------------------------------
+// Split-KV partials for the no-allocation decode entry: Q27_NOALLOC_MAX_LANES lanes x 24
+// heads x 128 splits x 258 floats. Lives in the library image: every GPU that loads the
+// library holds these bytes until the process exits. In host code `g_noalloc_scratch` is
+// only a handle; the device address comes from cudaGetSymbolAddress, once per device.
+constexpr size_t NOALLOC_FLOATS =
+    (size_t)Q27_NOALLOC_MAX_LANES * 24 * Q27_MAX_SPLITS * Q27_PART_STRIDE;
+static __device__ __align__(256) float g_noalloc_scratch[NOALLOC_FLOATS];
+
+// Device address of the static scratch on the current device (set up on first use).
+int noalloc_scratch_ptr(float** out) {
+    static float* by_device[64] = {nullptr};
+    int dev = 0;
+    Q27_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return Q27_ERR_INVALID_ARG;
+    if (!by_device[dev]) {
+        float* p = nullptr;
+        Q27_CUDA_TRY(cudaGetSymbolAddress((void**)&p, g_noalloc_scratch));
+        by_device[dev] = p;
+    }
+    *out = by_device[dev];
+    return Q27_OK;
+}
+
 } // namespace
 } // namespace q27b
 
@@ -190,6 +214,21 @@ int q27_attn_decode(const float* q, int q_stride, const void* const* ktab,
     pp.p[0] = d_pos;
     return q27_attn_decode3(&qp, q_stride, ktab, vtab, &op, scratch, &pp, max_ctx, n_q_heads,
                             n_kv_heads, head_dim, scale, stream, 1, kvk);
+}
+
+int q27_attn_decode3_noalloc(const q27_CP3* q, int q_stride, const void* const* ktab,
+                             const void* const* vtab, const q27_P3* out, const q27_IP3* pos,
+                             int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                             void* stream, int ntok, int kvk) {
+    if (!q || !out || !pos) return Q27_ERR_INVALID_ARG;
+    if (ntok < 1) return Q27_ERR_UNSUPPORTED_WIDTH;
+    if (ntok > Q27_NOALLOC_MAX_LANES || n_q_heads > 24) return Q27_ERR_TOO_LARGE;
+    float* scratch = nullptr;
+    int rc = noalloc_scratch_ptr(&scratch);
+    if (rc) return rc;
+    q27_slot s = single_slot(q, ktab, vtab, out, scratch, pos, ntok);
+    return run_decode(&s, 1, 0, q_stride, n_q_heads, n_kv_heads, head_dim, scale, nullptr, stream,
+                      kvk, FAM_AUTO);
 }
 
 int q27_attn_decode_batched(const q27_slot* slots, int nslots, int q_stride, int n_q_heads,
