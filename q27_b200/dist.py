@@ -71,7 +71,8 @@ def all_gather_partials(ex: PartialExchange, group=None) -> torch.Tensor:
     if ex.world == 1:
         ex.gathered[0].copy_(ex.local)
     else:
-        dist.all_gather_into_tensor(ex.gathered, ex.local, group=group)
+        # flat views: the concatenated form is accepted by NCCL and gloo alike
+        dist.all_gather_into_tensor(ex.gathered.view(-1), ex.local.view(-1), group=group)
     return ex.gathered
 
 
