@@ -44,7 +44,10 @@ WORKLOADS = {
     "c2": (KV_FP8, 1, 6, 32768, 0.0),
     "c3": (KV_T3, 2, 1, 131072, 0.02),     # BASELINE config 3 (the headline, default)
     "c5": (KV_T3, 8, 6, 262144, 0.02),     # rows are split over ranks
+    # prefill, 8192 cached prefix + 16384 new tokens in 2048-token chunks
+    "c4": (KV_F16, 1, 0, 8192 + 16384, 0.0),
 }
+PREFILL_METRIC = "prefill attn TFLOP/s"
 METRIC = "decode/verify attn KV GB/s (frac of HBM peak) @131K ctx"
 L2_BYTES = 126 * 2**20
 FP8_DEQ_SCALE = 6.0 / 448.0
@@ -343,6 +346,118 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_prefill(args):
+    """BASELINE config 4 on one GPU: one step = the 8 chunks of 2048 new tokens (store the
+    chunk's K/V rows, then causal attention over prefix + chunk)."""
+    import torch
+
+    import q27_b200 as Q
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"metric": PREFILL_METRIC, "unavailable": "config 4 is single-GPU "
+                              "(replicas only); run with --gpus 1"}))
+        return
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(0)
+    PREFIX, NEW, CH = 8192, 16384, 2048
+    rows = PREFIX + NEW
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+
+    def bf16_vals(shape):   # N(0,1) rounded to bf16; tiny magnitudes flushed (exact in fp16)
+        x = torch.randn(shape, generator=g, device=dev).bfloat16().float()
+        return torch.where(x.abs() < 2.0 ** -14, torch.zeros_like(x), x)
+
+    rb = ROW_BYTES[KV_F16]
+    sides = []
+    for _ in range(2):
+        store = torch.empty(((rows + 63) // 64) * 64 * rb, dtype=torch.uint8, device=dev)
+        sides.append((store, Q.mk_tab(store, rb, rows)))
+    ktab, vtab = sides[0][1], sides[1][1]
+    for r0 in range(0, PREFIX, 4096):
+        Q.kv_store_T(bf16_vals((4096, N_KV * HD)), bf16_vals((4096, N_KV * HD)), ktab, vtab, r0,
+                     N_KV * HD, 4096)
+    qT = bf16_vals((NEW, N_Q * Q_STRIDE))
+    kT = bf16_vals((NEW, N_KV * HD))
+    vT = bf16_vals((NEW, N_KV * HD))
+    outT = torch.zeros((NEW, N_Q * HD), device=dev)
+    part = torch.empty(Q.prefill_part_floats(CH), device=dev)
+    out_host = torch.zeros((CH, N_Q * HD)).pin_memory()
+    q_host = qT[:CH].cpu().pin_memory()
+
+    def step(e2e=False):
+        for c in range(NEW // CH):
+            sl = slice(c * CH, (c + 1) * CH)
+            if e2e:   # the chunk's Q rows come from the host, its output rows go back
+                qT[sl].copy_(q_host, non_blocking=True)
+            Q.kv_store_T(kT[sl], vT[sl], ktab, vtab, PREFIX + c * CH, N_KV * HD, CH)
+            Q.attn_prefill_T(qT[sl], Q_STRIDE, N_Q * Q_STRIDE, ktab, vtab, outT[sl], N_Q * HD, part,
+                             PREFIX + c * CH, 0, CH, N_Q, N_KV, HD, SCALE, kvk=KV_F16)
+            if e2e:
+                out_host.copy_(outT[sl], non_blocking=True)
+        if e2e:
+            torch.cuda.current_stream().synchronize()
+
+    pairs = sum(CH * (PREFIX + CH * c) + CH * (CH + 1) // 2 for c in range(NEW // CH))
+    flops = pairs * N_Q * 4 * HD
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(0)
+    sampler.start()
+    time.sleep(0.15)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    # attention kernels alone
+    ka = [torch.cuda.Event(enable_timing=True) for _ in range(2 * (NEW // CH))]
+    for c in range(NEW // CH):
+        sl = slice(c * CH, (c + 1) * CH)
+        ka[2 * c].record()
+        Q.attn_prefill_T(qT[sl], Q_STRIDE, N_Q * Q_STRIDE, ktab, vtab, outT[sl], N_Q * HD, part,
+                         PREFIX + c * CH, 0, CH, N_Q, N_KV, HD, SCALE, kvk=KV_F16)
+        ka[2 * c + 1].record()
+    torch.cuda.synchronize()
+    kernel_ms = sum(ka[2 * c].elapsed_time(ka[2 * c + 1]) for c in range(NEW // CH))
+    for _ in range(2):
+        step(e2e=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step(e2e=True)
+    torch.cuda.synchronize()
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    clocks = sampler.stop()
+    try:
+        pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        peak, which = float(pk["bf16_tflops_sustained"]), "measured sustained cuBLAS bf16"
+    except Exception:
+        peak, which = 1400.0, "fallback"
+    line = {
+        "metric": PREFILL_METRIC, "value": round(flops / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic",
+        "config": {"workload": "c4", "kv_kind": "fp16 cache, bf16-rounded values", "prefix": PREFIX,
+                   "new_tokens": NEW, "chunk": CH, "heads": "24q/4kv", "head_dim": HD,
+                   "l2_policy": "Q + KV + out of a step = 1.3 GB > L2"},
+        "e2e": {"value": round(flops / e2e_s / 1e12, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": int(q_host.numel() * 4 * (NEW // CH)),
+                "d2h_bytes_per_step": int(out_host.numel() * 4 * (NEW // CH))},
+        "gpu_launches": 2 * (NEW // CH) * args.steps, "clocks": clocks,
+        "roofline": {"bound": "tensor", "achieved": round(flops / (kernel_ms * 1e-3) / 1e12, 2),
+                     "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(flops / (kernel_ms * 1e-3) / 1e12 / peak, 4), "traffic": None,
+                     "peak_source": which, "kernel": "k_prefill_umma (tcgen05)",
+                     "kernel_ms": round(kernel_ms, 3), "algorithmic_flops_per_step": flops},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def cpu_baseline(args, cache_set, q_host, pos_host, kvk, nslots, lanes, rows, out_dev_check=None,
                  budget_s=20.0):
     """Times the CPU oracle (a port of the reference's scalar host attention) on the host
@@ -456,6 +571,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "c4":
+        run_prefill(args)
     else:
         run_ours(args)
 

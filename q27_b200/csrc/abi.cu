@@ -3,6 +3,7 @@
 #include <limits.h>
 
 #include "common.cuh"
+#include "attn_umma.cuh"
 #include "decode_mma.cuh"
 
 namespace q27b {
@@ -93,7 +94,11 @@ int run_decode(const q27_slot* slots, int nslots, int lanes_stride, int q_stride
     bool done = false;
     if (g_ev_start) Q27_CUDA_TRY(cudaEventRecord(g_ev_start, st));
     if (fam == FAM_AUTO) {
-        rc = launch_decode_mma(b, kvk, sms, st, &done);
+        // two or more lanes: one pass over the cache for all of them (tcgen05 tile kernel);
+        // a single lane: the mma.sync streaming kernel
+        if (b.max_ntok >= 2) rc = launch_verify_umma(b, kvk, sms, st, &done);
+        if (rc) return rc;
+        if (!done) rc = launch_decode_mma(b, kvk, sms, st, &done);
         if (rc) return rc;
     }
     if (!done) {
@@ -280,6 +285,17 @@ int q27_attn_prefill_T(const float* qT, int q_stride, int q_row, const void* con
                        const void* const* vtab, float* outT, int out_row, float* part,
                        int base_pos, int t0, int SB, int n_q_heads, int n_kv_heads,
                        int head_dim, float scale, void* stream, int kvk) {
+    int rc = check_geometry(q_stride, n_q_heads, n_kv_heads, head_dim, kvk);
+    if (rc) return rc;
+    if (!qT || !ktab || !vtab || !outT || base_pos < 0 || t0 < 0 || SB < 0 ||
+        q_row < n_q_heads * HD || out_row < n_q_heads * HD)
+        return Q27_ERR_INVALID_ARG;
+    if (SB == 0) return Q27_OK;
+    bool done = false;
+    rc = launch_prefill_umma(qT, q_stride, q_row, ktab, vtab, outT, out_row, base_pos, t0, SB,
+                             n_q_heads, n_kv_heads, scale, static_cast<cudaStream_t>(stream), kvk,
+                             &done);
+    if (rc || done) return rc;
     return q27_attn_prefill_T_exact(qT, q_stride, q_row, ktab, vtab, outT, out_row, part, base_pos,
                                     t0, SB, n_q_heads, n_kv_heads, head_dim, scale, stream, kvk);
 }

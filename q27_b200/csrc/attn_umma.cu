@@ -1,0 +1,649 @@
+// Attention on the 5th-generation tensor cores (tcgen05.mma, accumulators in tensor memory).
+//
+// One CTA = one Q tile of up to 128 rows against a range of cache rows of ONE kv head. The
+// rows of the tile are (token, GQA head) pairs -- 21 tokens x 6 heads for prefill, ntok lanes
+// x 6 heads for verify -- so every K/V tile that is staged serves all six heads (and, for
+// verify, all draft lanes: one pass over the cache). Each row carries its own causal bound.
+//
+//   S  = Q . K^T   M=128 rows, N=64 keys, K=256 dims     -> TMEM (two S buffers)
+//   O += P . V     M=128 rows, N=256 dims, K=64 keys      -> TMEM (256 columns)
+//
+// Operands are fp16 in shared memory in the 128-byte-swizzled canonical layouts (Q and K
+// K-major, V MN-major = its natural [key][dim] rows, P K-major), accumulation is fp32.
+// Warp roles: warps 0-3 softmax (thread = row = TMEM lane), warp 4 issues the MMAs, warps
+// 5-8 stage K/V tiles (cp.async for fp16 rows; load + convert for fp8 / turbo3). The running
+// max is only advanced when it grows by more than 2^8, so O in TMEM is rarely rescaled.
+// Every mbarrier wait is bounded; a timeout sets the library's flag and the CTA drains.
+#include "attn_umma.cuh"
+#include "t3_lut.cuh"
+
+namespace q27b {
+
+extern __device__ int g_wait_timeout_flag;
+
+namespace {
+
+constexpr int BM = 128;                 // Q rows per CTA (TMEM lanes)
+constexpr int BN = 64;                  // keys per tile = one cache page
+constexpr int TOK_PER_TILE = 21;        // 21 tokens x 6 heads = 126 rows
+constexpr int KV_STAGES = 2;
+constexpr int Q_BYTES = BM * HD * 2;            // 65536: 4 blocks of [128 rows][128 B]
+constexpr int KT_BYTES = BN * HD * 2;           // 32768: 4 blocks of [64 rows][128 B]
+constexpr int P_BYTES = BM * BN * 2;            // 16384: 1 block of [128 rows][128 B]
+constexpr int STAGE_BYTES = 2 * KT_BYTES;       // K then V
+constexpr int SMEM_BAR = 1024;                  // barriers + tmem slot, keeps tiles 1024-aligned
+constexpr int UMMA_SMEM = SMEM_BAR + Q_BYTES + P_BYTES + KV_STAGES * STAGE_BYTES + 1024;
+constexpr int TMEM_COLS = 512;
+constexpr int COL_S0 = 0, COL_S1 = 64, COL_O = 128;
+constexpr float LOG2E_F = 1.4426950408889634f;
+constexpr float RESCALE_THRESHOLD = 8.0f;       // log2 units
+
+constexpr int N_SOFTMAX_WARPS = 4, MMA_WARP = 4, FIRST_LOAD_WARP = 5, N_LOAD_WARPS = 4;
+constexpr int UMMA_THREADS = (FIRST_LOAD_WARP + N_LOAD_WARPS) * 32;   // 288
+
+// ---- small PTX wrappers -------------------------------------------------------------------
+__device__ __forceinline__ uint32_t s32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void bar_init(uint32_t bar, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void bar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
+    for (int i = 0; i < (1 << 20); i++) {
+        if (bar_try(bar, parity)) return true;
+        if (i > 2048) __nanosleep(64);
+    }
+    atomicExch(&g_wait_timeout_flag, 2);
+    return false;
+}
+__device__ __forceinline__ void fence_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// 32 consecutive fp32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float* v) {
+    uint32_t* r = reinterpret_cast<uint32_t*>(v);
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,"
+        "%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr) : "memory");
+}
+__device__ __forceinline__ void tc_st32(uint32_t taddr, const float* v) {
+    const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,"
+        "%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+          "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]),
+          "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]),
+          "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+          "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ float ex2f(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), descriptor version 1.
+// lbo / sbo in bytes (see the canonical layouts in the header comment of make_desc users).
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+// Instruction descriptor, kind::f16: D fp32, A/B fp16, M x N, B optionally MN-major.
+constexpr uint32_t make_idesc(int M, int N, bool b_mn_major) {
+    return (1u << 4) | (b_mn_major ? (1u << 16) : 0u) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
+}
+// byte offset of (row, 16-byte chunk 0..7) inside a [rows][128 B] block, 128-byte swizzle
+__device__ __forceinline__ uint32_t sw128(int row, int chunk) {
+    return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+// ---- what a CTA works on -----------------------------------------------------------------
+struct TileArgs {
+    // prefill (mode 0)
+    const float* qT;
+    const void* const* ktab;
+    const void* const* vtab;
+    float* outT;
+    int q_stride, q_row, out_row;
+    int base_pos, t0, t_end;
+    int n_kv;
+    float scale;
+};
+
+struct RowInfo {        // one Q row of the tile, owned by one softmax thread
+    const float* q;     // 256 floats, or nullptr for a padding row
+    int bound;          // keys [0, bound) of the tables are visible to this row
+    float* out;         // prefill: 256 normalised floats
+    float* part;        // verify: {m, l, acc[256]} of this split
+};
+
+// MODE 0: prefill tile (TileArgs). MODE 1: verify, all lanes of one slot (DevBatch).
+template <int MODE>
+struct Problem {
+    const TileArgs* ta;
+    const DevBatch* vb;
+    const DevSlot* slot;
+    int kvh, tile_t0, lo, hi, sp;
+
+    __device__ __forceinline__ RowInfo row(int r) const {
+        RowInfo ri{nullptr, 0, nullptr, nullptr};
+        const int tok = r / GQA, j = r % GQA;
+        if (MODE == 0) {
+            const int t = tile_t0 + tok;
+            if (tok < TOK_PER_TILE && t < ta->t_end) {
+                const int h = kvh * GQA + j;
+                ri.q = ta->qT + (size_t)t * ta->q_row + (size_t)h * ta->q_stride;
+                ri.bound = ta->base_pos + t + 1;
+                ri.out = ta->outT + (size_t)t * ta->out_row + (size_t)h * HD;
+            }
+        } else {
+            if (tok < slot->ntok) {
+                const int h = kvh * GQA + j;
+                ri.q = slot->q[tok] + (size_t)h * vb->q_stride;
+                ri.bound = min(hi, local_len(__ldg(slot->pos[tok]), slot->row_base, slot->row_count));
+                ri.part = slot->scratch + (((size_t)tok * vb->n_q + h) * vb->nsplit + sp) * PART;
+            }
+        }
+        return ri;
+    }
+};
+
+// Staging of one 64-key tile of K and V as fp16 into the swizzled operand layouts, in two
+// halves: `load` pulls the raw bytes of the tile into registers (issued before the ring slot
+// is free, so the global latency hides behind the tiles in flight), `store` converts and
+// writes them once the slot has been released.
+template <int KVK> struct RawTile;
+template <> struct RawTile<Q27_KV_F16> { uint4 k[16], v[16]; };
+template <> struct RawTile<Q27_KV_FP8> { uint2 k[16], v[16]; };
+template <> struct RawTile<Q27_KV_T3> { uint32_t w[26]; };
+
+template <int KVK>
+__device__ __forceinline__ void tile_load(RawTile<KVK>& t, const uint8_t* kpage, const uint8_t* vpage,
+                                          int nkeys, int n_kv, int kvh, int ptid) {
+    if constexpr (KVK == Q27_KV_T3) {
+        // one thread = one (key, side) slice of 100 bytes = two 50-byte blocks
+        const int key = ptid & 63, side = ptid >> 6;
+#pragma unroll
+        for (int i = 0; i < 26; i++) t.w[i] = 0;
+        if (key < nkeys) {
+            const uint32_t* src = reinterpret_cast<const uint32_t*>(
+                (side ? vpage : kpage) + ((size_t)key * n_kv + kvh) * (2 * T3_BLK));
+#pragma unroll
+            for (int i = 0; i < 25; i++) t.w[i] = __ldg(src + i);
+        }
+    } else {
+        constexpr int CB = KVK == Q27_KV_F16 ? 16 : 8;      // bytes per 8-dim chunk
+#pragma unroll
+        for (int n = 0; n < 16; n++) {
+            const int q = ptid + 128 * n;
+            const int key = q >> 5, ch = q & 31;
+            const size_t src = ((size_t)key * n_kv + kvh) * (HD * CB / 8) + (size_t)ch * CB;
+            if constexpr (KVK == Q27_KV_F16) {
+                t.k[n] = t.v[n] = make_uint4(0, 0, 0, 0);   // rows past the range: exact zeros
+                if (key < nkeys) {
+                    t.k[n] = __ldg(reinterpret_cast<const uint4*>(kpage + src));
+                    t.v[n] = __ldg(reinterpret_cast<const uint4*>(vpage + src));
+                }
+            } else {
+                t.k[n] = t.v[n] = make_uint2(0, 0);
+                if (key < nkeys) {
+                    t.k[n] = __ldg(reinterpret_cast<const uint2*>(kpage + src));
+                    t.v[n] = __ldg(reinterpret_cast<const uint2*>(vpage + src));
+                }
+            }
+        }
+    }
+}
+
+template <int KVK>
+__device__ __forceinline__ void tile_store(const RawTile<KVK>& t, uint8_t* dstK, int nkeys, int ptid) {
+    uint8_t* dstV = dstK + KT_BYTES;
+    if constexpr (KVK == Q27_KV_F16) {
+#pragma unroll
+        for (int n = 0; n < 16; n++) {
+            const int q = ptid + 128 * n;
+            const int key = q >> 5, ch = q & 31;
+            const uint32_t off = (uint32_t)(ch >> 3) * (BN * 128) + sw128(key, ch & 7);
+            *reinterpret_cast<uint4*>(dstK + off) = t.k[n];
+            *reinterpret_cast<uint4*>(dstV + off) = t.v[n];
+        }
+    } else if constexpr (KVK == Q27_KV_FP8) {
+#pragma unroll
+        for (int n = 0; n < 16; n++) {
+            const int q = ptid + 128 * n;
+            const int key = q >> 5, ch = q & 31;
+            const uint32_t off = (uint32_t)(ch >> 3) * (BN * 128) + sw128(key, ch & 7);
+            auto cv = [](uint32_t two) {
+                __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two, __NV_E4M3);
+                return (uint32_t)h.x | ((uint32_t)h.y << 16);
+            };
+            *reinterpret_cast<uint4*>(dstK + off) = make_uint4(
+                cv(t.k[n].x & 0xffffu), cv(t.k[n].x >> 16), cv(t.k[n].y & 0xffffu), cv(t.k[n].y >> 16));
+            *reinterpret_cast<uint4*>(dstV + off) = make_uint4(
+                cv(t.v[n].x & 0xffffu), cv(t.v[n].x >> 16), cv(t.v[n].y & 0xffffu), cv(t.v[n].y >> 16));
+        }
+    } else {
+        const int key = ptid & 63, side = ptid >> 6;
+        uint8_t* dst = side ? dstV : dstK;
+        const uint32_t* w = t.w;
+        const T3Tab tab = t3_tables();
+#pragma unroll
+        for (int b = 0; b < 2; b++) {
+            // 32-bit little-endian word starting at byte `o` of the slice (o even, compile time)
+            auto word_at = [&](int o) {
+                return (o & 3) ? __funnelshift_r(w[o >> 2], w[(o >> 2) + 1], 16) : w[o >> 2];
+            };
+            const __half nh = __ushort_as_half((unsigned short)(word_at(50 * b) & 0xffffu));
+            const float nf = key < nkeys ? __half2float(nh) : 0.f;
+#pragma unroll
+            for (int g8 = 0; g8 < 8; g8++) {         // 16 dims per group
+                const uint32_t Qw = word_at(50 * b + 2 + 4 * g8);
+                const uint32_t S16 = (word_at(50 * b + 34 + 2 * (g8 & ~1)) >> (16 * (g8 & 1))) & 0xffffu;
+                uint32_t ze, zo, e[4], o[4];
+                t3_selectors(Qw, S16, ze, zo);
+                t3_lookup(tab, ze, e);                // (0,2) (4,6) (8,10) (12,14)
+                t3_lookup(tab, zo, o);                // (1,3) (5,7) (9,11) (13,15)
+                uint32_t nat[8];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    nat[2 * i] = prmt(e[i], o[i], 0x5410u);      // dims 4i, 4i+1
+                    nat[2 * i + 1] = prmt(e[i], o[i], 0x7632u);  // dims 4i+2, 4i+3
+                }
+#pragma unroll
+                for (int i = 0; i < 8; i++) {   // product in fp32, one rounding to fp16
+                    const float2 cf = __half22float2(*reinterpret_cast<__half2*>(&nat[i]));
+                    __half2 h = __floats2half2_rn(cf.x * nf, cf.y * nf);
+                    nat[i] = *reinterpret_cast<uint32_t*>(&h);
+                }
+                const int ch = 16 * b + 2 * g8;      // 8-dim chunk index within the head
+                *reinterpret_cast<uint4*>(dst + (ch >> 3) * (BN * 128) + sw128(key, ch & 7)) =
+                    make_uint4(nat[0], nat[1], nat[2], nat[3]);
+                *reinterpret_cast<uint4*>(dst + ((ch + 1) >> 3) * (BN * 128) + sw128(key, (ch + 1) & 7)) =
+                    make_uint4(nat[4], nat[5], nat[6], nat[7]);
+            }
+        }
+    }
+}
+
+template <int KVK, int MODE>
+__device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* const* ktab,
+                                          const void* const* vtab, int n_kv, float scale,
+                                          uint8_t* smem_raw) {
+    uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + 512);
+    uint8_t* q_sm = base + SMEM_BAR;
+    uint8_t* p_sm = q_sm + Q_BYTES;
+    uint8_t* kv_sm = p_sm + P_BYTES;
+    const uint32_t kv_full = s32(&bars[0]), kv_empty = s32(&bars[2]), s_full = s32(&bars[4]),
+                   s_free = s32(&bars[6]), p_full = s32(&bars[8]), pv_done = s32(&bars[9]);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntiles = (pb.hi - pb.lo + BN - 1) / BN;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < 2; s++) {
+            bar_init(kv_full + 8 * s, N_LOAD_WARPS * 32);
+            bar_init(kv_empty + 8 * s, 1);
+            bar_init(s_full + 8 * s, 1);
+            bar_init(s_free + 8 * s, N_SOFTMAX_WARPS * 32);
+        }
+        bar_init(p_full, N_SOFTMAX_WARPS * 32);
+        bar_init(pv_done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == MMA_WARP) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(s32(tmem_slot)), "n"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    // Q tile: fp32 -> fp16, K-major, 4 blocks of [128 rows][64 dims], 128-byte swizzle
+    for (int idx = threadIdx.x; idx < BM * 32; idx += blockDim.x) {
+        const int r = idx >> 5, ch = idx & 31;
+        const RowInfo ri = pb.row(r);
+        uint4 packed = make_uint4(0, 0, 0, 0);
+        if (ri.q) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(ri.q + 8 * ch));
+            const float4 b = __ldg(reinterpret_cast<const float4*>(ri.q + 8 * ch) + 1);
+            __half2 h[4] = {__floats2half2_rn(a.x, a.y), __floats2half2_rn(a.z, a.w),
+                            __floats2half2_rn(b.x, b.y), __floats2half2_rn(b.z, b.w)};
+            packed = *reinterpret_cast<uint4*>(h);
+        }
+        *reinterpret_cast<uint4*>(q_sm + (ch >> 3) * (BM * 128) + sw128(r, ch & 7)) = packed;
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp < N_SOFTMAX_WARPS) {
+        // ------------------------------ softmax: thread = row ------------------------------
+        const int r = threadIdx.x;
+        const RowInfo ri = pb.row(r);
+        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        const float sc2 = scale * LOG2E_F;
+        float m_ref = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int i = 0; i < ntiles && ok; i++) {
+            const int bsel = i & 1;
+            ok = __all_sync(0xffffffffu, bar_wait(s_full + 8 * bsel, (uint32_t)((i >> 1) & 1)));
+            if (!ok) break;
+            tc_fence_after();
+            float s[BN];
+            tc_ld32(lane_base + (bsel ? COL_S1 : COL_S0), s);
+            tc_ld32(lane_base + (bsel ? COL_S1 : COL_S0) + 32, s + 32);
+            tc_wait_ld();
+            tc_fence_before();
+            bar_arrive(s_free + 8 * bsel);
+            const int k0 = pb.lo + i * BN;
+            const int vis = ri.bound - k0;            // columns [0, vis) are visible
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < BN; j++) {
+                s[j] = j < vis ? s[j] * sc2 : -INFINITY;
+                mx = fmaxf(mx, s[j]);
+            }
+            float alpha = 1.f;
+            bool need = false;
+            if (mx > m_ref + RESCALE_THRESHOLD || (m_ref == -INFINITY && mx > -INFINITY)) {
+                alpha = m_ref == -INFINITY ? 0.f : ex2f(m_ref - mx);
+                m_ref = mx;
+                need = i > 0;                          // O holds nothing before the first PV
+            }
+            const float mu = m_ref == -INFINITY ? 0.f : m_ref;
+            float sum = 0.f;
+            uint32_t ph[BN / 2];
+#pragma unroll
+            for (int j = 0; j < BN; j += 2) {
+                const float p0 = ex2f(s[j] - mu), p1 = ex2f(s[j + 1] - mu);
+                sum += p0 + p1;
+                __half2 h = __floats2half2_rn(p0, p1);
+                ph[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
+            }
+            l = l * alpha + sum;
+            if (i > 0) {
+                ok = __all_sync(0xffffffffu, bar_wait(pv_done, (uint32_t)((i - 1) & 1)));
+                if (!ok) break;
+                tc_fence_after();
+            }
+            if (__any_sync(0xffffffffu, need)) {       // warp-collective TMEM round trip
+#pragma unroll 1
+                for (int c = 0; c < HD; c += 32) {
+                    float o[32];
+                    tc_ld32(lane_base + COL_O + c, o);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; e++) o[e] *= alpha;
+                    tc_st32(lane_base + COL_O + c, o);
+                }
+                tc_wait_st();
+            }
+#pragma unroll
+            for (int c = 0; c < 8; c++)
+                *reinterpret_cast<uint4*>(p_sm + sw128(r, c)) =
+                    make_uint4(ph[4 * c], ph[4 * c + 1], ph[4 * c + 2], ph[4 * c + 3]);
+            fence_async_smem();
+            tc_fence_before();
+            bar_arrive(p_full);
+        }
+        if (ok) ok = bar_wait(pv_done, (uint32_t)((ntiles - 1) & 1));
+        ok = __all_sync(0xffffffffu, ok);
+        tc_fence_after();
+        if (ok) {
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            if (ri.part) {
+                ri.part[0] = m_ref == -INFINITY ? NEG_SENTINEL : m_ref * 0.6931471805599453f;
+                ri.part[1] = l;
+            }
+            // the TMEM loads are warp-collective: every lane runs them, padding rows just
+            // drop what they read
+#pragma unroll 1
+            for (int c = 0; c < HD; c += 32) {
+                float o[32];
+                tc_ld32(lane_base + COL_O + c, o);
+                tc_wait_ld();
+                if (ri.out) {
+#pragma unroll
+                    for (int e = 0; e < 32; e += 4)
+                        *reinterpret_cast<float4*>(ri.out + c + e) =
+                            make_float4(o[e] * inv, o[e + 1] * inv, o[e + 2] * inv, o[e + 3] * inv);
+                } else if (ri.part) {
+#pragma unroll
+                    for (int e = 0; e < 32; e++) ri.part[2 + c + e] = o[e];
+                }
+            }
+        }
+        tc_fence_before();
+    } else if (warp == MMA_WARP) {
+        // ------------------------------ MMA issue: one thread ------------------------------
+        if (lane == 0) {
+            constexpr uint32_t IDESC_S = make_idesc(BM, BN, false);
+            constexpr uint32_t IDESC_O = make_idesc(BM, HD, true);
+            const uint32_t q_s = s32(q_sm), p_s = s32(p_sm), kv_s = s32(kv_sm);
+            bool ok = true;
+            auto issue_s = [&](int i) {
+                const int st = i % KV_STAGES, bsel = i & 1;
+                ok = ok && bar_wait(kv_full + 8 * st, (uint32_t)((i / KV_STAGES) & 1));
+                if (ok && i >= 2) ok = bar_wait(s_free + 8 * bsel, (uint32_t)(((i >> 1) - 1) & 1));
+                if (!ok) return;
+                tc_fence_after();
+                const uint32_t k_s = kv_s + st * STAGE_BYTES;
+#pragma unroll
+                for (int ks = 0; ks < HD / 16; ks++) {
+                    const uint64_t da = make_desc(q_s + (ks >> 2) * (BM * 128) + (ks & 3) * 32, 0, 1024);
+                    const uint64_t db = make_desc(k_s + (ks >> 2) * (BN * 128) + (ks & 3) * 32, 0, 1024);
+                    tc_mma_f16(tmem + (bsel ? COL_S1 : COL_S0), da, db, IDESC_S, ks > 0);
+                }
+                tc_commit(s_full + 8 * bsel);
+            };
+            issue_s(0);
+            for (int i = 0; i < ntiles && ok; i++) {
+                if (i + 1 < ntiles) issue_s(i + 1);
+                if (!ok) break;
+                ok = bar_wait(p_full, (uint32_t)(i & 1));
+                if (!ok) break;
+                tc_fence_after();
+                const int st = i % KV_STAGES;
+                const uint32_t v_s = kv_s + st * STAGE_BYTES + KT_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < BN / 16; kk++) {
+                    const uint64_t da = make_desc(p_s + kk * 32, 0, 1024);
+                    const uint64_t db = make_desc(v_s + kk * 2048, BN * 128, 1024);
+                    tc_mma_f16(tmem + COL_O, da, db, IDESC_O, (i > 0 || kk > 0));
+                }
+                tc_commit(pv_done);
+                tc_commit(kv_empty + 8 * st);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------ K/V staging ----------------------------------------
+        const int ptid = threadIdx.x - FIRST_LOAD_WARP * 32;
+        RawTile<KVK> raw;
+        for (int i = 0; i < ntiles; i++) {
+            const int st = i % KV_STAGES;
+            const int k0 = pb.lo + i * BN;
+            const int nkeys = min(BN, pb.hi - k0);
+            // a tile is exactly one cache page (k0 is a multiple of 64)
+            tile_load<KVK>(raw, static_cast<const uint8_t*>(ktab[k0 >> PAGE_SHIFT]),
+                           static_cast<const uint8_t*>(vtab[k0 >> PAGE_SHIFT]), nkeys, n_kv, pb.kvh,
+                           ptid);
+            if (i >= KV_STAGES && !bar_wait(kv_empty + 8 * st, (uint32_t)(((i / KV_STAGES) - 1) & 1)))
+                break;
+            tile_store<KVK>(raw, kv_sm + st * STAGE_BYTES, nkeys, ptid);
+            fence_async_smem();
+            bar_arrive(kv_full + 8 * st);
+        }
+    }
+    __syncthreads();
+    if (warp == MMA_WARP) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "n"(TMEM_COLS) : "memory");
+    }
+}
+
+template <int KVK>
+__global__ void __launch_bounds__(UMMA_THREADS, 1)
+k_prefill_umma(const __grid_constant__ TileArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    Problem<0> pb;
+    pb.ta = &a;
+    pb.vb = nullptr;
+    pb.slot = nullptr;
+    pb.kvh = blockIdx.y;
+    pb.tile_t0 = a.t0 + blockIdx.x * TOK_PER_TILE;
+    pb.lo = 0;
+    pb.hi = a.base_pos + min(pb.tile_t0 + TOK_PER_TILE, a.t_end);
+    pb.sp = 0;
+    attn_tile<KVK, 0>(pb, a.ktab, a.vtab, a.n_kv, a.scale, smem_raw);
+}
+
+template <int KVK>
+__global__ void __launch_bounds__(UMMA_THREADS, 1)
+k_verify_umma(const __grid_constant__ DevBatch b) {
+    extern __shared__ uint8_t smem_raw[];
+    const DevSlot& S = b.s[blockIdx.z];
+    int max_len = 0;
+    for (int u = 0; u < S.ntok; u++)
+        max_len = max(max_len, local_len(__ldg(S.pos[u]), S.row_base, S.row_count));
+    const int chunk = split_chunk(max_len, b.nsplit, b.unit);
+    Problem<1> pb;
+    pb.ta = nullptr;
+    pb.vb = &b;
+    pb.slot = &S;
+    pb.kvh = blockIdx.y;
+    pb.tile_t0 = 0;
+    pb.sp = blockIdx.x;
+    pb.lo = pb.sp * chunk;
+    pb.hi = min(max_len, pb.lo + chunk);
+    if (pb.lo >= pb.hi) { // nothing of this split is visible to any lane: sentinels only
+        for (int r = threadIdx.x; r < S.ntok * GQA; r += blockDim.x) {
+            float* d = S.scratch + (((size_t)(r / GQA) * b.n_q + pb.kvh * GQA + r % GQA) * b.nsplit + pb.sp) * PART;
+            d[0] = NEG_SENTINEL;
+            d[1] = 0.f;
+        }
+        return;
+    }
+    attn_tile<KVK, 1>(pb, S.ktab, S.vtab, b.n_kv, b.scale, smem_raw);
+}
+
+template <int KVK>
+int set_attrs() {
+    static bool done = false;
+    if (!done) {
+        Q27_CUDA_TRY(cudaFuncSetAttribute(k_prefill_umma<KVK>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, UMMA_SMEM));
+        Q27_CUDA_TRY(cudaFuncSetAttribute(k_verify_umma<KVK>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, UMMA_SMEM));
+        done = true;
+    }
+    return Q27_OK;
+}
+
+} // namespace
+
+int launch_prefill_umma(const float* qT, int q_stride, int q_row, const void* const* ktab,
+                        const void* const* vtab, float* outT, int out_row, int base_pos, int t0,
+                        int SB, int n_q, int n_kv, float scale, cudaStream_t st, int kvk,
+                        bool* done) {
+    *done = false;
+    (void)n_q;
+    // float4 loads of Q rows and float4 stores of output rows
+    if ((q_stride & 3) || (q_row & 3) || (out_row & 3) || ((uintptr_t)qT & 15) || ((uintptr_t)outT & 15))
+        return Q27_OK;
+    TileArgs a{qT, ktab, vtab, outT, q_stride, q_row, out_row, base_pos, t0, t0 + SB, n_kv, scale};
+    dim3 grid((SB + TOK_PER_TILE - 1) / TOK_PER_TILE, n_kv);
+    int rc;
+    if (kvk == Q27_KV_F16) {
+        if ((rc = set_attrs<Q27_KV_F16>())) return rc;
+        k_prefill_umma<Q27_KV_F16><<<grid, UMMA_THREADS, UMMA_SMEM, st>>>(a);
+    } else if (kvk == Q27_KV_FP8) {
+        if ((rc = set_attrs<Q27_KV_FP8>())) return rc;
+        k_prefill_umma<Q27_KV_FP8><<<grid, UMMA_THREADS, UMMA_SMEM, st>>>(a);
+    } else if (kvk == Q27_KV_T3) {
+        if ((rc = set_attrs<Q27_KV_T3>())) return rc;
+        k_prefill_umma<Q27_KV_T3><<<grid, UMMA_THREADS, UMMA_SMEM, st>>>(a);
+    } else {
+        return Q27_ERR_UNSUPPORTED_KIND;
+    }
+    Q27_CUDA_TRY(cudaGetLastError());
+    *done = true;
+    return Q27_OK;
+}
+
+int launch_verify_umma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool* done) {
+    *done = false;
+    if (b.q_stride & 3) return Q27_OK;
+    for (int i = 0; i < b.nslots; i++)
+        for (int t = 0; t < b.s[i].ntok; t++)
+            if ((uintptr_t)b.s[i].q[t] & 15) return Q27_OK;
+    int ns = sm_count / (b.nslots * b.n_kv);
+    b.nsplit = ns < 1 ? 1 : ns > Q27_MAX_SPLITS ? Q27_MAX_SPLITS : ns;
+    b.unit = BN;
+    dim3 grid(b.nsplit, b.n_kv, b.nslots);
+    int rc;
+    if (kvk == Q27_KV_F16) {
+        if ((rc = set_attrs<Q27_KV_F16>())) return rc;
+        k_verify_umma<Q27_KV_F16><<<grid, UMMA_THREADS, UMMA_SMEM, st>>>(b);
+    } else if (kvk == Q27_KV_FP8) {
+        if ((rc = set_attrs<Q27_KV_FP8>())) return rc;
+        k_verify_umma<Q27_KV_FP8><<<grid, UMMA_THREADS, UMMA_SMEM, st>>>(b);
+    } else if (kvk == Q27_KV_T3) {
+        if ((rc = set_attrs<Q27_KV_T3>())) return rc;
+        k_verify_umma<Q27_KV_T3><<<grid, UMMA_THREADS, UMMA_SMEM, st>>>(b);
+    } else {
+        return Q27_ERR_UNSUPPORTED_KIND;
+    }
+    Q27_CUDA_TRY(cudaGetLastError());
+    *done = true;
+    return Q27_OK;
+}
+
+} // namespace q27b

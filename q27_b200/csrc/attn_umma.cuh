@@ -1,0 +1,17 @@
+// tcgen05 / TMEM attention tile kernel: causal GQA prefill over a reused prefix and the
+// one-pass shared-KV verify step. Launchers set *done = false when the shape is not covered.
+#pragma once
+#include "common.cuh"
+
+namespace q27b {
+
+int launch_prefill_umma(const float* qT, int q_stride, int q_row, const void* const* ktab,
+                        const void* const* vtab, float* outT, int out_row, int base_pos, int t0,
+                        int SB, int n_q, int n_kv, float scale, cudaStream_t st, int kvk,
+                        bool* done);
+
+// Writes split-KV partials for every lane of every slot in ONE pass over the cache per
+// (slot, kv head, split); fills b.nsplit / b.unit for the combine.
+int launch_verify_umma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool* done);
+
+} // namespace q27b

@@ -19,6 +19,7 @@
 // fragment registers come from contiguous packed bytes; Q^T fragments and the output rows
 // use the same maps (kdim_* / vdim_* below), so the permutation cancels.
 #include "decode_mma.cuh"
+#include "t3_lut.cuh"
 
 namespace q27b {
 
@@ -26,10 +27,16 @@ __device__ int g_wait_timeout_flag = 0; // set when a bounded mbarrier wait ran 
 
 namespace {
 
-constexpr int NCW = 8;            // consumer warps
+#ifndef Q27_NCW
+#define Q27_NCW 8
+#endif
+constexpr int NCW = Q27_NCW;      // consumer warps
 constexpr int STAGE_ROWS = 32;    // rows per ring stage (= 2 key tiles; never crosses a page)
 constexpr int TILE = 16;          // keys per MMA tile
 constexpr float LOG2E = 1.4426950408889634f;
+#ifndef Q27_KERNEL_ATTR
+#define Q27_KERNEL_ATTR __launch_bounds__((NCW + 1) * 32, 1)
+#endif
 #ifndef Q27_ABLATE
 #define Q27_ABLATE 0   // timing experiments only: 1 skip K lookups, 2 skip V lookups, 4 skip MMAs
 #endif
@@ -47,11 +54,14 @@ template <> struct Fmt<Q27_KV_FP8> {
     static constexpr int SLICE = 256;
     static constexpr int STAGES = 8;
 };
+#ifndef Q27_T3_STAGES
+#define Q27_T3_STAGES 5
+#endif
 template <> struct Fmt<Q27_KV_T3> {
     static constexpr int KVH = 4;               // whole 400-byte rows: all four kv heads
     static constexpr int PITCH = 400;
     static constexpr int SLICE = 400;
-    static constexpr int STAGES = 5;
+    static constexpr int STAGES = Q27_T3_STAGES;
 };
 template <int KVK> constexpr int stage_bytes() { return 2 * STAGE_ROWS * Fmt<KVK>::PITCH; }
 template <int KVK> constexpr int ring_bytes() { return stage_bytes<KVK>() * Fmt<KVK>::STAGES; }
@@ -96,11 +106,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
         ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t d;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-    return d;
 }
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -198,44 +203,6 @@ template <int KVK>
 __host__ __device__ __forceinline__ int keyperm(int k) {
     if (KVK == Q27_KV_FP8) return ((k >> 1) & 3) + 4 * (k & 1) + 8 * (k >> 3);
     return k;
-}
-
-// ---- turbo3 selector / lookup machinery ----------------------------------------------
-// fp16 bit patterns of the centroids (src/turbo3.cuh:38-40), split into low and high bytes
-// and packed as PRMT pools: pool byte i (0..7) = byte of centroid i.
-struct T3Tab {
-    uint32_t lo_a, lo_b, hi_a, hi_b;
-};
-__device__ __forceinline__ T3Tab t3_tables() {
-    uint32_t lo[2] = {0, 0}, hi[2] = {0, 0};
-    const float c[8] = {-0.190207f, -0.118786f, -0.066822f, -0.021663f,
-                        0.021663f,  0.066822f,  0.118786f,  0.190207f};
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const uint32_t bits = __half_as_ushort(__float2half_rn(c[i]));
-        lo[i >> 2] |= (bits & 0xffu) << (8 * (i & 3));
-        hi[i >> 2] |= (bits >> 8) << (8 * (i & 3));
-    }
-    return T3Tab{lo[0], lo[1], hi[0], hi[1]};
-}
-// 16 elements: qs word Q (2 bits each) + 16 sign bits -> selectors with one nibble
-// (hi<<2 | low2) per element; ze holds elements 0,2,..,14 and zo elements 1,3,..,15.
-__device__ __forceinline__ void t3_selectors(uint32_t Q, uint32_t S16, uint32_t& ze, uint32_t& zo) {
-    // byte LUT spreading sign bits (b0, b2 of a nibble) to bit 2 of two output nibbles
-    const uint32_t he = prmt(0x04000400u, 0x44404440u, S16 & 0x7777u);
-    const uint32_t ho = prmt(0x04000400u, 0x44404440u, (S16 >> 1) & 0x7777u);
-    ze = (Q & 0x33333333u) | he;
-    zo = ((Q >> 2) & 0x33333333u) | ho;
-}
-// 8 selector nibbles -> 4 half2 registers (nibbles 2i, 2i+1 -> h[i])
-__device__ __forceinline__ void t3_lookup(const T3Tab& t, uint32_t z, uint32_t* h) {
-    const uint32_t zh = z >> 16;
-    const uint32_t l0 = prmt(t.lo_a, t.lo_b, z), h0 = prmt(t.hi_a, t.hi_b, z);
-    const uint32_t l1 = prmt(t.lo_a, t.lo_b, zh), h1 = prmt(t.hi_a, t.hi_b, zh);
-    h[0] = prmt(l0, h0, 0x5140u);
-    h[1] = prmt(l0, h0, 0x7362u);
-    h[2] = prmt(l1, h1, 0x5140u);
-    h[3] = prmt(l1, h1, 0x7362u);
 }
 
 // ---- per-warp state -----------------------------------------------------------------------
@@ -469,7 +436,7 @@ __device__ __forceinline__ void tile_t3(WarpAcc& A, uint32_t ks, uint32_t vs, in
 
 // ---- the kernel -------------------------------------------------------------------------
 template <int KVK>
-__global__ void __launch_bounds__((NCW + 1) * 32, 1)
+__global__ void Q27_KERNEL_ATTR
 k_decode_mma(const __grid_constant__ DevBatch b) {
     using F = Fmt<KVK>;
     constexpr int WAYS = NCW / F::KVH;             // consumer warps per kv head

@@ -108,7 +108,10 @@ def test_turbo3_pipeline_end_to_end(oracle, cuda):
     got = out.cpu().numpy()
     rot = oracle.attn_decode(c.q, c.k, c.v, KV_T3, pos)
     want = oracle.wht(rot.reshape(-1, 128), inverse=True).reshape(rot.shape)
-    assert synth.tolerance_ok(got, want)[0]
+    # after the inverse rotation every output mixes 128 rotated ones: judged with the
+    # reference's own gate for its tensor-core paths (max-abs/RMS, src/test_kernels.cu:1521)
+    rms = np.sqrt((want.astype(np.float64) ** 2).mean())
+    assert np.abs(got - want).max() / rms < 1e-2
     c16 = synth.make_case(oracle, KV_F16, rows=rows, pos=pos, seed=29, outlier_frac=0.02)
     plain = oracle.attn_decode(c16.q, c16.k, c16.v, KV_F16, pos)
     cos = (got * plain).sum() / np.sqrt((got ** 2).sum() * (plain ** 2).sum())
