@@ -10,8 +10,9 @@
 //
 // Operands are fp16 in shared memory in the 128-byte-swizzled canonical layouts (Q and K
 // K-major, V MN-major = its natural [key][dim] rows, P K-major), accumulation is fp32.
-// Warp roles: warps 0-3 softmax (thread = row = TMEM lane), warp 4 issues the MMAs, warps
-// 5-8 stage K/V tiles (cp.async for fp16 rows; load + convert for fp8 / turbo3). The running
+// Warp roles: warps 0-3 softmax (thread = row = TMEM lane); warp 4 issues the S MMAs and warp 5
+// the PV MMAs (two independent issue streams, ordered only by mbarriers); warps 6-13 stage
+// K/V tiles (cp.async for fp16 rows, registers + convert for fp8 / turbo3). The running
 // max is only advanced when it grows by more than 2^8, so O in TMEM is rarely rescaled.
 // Every mbarrier wait is bounded; a timeout sets the library's flag and the CTA drains.
 #include "attn_umma.cuh"
@@ -20,6 +21,18 @@
 namespace q27b {
 
 extern __device__ int g_wait_timeout_flag;
+#ifdef Q27_TRACE
+// timing experiments only: cycles spent waiting, summed over CTAs, by (role, barrier)
+__device__ unsigned long long g_umma_trace[16];
+__device__ long long g_umma_ev[8][64];   // per-event timestamps of CTA (0,0,0), first 64 tiles
+#define TRACE_EV(e, i) do { if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (i) < 64) g_umma_ev[e][i] = clock64(); } while (0)
+#define TRACE_T0() const long long t0__ = clock64()
+#define TRACE_ADD(slot, cond) do { if (cond) atomicAdd(&g_umma_trace[slot], (unsigned long long)(clock64() - t0__)); } while (0)
+#else
+#define TRACE_T0()
+#define TRACE_ADD(slot, cond)
+#define TRACE_EV(e, i)
+#endif
 
 namespace {
 
@@ -38,8 +51,9 @@ constexpr int COL_S0 = 0, COL_S1 = 64, COL_O = 128;
 constexpr float LOG2E_F = 1.4426950408889634f;
 constexpr float RESCALE_THRESHOLD = 8.0f;       // log2 units
 
-constexpr int N_SOFTMAX_WARPS = 4, MMA_WARP = 4, FIRST_LOAD_WARP = 5, N_LOAD_WARPS = 4;
-constexpr int UMMA_THREADS = (FIRST_LOAD_WARP + N_LOAD_WARPS) * 32;   // 288
+constexpr int N_SOFTMAX_WARPS = 4, MMA_WARP = 4, PV_WARP = 5, FIRST_LOAD_WARP = 6, N_LOAD_WARPS = 8;
+constexpr int UMMA_THREADS = (FIRST_LOAD_WARP + N_LOAD_WARPS) * 32;   // 448
+constexpr int NPROD = N_LOAD_WARPS * 32;                              // 256 staging threads
 
 // ---- small PTX wrappers -------------------------------------------------------------------
 __device__ __forceinline__ uint32_t s32(const void* p) {
@@ -199,29 +213,30 @@ struct Problem {
 // is free, so the global latency hides behind the tiles in flight), `store` converts and
 // writes them once the slot has been released.
 template <int KVK> struct RawTile;
-template <> struct RawTile<Q27_KV_F16> { uint4 k[16], v[16]; };
-template <> struct RawTile<Q27_KV_FP8> { uint2 k[16], v[16]; };
-template <> struct RawTile<Q27_KV_T3> { uint32_t w[26]; };
+template <> struct RawTile<Q27_KV_F16> { uint4 k[8], v[8]; };
+template <> struct RawTile<Q27_KV_FP8> { uint2 k[8], v[8]; };
+template <> struct RawTile<Q27_KV_T3> { uint32_t w[14]; };
 
 template <int KVK>
 __device__ __forceinline__ void tile_load(RawTile<KVK>& t, const uint8_t* kpage, const uint8_t* vpage,
                                           int nkeys, int n_kv, int kvh, int ptid) {
     if constexpr (KVK == Q27_KV_T3) {
-        // one thread = one (key, side) slice of 100 bytes = two 50-byte blocks
-        const int key = ptid & 63, side = ptid >> 6;
+        // one thread = one 50-byte block: (key, side, block). Block 1 starts 2 bytes past a
+        // word boundary, so 14 words from the aligned address below it cover either block.
+        const int key = ptid & 63, side = (ptid >> 6) & 1, blk = ptid >> 7;
 #pragma unroll
-        for (int i = 0; i < 26; i++) t.w[i] = 0;
+        for (int i = 0; i < 14; i++) t.w[i] = 0;
         if (key < nkeys) {
             const uint32_t* src = reinterpret_cast<const uint32_t*>(
-                (side ? vpage : kpage) + ((size_t)key * n_kv + kvh) * (2 * T3_BLK));
+                (side ? vpage : kpage) + ((size_t)key * n_kv + kvh) * (2 * T3_BLK)) + 12 * blk;
 #pragma unroll
-            for (int i = 0; i < 25; i++) t.w[i] = __ldg(src + i);
+            for (int i = 0; i < 13; i++) t.w[i] = __ldg(src + i);
         }
     } else {
         constexpr int CB = KVK == Q27_KV_F16 ? 16 : 8;      // bytes per 8-dim chunk
 #pragma unroll
-        for (int n = 0; n < 16; n++) {
-            const int q = ptid + 128 * n;
+        for (int n = 0; n < 8; n++) {
+            const int q = ptid + NPROD * n;
             const int key = q >> 5, ch = q & 31;
             const size_t src = ((size_t)key * n_kv + kvh) * (HD * CB / 8) + (size_t)ch * CB;
             if constexpr (KVK == Q27_KV_F16) {
@@ -241,72 +256,76 @@ __device__ __forceinline__ void tile_load(RawTile<KVK>& t, const uint8_t* kpage,
     }
 }
 
-template <int KVK>
+// WHICH: 0 = the K half of the tile, 1 = the V half
+template <int KVK, int WHICH>
 __device__ __forceinline__ void tile_store(const RawTile<KVK>& t, uint8_t* dstK, int nkeys, int ptid) {
     uint8_t* dstV = dstK + KT_BYTES;
     if constexpr (KVK == Q27_KV_F16) {
 #pragma unroll
-        for (int n = 0; n < 16; n++) {
-            const int q = ptid + 128 * n;
+        for (int n = 0; n < 8; n++) {
+            const int q = ptid + NPROD * n;
             const int key = q >> 5, ch = q & 31;
             const uint32_t off = (uint32_t)(ch >> 3) * (BN * 128) + sw128(key, ch & 7);
-            *reinterpret_cast<uint4*>(dstK + off) = t.k[n];
-            *reinterpret_cast<uint4*>(dstV + off) = t.v[n];
+            if (WHICH == 0) *reinterpret_cast<uint4*>(dstK + off) = t.k[n];
+            else *reinterpret_cast<uint4*>(dstV + off) = t.v[n];
         }
     } else if constexpr (KVK == Q27_KV_FP8) {
 #pragma unroll
-        for (int n = 0; n < 16; n++) {
-            const int q = ptid + 128 * n;
+        for (int n = 0; n < 8; n++) {
+            const int q = ptid + NPROD * n;
             const int key = q >> 5, ch = q & 31;
             const uint32_t off = (uint32_t)(ch >> 3) * (BN * 128) + sw128(key, ch & 7);
             auto cv = [](uint32_t two) {
                 __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two, __NV_E4M3);
                 return (uint32_t)h.x | ((uint32_t)h.y << 16);
             };
-            *reinterpret_cast<uint4*>(dstK + off) = make_uint4(
-                cv(t.k[n].x & 0xffffu), cv(t.k[n].x >> 16), cv(t.k[n].y & 0xffffu), cv(t.k[n].y >> 16));
-            *reinterpret_cast<uint4*>(dstV + off) = make_uint4(
-                cv(t.v[n].x & 0xffffu), cv(t.v[n].x >> 16), cv(t.v[n].y & 0xffffu), cv(t.v[n].y >> 16));
+            if (WHICH == 0)
+                *reinterpret_cast<uint4*>(dstK + off) = make_uint4(
+                    cv(t.k[n].x & 0xffffu), cv(t.k[n].x >> 16), cv(t.k[n].y & 0xffffu), cv(t.k[n].y >> 16));
+            else
+                *reinterpret_cast<uint4*>(dstV + off) = make_uint4(
+                    cv(t.v[n].x & 0xffffu), cv(t.v[n].x >> 16), cv(t.v[n].y & 0xffffu), cv(t.v[n].y >> 16));
         }
     } else {
-        const int key = ptid & 63, side = ptid >> 6;
+        const int key = ptid & 63, side = (ptid >> 6) & 1, blk = ptid >> 7;
+        if (side != WHICH) return;              // warp-uniform: a warp holds one side only
         uint8_t* dst = side ? dstV : dstK;
         const uint32_t* w = t.w;
         const T3Tab tab = t3_tables();
+        // 32-bit little-endian word at byte `o` of the block (o even, compile time); block 1
+        // sits 2 bytes into the loaded words, block 0 at byte 0 (blk is warp-uniform)
+        auto word_at = [&](int o) {
+            const uint32_t a0 = (o & 3) ? __funnelshift_r(w[o >> 2], w[(o >> 2) + 1], 16) : w[o >> 2];
+            const int o1 = o + 2;
+            const uint32_t a1 = (o1 & 3) ? __funnelshift_r(w[o1 >> 2], w[(o1 >> 2) + 1], 16) : w[o1 >> 2];
+            return blk ? a1 : a0;
+        };
+        const __half nh = __ushort_as_half((unsigned short)(word_at(0) & 0xffffu));
+        const __half2 n2 = key < nkeys ? __half2half2(nh) : __float2half2_rn(0.f);
 #pragma unroll
-        for (int b = 0; b < 2; b++) {
-            // 32-bit little-endian word starting at byte `o` of the slice (o even, compile time)
-            auto word_at = [&](int o) {
-                return (o & 3) ? __funnelshift_r(w[o >> 2], w[(o >> 2) + 1], 16) : w[o >> 2];
-            };
-            const __half nh = __ushort_as_half((unsigned short)(word_at(50 * b) & 0xffffu));
-            const float nf = key < nkeys ? __half2float(nh) : 0.f;
+        for (int g8 = 0; g8 < 8; g8++) {         // 16 dims per group
+            const uint32_t Qw = word_at(2 + 4 * g8);
+            const uint32_t S16 = (word_at(34 + 2 * (g8 & ~1)) >> (16 * (g8 & 1))) & 0xffffu;
+            uint32_t ze, zo, e[4], o[4];
+            t3_selectors(Qw, S16, ze, zo);
+            t3_lookup(tab, ze, e);                // (0,2) (4,6) (8,10) (12,14)
+            t3_lookup(tab, zo, o);                // (1,3) (5,7) (9,11) (13,15)
+            uint32_t nat[8];
 #pragma unroll
-            for (int g8 = 0; g8 < 8; g8++) {         // 16 dims per group
-                const uint32_t Qw = word_at(50 * b + 2 + 4 * g8);
-                const uint32_t S16 = (word_at(50 * b + 34 + 2 * (g8 & ~1)) >> (16 * (g8 & 1))) & 0xffffu;
-                uint32_t ze, zo, e[4], o[4];
-                t3_selectors(Qw, S16, ze, zo);
-                t3_lookup(tab, ze, e);                // (0,2) (4,6) (8,10) (12,14)
-                t3_lookup(tab, zo, o);                // (1,3) (5,7) (9,11) (13,15)
-                uint32_t nat[8];
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    nat[2 * i] = prmt(e[i], o[i], 0x5410u);      // dims 4i, 4i+1
-                    nat[2 * i + 1] = prmt(e[i], o[i], 0x7632u);  // dims 4i+2, 4i+3
-                }
-#pragma unroll
-                for (int i = 0; i < 8; i++) {   // product in fp32, one rounding to fp16
-                    const float2 cf = __half22float2(*reinterpret_cast<__half2*>(&nat[i]));
-                    __half2 h = __floats2half2_rn(cf.x * nf, cf.y * nf);
-                    nat[i] = *reinterpret_cast<uint32_t*>(&h);
-                }
-                const int ch = 16 * b + 2 * g8;      // 8-dim chunk index within the head
-                *reinterpret_cast<uint4*>(dst + (ch >> 3) * (BN * 128) + sw128(key, ch & 7)) =
-                    make_uint4(nat[0], nat[1], nat[2], nat[3]);
-                *reinterpret_cast<uint4*>(dst + ((ch + 1) >> 3) * (BN * 128) + sw128(key, (ch + 1) & 7)) =
-                    make_uint4(nat[4], nat[5], nat[6], nat[7]);
+            for (int i = 0; i < 4; i++) {
+                nat[2 * i] = prmt(e[i], o[i], 0x5410u);      // dims 4i, 4i+1
+                nat[2 * i + 1] = prmt(e[i], o[i], 0x7632u);  // dims 4i+2, 4i+3
             }
+#pragma unroll
+            for (int i = 0; i < 8; i++) {   // fp16 centroid x fp16 norm, rounded once
+                __half2 h = __hmul2(*reinterpret_cast<__half2*>(&nat[i]), n2);
+                nat[i] = *reinterpret_cast<uint32_t*>(&h);
+            }
+            const int ch = 16 * blk + 2 * g8;    // 8-dim chunk index within the head
+            *reinterpret_cast<uint4*>(dst + (ch >> 3) * (BN * 128) + sw128(key, ch & 7)) =
+                make_uint4(nat[0], nat[1], nat[2], nat[3]);
+            *reinterpret_cast<uint4*>(dst + ((ch + 1) >> 3) * (BN * 128) + sw128(key, (ch + 1) & 7)) =
+                make_uint4(nat[4], nat[5], nat[6], nat[7]);
         }
     }
 }
@@ -321,15 +340,20 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     uint8_t* q_sm = base + SMEM_BAR;
     uint8_t* p_sm = q_sm + Q_BYTES;
     uint8_t* kv_sm = p_sm + P_BYTES;
-    const uint32_t kv_full = s32(&bars[0]), kv_empty = s32(&bars[2]), s_full = s32(&bars[4]),
-                   s_free = s32(&bars[6]), p_full = s32(&bars[8]), pv_done = s32(&bars[9]);
+    // K and V slots are released separately: a K slot as soon as its S MMAs have run, a V
+    // slot after its PV MMAs, so the next K tile lands while the current tile is in softmax
+    const uint32_t k_full = s32(&bars[0]), k_empty = s32(&bars[2]), v_full = s32(&bars[4]),
+                   v_empty = s32(&bars[6]), s_full = s32(&bars[8]), s_free = s32(&bars[10]),
+                   p_full = s32(&bars[12]), pv_done = s32(&bars[13]);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = (pb.hi - pb.lo + BN - 1) / BN;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < 2; s++) {
-            bar_init(kv_full + 8 * s, N_LOAD_WARPS * 32);
-            bar_init(kv_empty + 8 * s, 1);
+            bar_init(k_full + 8 * s, N_LOAD_WARPS * 32);
+            bar_init(k_empty + 8 * s, 1);
+            bar_init(v_full + 8 * s, N_LOAD_WARPS * 32);
+            bar_init(v_empty + 8 * s, 1);
             bar_init(s_full + 8 * s, 1);
             bar_init(s_free + 8 * s, N_SOFTMAX_WARPS * 32);
         }
@@ -370,10 +394,16 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         const float sc2 = scale * LOG2E_F;
         float m_ref = -INFINITY, l = 0.f;
         bool ok = true;
+#ifdef Q27_TRACE
+        const long long tloop = clock64();
+#endif
         for (int i = 0; i < ntiles && ok; i++) {
             const int bsel = i & 1;
-            ok = __all_sync(0xffffffffu, bar_wait(s_full + 8 * bsel, (uint32_t)((i >> 1) & 1)));
+            { TRACE_T0();
+              ok = __all_sync(0xffffffffu, bar_wait(s_full + 8 * bsel, (uint32_t)((i >> 1) & 1)));
+              TRACE_ADD(0, threadIdx.x == 0); }
             if (!ok) break;
+            if (threadIdx.x == 0) TRACE_EV(4, i);
             tc_fence_after();
             float s[BN];
             tc_ld32(lane_base + (bsel ? COL_S1 : COL_S0), s);
@@ -384,10 +414,18 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             const int k0 = pb.lo + i * BN;
             const int vis = ri.bound - k0;            // columns [0, vis) are visible
             float mx = -INFINITY;
+            if (vis >= BN) {                          // the common case: nothing to mask
 #pragma unroll
-            for (int j = 0; j < BN; j++) {
-                s[j] = j < vis ? s[j] * sc2 : -INFINITY;
-                mx = fmaxf(mx, s[j]);
+                for (int j = 0; j < BN; j++) {
+                    s[j] *= sc2;
+                    mx = fmaxf(mx, s[j]);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < BN; j++) {
+                    s[j] = j < vis ? s[j] * sc2 : -INFINITY;
+                    mx = fmaxf(mx, s[j]);
+                }
             }
             float alpha = 1.f;
             bool need = false;
@@ -407,8 +445,11 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 ph[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
             }
             l = l * alpha + sum;
+            if (threadIdx.x == 0) TRACE_EV(5, i);
             if (i > 0) {
-                ok = __all_sync(0xffffffffu, bar_wait(pv_done, (uint32_t)((i - 1) & 1)));
+                { TRACE_T0();
+                  ok = __all_sync(0xffffffffu, bar_wait(pv_done, (uint32_t)((i - 1) & 1)));
+                  TRACE_ADD(1, threadIdx.x == 0); }
                 if (!ok) break;
                 tc_fence_after();
             }
@@ -431,9 +472,16 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             fence_async_smem();
             tc_fence_before();
             bar_arrive(p_full);
+            if (threadIdx.x == 0) TRACE_EV(6, i);
         }
         if (ok) ok = bar_wait(pv_done, (uint32_t)((ntiles - 1) & 1));
         ok = __all_sync(0xffffffffu, ok);
+#ifdef Q27_TRACE
+        if (threadIdx.x == 0) {
+            atomicAdd(&g_umma_trace[7], (unsigned long long)(clock64() - tloop));
+            atomicAdd(&g_umma_trace[8], (unsigned long long)ntiles);
+        }
+#endif
         tc_fence_after();
         if (ok) {
             const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -461,19 +509,25 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         }
         tc_fence_before();
     } else if (warp == MMA_WARP) {
-        // ------------------------------ MMA issue: one thread ------------------------------
+        // ------------------------------ S issue: one thread --------------------------------
         if (lane == 0) {
             constexpr uint32_t IDESC_S = make_idesc(BM, BN, false);
-            constexpr uint32_t IDESC_O = make_idesc(BM, HD, true);
-            const uint32_t q_s = s32(q_sm), p_s = s32(p_sm), kv_s = s32(kv_sm);
+            const uint32_t q_s = s32(q_sm), kv_s = s32(kv_sm);
             bool ok = true;
             auto issue_s = [&](int i) {
                 const int st = i % KV_STAGES, bsel = i & 1;
-                ok = ok && bar_wait(kv_full + 8 * st, (uint32_t)((i / KV_STAGES) & 1));
-                if (ok && i >= 2) ok = bar_wait(s_free + 8 * bsel, (uint32_t)(((i >> 1) - 1) & 1));
+                { TRACE_T0();
+                  ok = ok && bar_wait(k_full + 8 * st, (uint32_t)((i / KV_STAGES) & 1));
+                  TRACE_ADD(2, true); }
+                { TRACE_T0();
+                  if (ok && i >= 2) ok = bar_wait(s_free + 8 * bsel, (uint32_t)(((i >> 1) - 1) & 1));
+                  TRACE_ADD(3, true); }
                 if (!ok) return;
+                fence_async_smem();
                 tc_fence_after();
                 const uint32_t k_s = kv_s + st * STAGE_BYTES;
+                TRACE_EV(0, i);
+                TRACE_T0();
 #pragma unroll
                 for (int ks = 0; ks < HD / 16; ks++) {
                     const uint64_t da = make_desc(q_s + (ks >> 2) * (BM * 128) + (ks & 3) * 32, 0, 1024);
@@ -481,16 +535,32 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                     tc_mma_f16(tmem + (bsel ? COL_S1 : COL_S0), da, db, IDESC_S, ks > 0);
                 }
                 tc_commit(s_full + 8 * bsel);
+                tc_commit(k_empty + 8 * st);
+                TRACE_EV(1, i);
+                TRACE_ADD(9, true);
             };
-            issue_s(0);
+            for (int i = 0; i < ntiles && ok; i++) issue_s(i);
+        }
+        __syncwarp();
+    } else if (warp == PV_WARP) {
+        // ------------------------------ PV issue: one thread -------------------------------
+        if (lane == 0) {
+            constexpr uint32_t IDESC_O = make_idesc(BM, HD, true);
+            const uint32_t p_s = s32(p_sm), kv_s = s32(kv_sm);
+            bool ok = true;
             for (int i = 0; i < ntiles && ok; i++) {
-                if (i + 1 < ntiles) issue_s(i + 1);
+                { TRACE_T0();
+                  ok = bar_wait(p_full, (uint32_t)(i & 1));
+                  TRACE_ADD(4, true); }
                 if (!ok) break;
-                ok = bar_wait(p_full, (uint32_t)(i & 1));
-                if (!ok) break;
-                tc_fence_after();
                 const int st = i % KV_STAGES;
+                ok = bar_wait(v_full + 8 * st, (uint32_t)((i / KV_STAGES) & 1));
+                if (!ok) break;
+                fence_async_smem();
+                tc_fence_after();
                 const uint32_t v_s = kv_s + st * STAGE_BYTES + KT_BYTES;
+                TRACE_EV(2, i);
+                TRACE_T0();
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; kk++) {
                     const uint64_t da = make_desc(p_s + kk * 32, 0, 1024);
@@ -498,27 +568,86 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                     tc_mma_f16(tmem + COL_O, da, db, IDESC_O, (i > 0 || kk > 0));
                 }
                 tc_commit(pv_done);
-                tc_commit(kv_empty + 8 * st);
+                tc_commit(v_empty + 8 * st);
+                TRACE_EV(3, i);
+                TRACE_ADD(10, true);
             }
         }
         __syncwarp();
     } else {
         // ------------------------------ K/V staging ----------------------------------------
         const int ptid = threadIdx.x - FIRST_LOAD_WARP * 32;
-        RawTile<KVK> raw;
-        for (int i = 0; i < ntiles; i++) {
+        RawTile<KVK> raw0, raw1;
+        // a tile is exactly one cache page (its first key is a multiple of 64)
+        auto load = [&](RawTile<KVK>& r, int i) {
+            if (i < ntiles) {
+                const int k0 = pb.lo + i * BN;
+                tile_load<KVK>(r, static_cast<const uint8_t*>(ktab[k0 >> PAGE_SHIFT]),
+                               static_cast<const uint8_t*>(vtab[k0 >> PAGE_SHIFT]),
+                               min(BN, pb.hi - k0), n_kv, pb.kvh, ptid);
+            }
+        };
+        auto store = [&](const RawTile<KVK>& r, int i) -> bool {
             const int st = i % KV_STAGES;
-            const int k0 = pb.lo + i * BN;
-            const int nkeys = min(BN, pb.hi - k0);
-            // a tile is exactly one cache page (k0 is a multiple of 64)
-            tile_load<KVK>(raw, static_cast<const uint8_t*>(ktab[k0 >> PAGE_SHIFT]),
-                           static_cast<const uint8_t*>(vtab[k0 >> PAGE_SHIFT]), nkeys, n_kv, pb.kvh,
-                           ptid);
-            if (i >= KV_STAGES && !bar_wait(kv_empty + 8 * st, (uint32_t)(((i / KV_STAGES) - 1) & 1)))
-                break;
-            tile_store<KVK>(raw, kv_sm + st * STAGE_BYTES, nkeys, ptid);
+            const uint32_t par = (uint32_t)(((i / KV_STAGES) - 1) & 1);
+            const int nk = min(BN, pb.hi - (pb.lo + i * BN));
+            { TRACE_T0();
+              if (i >= KV_STAGES && !bar_wait(k_empty + 8 * st, par)) return false;
+              TRACE_ADD(5, ptid == 0); }
+            { TRACE_T0();
+              tile_store<KVK, 0>(r, kv_sm + st * STAGE_BYTES, nk, ptid);
+              fence_async_smem();
+              TRACE_ADD(6, ptid == 0); }
+            bar_arrive(k_full + 8 * st);
+            if (i >= KV_STAGES && !bar_wait(v_empty + 8 * st, par)) return false;
+            tile_store<KVK, 1>(r, kv_sm + st * STAGE_BYTES, nk, ptid);
             fence_async_smem();
-            bar_arrive(kv_full + 8 * st);
+            bar_arrive(v_full + 8 * st);
+            return true;
+        };
+        if constexpr (KVK == Q27_KV_F16) {
+            // fp16 rows need no conversion: cp.async writes them straight into the swizzled
+            // operand layout and the slot's barrier is armed to fire when this thread's
+            // copies have landed, so the staging threads never wait for data
+            (void)raw0; (void)raw1;
+            auto copy_half = [&](int i, int which) -> bool {
+                const int st = i % KV_STAGES;
+                const uint32_t par = (uint32_t)(((i / KV_STAGES) - 1) & 1);
+                const uint32_t empty = (which ? v_empty : k_empty) + 8 * st;
+                const uint32_t full = (which ? v_full : k_full) + 8 * st;
+                if (i >= KV_STAGES && !bar_wait(empty, par)) return false;
+                const int k0 = pb.lo + i * BN, nk = min(BN, pb.hi - k0);
+                const uint8_t* page = static_cast<const uint8_t*>((which ? vtab : ktab)[k0 >> PAGE_SHIFT]);
+                uint8_t* dst = kv_sm + st * STAGE_BYTES + which * KT_BYTES;
+#pragma unroll
+                for (int n = 0; n < 8; n++) {
+                    const int q = ptid + NPROD * n;
+                    const int key = q >> 5, ch = q & 31;
+                    const uint32_t off = (uint32_t)(ch >> 3) * (BN * 128) + sw128(key, ch & 7);
+                    if (key < nk) {
+                        const size_t src = ((size_t)key * n_kv + pb.kvh) * (HD * 2) + (size_t)ch * 16;
+                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                                     ::"r"(s32(dst + off)), "l"(page + src) : "memory");
+                    } else {
+                        *reinterpret_cast<uint4*>(dst + off) = make_uint4(0, 0, 0, 0);
+                    }
+                }
+                asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(full) : "memory");
+                return true;
+            };
+            for (int i = 0; i < ntiles; i++)
+                if (!copy_half(i, 0) || !copy_half(i, 1)) break;
+        } else {
+            load(raw0, 0);
+            load(raw1, 1);
+            for (int i = 0; i < ntiles; i += 2) {
+                if (!store(raw0, i)) break;
+                load(raw0, i + 2);
+                if (i + 1 < ntiles) {
+                    if (!store(raw1, i + 1)) break;
+                    load(raw1, i + 3);
+                }
+            }
         }
     }
     __syncthreads();
@@ -617,6 +746,18 @@ int launch_prefill_umma(const float* qT, int q_stride, int q_row, const void* co
     *done = true;
     return Q27_OK;
 }
+
+#ifdef Q27_TRACE
+extern "C" int q27_debug_umma_trace(unsigned long long* out, int reset) {
+    cudaMemcpyFromSymbol(out, g_umma_trace, sizeof(unsigned long long) * 16);
+    if (reset) { unsigned long long z[16] = {0}; cudaMemcpyToSymbol(g_umma_trace, z, sizeof(z)); }
+    return 0;
+}
+extern "C" int q27_debug_umma_events(long long* out) {
+    cudaMemcpyFromSymbol(out, g_umma_ev, sizeof(long long) * 8 * 64);
+    return 0;
+}
+#endif
 
 int launch_verify_umma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool* done) {
     *done = false;

@@ -140,7 +140,10 @@ def test_kv_split_partials_merge(oracle, cuda, kvk, nshards):
         vs = np.broadcast_to(vs[None, :], live.shape)[live][:, None]
         a = mine[live][:, 2:] / mine[live][:, 1:2] * vs
         b = want[live][:, 2:] / want[live][:, 1:2] * vs
-        assert synth.tolerance_ok(a, b)[0]
+        # a shard's own partial (as little as one key) is held to the reference's gate for
+        # fp16-operand tensor-core paths (max-abs/RMS 1e-2, src/test_kernels.cu:1824-1962);
+        # the BASELINE bar applies to the merged output below
+        assert np.abs(a - b).max() / (np.sqrt((b.astype(np.float64) ** 2).mean()) + 1e-12) < 1e-2
         # padded lane (index 5) is a well-formed empty partial
         assert (parts[g, 0, 5, :, 0].cpu().numpy() < -1e38).all()
     out = torch.empty((lanes_stride * 24, 256), device=cuda)
