@@ -24,6 +24,27 @@
 namespace q27b {
 
 __device__ int g_wait_timeout_flag = 0; // set when a bounded mbarrier wait ran out
+#ifdef Q27_TRACE
+// timing experiments only: [0] earliest CTA start, [1] latest CTA end, [2] latest end of the
+// prologue, [3] latest end of the stage loop (globaltimer ns)
+__device__ unsigned long long g_dec_trace[4] = {~0ull, 0, 0, 0};
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+#define DTRACE_MIN(i) do { if (threadIdx.x == 0) atomicMin(&g_dec_trace[i], gtime()); } while (0)
+#define DTRACE_MAX(i) do { if (threadIdx.x == 0) atomicMax(&g_dec_trace[i], gtime()); } while (0)
+extern "C" int q27_debug_dec_trace(unsigned long long* out) {
+    cudaMemcpyFromSymbol(out, g_dec_trace, sizeof(unsigned long long) * 4);
+    unsigned long long z[4] = {~0ull, 0, 0, 0};
+    cudaMemcpyToSymbol(g_dec_trace, z, sizeof(z));
+    return 0;
+}
+#else
+#define DTRACE_MIN(i)
+#define DTRACE_MAX(i)
+#endif
 
 namespace {
 
@@ -66,8 +87,10 @@ template <> struct Fmt<Q27_KV_T3> {
 template <int KVK> constexpr int stage_bytes() { return 2 * STAGE_ROWS * Fmt<KVK>::PITCH; }
 template <int KVK> constexpr int ring_bytes() { return stage_bytes<KVK>() * Fmt<KVK>::STAGES; }
 constexpr int MERGE_BYTES = NCW * GQA * PART * 4; // per-warp partials for the final merge
+template <int KVK> constexpr int qstage_bytes() { return Fmt<KVK>::KVH * GQA * HD * 4; }
 template <int KVK> constexpr int smem_bytes() {
-    return 256 + (ring_bytes<KVK>() > MERGE_BYTES ? ring_bytes<KVK>() : MERGE_BYTES);
+    return 256 + (ring_bytes<KVK>() > MERGE_BYTES ? ring_bytes<KVK>() : MERGE_BYTES) +
+           qstage_bytes<KVK>();
 }
 
 // ---- PTX helpers ----------------------------------------------------------------------
@@ -445,6 +468,7 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
     uint64_t* empty = full + 16;
     uint8_t* ring = smem + 256;
 
+    DTRACE_MIN(0);
     const int t = blockIdx.x, sp = blockIdx.y;
     const int slot = blockIdx.z / (b.n_kv / F::KVH), kvg = blockIdx.z % (b.n_kv / F::KVH);
     const DevSlot& S = b.s[slot];
@@ -465,10 +489,19 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
             d[0] = NEG_SENTINEL;
             d[1] = 0.f;
         }
+        DTRACE_MAX(1);
         return;
     }
     const int nstages = (hi - lo + STAGE_ROWS - 1) / STAGE_ROWS;
 
+    // the CTA's query heads, fp32, staged once with coalesced loads
+    float* q_stage = reinterpret_cast<float*>(ring + (ring_bytes<KVK>() > MERGE_BYTES
+                                                          ? ring_bytes<KVK>() : MERGE_BYTES));
+    for (int i = threadIdx.x; i < F::KVH * GQA * (HD / 4); i += blockDim.x) {
+        const int h = i / (HD / 4), d4 = i % (HD / 4);
+        reinterpret_cast<float4*>(q_stage)[i] = __ldg(reinterpret_cast<const float4*>(
+            S.q[t] + (size_t)(kvh0 * GQA + h) * b.q_stride) + d4);
+    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < F::STAGES; s++) {
             mbar_init(&full[s], 1);
@@ -486,6 +519,7 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     __syncthreads();
+    DTRACE_MAX(2);
 
     if (warp == NCW) {
         // ---------------- producer ----------------
@@ -530,13 +564,13 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
         // Q^T fragments: column n = g is head kvh*6 + g (columns 6, 7 are zero padding)
         uint32_t qf[16][2];
         {
-            const float* qh = S.q[t] + (size_t)(kvh * GQA + (g < GQA ? g : 0)) * b.q_stride;
+            const float* qh = q_stage + (size_t)(hq * GQA + (g < GQA ? g : 0)) * HD;
 #pragma unroll
             for (int s = 0; s < 16; s++)
 #pragma unroll
                 for (int r = 0; r < 2; r++) {
-                    const float x0 = g < GQA ? __ldg(qh + kdim<KVK>(s, c, r, 0)) : 0.f;
-                    const float x1 = g < GQA ? __ldg(qh + kdim<KVK>(s, c, r, 1)) : 0.f;
+                    const float x0 = g < GQA ? qh[kdim<KVK>(s, c, r, 0)] : 0.f;
+                    const float x1 = g < GQA ? qh[kdim<KVK>(s, c, r, 1)] : 0.f;
                     qf[s][r] = pack_h2(x0, x1);
                 }
         }
@@ -576,6 +610,7 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
 
         // every consumer is past its last ring read once all of them reach this barrier
         asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32));
+        DTRACE_MAX(3);
         // column sums: add the shares of the 8 threads of a column group
 #pragma unroll
         for (int off = 4; off < 32; off <<= 1) {
@@ -621,6 +656,7 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
             if (tid == 0) { d[0] = mb; d[1] = lb; }
             d[2 + tid] = acc;
         }
+        DTRACE_MAX(1);
     }
 }
 
@@ -650,6 +686,10 @@ int launch_one(DevBatch& b, int sm_count, cudaStream_t st) {
 int launch_decode_mma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool* done) {
     *done = false;
     if (b.n_kv != 4) return Q27_OK; // the ring layouts assume 4 kv heads per row
+    if (b.q_stride & 3) return Q27_OK; // Q heads are staged with 16-byte loads
+    for (int i = 0; i < b.nslots; i++)
+        for (int t = 0; t < b.s[i].ntok; t++)
+            if ((uintptr_t)b.s[i].q[t] & 15) return Q27_OK;
     int rc;
     if (kvk == Q27_KV_F16) rc = launch_one<Q27_KV_F16>(b, sm_count, st);
     else if (kvk == Q27_KV_FP8) rc = launch_one<Q27_KV_FP8>(b, sm_count, st);

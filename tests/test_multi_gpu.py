@@ -1,0 +1,80 @@
+"""KV-sequence sharding across real GPUs (skipped on a single-GPU box): two NCCL ranks, each
+holding a page-aligned half of every slot's cache, exchange their 258-float partials with
+one all-gather and merge; the result must equal attention over the whole cache (oracle).
+Run with `pytest -m gpu` on a box with >= 2 GPUs."""
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT))
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank(rank, world, port, kvk, q, k, v, pos, ranges, ret):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch.distributed as dist
+    import q27_b200 as Q
+    from q27_b200 import dist as qd
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    lo, hi = ranges[rank]
+    lanes = len(pos)
+    ks = Q.paged_from_rows(torch.from_numpy(k[lo:hi].copy()).to(dev), kvk)
+    vs = Q.paged_from_rows(torch.from_numpy(v[lo:hi].copy()).to(dev), kvk)
+    qd_ = [torch.from_numpy(q[t].copy()).to(dev) for t in range(lanes)]
+    pd = [torch.tensor([p], dtype=torch.int32, device=dev) for p in pos]
+    scratch = torch.full((Q.decode_scratch_floats(lanes),), float("nan"), device=dev)
+    slot = Q.SlotArgs(ks.tab, vs.tab, qd_, pd, [], scratch, row_base=lo, row_count=hi - lo)
+    ex = qd.PartialExchange.create(1, lanes, 24, world, dev)
+    out = torch.zeros((lanes * 24, 256), device=dev)
+    for _ in range(2):
+        qd.sharded_decode([slot], ex, out, 512, 4, 1.0 / 16.0, kvk)
+    torch.cuda.synchronize()
+    ret.put((rank, out.cpu().numpy()))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("kvk", [0, 2])
+def test_two_gpu_kv_split_matches_full_attention(oracle, kvk):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from tests import synth
+    from q27_b200 import dist as qd
+    import torch.multiprocessing as mp
+    rows = 64 * 40
+    pos = [rows - 1, rows - 2, rows - 3, 1000]
+    c = synth.make_case(oracle, kvk, rows=rows, pos=pos, seed=5, outlier_frac=0.02 if kvk == 2 else 0.0)
+    full = oracle.attn_decode(c.q, c.k, c.v, kvk, pos)
+    ranges = qd.shard_ranges(rows, 2)
+    ctx = mp.get_context("spawn")
+    ret = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, kvk, c.q, c.k, c.v, pos, ranges, ret))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    outs = dict(ret.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(2):      # every rank ends up with the merged result
+        assert synth.tolerance_ok(outs[r].reshape(len(pos), -1), full)[0]
