@@ -39,15 +39,18 @@ namespace {
 constexpr int BM = 128;                 // Q rows per CTA (TMEM lanes)
 constexpr int BN = 64;                  // keys per tile = one cache page
 constexpr int TOK_PER_TILE = 21;        // 21 tokens x 6 heads = 126 rows
-constexpr int KV_STAGES = 2;
+constexpr int KV_STAGES = 3;
 constexpr int Q_BYTES = BM * HD * 2;            // 65536: 4 blocks of [128 rows][128 B]
 constexpr int KT_BYTES = BN * HD * 2;           // 32768: 4 blocks of [64 rows][128 B]
 constexpr int P_BYTES = BM * BN * 2;            // 16384: 1 block of [128 rows][128 B]
 constexpr int STAGE_BYTES = 2 * KT_BYTES;       // K then V
 constexpr int SMEM_BAR = 1024;                  // barriers + tmem slot, keeps tiles 1024-aligned
-constexpr int UMMA_SMEM = SMEM_BAR + Q_BYTES + P_BYTES + KV_STAGES * STAGE_BYTES + 1024;
+constexpr int UMMA_SMEM = SMEM_BAR + P_BYTES + KV_STAGES * STAGE_BYTES + 1024;
 constexpr int TMEM_COLS = 512;
-constexpr int COL_S0 = 0, COL_S1 = 64, COL_O = 128;
+// TMEM columns: two S buffers, O, and the Q tile itself (fp16 pairs, 8 columns per k-step):
+// Q is the A operand of every S MMA, so keeping it in tensor memory takes its re-reads off
+// the shared-memory port and leaves room for a third K/V stage
+constexpr int COL_S0 = 0, COL_S1 = 64, COL_O = 128, COL_Q = 384;
 constexpr float LOG2E_F = 1.4426950408889634f;
 constexpr float RESCALE_THRESHOLD = 8.0f;       // log2 units
 
@@ -93,6 +96,14 @@ __device__ __forceinline__ void tc_fence_after() {
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                  ::"r"(bar) : "memory");
+}
+// A operand taken from tensor memory (row = lane, 16 fp16 of K per 8 columns)
+__device__ __forceinline__ void tc_mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
 }
 __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                            uint32_t idesc, uint32_t accumulate) {
@@ -337,23 +348,24 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(base);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + 512);
-    uint8_t* q_sm = base + SMEM_BAR;
-    uint8_t* p_sm = q_sm + Q_BYTES;
+    uint8_t* p_sm = base + SMEM_BAR;
     uint8_t* kv_sm = p_sm + P_BYTES;
     // K and V slots are released separately: a K slot as soon as its S MMAs have run, a V
     // slot after its PV MMAs, so the next K tile lands while the current tile is in softmax
-    const uint32_t k_full = s32(&bars[0]), k_empty = s32(&bars[2]), v_full = s32(&bars[4]),
-                   v_empty = s32(&bars[6]), s_full = s32(&bars[8]), s_free = s32(&bars[10]),
-                   p_full = s32(&bars[12]), pv_done = s32(&bars[13]);
+    const uint32_t k_full = s32(&bars[0]), k_empty = s32(&bars[4]), v_full = s32(&bars[8]),
+                   v_empty = s32(&bars[12]), s_full = s32(&bars[16]), s_free = s32(&bars[18]),
+                   p_full = s32(&bars[20]), pv_done = s32(&bars[21]);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = (pb.hi - pb.lo + BN - 1) / BN;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < 2; s++) {
+        for (int s = 0; s < KV_STAGES; s++) {
             bar_init(k_full + 8 * s, N_LOAD_WARPS * 32);
             bar_init(k_empty + 8 * s, 1);
             bar_init(v_full + 8 * s, N_LOAD_WARPS * 32);
             bar_init(v_empty + 8 * s, 1);
+        }
+        for (int s = 0; s < 2; s++) {
             bar_init(s_full + 8 * s, 1);
             bar_init(s_free + 8 * s, N_SOFTMAX_WARPS * 32);
         }
@@ -366,25 +378,32 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                      ::"r"(s32(tmem_slot)), "n"(TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    // Q tile: fp32 -> fp16, K-major, 4 blocks of [128 rows][64 dims], 128-byte swizzle
-    for (int idx = threadIdx.x; idx < BM * 32; idx += blockDim.x) {
-        const int r = idx >> 5, ch = idx & 31;
-        const RowInfo ri = pb.row(r);
-        uint4 packed = make_uint4(0, 0, 0, 0);
-        if (ri.q) {
-            const float4 a = __ldg(reinterpret_cast<const float4*>(ri.q + 8 * ch));
-            const float4 b = __ldg(reinterpret_cast<const float4*>(ri.q + 8 * ch) + 1);
-            __half2 h[4] = {__floats2half2_rn(a.x, a.y), __floats2half2_rn(a.z, a.w),
-                            __floats2half2_rn(b.x, b.y), __floats2half2_rn(b.z, b.w)};
-            packed = *reinterpret_cast<uint4*>(h);
-        }
-        *reinterpret_cast<uint4*>(q_sm + (ch >> 3) * (BM * 128) + sw128(r, ch & 7)) = packed;
-    }
-    fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (warp < N_SOFTMAX_WARPS) {
+        // Q tile: fp32 -> fp16 pairs, row r into TMEM lane r, dims 2c, 2c+1 into column COL_Q + c
+        const RowInfo rq = pb.row(threadIdx.x);
+        const uint32_t qaddr = tmem + ((uint32_t)(warp * 32) << 16) + COL_Q;
+#pragma unroll 1
+        for (int c = 0; c < HD / 2; c += 32) {
+            float packed[32];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+                float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (rq.q) a = __ldg(reinterpret_cast<const float4*>(rq.q + 2 * (c + e)));
+                __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+                packed[e] = __uint_as_float(*reinterpret_cast<uint32_t*>(&h0));
+                packed[e + 1] = __uint_as_float(*reinterpret_cast<uint32_t*>(&h1));
+            }
+            tc_st32(qaddr + c, packed);
+        }
+        tc_wait_st();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
 
     if (warp < N_SOFTMAX_WARPS) {
         // ------------------------------ softmax: thread = row ------------------------------
@@ -512,7 +531,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         // ------------------------------ S issue: one thread --------------------------------
         if (lane == 0) {
             constexpr uint32_t IDESC_S = make_idesc(BM, BN, false);
-            const uint32_t q_s = s32(q_sm), kv_s = s32(kv_sm);
+            const uint32_t kv_s = s32(kv_sm);
             bool ok = true;
             auto issue_s = [&](int i) {
                 const int st = i % KV_STAGES, bsel = i & 1;
@@ -530,9 +549,9 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 TRACE_T0();
 #pragma unroll
                 for (int ks = 0; ks < HD / 16; ks++) {
-                    const uint64_t da = make_desc(q_s + (ks >> 2) * (BM * 128) + (ks & 3) * 32, 0, 1024);
                     const uint64_t db = make_desc(k_s + (ks >> 2) * (BN * 128) + (ks & 3) * 32, 0, 1024);
-                    tc_mma_f16(tmem + (bsel ? COL_S1 : COL_S0), da, db, IDESC_S, ks > 0);
+                    tc_mma_f16_ta(tmem + (bsel ? COL_S1 : COL_S0), tmem + COL_Q + 8 * ks, db, IDESC_S,
+                                  ks > 0);
                 }
                 tc_commit(s_full + 8 * bsel);
                 tc_commit(k_empty + 8 * st);

@@ -196,3 +196,47 @@ def test_kvpool_on_device(cuda):
     again = []
     assert pool.reserve(0, 1, again) and again == [2]                   # LIFO
     pool.close()
+
+
+@pytest.mark.parametrize("kvk", KINDS)
+def test_sixteen_lanes_ragged_positions(oracle, cuda, kvk):
+    # the widest verify the lane bundles allow (p[16], src/kernels.cuh:67-68), lanes of very
+    # different lengths, one of them a single key
+    rows = 5000
+    pos = [rows - 1 - 3 * t for t in range(12)] + [2500, 64, 63, 0]
+    c = synth.make_case(oracle, kvk, rows=rows, pos=pos, seed=61, outlier_frac=OUTLIERS[kvk])
+    ref = synth.scale_out(c, oracle.attn_decode(c.q, c.k, c.v, kvk, c.pos))
+    dc = DeviceCase(c, cuda, scatter_seed=9)
+    for exact in (True, False):
+        got = synth.scale_out(c, dc.run3(exact=exact))
+        ok, excess, rel = synth.tolerance_ok(got, ref)
+        assert ok, (exact, excess, rel)
+
+
+def test_other_head_counts_run_the_fp32_family(oracle, cuda):
+    # geometry other than 24/4 but still 6 query heads per kv head: accepted, served by the
+    # fp32 kernels (the tensor-core ring layouts are specialised for 4 kv heads)
+    import ctypes as C
+    from q27_b200 import _lib as L
+    n_kv, n_q, rows = 2, 12, 300
+    rng = np.random.default_rng(3)
+    kf = oracle.randn(rows * n_kv * 256, 7).reshape(rows, n_kv, 256)
+    vf = oracle.randn(rows * n_kv * 256, 8).reshape(rows, n_kv, 256)
+    k = oracle.to_half_bits(kf).view(np.uint8).reshape(rows, -1)
+    v = oracle.to_half_bits(vf).view(np.uint8).reshape(rows, -1)
+    q = oracle.randn(n_q * 512, 9).reshape(1, n_q, 512)
+    ref = oracle.attn_decode(q, k, v, KV_F16, [rows - 1], n_q=n_q, n_kv=n_kv)
+    ks = Q.paged_from_rows(torch.from_numpy(k).to(cuda), KV_F16, n_kv_heads=n_kv)
+    vs = Q.paged_from_rows(torch.from_numpy(v).to(cuda), KV_F16, n_kv_heads=n_kv)
+    qd = torch.from_numpy(q[0].copy()).to(cuda)
+    out = torch.zeros(n_q * 256, device=cuda)
+    scratch = torch.empty(Q.decode_scratch_floats(1, n_q), device=cuda)
+    pos = torch.tensor([rows - 1], dtype=torch.int32, device=cuda)
+    Q.attn_decode(qd, 512, ks.tab, vs.tab, out, scratch, pos, 0, n_q, n_kv, 256, SCALE, kvk=KV_F16)
+    torch.cuda.synchronize()
+    assert synth.tolerance_ok(out.cpu().numpy()[None], ref)[0]
+    # 5 query heads per kv head is not this model family: refused as a width
+    rc = L.lib().q27_attn_decode(qd.data_ptr(), 512, ks.tab.data_ptr(), vs.tab.data_ptr(),
+                                 out.data_ptr(), scratch.data_ptr(), pos.data_ptr(), 0, 10, 2, 256,
+                                 SCALE, None, KV_F16)
+    assert rc == L.ERR_UNSUPPORTED_WIDTH
