@@ -45,7 +45,7 @@ constexpr int KT_BYTES = BN * HD * 2;           // 32768: 4 blocks of [64 rows][
 constexpr int P_BYTES = BM * BN * 2;            // 16384: 1 block of [128 rows][128 B]
 constexpr int STAGE_BYTES = 2 * KT_BYTES;       // K then V
 constexpr int SMEM_BAR = 1024;                  // barriers + tmem slot, keeps tiles 1024-aligned
-constexpr int UMMA_SMEM = SMEM_BAR + P_BYTES + KV_STAGES * STAGE_BYTES + 1024;
+constexpr int UMMA_SMEM = SMEM_BAR + KV_STAGES * STAGE_BYTES + 1024;
 constexpr int TMEM_COLS = 512;
 // TMEM columns: two S buffers, O, and the Q tile itself (fp16 pairs, 8 columns per k-step):
 // Q is the A operand of every S MMA, so keeping it in tensor memory takes its re-reads off
@@ -348,13 +348,14 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(base);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + 512);
-    uint8_t* p_sm = base + SMEM_BAR;
-    uint8_t* kv_sm = p_sm + P_BYTES;
+    uint8_t* kv_sm = base + SMEM_BAR;
     // K and V slots are released separately: a K slot as soon as its S MMAs have run, a V
     // slot after its PV MMAs, so the next K tile lands while the current tile is in softmax
     const uint32_t k_full = s32(&bars[0]), k_empty = s32(&bars[4]), v_full = s32(&bars[8]),
-                   v_empty = s32(&bars[12]), s_full = s32(&bars[16]), s_free = s32(&bars[18]),
-                   p_full = s32(&bars[20]), pv_done = s32(&bars[21]);
+                   v_empty = s32(&bars[12]), s_full = s32(&bars[16]), pvb = s32(&bars[18]),
+                   p_full = s32(&bars[20]);
+    // pvb[b] completes when the PV MMAs of a tile that used S/P buffer b have run: it frees the
+    // buffer for S(i+2) and tells the softmax warps that O may be touched
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = (pb.hi - pb.lo + BN - 1) / BN;
 
@@ -367,10 +368,9 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         }
         for (int s = 0; s < 2; s++) {
             bar_init(s_full + 8 * s, 1);
-            bar_init(s_free + 8 * s, N_SOFTMAX_WARPS * 32);
+            bar_init(pvb + 8 * s, 1);
         }
         bar_init(p_full, N_SOFTMAX_WARPS * 32);
-        bar_init(pv_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == MMA_WARP) {
@@ -428,8 +428,6 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             tc_ld32(lane_base + (bsel ? COL_S1 : COL_S0), s);
             tc_ld32(lane_base + (bsel ? COL_S1 : COL_S0) + 32, s + 32);
             tc_wait_ld();
-            tc_fence_before();
-            bar_arrive(s_free + 8 * bsel);
             const int k0 = pb.lo + i * BN;
             const int vis = ri.bound - k0;            // columns [0, vis) are visible
             float mx = -INFINITY;
@@ -465,14 +463,13 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             }
             l = l * alpha + sum;
             if (threadIdx.x == 0) TRACE_EV(5, i);
-            if (i > 0) {
+            if (__any_sync(0xffffffffu, need)) {       // warp-collective TMEM round trip on O
                 { TRACE_T0();
-                  ok = __all_sync(0xffffffffu, bar_wait(pv_done, (uint32_t)((i - 1) & 1)));
+                  ok = __all_sync(0xffffffffu,
+                                  bar_wait(pvb + 8 * ((i - 1) & 1), (uint32_t)(((i - 1) >> 1) & 1)));
                   TRACE_ADD(1, threadIdx.x == 0); }
                 if (!ok) break;
                 tc_fence_after();
-            }
-            if (__any_sync(0xffffffffu, need)) {       // warp-collective TMEM round trip
 #pragma unroll 1
                 for (int c = 0; c < HD; c += 32) {
                     float o[32];
@@ -482,18 +479,16 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                     for (int e = 0; e < 32; e++) o[e] *= alpha;
                     tc_st32(lane_base + COL_O + c, o);
                 }
-                tc_wait_st();
             }
-#pragma unroll
-            for (int c = 0; c < 8; c++)
-                *reinterpret_cast<uint4*>(p_sm + sw128(r, c)) =
-                    make_uint4(ph[4 * c], ph[4 * c + 1], ph[4 * c + 2], ph[4 * c + 3]);
-            fence_async_smem();
+            // P (fp16 pairs) over the first 32 columns of this tile's S buffer: the A operand
+            // of the PV MMAs, straight from tensor memory
+            tc_st32(lane_base + (bsel ? COL_S1 : COL_S0), reinterpret_cast<const float*>(ph));
+            tc_wait_st();
             tc_fence_before();
             bar_arrive(p_full);
             if (threadIdx.x == 0) TRACE_EV(6, i);
         }
-        if (ok) ok = bar_wait(pv_done, (uint32_t)((ntiles - 1) & 1));
+        if (ok) ok = bar_wait(pvb + 8 * ((ntiles - 1) & 1), (uint32_t)(((ntiles - 1) >> 1) & 1));
         ok = __all_sync(0xffffffffu, ok);
 #ifdef Q27_TRACE
         if (threadIdx.x == 0) {
@@ -539,7 +534,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                   ok = ok && bar_wait(k_full + 8 * st, (uint32_t)((i / KV_STAGES) & 1));
                   TRACE_ADD(2, true); }
                 { TRACE_T0();
-                  if (ok && i >= 2) ok = bar_wait(s_free + 8 * bsel, (uint32_t)(((i >> 1) - 1) & 1));
+                  if (ok && i >= 2) ok = bar_wait(pvb + 8 * bsel, (uint32_t)(((i >> 1) - 1) & 1));
                   TRACE_ADD(3, true); }
                 if (!ok) return;
                 fence_async_smem();
@@ -565,7 +560,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         // ------------------------------ PV issue: one thread -------------------------------
         if (lane == 0) {
             constexpr uint32_t IDESC_O = make_idesc(BM, HD, true);
-            const uint32_t p_s = s32(p_sm), kv_s = s32(kv_sm);
+            const uint32_t kv_s = s32(kv_sm);
             bool ok = true;
             for (int i = 0; i < ntiles && ok; i++) {
                 { TRACE_T0();
@@ -582,11 +577,11 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 TRACE_T0();
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; kk++) {
-                    const uint64_t da = make_desc(p_s + kk * 32, 0, 1024);
                     const uint64_t db = make_desc(v_s + kk * 2048, BN * 128, 1024);
-                    tc_mma_f16(tmem + COL_O, da, db, IDESC_O, (i > 0 || kk > 0));
+                    tc_mma_f16_ta(tmem + COL_O, tmem + ((i & 1) ? COL_S1 : COL_S0) + 8 * kk, db, IDESC_O,
+                                  (i > 0 || kk > 0));
                 }
-                tc_commit(pv_done);
+                tc_commit(pvb + 8 * (i & 1));
                 tc_commit(v_empty + 8 * st);
                 TRACE_EV(3, i);
                 TRACE_ADD(10, true);
