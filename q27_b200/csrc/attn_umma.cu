@@ -5,15 +5,20 @@
 // x 6 heads for verify -- so every K/V tile that is staged serves all six heads (and, for
 // verify, all draft lanes: one pass over the cache). Each row carries its own causal bound.
 //
-//   S  = Q . K^T   M=128 rows, N=64 keys, K=256 dims     -> TMEM (two S buffers)
+//   S  = Q . K^T   M=128 rows, N=64 keys, K=256 dims     -> TMEM (a ring of four S buffers)
 //   O += P . V     M=128 rows, N=256 dims, K=64 keys      -> TMEM (256 columns)
 //
-// Operands are fp16 in shared memory in the 128-byte-swizzled canonical layouts (Q and K
-// K-major, V MN-major = its natural [key][dim] rows, P K-major), accumulation is fp32.
+// Q, K and V are fp16 in shared memory in the 128-byte-swizzled canonical layouts (Q and K
+// K-major, V MN-major = its natural [key][dim] rows); P is written as fp16 over the S buffer
+// it came from and is the A operand of the PV MMAs straight from tensor memory; accumulation
+// is fp32. The S ring is four deep because the chain S -> softmax -> PV -> (buffer free) is
+// several thousand cycles of mbarrier hops and MMA latency long: four tiles in flight keep
+// the tensor pipe and the softmax warps busy through it.
 // Warp roles: warps 0-3 softmax (thread = row = TMEM lane); warp 4 issues the S MMAs and warp 5
-// the PV MMAs (two independent issue streams, ordered only by mbarriers); warps 6-13 stage
-// K/V tiles (cp.async for fp16 rows, registers + convert for fp8 / turbo3). The running
-// max is only advanced when it grows by more than 2^8, so O in TMEM is rarely rescaled.
+// the PV MMAs (two independent issue streams, ordered only by mbarriers); warps 6-9 stage
+// K tiles (ring of three) and warps 10-13 V tiles (ring of two): cp.async for fp16 rows,
+// registers + convert for fp8 / turbo3. The running max is only advanced when it grows by
+// more than 2^8, so O in TMEM is rarely rescaled.
 // Every mbarrier wait is bounded; a timeout sets the library's flag and the CTA drains.
 #include "attn_umma.cuh"
 #include "t3_lut.cuh"
@@ -26,12 +31,14 @@ extern __device__ int g_wait_timeout_flag;
 __device__ unsigned long long g_umma_trace[16];
 __device__ long long g_umma_ev[8][64];   // per-event timestamps of CTA (0,0,0), first 64 tiles
 #define TRACE_EV(e, i) do { if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (i) < 64) g_umma_ev[e][i] = clock64(); } while (0)
+#define TRACE_EVMAX(e, i) do { if ((threadIdx.x & 31) == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (i) < 64) atomicMax(&g_umma_ev[e][i], clock64()); } while (0)
 #define TRACE_T0() const long long t0__ = clock64()
 #define TRACE_ADD(slot, cond) do { if (cond) atomicAdd(&g_umma_trace[slot], (unsigned long long)(clock64() - t0__)); } while (0)
 #else
 #define TRACE_T0()
 #define TRACE_ADD(slot, cond)
 #define TRACE_EV(e, i)
+#define TRACE_EVMAX(e, i)
 #endif
 
 namespace {
@@ -39,24 +46,21 @@ namespace {
 constexpr int BM = 128;                 // Q rows per CTA (TMEM lanes)
 constexpr int BN = 64;                  // keys per tile = one cache page
 constexpr int TOK_PER_TILE = 21;        // 21 tokens x 6 heads = 126 rows
-constexpr int KV_STAGES = 3;
+constexpr int K_SLOTS = 3, V_SLOTS = 2;         // separate rings: K runs ahead with the S MMAs
+constexpr int S_BUFS = 4;                       // S / P buffers in tensor memory
 constexpr int Q_BYTES = BM * HD * 2;            // 65536: 4 blocks of [128 rows][128 B]
 constexpr int KT_BYTES = BN * HD * 2;           // 32768: 4 blocks of [64 rows][128 B]
-constexpr int P_BYTES = BM * BN * 2;            // 16384: 1 block of [128 rows][128 B]
-constexpr int STAGE_BYTES = 2 * KT_BYTES;       // K then V
 constexpr int SMEM_BAR = 1024;                  // barriers + tmem slot, keeps tiles 1024-aligned
-constexpr int UMMA_SMEM = SMEM_BAR + KV_STAGES * STAGE_BYTES + 1024;
+constexpr int UMMA_SMEM = SMEM_BAR + Q_BYTES + (K_SLOTS + V_SLOTS) * KT_BYTES + 1024;
 constexpr int TMEM_COLS = 512;
-// TMEM columns: two S buffers, O, and the Q tile itself (fp16 pairs, 8 columns per k-step):
-// Q is the A operand of every S MMA, so keeping it in tensor memory takes its re-reads off
-// the shared-memory port and leaves room for a third K/V stage
-constexpr int COL_S0 = 0, COL_S1 = 64, COL_O = 128, COL_Q = 384;
+// TMEM columns: S buffer b at 64 b (its first 32 columns are reused for P), O behind them
+constexpr int COL_S = 0, COL_O = S_BUFS * BN;
 constexpr float LOG2E_F = 1.4426950408889634f;
 constexpr float RESCALE_THRESHOLD = 8.0f;       // log2 units
 
 constexpr int N_SOFTMAX_WARPS = 4, MMA_WARP = 4, PV_WARP = 5, FIRST_LOAD_WARP = 6, N_LOAD_WARPS = 8;
 constexpr int UMMA_THREADS = (FIRST_LOAD_WARP + N_LOAD_WARPS) * 32;   // 448
-constexpr int NPROD = N_LOAD_WARPS * 32;                              // 256 staging threads
+constexpr int NPROD = N_LOAD_WARPS * 16;        // 128 staging threads per side (K or V)
 
 // ---- small PTX wrappers -------------------------------------------------------------------
 __device__ __forceinline__ uint32_t s32(const void* p) {
@@ -141,6 +145,11 @@ __device__ __forceinline__ void tc_st32(uint32_t taddr, const float* v) {
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float y;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+    return y;
+}
 __device__ __forceinline__ float ex2f(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -219,88 +228,61 @@ struct Problem {
     }
 };
 
-// Staging of one 64-key tile of K and V as fp16 into the swizzled operand layouts, in two
-// halves: `load` pulls the raw bytes of the tile into registers (issued before the ring slot
-// is free, so the global latency hides behind the tiles in flight), `store` converts and
-// writes them once the slot has been released.
-template <int KVK> struct RawTile;
-template <> struct RawTile<Q27_KV_F16> { uint4 k[8], v[8]; };
-template <> struct RawTile<Q27_KV_FP8> { uint2 k[8], v[8]; };
-template <> struct RawTile<Q27_KV_T3> { uint32_t w[14]; };
+// Staging of one 64-key tile of ONE side (K or V) as fp16 into the swizzled operand layout
+// by that side's 128 threads: `half_load` pulls the raw bytes into registers (issued before
+// the ring slot is free, so the global latency hides behind the tiles in flight),
+// `half_store` converts and writes them once the slot has been released. fp16 rows need
+// neither: they go from global to shared memory with cp.async.
+template <int KVK> struct RawHalf;
+template <> struct RawHalf<Q27_KV_F16> { };
+template <> struct RawHalf<Q27_KV_FP8> { uint2 d[16]; };
+template <> struct RawHalf<Q27_KV_T3> { uint32_t w[14]; };
 
 template <int KVK>
-__device__ __forceinline__ void tile_load(RawTile<KVK>& t, const uint8_t* kpage, const uint8_t* vpage,
-                                          int nkeys, int n_kv, int kvh, int ptid) {
+__device__ __forceinline__ void half_load(RawHalf<KVK>& t, const uint8_t* page, int nkeys, int n_kv,
+                                          int kvh, int p) {
     if constexpr (KVK == Q27_KV_T3) {
-        // one thread = one 50-byte block: (key, side, block). Block 1 starts 2 bytes past a
-        // word boundary, so 14 words from the aligned address below it cover either block.
-        const int key = ptid & 63, side = (ptid >> 6) & 1, blk = ptid >> 7;
+        // one thread = one 50-byte block: (key, block). Block 1 starts 2 bytes past a word
+        // boundary, so 14 words from the aligned address below it cover either block.
+        const int key = p & 63, blk = p >> 6;
 #pragma unroll
         for (int i = 0; i < 14; i++) t.w[i] = 0;
         if (key < nkeys) {
             const uint32_t* src = reinterpret_cast<const uint32_t*>(
-                (side ? vpage : kpage) + ((size_t)key * n_kv + kvh) * (2 * T3_BLK)) + 12 * blk;
+                page + ((size_t)key * n_kv + kvh) * (2 * T3_BLK)) + 12 * blk;
 #pragma unroll
             for (int i = 0; i < 13; i++) t.w[i] = __ldg(src + i);
         }
-    } else {
-        constexpr int CB = KVK == Q27_KV_F16 ? 16 : 8;      // bytes per 8-dim chunk
+    } else if constexpr (KVK == Q27_KV_FP8) {
 #pragma unroll
-        for (int n = 0; n < 8; n++) {
-            const int q = ptid + NPROD * n;
+        for (int n = 0; n < 16; n++) {
+            const int q = p + NPROD * n;
             const int key = q >> 5, ch = q & 31;
-            const size_t src = ((size_t)key * n_kv + kvh) * (HD * CB / 8) + (size_t)ch * CB;
-            if constexpr (KVK == Q27_KV_F16) {
-                t.k[n] = t.v[n] = make_uint4(0, 0, 0, 0);   // rows past the range: exact zeros
-                if (key < nkeys) {
-                    t.k[n] = __ldg(reinterpret_cast<const uint4*>(kpage + src));
-                    t.v[n] = __ldg(reinterpret_cast<const uint4*>(vpage + src));
-                }
-            } else {
-                t.k[n] = t.v[n] = make_uint2(0, 0);
-                if (key < nkeys) {
-                    t.k[n] = __ldg(reinterpret_cast<const uint2*>(kpage + src));
-                    t.v[n] = __ldg(reinterpret_cast<const uint2*>(vpage + src));
-                }
-            }
+            t.d[n] = make_uint2(0, 0);                  // rows past the range: exact zeros
+            if (key < nkeys)
+                t.d[n] = __ldg(reinterpret_cast<const uint2*>(
+                    page + ((size_t)key * n_kv + kvh) * HD + (size_t)ch * 8));
         }
     }
 }
 
-// WHICH: 0 = the K half of the tile, 1 = the V half
-template <int KVK, int WHICH>
-__device__ __forceinline__ void tile_store(const RawTile<KVK>& t, uint8_t* dstK, int nkeys, int ptid) {
-    uint8_t* dstV = dstK + KT_BYTES;
-    if constexpr (KVK == Q27_KV_F16) {
+template <int KVK>
+__device__ __forceinline__ void half_store(const RawHalf<KVK>& t, uint8_t* dst, int nkeys, int p) {
+    if constexpr (KVK == Q27_KV_FP8) {
 #pragma unroll
-        for (int n = 0; n < 8; n++) {
-            const int q = ptid + NPROD * n;
-            const int key = q >> 5, ch = q & 31;
-            const uint32_t off = (uint32_t)(ch >> 3) * (BN * 128) + sw128(key, ch & 7);
-            if (WHICH == 0) *reinterpret_cast<uint4*>(dstK + off) = t.k[n];
-            else *reinterpret_cast<uint4*>(dstV + off) = t.v[n];
-        }
-    } else if constexpr (KVK == Q27_KV_FP8) {
-#pragma unroll
-        for (int n = 0; n < 8; n++) {
-            const int q = ptid + NPROD * n;
+        for (int n = 0; n < 16; n++) {
+            const int q = p + NPROD * n;
             const int key = q >> 5, ch = q & 31;
             const uint32_t off = (uint32_t)(ch >> 3) * (BN * 128) + sw128(key, ch & 7);
             auto cv = [](uint32_t two) {
                 __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)two, __NV_E4M3);
                 return (uint32_t)h.x | ((uint32_t)h.y << 16);
             };
-            if (WHICH == 0)
-                *reinterpret_cast<uint4*>(dstK + off) = make_uint4(
-                    cv(t.k[n].x & 0xffffu), cv(t.k[n].x >> 16), cv(t.k[n].y & 0xffffu), cv(t.k[n].y >> 16));
-            else
-                *reinterpret_cast<uint4*>(dstV + off) = make_uint4(
-                    cv(t.v[n].x & 0xffffu), cv(t.v[n].x >> 16), cv(t.v[n].y & 0xffffu), cv(t.v[n].y >> 16));
+            *reinterpret_cast<uint4*>(dst + off) = make_uint4(
+                cv(t.d[n].x & 0xffffu), cv(t.d[n].x >> 16), cv(t.d[n].y & 0xffffu), cv(t.d[n].y >> 16));
         }
-    } else {
-        const int key = ptid & 63, side = (ptid >> 6) & 1, blk = ptid >> 7;
-        if (side != WHICH) return;              // warp-uniform: a warp holds one side only
-        uint8_t* dst = side ? dstV : dstK;
+    } else if constexpr (KVK == Q27_KV_T3) {
+        const int key = p & 63, blk = p >> 6;
         const uint32_t* w = t.w;
         const T3Tab tab = t3_tables();
         // 32-bit little-endian word at byte `o` of the block (o even, compile time); block 1
@@ -348,29 +330,32 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(base);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + 512);
-    uint8_t* kv_sm = base + SMEM_BAR;
-    // K and V slots are released separately: a K slot as soon as its S MMAs have run, a V
-    // slot after its PV MMAs, so the next K tile lands while the current tile is in softmax
+    uint8_t* q_sm = base + SMEM_BAR;
+    uint8_t* k_sm = q_sm + Q_BYTES;
+    uint8_t* v_sm = k_sm + K_SLOTS * KT_BYTES;
+    // A K slot is released as soon as its S MMAs have run, a V slot after its PV MMAs.
+    // pvb[b] completes when the PV MMAs of a tile that used S/P buffer b have run: it frees
+    // the buffer for the S MMAs four tiles on and tells the softmax warps that O may be touched.
     const uint32_t k_full = s32(&bars[0]), k_empty = s32(&bars[4]), v_full = s32(&bars[8]),
-                   v_empty = s32(&bars[12]), s_full = s32(&bars[16]), pvb = s32(&bars[18]),
-                   p_full = s32(&bars[20]);
-    // pvb[b] completes when the PV MMAs of a tile that used S/P buffer b have run: it frees the
-    // buffer for S(i+2) and tells the softmax warps that O may be touched
+                   v_empty = s32(&bars[12]), s_full = s32(&bars[16]), pvb = s32(&bars[20]),
+                   p_full = s32(&bars[24]);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = (pb.hi - pb.lo + BN - 1) / BN;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < KV_STAGES; s++) {
-            bar_init(k_full + 8 * s, N_LOAD_WARPS * 32);
+        for (int s = 0; s < K_SLOTS; s++) {
+            bar_init(k_full + 8 * s, NPROD);
             bar_init(k_empty + 8 * s, 1);
-            bar_init(v_full + 8 * s, N_LOAD_WARPS * 32);
+        }
+        for (int s = 0; s < V_SLOTS; s++) {
+            bar_init(v_full + 8 * s, NPROD);
             bar_init(v_empty + 8 * s, 1);
         }
-        for (int s = 0; s < 2; s++) {
+        for (int s = 0; s < S_BUFS; s++) {
             bar_init(s_full + 8 * s, 1);
             bar_init(pvb + 8 * s, 1);
+            bar_init(p_full + 8 * s, N_SOFTMAX_WARPS * 32);
         }
-        bar_init(p_full, N_SOFTMAX_WARPS * 32);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == MMA_WARP) {
@@ -378,72 +363,63 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                      ::"r"(s32(tmem_slot)), "n"(TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
     if (warp < N_SOFTMAX_WARPS) {
-        // Q tile: fp32 -> fp16 pairs, row r into TMEM lane r, dims 2c, 2c+1 into column COL_Q + c
+        // Q tile: fp32 -> fp16, row r of the tile into row r of the four [128][128 B] blocks
         const RowInfo rq = pb.row(threadIdx.x);
-        const uint32_t qaddr = tmem + ((uint32_t)(warp * 32) << 16) + COL_Q;
-#pragma unroll 1
-        for (int c = 0; c < HD / 2; c += 32) {
-            float packed[32];
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-                float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (rq.q) a = __ldg(reinterpret_cast<const float4*>(rq.q + 2 * (c + e)));
-                __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
-                packed[e] = __uint_as_float(*reinterpret_cast<uint32_t*>(&h0));
-                packed[e + 1] = __uint_as_float(*reinterpret_cast<uint32_t*>(&h1));
+#pragma unroll 4
+        for (int ch = 0; ch < HD / 8; ch++) {
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+            if (rq.q) {
+                a = __ldg(reinterpret_cast<const float4*>(rq.q + 8 * ch));
+                b = __ldg(reinterpret_cast<const float4*>(rq.q + 8 * ch + 4));
             }
-            tc_st32(qaddr + c, packed);
+            __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+            __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
+            *reinterpret_cast<uint4*>(q_sm + (ch >> 3) * (BM * 128) + sw128(threadIdx.x, ch & 7)) =
+                make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                           *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
         }
-        tc_wait_st();
+        fence_async_smem();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
 
     if (warp < N_SOFTMAX_WARPS) {
         // ------------------------------ softmax: thread = row ------------------------------
         const int r = threadIdx.x;
         const RowInfo ri = pb.row(r);
         const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-        const float sc2 = scale * LOG2E_F;
+        const float sc2 = scale * LOG2E_F;      // > 0: the row max may be taken before scaling
         float m_ref = -INFINITY, l = 0.f;
         bool ok = true;
 #ifdef Q27_TRACE
         const long long tloop = clock64();
 #endif
         for (int i = 0; i < ntiles && ok; i++) {
-            const int bsel = i & 1;
+            const int b = i % S_BUFS;
+            const uint32_t s_col = lane_base + COL_S + b * BN;
             { TRACE_T0();
-              ok = __all_sync(0xffffffffu, bar_wait(s_full + 8 * bsel, (uint32_t)((i >> 1) & 1)));
+              ok = __all_sync(0xffffffffu, bar_wait(s_full + 8 * b, (uint32_t)((i / S_BUFS) & 1)));
               TRACE_ADD(0, threadIdx.x == 0); }
             if (!ok) break;
             if (threadIdx.x == 0) TRACE_EV(4, i);
             tc_fence_after();
             float s[BN];
-            tc_ld32(lane_base + (bsel ? COL_S1 : COL_S0), s);
-            tc_ld32(lane_base + (bsel ? COL_S1 : COL_S0) + 32, s + 32);
+            tc_ld32(s_col, s);
+            tc_ld32(s_col + 32, s + 32);
             tc_wait_ld();
             const int k0 = pb.lo + i * BN;
             const int vis = ri.bound - k0;            // columns [0, vis) are visible
-            float mx = -INFINITY;
-            if (vis >= BN) {                          // the common case: nothing to mask
+            if (vis < BN) {                           // rare: the diagonal and the ragged tail
 #pragma unroll
-                for (int j = 0; j < BN; j++) {
-                    s[j] *= sc2;
-                    mx = fmaxf(mx, s[j]);
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < BN; j++) {
-                    s[j] = j < vis ? s[j] * sc2 : -INFINITY;
-                    mx = fmaxf(mx, s[j]);
-                }
+                for (int j = 0; j < BN; j++) s[j] = j < vis ? s[j] : -INFINITY;
             }
+            float mx = fmaxf(s[0], s[1]);
+#pragma unroll
+            for (int j = 2; j < BN; j += 2) mx = max3f(mx, s[j], s[j + 1]);
+            mx *= sc2;
             float alpha = 1.f;
             bool need = false;
             if (mx > m_ref + RESCALE_THRESHOLD || (m_ref == -INFINITY && mx > -INFINITY)) {
@@ -451,22 +427,24 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 m_ref = mx;
                 need = i > 0;                          // O holds nothing before the first PV
             }
-            const float mu = m_ref == -INFINITY ? 0.f : m_ref;
-            float sum = 0.f;
+            const float nmu = m_ref == -INFINITY ? 0.f : -m_ref;
+            float sum0 = 0.f, sum1 = 0.f;
             uint32_t ph[BN / 2];
 #pragma unroll
             for (int j = 0; j < BN; j += 2) {
-                const float p0 = ex2f(s[j] - mu), p1 = ex2f(s[j + 1] - mu);
-                sum += p0 + p1;
+                const float p0 = ex2f(fmaf(s[j], sc2, nmu)), p1 = ex2f(fmaf(s[j + 1], sc2, nmu));
+                sum0 += p0;
+                sum1 += p1;
                 __half2 h = __floats2half2_rn(p0, p1);
                 ph[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
             }
-            l = l * alpha + sum;
+            l = l * alpha + (sum0 + sum1);
             if (threadIdx.x == 0) TRACE_EV(5, i);
             if (__any_sync(0xffffffffu, need)) {       // warp-collective TMEM round trip on O
+                const int pi = i - 1;
                 { TRACE_T0();
                   ok = __all_sync(0xffffffffu,
-                                  bar_wait(pvb + 8 * ((i - 1) & 1), (uint32_t)(((i - 1) >> 1) & 1)));
+                                  bar_wait(pvb + 8 * (pi % S_BUFS), (uint32_t)((pi / S_BUFS) & 1)));
                   TRACE_ADD(1, threadIdx.x == 0); }
                 if (!ok) break;
                 tc_fence_after();
@@ -482,13 +460,13 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             }
             // P (fp16 pairs) over the first 32 columns of this tile's S buffer: the A operand
             // of the PV MMAs, straight from tensor memory
-            tc_st32(lane_base + (bsel ? COL_S1 : COL_S0), reinterpret_cast<const float*>(ph));
+            tc_st32(s_col, reinterpret_cast<const float*>(ph));
             tc_wait_st();
             tc_fence_before();
-            bar_arrive(p_full);
-            if (threadIdx.x == 0) TRACE_EV(6, i);
+            bar_arrive(p_full + 8 * b);
+            TRACE_EVMAX(6, i);
         }
-        if (ok) ok = bar_wait(pvb + 8 * ((ntiles - 1) & 1), (uint32_t)(((ntiles - 1) >> 1) & 1));
+        if (ok) ok = bar_wait(pvb + 8 * ((ntiles - 1) % S_BUFS), (uint32_t)(((ntiles - 1) / S_BUFS) & 1));
         ok = __all_sync(0xffffffffu, ok);
 #ifdef Q27_TRACE
         if (threadIdx.x == 0) {
@@ -526,116 +504,98 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         // ------------------------------ S issue: one thread --------------------------------
         if (lane == 0) {
             constexpr uint32_t IDESC_S = make_idesc(BM, BN, false);
-            const uint32_t kv_s = s32(kv_sm);
+            const uint64_t qd0 = make_desc(s32(q_sm), 0, 1024);
             bool ok = true;
-            auto issue_s = [&](int i) {
-                const int st = i % KV_STAGES, bsel = i & 1;
+            for (int i = 0; i < ntiles && ok; i++) {
+                const int ks_ = i % K_SLOTS, b = i % S_BUFS;
                 { TRACE_T0();
-                  ok = ok && bar_wait(k_full + 8 * st, (uint32_t)((i / KV_STAGES) & 1));
+                  ok = bar_wait(k_full + 8 * ks_, (uint32_t)((i / K_SLOTS) & 1));
                   TRACE_ADD(2, true); }
                 { TRACE_T0();
-                  if (ok && i >= 2) ok = bar_wait(pvb + 8 * bsel, (uint32_t)(((i >> 1) - 1) & 1));
+                  if (ok && i >= S_BUFS) ok = bar_wait(pvb + 8 * b, (uint32_t)(((i / S_BUFS) - 1) & 1));
                   TRACE_ADD(3, true); }
-                if (!ok) return;
+                if (!ok) break;
                 fence_async_smem();
                 tc_fence_after();
-                const uint32_t k_s = kv_s + st * STAGE_BYTES;
+                const uint64_t kd0 = make_desc(s32(k_sm) + ks_ * KT_BYTES, 0, 1024);
                 TRACE_EV(0, i);
                 TRACE_T0();
 #pragma unroll
                 for (int ks = 0; ks < HD / 16; ks++) {
-                    const uint64_t db = make_desc(k_s + (ks >> 2) * (BN * 128) + (ks & 3) * 32, 0, 1024);
-                    tc_mma_f16_ta(tmem + (bsel ? COL_S1 : COL_S0), tmem + COL_Q + 8 * ks, db, IDESC_S,
-                                  ks > 0);
+                    const uint64_t da = qd0 + (uint64_t)(((ks >> 2) * (BM * 128) + (ks & 3) * 32) >> 4);
+                    const uint64_t db = kd0 + (uint64_t)(((ks >> 2) * (BN * 128) + (ks & 3) * 32) >> 4);
+                    tc_mma_f16(tmem + COL_S + b * BN, da, db, IDESC_S, ks > 0);
                 }
-                tc_commit(s_full + 8 * bsel);
-                tc_commit(k_empty + 8 * st);
+                tc_commit(s_full + 8 * b);
+                tc_commit(k_empty + 8 * ks_);
                 TRACE_EV(1, i);
                 TRACE_ADD(9, true);
-            };
-            for (int i = 0; i < ntiles && ok; i++) issue_s(i);
+            }
         }
         __syncwarp();
     } else if (warp == PV_WARP) {
         // ------------------------------ PV issue: one thread -------------------------------
         if (lane == 0) {
             constexpr uint32_t IDESC_O = make_idesc(BM, HD, true);
-            const uint32_t kv_s = s32(kv_sm);
             bool ok = true;
             for (int i = 0; i < ntiles && ok; i++) {
+                const int vs_ = i % V_SLOTS, b = i % S_BUFS;
                 { TRACE_T0();
-                  ok = bar_wait(p_full, (uint32_t)(i & 1));
+                  ok = bar_wait(p_full + 8 * b, (uint32_t)((i / S_BUFS) & 1));
                   TRACE_ADD(4, true); }
+                TRACE_EV(7, i);
                 if (!ok) break;
-                const int st = i % KV_STAGES;
-                ok = bar_wait(v_full + 8 * st, (uint32_t)((i / KV_STAGES) & 1));
+                { TRACE_T0();
+                  ok = bar_wait(v_full + 8 * vs_, (uint32_t)((i / V_SLOTS) & 1));
+                  TRACE_ADD(12, true); }
                 if (!ok) break;
                 fence_async_smem();
                 tc_fence_after();
-                const uint32_t v_s = kv_s + st * STAGE_BYTES + KT_BYTES;
+                const uint64_t vd0 = make_desc(s32(v_sm) + vs_ * KT_BYTES, BN * 128, 1024);
                 TRACE_EV(2, i);
                 TRACE_T0();
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; kk++) {
-                    const uint64_t db = make_desc(v_s + kk * 2048, BN * 128, 1024);
-                    tc_mma_f16_ta(tmem + COL_O, tmem + ((i & 1) ? COL_S1 : COL_S0) + 8 * kk, db, IDESC_O,
-                                  (i > 0 || kk > 0));
-                }
-                tc_commit(pvb + 8 * (i & 1));
-                tc_commit(v_empty + 8 * st);
+                for (int kk = 0; kk < BN / 16; kk++)
+                    tc_mma_f16_ta(tmem + COL_O, tmem + COL_S + b * BN + 8 * kk,
+                                  vd0 + (uint64_t)((kk * 2048) >> 4), IDESC_O, (i > 0 || kk > 0));
+                tc_commit(pvb + 8 * b);
+                tc_commit(v_empty + 8 * vs_);
                 TRACE_EV(3, i);
                 TRACE_ADD(10, true);
             }
         }
         __syncwarp();
     } else {
-        // ------------------------------ K/V staging ----------------------------------------
-        const int ptid = threadIdx.x - FIRST_LOAD_WARP * 32;
-        RawTile<KVK> raw0, raw1;
-        // a tile is exactly one cache page (its first key is a multiple of 64)
-        auto load = [&](RawTile<KVK>& r, int i) {
-            if (i < ntiles) {
-                const int k0 = pb.lo + i * BN;
-                tile_load<KVK>(r, static_cast<const uint8_t*>(ktab[k0 >> PAGE_SHIFT]),
-                               static_cast<const uint8_t*>(vtab[k0 >> PAGE_SHIFT]),
-                               min(BN, pb.hi - k0), n_kv, pb.kvh, ptid);
-            }
+        // ------------------------------ K / V staging --------------------------------------
+        // warps 6-9 feed the K ring, warps 10-13 the V ring; a tile is exactly one cache page
+        const int side = (warp - FIRST_LOAD_WARP) >> 2;                 // 0 = K, 1 = V
+        const int p = threadIdx.x - (FIRST_LOAD_WARP + 4 * side) * 32;  // 0..127 within the side
+        const int nslots = side ? V_SLOTS : K_SLOTS;
+        const uint32_t full = side ? v_full : k_full, empty = side ? v_empty : k_empty;
+        uint8_t* ring = side ? v_sm : k_sm;
+        const void* const* tab = side ? vtab : ktab;
+        auto page_of = [&](int i) {
+            return static_cast<const uint8_t*>(tab[(pb.lo + i * BN) >> PAGE_SHIFT]);
         };
-        auto store = [&](const RawTile<KVK>& r, int i) -> bool {
-            const int st = i % KV_STAGES;
-            const uint32_t par = (uint32_t)(((i / KV_STAGES) - 1) & 1);
-            const int nk = min(BN, pb.hi - (pb.lo + i * BN));
-            { TRACE_T0();
-              if (i >= KV_STAGES && !bar_wait(k_empty + 8 * st, par)) return false;
-              TRACE_ADD(5, ptid == 0); }
-            { TRACE_T0();
-              tile_store<KVK, 0>(r, kv_sm + st * STAGE_BYTES, nk, ptid);
-              fence_async_smem();
-              TRACE_ADD(6, ptid == 0); }
-            bar_arrive(k_full + 8 * st);
-            if (i >= KV_STAGES && !bar_wait(v_empty + 8 * st, par)) return false;
-            tile_store<KVK, 1>(r, kv_sm + st * STAGE_BYTES, nk, ptid);
-            fence_async_smem();
-            bar_arrive(v_full + 8 * st);
-            return true;
+        auto nkeys_of = [&](int i) { return min(BN, pb.hi - (pb.lo + i * BN)); };
+        auto wait_slot = [&](int i) -> bool {
+            bool okw = true;
+            TRACE_T0();
+            if (i >= nslots) okw = bar_wait(empty + 8 * (i % nslots), (uint32_t)(((i / nslots) - 1) & 1));
+            TRACE_ADD(5, p == 0 && side == 0);
+            return okw;
         };
         if constexpr (KVK == Q27_KV_F16) {
             // fp16 rows need no conversion: cp.async writes them straight into the swizzled
-            // operand layout and the slot's barrier is armed to fire when this thread's
-            // copies have landed, so the staging threads never wait for data
-            (void)raw0; (void)raw1;
-            auto copy_half = [&](int i, int which) -> bool {
-                const int st = i % KV_STAGES;
-                const uint32_t par = (uint32_t)(((i / KV_STAGES) - 1) & 1);
-                const uint32_t empty = (which ? v_empty : k_empty) + 8 * st;
-                const uint32_t full = (which ? v_full : k_full) + 8 * st;
-                if (i >= KV_STAGES && !bar_wait(empty, par)) return false;
-                const int k0 = pb.lo + i * BN, nk = min(BN, pb.hi - k0);
-                const uint8_t* page = static_cast<const uint8_t*>((which ? vtab : ktab)[k0 >> PAGE_SHIFT]);
-                uint8_t* dst = kv_sm + st * STAGE_BYTES + which * KT_BYTES;
+            // operand layout and the slot's barrier is arrived when the copies have landed
+            for (int i = 0; i < ntiles; i++) {
+                if (!wait_slot(i)) break;
+                const int st = i % nslots, nk = nkeys_of(i);
+                const uint8_t* page = page_of(i);
+                uint8_t* dst = ring + st * KT_BYTES;
 #pragma unroll
-                for (int n = 0; n < 8; n++) {
-                    const int q = ptid + NPROD * n;
+                for (int n = 0; n < 16; n++) {
+                    const int q = p + NPROD * n;
                     const int key = q >> 5, ch = q & 31;
                     const uint32_t off = (uint32_t)(ch >> 3) * (BN * 128) + sw128(key, ch & 7);
                     if (key < nk) {
@@ -646,12 +606,25 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                         *reinterpret_cast<uint4*>(dst + off) = make_uint4(0, 0, 0, 0);
                     }
                 }
-                asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(full) : "memory");
+                asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
+                             ::"r"(full + 8 * st) : "memory");
+            }
+            asm volatile("cp.async.wait_all;" ::: "memory");
+        } else {
+            RawHalf<KVK> raw0, raw1;
+            auto load = [&](RawHalf<KVK>& rw, int i) {
+                if (i < ntiles) half_load<KVK>(rw, page_of(i), nkeys_of(i), n_kv, pb.kvh, p);
+            };
+            auto store = [&](const RawHalf<KVK>& rw, int i) -> bool {
+                if (!wait_slot(i)) return false;
+                const int st = i % nslots;
+                { TRACE_T0();
+                  half_store<KVK>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
+                  fence_async_smem();
+                  TRACE_ADD(6, p == 0 && side == 0); }
+                bar_arrive(full + 8 * st);
                 return true;
             };
-            for (int i = 0; i < ntiles; i++)
-                if (!copy_half(i, 0) || !copy_half(i, 1)) break;
-        } else {
             load(raw0, 0);
             load(raw1, 1);
             for (int i = 0; i < ntiles; i += 2) {
@@ -769,6 +742,8 @@ extern "C" int q27_debug_umma_trace(unsigned long long* out, int reset) {
 }
 extern "C" int q27_debug_umma_events(long long* out) {
     cudaMemcpyFromSymbol(out, g_umma_ev, sizeof(long long) * 8 * 64);
+    static long long z[8 * 64];
+    cudaMemcpyToSymbol(g_umma_ev, z, sizeof(z));
     return 0;
 }
 #endif
