@@ -29,16 +29,20 @@ extern __device__ int g_wait_timeout_flag;
 #ifdef Q27_TRACE
 // timing experiments only: cycles spent waiting, summed over CTAs, by (role, barrier)
 __device__ unsigned long long g_umma_trace[16];
-__device__ long long g_umma_ev[8][64];   // per-event timestamps of CTA (0,0,0), first 64 tiles
+__device__ long long g_umma_ev[12][64];   // per-event timestamps of CTA (0,0,0), first 64 tiles
 #define TRACE_EV(e, i) do { if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (i) < 64) g_umma_ev[e][i] = clock64(); } while (0)
 #define TRACE_EVMAX(e, i) do { if ((threadIdx.x & 31) == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (i) < 64) atomicMax(&g_umma_ev[e][i], clock64()); } while (0)
 #define TRACE_T0() const long long t0__ = clock64()
-#define TRACE_ADD(slot, cond) do { if (cond) atomicAdd(&g_umma_trace[slot], (unsigned long long)(clock64() - t0__)); } while (0)
+#define TRACE_ADD(slot, cond) do { if (cond) tr_acc__[slot] += (unsigned long long)(clock64() - t0__); } while (0)
+#define TRACE_DECL() unsigned long long tr_acc__[16] = {0}
+#define TRACE_FLUSH() do { for (int q__ = 0; q__ < 16; q__++) if (tr_acc__[q__]) atomicAdd(&g_umma_trace[q__], tr_acc__[q__]); } while (0)
 #else
 #define TRACE_T0()
 #define TRACE_ADD(slot, cond)
 #define TRACE_EV(e, i)
 #define TRACE_EVMAX(e, i)
+#define TRACE_DECL()
+#define TRACE_FLUSH()
 #endif
 
 namespace {
@@ -46,15 +50,21 @@ namespace {
 constexpr int BM = 128;                 // Q rows per CTA (TMEM lanes)
 constexpr int BN = 64;                  // keys per tile = one cache page
 constexpr int TOK_PER_TILE = 21;        // 21 tokens x 6 heads = 126 rows
-constexpr int K_SLOTS = 3, V_SLOTS = 2;         // separate rings: K runs ahead with the S MMAs
-constexpr int S_BUFS = 4;                       // S / P buffers in tensor memory
-constexpr int Q_BYTES = BM * HD * 2;            // 65536: 4 blocks of [128 rows][128 B]
+constexpr int K_SLOTS = 3, V_SLOTS = 3;         // separate rings: K runs ahead with the S MMAs
+constexpr int S_BUFS = 3;                       // S / P buffers in tensor memory
+constexpr int Q_TMEM_DIMS = 128;                // dims 0..127 of Q live in tensor memory ...
+constexpr int Q_BYTES = BM * (HD - Q_TMEM_DIMS) * 2;   // ... the rest in 2 blocks of [128 rows][128 B]
 constexpr int KT_BYTES = BN * HD * 2;           // 32768: 4 blocks of [64 rows][128 B]
 constexpr int SMEM_BAR = 1024;                  // barriers + tmem slot, keeps tiles 1024-aligned
 constexpr int UMMA_SMEM = SMEM_BAR + Q_BYTES + (K_SLOTS + V_SLOTS) * KT_BYTES + 1024;
 constexpr int TMEM_COLS = 512;
-// TMEM columns: S buffer b at 64 b (its first 32 columns are reused for P), O behind them
-constexpr int COL_S = 0, COL_O = S_BUFS * BN;
+// TMEM columns: S buffer b at 64 b (its first 32 columns are reused for P), O behind them,
+// then the first half of the Q tile as fp16 pairs (8 columns per k-step of 16 dims). Q is
+// the A operand of every S MMA: each half kept out of shared memory takes 32 KB per K tile
+// off the shared-memory port, which the operand reads of the MMAs and the staging writes
+// otherwise saturate; all of Q does not fit beside three S buffers.
+constexpr int COL_S = 0, COL_O = S_BUFS * BN, COL_Q = COL_O + HD;
+static_assert(COL_Q + Q_TMEM_DIMS / 2 <= TMEM_COLS, "tensor memory budget");
 constexpr float LOG2E_F = 1.4426950408889634f;
 constexpr float RESCALE_THRESHOLD = 8.0f;       // log2 units
 
@@ -115,6 +125,29 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uin
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
         ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// the same two with the accumulate flag known at compile time (no predicate set-up per MMA)
+template <int ACC>
+__device__ __forceinline__ void tc_mma_f16_ta_c(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                uint32_t idesc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "n"(ACC) : "memory");
+}
+template <int ACC>
+__device__ __forceinline__ void tc_mma_f16_c(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "n"(ACC) : "memory");
+}
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}"
+                 : "=r"(pred));
+    return pred != 0;
 }
 // 32 consecutive fp32 columns of this thread's TMEM lane
 __device__ __forceinline__ void tc_ld32(uint32_t taddr, float* v) {
@@ -341,6 +374,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                    p_full = s32(&bars[24]);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = (pb.hi - pb.lo + BN - 1) / BN;
+    TRACE_DECL();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < K_SLOTS; s++) {
@@ -364,10 +398,10 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (warp < N_SOFTMAX_WARPS) {
-        // Q tile: fp32 -> fp16, row r of the tile into row r of the four [128][128 B] blocks
+        // Q tile, fp32 -> fp16: dims 128..255 of row r into row r of two [128][128 B] blocks
         const RowInfo rq = pb.row(threadIdx.x);
 #pragma unroll 4
-        for (int ch = 0; ch < HD / 8; ch++) {
+        for (int ch = Q_TMEM_DIMS / 8; ch < HD / 8; ch++) {
             float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
             if (rq.q) {
                 a = __ldg(reinterpret_cast<const float4*>(rq.q + 8 * ch));
@@ -375,7 +409,8 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             }
             __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
             __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
-            *reinterpret_cast<uint4*>(q_sm + (ch >> 3) * (BM * 128) + sw128(threadIdx.x, ch & 7)) =
+            const int c2 = ch - Q_TMEM_DIMS / 8;
+            *reinterpret_cast<uint4*>(q_sm + (c2 >> 3) * (BM * 128) + sw128(threadIdx.x, c2 & 7)) =
                 make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
                            *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
         }
@@ -385,6 +420,28 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (warp < N_SOFTMAX_WARPS) {
+        // dims 0..127 of row r into TMEM lane r, dims 2c, 2c+1 into column COL_Q + c
+        const RowInfo rq = pb.row(threadIdx.x);
+        const uint32_t qaddr = tmem + ((uint32_t)(warp * 32) << 16) + COL_Q;
+#pragma unroll 1
+        for (int c = 0; c < Q_TMEM_DIMS / 2; c += 32) {
+            float packed[32];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+                float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (rq.q) a = __ldg(reinterpret_cast<const float4*>(rq.q + 2 * (c + e)));
+                __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+                packed[e] = __uint_as_float(*reinterpret_cast<uint32_t*>(&h0));
+                packed[e + 1] = __uint_as_float(*reinterpret_cast<uint32_t*>(&h1));
+            }
+            tc_st32(qaddr + c, packed);
+        }
+        tc_wait_st();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
 
     if (warp < N_SOFTMAX_WARPS) {
         // ------------------------------ softmax: thread = row ------------------------------
@@ -470,8 +527,8 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         ok = __all_sync(0xffffffffu, ok);
 #ifdef Q27_TRACE
         if (threadIdx.x == 0) {
-            atomicAdd(&g_umma_trace[7], (unsigned long long)(clock64() - tloop));
-            atomicAdd(&g_umma_trace[8], (unsigned long long)ntiles);
+            tr_acc__[7] += (unsigned long long)(clock64() - tloop);
+            tr_acc__[8] += (unsigned long long)ntiles;
         }
 #endif
         tc_fence_after();
@@ -501,70 +558,96 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         }
         tc_fence_before();
     } else if (warp == MMA_WARP) {
-        // ------------------------------ S issue: one thread --------------------------------
-        if (lane == 0) {
+        // ------------------------------ S issue ------------------------------------------
+        // The whole warp runs the loop (waits and address arithmetic stay warp-uniform, so the
+        // descriptors live in uniform registers); one elected lane issues the MMAs.
+        {
             constexpr uint32_t IDESC_S = make_idesc(BM, BN, false);
             const uint64_t qd0 = make_desc(s32(q_sm), 0, 1024);
+            const uint64_t kd_base = make_desc(s32(k_sm), 0, 1024);
             bool ok = true;
+            int ks_ = 0, b = 0;
+            uint32_t kpar = 0, bpar = 1;          // bpar: parity of the PREVIOUS use of buffer b
             for (int i = 0; i < ntiles && ok; i++) {
-                const int ks_ = i % K_SLOTS, b = i % S_BUFS;
                 { TRACE_T0();
-                  ok = bar_wait(k_full + 8 * ks_, (uint32_t)((i / K_SLOTS) & 1));
-                  TRACE_ADD(2, true); }
+                  ok = bar_wait(k_full + 8 * ks_, kpar);
+                  TRACE_ADD(2, lane == 0); }
+                if (lane == 0) TRACE_EV(8, i);
                 { TRACE_T0();
-                  if (ok && i >= S_BUFS) ok = bar_wait(pvb + 8 * b, (uint32_t)(((i / S_BUFS) - 1) & 1));
-                  TRACE_ADD(3, true); }
+                  if (ok && i >= S_BUFS) ok = bar_wait(pvb + 8 * b, bpar);
+                  TRACE_ADD(3, lane == 0); }
+                if (lane == 0) TRACE_EV(9, i);
                 if (!ok) break;
                 fence_async_smem();
                 tc_fence_after();
-                const uint64_t kd0 = make_desc(s32(k_sm) + ks_ * KT_BYTES, 0, 1024);
-                TRACE_EV(0, i);
+                const uint64_t kd0 = kd_base + (uint64_t)((ks_ * KT_BYTES) >> 4);
+                const uint32_t d = tmem + COL_S + b * BN;
+                if (lane == 0) TRACE_EV(0, i);
                 TRACE_T0();
+                if (elect_one()) {
 #pragma unroll
-                for (int ks = 0; ks < HD / 16; ks++) {
-                    const uint64_t da = qd0 + (uint64_t)(((ks >> 2) * (BM * 128) + (ks & 3) * 32) >> 4);
-                    const uint64_t db = kd0 + (uint64_t)(((ks >> 2) * (BN * 128) + (ks & 3) * 32) >> 4);
-                    tc_mma_f16(tmem + COL_S + b * BN, da, db, IDESC_S, ks > 0);
+                    for (int ks = 0; ks < HD / 16; ks++) {
+                        const uint64_t db = kd0 + (uint64_t)(((ks >> 2) * (BN * 128) + (ks & 3) * 32) >> 4);
+                        if (ks == 0) {
+                            tc_mma_f16_ta_c<0>(d, tmem + COL_Q, db, IDESC_S);
+                        } else if (ks < Q_TMEM_DIMS / 16) {
+                            tc_mma_f16_ta_c<1>(d, tmem + COL_Q + 8 * ks, db, IDESC_S);
+                        } else {
+                            const int k2 = ks - Q_TMEM_DIMS / 16;
+                            const uint64_t da = qd0 + (uint64_t)(((k2 >> 2) * (BM * 128) + (k2 & 3) * 32) >> 4);
+                            tc_mma_f16_c<1>(d, da, db, IDESC_S);
+                        }
+                    }
+                    tc_commit(s_full + 8 * b);
+                    tc_commit(k_empty + 8 * ks_);
                 }
-                tc_commit(s_full + 8 * b);
-                tc_commit(k_empty + 8 * ks_);
-                TRACE_EV(1, i);
-                TRACE_ADD(9, true);
+                __syncwarp();
+                if (lane == 0) TRACE_EV(1, i);
+                TRACE_ADD(9, lane == 0);
+                if (++ks_ == K_SLOTS) { ks_ = 0; kpar ^= 1; }
+                if (++b == S_BUFS) { b = 0; bpar ^= 1; }
             }
         }
-        __syncwarp();
     } else if (warp == PV_WARP) {
-        // ------------------------------ PV issue: one thread -------------------------------
-        if (lane == 0) {
+        // ------------------------------ PV issue -----------------------------------------
+        {
             constexpr uint32_t IDESC_O = make_idesc(BM, HD, true);
+            const uint64_t vd_base = make_desc(s32(v_sm), BN * 128, 1024);
             bool ok = true;
+            int vs_ = 0, b = 0;
+            uint32_t vpar = 0, bpar = 0;
             for (int i = 0; i < ntiles && ok; i++) {
-                const int vs_ = i % V_SLOTS, b = i % S_BUFS;
                 { TRACE_T0();
-                  ok = bar_wait(p_full + 8 * b, (uint32_t)((i / S_BUFS) & 1));
-                  TRACE_ADD(4, true); }
-                TRACE_EV(7, i);
+                  ok = bar_wait(p_full + 8 * b, bpar);
+                  TRACE_ADD(4, lane == 0); }
+                if (lane == 0) TRACE_EV(7, i);
                 if (!ok) break;
                 { TRACE_T0();
-                  ok = bar_wait(v_full + 8 * vs_, (uint32_t)((i / V_SLOTS) & 1));
-                  TRACE_ADD(12, true); }
+                  ok = bar_wait(v_full + 8 * vs_, vpar);
+                  TRACE_ADD(12, lane == 0); }
                 if (!ok) break;
                 fence_async_smem();
                 tc_fence_after();
-                const uint64_t vd0 = make_desc(s32(v_sm) + vs_ * KT_BYTES, BN * 128, 1024);
-                TRACE_EV(2, i);
+                const uint64_t vd0 = vd_base + (uint64_t)((vs_ * KT_BYTES) >> 4);
+                const uint32_t pa = tmem + COL_S + b * BN;
+                if (lane == 0) TRACE_EV(2, i);
                 TRACE_T0();
+                if (elect_one()) {
+                    if (i > 0) tc_mma_f16_ta_c<1>(tmem + COL_O, pa, vd0, IDESC_O);
+                    else tc_mma_f16_ta_c<0>(tmem + COL_O, pa, vd0, IDESC_O);
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; kk++)
-                    tc_mma_f16_ta(tmem + COL_O, tmem + COL_S + b * BN + 8 * kk,
-                                  vd0 + (uint64_t)((kk * 2048) >> 4), IDESC_O, (i > 0 || kk > 0));
-                tc_commit(pvb + 8 * b);
-                tc_commit(v_empty + 8 * vs_);
-                TRACE_EV(3, i);
-                TRACE_ADD(10, true);
+                    for (int kk = 1; kk < BN / 16; kk++)
+                        tc_mma_f16_ta_c<1>(tmem + COL_O, pa + 8 * kk, vd0 + (uint64_t)((kk * 2048) >> 4), IDESC_O);
+                    tc_commit(pvb + 8 * b);
+                    tc_commit(v_empty + 8 * vs_);
+                }
+                __syncwarp();
+                if (lane == 0) TRACE_EV(3, i);
+                TRACE_ADD(10, lane == 0);
+                if (++vs_ == V_SLOTS) { vs_ = 0; vpar ^= 1; }
+                if (++b == S_BUFS) { b = 0; bpar ^= 1; }
             }
         }
-        __syncwarp();
     } else {
         // ------------------------------ K / V staging --------------------------------------
         // warps 6-9 feed the K ring, warps 10-13 the V ring; a tile is exactly one cache page
@@ -590,6 +673,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             // operand layout and the slot's barrier is arrived when the copies have landed
             for (int i = 0; i < ntiles; i++) {
                 if (!wait_slot(i)) break;
+                if (p == 0 && side == 0) TRACE_EV(10, i);
                 const int st = i % nslots, nk = nkeys_of(i);
                 const uint8_t* page = page_of(i);
                 uint8_t* dst = ring + st * KT_BYTES;
@@ -608,6 +692,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 }
                 asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
                              ::"r"(full + 8 * st) : "memory");
+                if (p == 0 && side == 0) TRACE_EV(11, i);
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
         } else {
@@ -637,6 +722,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             }
         }
     }
+    TRACE_FLUSH();
     __syncthreads();
     if (warp == MMA_WARP) {
         tc_fence_after();
@@ -741,8 +827,8 @@ extern "C" int q27_debug_umma_trace(unsigned long long* out, int reset) {
     return 0;
 }
 extern "C" int q27_debug_umma_events(long long* out) {
-    cudaMemcpyFromSymbol(out, g_umma_ev, sizeof(long long) * 8 * 64);
-    static long long z[8 * 64];
+    cudaMemcpyFromSymbol(out, g_umma_ev, sizeof(long long) * 12 * 64);
+    static long long z[12 * 64];
     cudaMemcpyToSymbol(g_umma_ev, z, sizeof(z));
     return 0;
 }
