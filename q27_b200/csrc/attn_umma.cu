@@ -5,18 +5,18 @@
 // x 6 heads for verify -- so every K/V tile that is staged serves all six heads (and, for
 // verify, all draft lanes: one pass over the cache). Each row carries its own causal bound.
 //
-//   S  = Q . K^T   M=128 rows, N=64 keys, K=256 dims     -> TMEM (a ring of four S buffers)
+//   S  = Q . K^T   M=128 rows, N=64 keys, K=256 dims     -> TMEM (a ring of three S buffers)
 //   O += P . V     M=128 rows, N=256 dims, K=64 keys      -> TMEM (256 columns)
 //
 // Q, K and V are fp16 in shared memory in the 128-byte-swizzled canonical layouts (Q and K
 // K-major, V MN-major = its natural [key][dim] rows); P is written as fp16 over the S buffer
 // it came from and is the A operand of the PV MMAs straight from tensor memory; accumulation
-// is fp32. The S ring is four deep because the chain S -> softmax -> PV -> (buffer free) is
-// several thousand cycles of mbarrier hops and MMA latency long: four tiles in flight keep
+// is fp32. The S ring is three deep because the chain S -> softmax -> PV -> (buffer free) is
+// several thousand cycles of mbarrier hops and MMA latency long: three tiles in flight keep
 // the tensor pipe and the softmax warps busy through it.
-// Warp roles: warps 0-3 softmax (thread = row = TMEM lane); warp 4 issues the S MMAs and warp 5
-// the PV MMAs (two independent issue streams, ordered only by mbarriers); warps 6-9 stage
-// K tiles (ring of three) and warps 10-13 V tiles (ring of two): cp.async for fp16 rows,
+// Warp roles: warps 0-3 softmax (thread = row = TMEM lane); warps 4-5 issue the S MMAs and warp
+// 6 the PV MMAs (independent issue streams, ordered only by mbarriers); warps 7-10 stage
+// K tiles and warps 11-14 V tiles (rings of three): cp.async for fp16 rows,
 // registers + convert for fp8 / turbo3. The running max is only advanced when it grows by
 // more than 2^8, so O in TMEM is rarely rescaled.
 // Every mbarrier wait is bounded; a timeout sets the library's flag and the CTA drains.
@@ -68,8 +68,9 @@ static_assert(COL_Q + Q_TMEM_DIMS / 2 <= TMEM_COLS, "tensor memory budget");
 constexpr float LOG2E_F = 1.4426950408889634f;
 constexpr float RESCALE_THRESHOLD = 8.0f;       // log2 units
 
-constexpr int N_SOFTMAX_WARPS = 4, MMA_WARP = 4, PV_WARP = 5, FIRST_LOAD_WARP = 6, N_LOAD_WARPS = 8;
-constexpr int UMMA_THREADS = (FIRST_LOAD_WARP + N_LOAD_WARPS) * 32;   // 448
+constexpr int N_SOFTMAX_WARPS = 4, MMA_WARP = 4, N_S_WARPS = 2, PV_WARP = 6, FIRST_LOAD_WARP = 7,
+              N_LOAD_WARPS = 8;
+constexpr int UMMA_THREADS = (FIRST_LOAD_WARP + N_LOAD_WARPS) * 32;   // 480
 constexpr int NPROD = N_LOAD_WARPS * 16;        // 128 staging threads per side (K or V)
 
 // ---- small PTX wrappers -------------------------------------------------------------------
@@ -85,9 +86,9 @@ __device__ __forceinline__ void bar_arrive(uint32_t bar) {
 __device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
         " selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+        : "=r"(ok) : "r"(bar), "r"(parity), "r"(4000u) : "memory");   // suspend-time hint, ns
     return ok != 0;
 }
 __device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
@@ -239,7 +240,9 @@ struct Problem {
     int kvh, tile_t0, lo, hi, sp;
 
     __device__ __forceinline__ RowInfo row(int r) const {
-        RowInfo ri{nullptr, 0, nullptr, nullptr};
+        // a padding row (no q) sees everything: its lanes stay on the unmasked path of their
+        // warp and what they compute from a zero Q row is dropped
+        RowInfo ri{nullptr, 0x3fffffff, nullptr, nullptr};
         const int tok = r / GQA, j = r % GQA;
         if (MODE == 0) {
             const int t = tile_t0 + tok;
@@ -462,6 +465,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
               TRACE_ADD(0, threadIdx.x == 0); }
             if (!ok) break;
             if (threadIdx.x == 0) TRACE_EV(4, i);
+            TRACE_T0();
             tc_fence_after();
             float s[BN];
             tc_ld32(s_col, s);
@@ -522,6 +526,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             tc_fence_before();
             bar_arrive(p_full + 8 * b);
             TRACE_EVMAX(6, i);
+            TRACE_ADD(warp == 3 ? 6 : 13 + warp, lane == 0);
         }
         if (ok) ok = bar_wait(pvb + 8 * ((ntiles - 1) % S_BUFS), (uint32_t)(((ntiles - 1) / S_BUFS) & 1));
         ok = __all_sync(0xffffffffu, ok);
@@ -557,8 +562,10 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             }
         }
         tc_fence_before();
-    } else if (warp == MMA_WARP) {
+    } else if (warp < MMA_WARP + N_S_WARPS) {
         // ------------------------------ S issue ------------------------------------------
+        // Two warps take alternate tiles: the waits and bookkeeping of one overlap the MMA issue
+        // of the other (the S buffers, K slots and barriers of consecutive tiles are distinct).
         // The whole warp runs the loop (waits and address arithmetic stay warp-uniform, so the
         // descriptors live in uniform registers); one elected lane issues the MMAs.
         {
@@ -566,9 +573,10 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             const uint64_t qd0 = make_desc(s32(q_sm), 0, 1024);
             const uint64_t kd_base = make_desc(s32(k_sm), 0, 1024);
             bool ok = true;
-            int ks_ = 0, b = 0;
-            uint32_t kpar = 0, bpar = 1;          // bpar: parity of the PREVIOUS use of buffer b
-            for (int i = 0; i < ntiles && ok; i++) {
+            for (int i = warp - MMA_WARP; i < ntiles && ok; i += N_S_WARPS) {
+                const int ks_ = i % K_SLOTS, b = i % S_BUFS;
+                const uint32_t kpar = (uint32_t)((i / K_SLOTS) & 1);
+                const uint32_t bpar = (uint32_t)(((i / S_BUFS) - 1) & 1);   // previous use of buffer b
                 { TRACE_T0();
                   ok = bar_wait(k_full + 8 * ks_, kpar);
                   TRACE_ADD(2, lane == 0); }
@@ -604,8 +612,6 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 __syncwarp();
                 if (lane == 0) TRACE_EV(1, i);
                 TRACE_ADD(9, lane == 0);
-                if (++ks_ == K_SLOTS) { ks_ = 0; kpar ^= 1; }
-                if (++b == S_BUFS) { b = 0; bpar ^= 1; }
             }
         }
     } else if (warp == PV_WARP) {
@@ -650,7 +656,8 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         }
     } else {
         // ------------------------------ K / V staging --------------------------------------
-        // warps 6-9 feed the K ring, warps 10-13 the V ring; a tile is exactly one cache page
+        // the first four staging warps feed the K ring, the other four the V ring; a tile is
+        // exactly one cache page
         const int side = (warp - FIRST_LOAD_WARP) >> 2;                 // 0 = K, 1 = V
         const int p = threadIdx.x - (FIRST_LOAD_WARP + 4 * side) * 32;  // 0..127 within the side
         const int nslots = side ? V_SLOTS : K_SLOTS;
