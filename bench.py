@@ -54,7 +54,7 @@ FP8_DEQ_SCALE = 6.0 / 448.0
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from the
 # ncu captures summarised under profiles/ (None until a capture exists for the workload)
-NCU_TRAFFIC = {}
+NCU_TRAFFIC = {"c3": 215.6e6}   # profiles/decode_mma_turbo3_c3.md
 
 
 def measured_peak_gbs() -> tuple[float, str]:
@@ -333,7 +333,9 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": NCU_TRAFFIC.get(args.workload),
                      "peak_source": f"{which} copy bandwidth (MEASURED_PEAKS.json)",
-                     "kernel": "k_decode_mma (split-KV partials)", "kernel_ms": round(kernel_ms, 5),
+                     "kernel": ("k_verify_umma (tcgen05, split-KV partials)" if lanes >= 2
+                                else "k_decode_mma (split-KV partials)"),
+                     "kernel_ms": round(kernel_ms, 5),
                      "algorithmic_bytes_per_launch": step_bytes_rank,
                      "frac_of_nominal_8TBps": round(achieved / 8000.0, 4)},
     }
