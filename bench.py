@@ -216,7 +216,11 @@ def run_ours(args):
     out_dev = torch.zeros((nslots, lanes, N_Q * HD), device=dev)
     out_host = torch.zeros((nslots, lanes, N_Q * HD)).pin_memory()
     scratch = [torch.empty(Q.decode_scratch_floats(lanes), device=dev) for _ in range(nslots)]
-    ex = qd.PartialExchange.create(nslots, lanes, N_Q, world, dev) if world > 1 else None
+    ex = boxes = None
+    if world > 1 and args.exchange == "peer":
+        boxes = qd.PeerMailboxes(nslots, lanes, N_Q)
+    elif world > 1:
+        ex = qd.PartialExchange.create(nslots, lanes, N_Q, world, dev)
     merged = torch.zeros((nslots * lanes * N_Q, HD), device=dev)
 
     def slots_for(c):
@@ -232,7 +236,9 @@ def run_ours(args):
 
     def step(i):
         sl = slot_sets[i % copies]
-        if world > 1:
+        if boxes is not None:
+            boxes.decode(sl, merged, Q_STRIDE, N_KV, SCALE, kvk)
+        elif world > 1:
             qd.sharded_decode(sl, ex, merged, Q_STRIDE, N_KV, SCALE, kvk)
         else:
             Q.attn_decode_batched(sl, Q_STRIDE, N_Q, N_KV, HD, SCALE, kvk=kvk)
@@ -310,7 +316,8 @@ def run_ours(args):
     e2e_value = total_bytes * args.steps / e2e_s / 1e9
     peak, which = measured_peak_gbs()
     achieved = step_bytes_rank / (kernel_ms * 1e-3) / 1e9
-    launches_per_step = 2 + (1 if world > 1 else 0)
+    # partial + combine, then across GPUs either push + merge (ours) or all-gather (NCCL) + merge
+    launches_per_step = 2 + (0 if world == 1 else 2 if boxes is not None else 1)
 
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
@@ -321,6 +328,9 @@ def run_ours(args):
                    "lanes": lanes, "context_rows_per_slot": rows_total,
                    "rows_per_gpu_per_slot": local_rows, "heads": "24q/4kv", "head_dim": HD,
                    "parallelism": f"kv-split x{world}" if world > 1 else "single gpu",
+                   "exchange": ("none" if world == 1 else
+                                "peer-memory mailboxes (P2P stores + flags, no collective)"
+                                if boxes is not None else "nccl all-gather"),
                    "l2_policy": f"inputs rotate over {copies} cache copies "
                                 f"({copies * step_bytes_rank / 2**20:.0f} MiB > 2 x L2)"},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
@@ -344,6 +354,8 @@ def run_ours(args):
                                             local_rows, out_dev_check=(slot_sets[0], out_dev, Q))
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if boxes is not None:
+        boxes.close()
     if world > 1:
         dist.destroy_process_group()
 
@@ -568,6 +580,8 @@ def main():
     ap.add_argument("--workload", default="c3", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: how the ranks' partials meet (peer-memory mailboxes or NCCL)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -45,6 +45,8 @@ enum { Q27_KV_F16 = 0, Q27_KV_FP8 = 1, Q27_KV_T3 = 2 };
 #define Q27_PF_SPLIT_MAX 8    /* src/prefill.cuh:88 */
 #define Q27_T3_BLOCK_BYTES 50 /* sizeof(block_turbo3), src/turbo3.cuh:26-32 */
 #define Q27_MAX_SLOTS 8       /* slots per batched launch */
+#define Q27_MAX_RANKS 8       /* GPUs of one node that share a KV-sequence split */
+#define Q27_XCHG_HANDLE_BYTES 64
 
 /* Lane pointer bundles: P3 / CP3 (src/kernels.cuh:67-68) and IP3 (src/spec3.cuh:13).
  * Slots >= ntok may hold garbage and are never dereferenced. */
@@ -165,6 +167,34 @@ int q27_attn_decode_partial(const q27_slot* slots, int nslots, int lanes_stride,
  * parts: [nparts][npairs][258]; out: [npairs][256] normalised. */
 int q27_attn_merge_partials(const float* parts, int nparts, int64_t npairs, float* out,
                             void* stream);
+
+/* ---- exchange of partials through peer memory (no reference counterpart: the reference
+ * is single-GPU). One MAILBOX per rank, in that rank's HBM, mapped into the other ranks'
+ * processes (one process per GPU) with CUDA IPC. ------------------------------------- */
+
+/* cudaMalloc'ed, zero-filled device buffer that other processes of this node can map;
+ * handle (Q27_XCHG_HANDLE_BYTES bytes, may be NULL) is what they pass to q27_xchg_open. */
+int q27_xchg_alloc(size_t bytes, void** ptr, void* handle);
+int q27_xchg_open(const void* handle, void** ptr);
+int q27_xchg_close(void* ptr);   /* a pointer from q27_xchg_open */
+int q27_xchg_free(void* ptr);    /* a pointer from q27_xchg_alloc */
+/* bytes of a mailbox for `world` ranks x npairs (slot, lane, head) partials */
+size_t q27_xchg_mailbox_bytes(int world, int64_t npairs);
+
+/* q27_attn_decode_partial whose result goes to slot `rank` of EVERY rank's mailbox
+ * (mailboxes[r] = rank r's mailbox as mapped here; mailboxes[rank] = the own one) with peer
+ * stores, followed by a release flag carrying `epoch`. epoch starts at 1 and grows by one
+ * per exchange on every rank; npairs = nslots * lanes_stride * n_q_heads. */
+int q27_attn_decode_partial_push(const q27_slot* slots, int nslots, int lanes_stride, int q_stride,
+                                 int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                                 void* const* mailboxes, int world, int rank, unsigned epoch,
+                                 void* stream, int kvk);
+
+/* Waits on the device (bounded; a timeout sets the flag q27_wait_timeout_flag reads and
+ * leaves `out` untouched) until all `world` ranks have pushed `epoch` into this rank's own
+ * mailbox, then log-sum-exp merges them: out [npairs][256] normalised. */
+int q27_attn_merge_pushed(const void* mailbox, int world, int64_t npairs, unsigned epoch,
+                          float* out, void* stream);
 
 /* ---- prefill ----------------------------------------------------------------------- */
 

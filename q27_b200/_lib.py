@@ -14,6 +14,8 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libq27_b200.so"
 MAX_LANES = 16
 MAX_SLOTS = 8
 MAX_SPLITS = 128
+XCHG_HANDLE_BYTES = 64
+MAX_RANKS = 8
 NOALLOC_MAX_LANES = 4
 PART_STRIDE = 258
 KV_PAGE = 64
@@ -63,6 +65,14 @@ SIGNATURES = {
     "q27_attn_decode_batched_exact": (_i, [C.POINTER(Slot), _i, _i, _i, _i, _i, _f, _vp, _i]),
     "q27_attn_decode_partial": (_i, [C.POINTER(Slot), _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _i]),
     "q27_attn_merge_partials": (_i, [_vp, _i, _i64, _vp, _vp]),
+    "q27_xchg_alloc": (_i, [_sz, C.POINTER(_vp), _vp]),
+    "q27_xchg_open": (_i, [_vp, C.POINTER(_vp)]),
+    "q27_xchg_close": (_i, [_vp]),
+    "q27_xchg_free": (_i, [_vp]),
+    "q27_xchg_mailbox_bytes": (_sz, [_i, _i64]),
+    "q27_attn_decode_partial_push": (_i, [C.POINTER(Slot), _i, _i, _i, _i, _i, _i, _f,
+                                          C.POINTER(_vp), _i, _i, C.c_uint, _vp, _i]),
+    "q27_attn_merge_pushed": (_i, [_vp, _i, _i64, C.c_uint, _vp, _vp]),
     "q27_attn_prefill_T": (_i, [_vp, _i, _i, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _f,
                                 _vp, _i]),
     "q27_attn_prefill_T_exact": (_i, [_vp, _i, _i, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i,

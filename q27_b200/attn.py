@@ -124,6 +124,25 @@ def attn_decode_partial(slots, lanes_stride, q_stride, n_q_heads, n_kv_heads, he
                                             stream_ptr(st), kvk), "q27_attn_decode_partial")
 
 
+def attn_decode_partial_push(slots, lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim, scale,
+                             mailboxes, rank, epoch, st=None, kvk=0):
+    """attn_decode_partial whose result lands in slot ``rank`` of every rank's mailbox
+    (``mailboxes``: device addresses, one per rank, as mapped in this process)."""
+    import ctypes as C
+    arr = _slots(slots)
+    boxes = (C.c_void_p * len(mailboxes))(*mailboxes)
+    L.check(L.lib().q27_attn_decode_partial_push(arr, len(slots), lanes_stride, q_stride, n_q_heads,
+                                                 n_kv_heads, head_dim, scale, boxes,
+                                                 len(mailboxes), rank, epoch, stream_ptr(st), kvk),
+            "q27_attn_decode_partial_push")
+
+
+def attn_merge_pushed(mailbox, world, npairs, epoch, out, st=None):
+    """Device-side wait for every rank's push of ``epoch``, then the LSE merge into out."""
+    L.check(L.lib().q27_attn_merge_pushed(mailbox, world, npairs, epoch, out.data_ptr(),
+                                          stream_ptr(st)), "q27_attn_merge_pushed")
+
+
 def attn_merge_partials(parts, nparts, npairs, out, st=None):
     """LSE merge of ``nparts`` partial sets [nparts][npairs][258] -> out [npairs][256]."""
     L.check(L.lib().q27_attn_merge_partials(parts.data_ptr(), nparts, npairs, out.data_ptr(),

@@ -1,8 +1,11 @@
 // The extern "C" surface: argument validation, split planning and dispatch. Nothing here
 // allocates or synchronises; every call only enqueues kernels on the caller's stream.
 #include <limits.h>
+#include <stdio.h>
+#include <string.h>
 
 #include "common.cuh"
+#include "p2p_exchange.cuh"
 #include "attn_umma.cuh"
 #include "decode_mma.cuh"
 
@@ -82,12 +85,13 @@ enum Family { FAM_AUTO = 0, FAM_EXACT = 1 };
 thread_local cudaEvent_t g_ev_start = nullptr, g_ev_stop = nullptr;
 
 int run_decode(const q27_slot* slots, int nslots, int lanes_stride, int q_stride, int n_q, int n_kv,
-               int head_dim, float scale, float* partial_out, void* stream, int kvk, Family fam) {
+               int head_dim, float scale, float* partial_out, void* stream, int kvk, Family fam,
+               const Peers* peers = nullptr) {
     DevBatch b;
     int rc = build_batch(slots, nslots, q_stride, n_q, n_kv, head_dim, scale, kvk,
-                         partial_out == nullptr, b);
+                         partial_out == nullptr && peers == nullptr, b);
     if (rc) return rc;
-    if (partial_out && (lanes_stride < b.max_ntok || lanes_stride > Q27_MAX_LANES))
+    if ((partial_out || peers) && (lanes_stride < b.max_ntok || lanes_stride > Q27_MAX_LANES))
         return Q27_ERR_INVALID_ARG;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int sms = sm_count();
@@ -111,6 +115,7 @@ int run_decode(const q27_slot* slots, int nslots, int lanes_stride, int q_stride
         if (rc) return rc;
     }
     if (g_ev_stop) Q27_CUDA_TRY(cudaEventRecord(g_ev_stop, st));
+    if (peers) return launch_combine_push(b, *peers, lanes_stride, st);
     return launch_combine(b, partial_out, partial_out ? lanes_stride : b.max_ntok, st);
 }
 
@@ -308,7 +313,87 @@ int q27_set_kernel_events(void* ev_start, void* ev_stop) {
 
 int q27_wait_timeout_flag(int* out) {
     if (!out) return Q27_ERR_INVALID_ARG;
-    return read_wait_timeout_flag(out);
+    int a = 0, b = 0, c = 0, rc;
+    if ((rc = read_wait_timeout_flag(&a))) return rc;
+    if ((rc = read_umma_timeout_flag(&b))) return rc;
+    if ((rc = read_xchg_timeout_flag(&c))) return rc;
+    *out = a | b | c;
+    return Q27_OK;
+}
+
+int q27_xchg_alloc(size_t bytes, void** ptr, void* handle) {
+    if (!ptr || bytes == 0) return Q27_ERR_INVALID_ARG;
+    static_assert(sizeof(cudaIpcMemHandle_t) == Q27_XCHG_HANDLE_BYTES, "IPC handle size");
+    void* p = nullptr;
+    Q27_CUDA_TRY(cudaMalloc(&p, bytes));
+    cudaError_t e = cudaMemset(p, 0, bytes);
+    if (e == cudaSuccess && handle) {
+        cudaIpcMemHandle_t h;
+        e = cudaIpcGetMemHandle(&h, p);
+        if (e == cudaSuccess) memcpy(handle, &h, sizeof(h));
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        fprintf(stderr, "q27_b200: %s at %s:%d\n", cudaGetErrorString(e), __FILE__, __LINE__);
+        return Q27_ERR_CUDA;
+    }
+    *ptr = p;
+    return Q27_OK;
+}
+
+int q27_xchg_open(const void* handle, void** ptr) {
+    if (!handle || !ptr) return Q27_ERR_INVALID_ARG;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    Q27_CUDA_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return Q27_OK;
+}
+
+int q27_xchg_close(void* ptr) {
+    if (!ptr) return Q27_ERR_INVALID_ARG;
+    Q27_CUDA_TRY(cudaIpcCloseMemHandle(ptr));
+    return Q27_OK;
+}
+
+int q27_xchg_free(void* ptr) {
+    if (!ptr) return Q27_ERR_INVALID_ARG;
+    Q27_CUDA_TRY(cudaFree(ptr));
+    return Q27_OK;
+}
+
+size_t q27_xchg_mailbox_bytes(int world, int64_t npairs) {
+    if (world < 1 || world > Q27_MAX_RANKS || npairs < 1) return 0;
+    return xchg_mailbox_bytes(world, npairs);
+}
+
+int q27_attn_decode_partial_push(const q27_slot* slots, int nslots, int lanes_stride, int q_stride,
+                                 int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                                 void* const* mailboxes, int world, int rank, unsigned epoch,
+                                 void* stream, int kvk) {
+    if (!mailboxes || world < 1 || world > Q27_MAX_RANKS || rank < 0 || rank >= world || epoch == 0)
+        return Q27_ERR_INVALID_ARG;
+    for (int r = 0; r < world; r++)
+        if (!mailboxes[r] || ((uintptr_t)mailboxes[r] & 255)) return Q27_ERR_INVALID_ARG;
+    if (nslots < 1 || lanes_stride < 1 || n_q_heads < 1 || ((n_q_heads * lanes_stride * nslots) & 1))
+        return Q27_ERR_INVALID_ARG;
+    Peers p{};
+    for (int r = 0; r < world; r++) p.box[r] = static_cast<uint8_t*>(mailboxes[r]);
+    p.world = world;
+    p.rank = rank;
+    p.npairs = (int64_t)nslots * lanes_stride * n_q_heads;
+    p.epoch = epoch;
+    return run_decode(slots, nslots, lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim, scale,
+                      nullptr, stream, kvk, FAM_AUTO, &p);
+}
+
+int q27_attn_merge_pushed(const void* mailbox, int world, int64_t npairs, unsigned epoch,
+                          float* out, void* stream) {
+    if (!mailbox || !out || world < 1 || world > Q27_MAX_RANKS || npairs < 1 || (npairs & 1) ||
+        epoch == 0)
+        return Q27_ERR_INVALID_ARG;
+    if (npairs > INT_MAX) return Q27_ERR_TOO_LARGE;
+    return launch_merge_pushed(mailbox, world, npairs, epoch, out, static_cast<cudaStream_t>(stream));
 }
 
 int q27_kv_dequant(const void* const* tab, int kvk, int row0, int nrows, int n_kv_heads,

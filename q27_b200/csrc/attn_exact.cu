@@ -5,6 +5,7 @@
 // and k_attn_prefill_T, src/prefill.cu:2293-2388). The tensor-core kernels are checked
 // against them on the GPU and against the CPU oracle.
 #include "common.cuh"
+#include "p2p_exchange.cuh"
 
 namespace q27b {
 
@@ -180,6 +181,60 @@ k_combine(const __grid_constant__ DevBatch b, float* __restrict__ partial_out, i
     }
 }
 
+// k_combine<false> with the exchange fused in: the merged {m, l, acc} row of (slot, lane,
+// head) goes straight into slot `rank` of EVERY rank's mailbox (peer stores over NVLink),
+// and the last block publishes the epoch. Padded lanes get sentinel rows like everyone else.
+__global__ void __launch_bounds__(256)
+k_combine_push(const __grid_constant__ DevBatch b, const __grid_constant__ Peers peers,
+               int lanes_stride) {
+    const int h = blockIdx.x, t = blockIdx.y, slot = blockIdx.z;
+    const DevSlot& S = b.s[slot];
+    const size_t row = peers.slot_floats() + (((size_t)slot * lanes_stride + t) * b.n_q + h) * PART;
+    __shared__ float s_m, s_l;
+    __shared__ float s_w[Q27_MAX_SPLITS];
+    if (t >= S.ntok) {
+        for (int i = threadIdx.x; i < PART; i += blockDim.x) {
+            const float v = i == 0 ? NEG_SENTINEL : 0.f;
+            for (int r = 0; r < peers.world; r++) reinterpret_cast<float*>(peers.box[r])[row + i] = v;
+        }
+    } else {
+        const float* pp = S.scratch + ((size_t)t * b.n_q + h) * b.nsplit * PART;
+        if (threadIdx.x < 32) {
+            float mg = NEG_SENTINEL;
+            for (int sp = threadIdx.x; sp < b.nsplit; sp += 32) mg = fmaxf(mg, pp[(size_t)sp * PART]);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, off));
+            float lg = 0.f;
+            for (int sp = threadIdx.x; sp < b.nsplit; sp += 32) {
+                const float ms = pp[(size_t)sp * PART];
+                const float w = ms == NEG_SENTINEL ? 0.f : expf(ms - mg);
+                s_w[sp] = w;
+                lg += pp[(size_t)sp * PART + 1] * w;
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) lg += __shfl_xor_sync(0xffffffffu, lg, off);
+            if (threadIdx.x == 0) { s_m = mg; s_l = lg; }
+        }
+        __syncthreads();
+        for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+            float a = 0.f;
+#pragma unroll 8
+            for (int sp = 0; sp < b.nsplit; sp++) {
+                const float w = s_w[sp];
+                const float v = pp[(size_t)sp * PART + 2 + d];
+                a += w != 0.f ? v * w : 0.f;
+            }
+            for (int r = 0; r < peers.world; r++) reinterpret_cast<float*>(peers.box[r])[row + 2 + d] = a;
+        }
+        if (threadIdx.x == 0)
+            for (int r = 0; r < peers.world; r++) {
+                reinterpret_cast<float*>(peers.box[r])[row] = s_m;
+                reinterpret_cast<float*>(peers.box[r])[row + 1] = s_l;
+            }
+    }
+    xchg_publish(peers, gridDim.x * gridDim.y * gridDim.z);
+}
+
 // parts: [nparts][npairs][258] -> out [npairs][256] normalised
 __global__ void __launch_bounds__(256)
 k_merge(const float* __restrict__ parts, int nparts, int64_t npairs, float* __restrict__ out) {
@@ -282,6 +337,13 @@ int launch_combine(const DevBatch& b, float* partial_out, int lanes_stride, cuda
         dim3 grid(b.n_q, b.max_ntok, b.nslots);
         k_combine<true><<<grid, 256, 0, st>>>(b, nullptr, b.max_ntok);
     }
+    Q27_CUDA_TRY(cudaGetLastError());
+    return Q27_OK;
+}
+
+int launch_combine_push(const DevBatch& b, const Peers& peers, int lanes_stride, cudaStream_t st) {
+    dim3 grid(b.n_q, lanes_stride, b.nslots);
+    k_combine_push<<<grid, 256, 0, st>>>(b, peers, lanes_stride);
     Q27_CUDA_TRY(cudaGetLastError());
     return Q27_OK;
 }

@@ -25,7 +25,9 @@
 
 namespace q27b {
 
-extern __device__ int g_wait_timeout_flag;
+// without relocatable device code a __device__ variable is private to its translation unit:
+// this file keeps its own timeout flag and the library's reader ORs them together
+__device__ int g_umma_timeout_flag = 0;
 #ifdef Q27_TRACE
 // timing experiments only: cycles spent waiting, summed over CTAs, by (role, barrier)
 __device__ unsigned long long g_umma_trace[16];
@@ -96,7 +98,7 @@ __device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
         if (bar_try(bar, parity)) return true;
         if (i > 2048) __nanosleep(64);
     }
-    atomicExch(&g_wait_timeout_flag, 2);
+    atomicExch(&g_umma_timeout_flag, 2);
     return false;
 }
 __device__ __forceinline__ void fence_async_smem() {
@@ -840,6 +842,11 @@ extern "C" int q27_debug_umma_events(long long* out) {
     return 0;
 }
 #endif
+
+int read_umma_timeout_flag(int* out) {
+    Q27_CUDA_TRY(cudaMemcpyFromSymbol(out, g_umma_timeout_flag, sizeof(int)));
+    return Q27_OK;
+}
 
 int launch_verify_umma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool* done) {
     *done = false;

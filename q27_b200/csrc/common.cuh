@@ -132,6 +132,14 @@ __host__ __device__ __forceinline__ int row_bytes_of(int kvk, int n_kv) {
 int launch_exact_partials(const DevBatch& b, int kvk, cudaStream_t st);
 int launch_combine(const DevBatch& b, float* partial_out, int lanes_stride, cudaStream_t st);
 int launch_merge(const float* parts, int nparts, int64_t npairs, float* out, cudaStream_t st);
+// peer-memory exchange of partials (p2p_exchange.cu)
+size_t xchg_mailbox_bytes(int world, int64_t npairs);
+struct Peers;
+int launch_combine_push(const DevBatch& b, const Peers& peers, int lanes_stride, cudaStream_t st);
+int launch_merge_pushed(const void* box, int world, int64_t npairs, uint32_t epoch, float* out,
+                        cudaStream_t st);
+int read_xchg_timeout_flag(int* out);
+int read_umma_timeout_flag(int* out);
 int launch_prefill_exact(const float* qT, int q_stride, int q_row, const void* const* ktab,
                          const void* const* vtab, float* outT, int out_row, int base_pos, int t0,
                          int SB, int n_q, int n_kv, float scale, cudaStream_t st, int kvk);

@@ -1,0 +1,83 @@
+// Exchange of split-KV partials between the GPUs of one node through peer memory.
+//
+// Every rank owns a MAILBOX in its own HBM, mapped into the other ranks' processes with CUDA
+// IPC: [2 parities][world][npairs][258] floats, then [2][world] release flags. A rank's
+// combine kernel stores each merged partial row into slot `rank` of every mailbox with plain
+// peer stores the moment it is formed and, once all rows are out, writes the step's epoch
+// into its flag in every mailbox. The merge kernel of each rank waits (bounded) until all
+// `world` flags of the step's parity hold the epoch and merges what its own memory then
+// holds. Nothing but these 258-float rows ever crosses NVLink, there is no host involvement
+// per step, and no collective library call. Two parities: a rank can be one step ahead of a
+// slow peer (it cannot be two ahead: its own merge of step e+1 needs the peer's push of e+1,
+// which the peer issues after its merge of step e).
+#include "p2p_exchange.cuh"
+
+namespace q27b {
+
+namespace {
+
+__device__ int g_xchg_timeout_flag = 0;
+
+// box: this rank's own mailbox. out [npairs][256] normalised.
+__global__ void __launch_bounds__(256)
+k_merge_pushed(const uint8_t* __restrict__ box, int world, int64_t npairs, uint32_t epoch,
+               float* __restrict__ out) {
+    const int par = epoch & 1;
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) s_ok = 1;
+    __syncthreads();
+    if (threadIdx.x < world) {
+        const volatile uint32_t* f = reinterpret_cast<const volatile uint32_t*>(
+            box + xchg_flags_offset(world, npairs) + ((size_t)par * world + threadIdx.x) * XCHG_FLAG_STRIDE);
+        bool got = false;
+        for (int i = 0; i < (1 << 21); i++) {          // about half a second, then give up
+            if (*f == epoch) { got = true; break; }
+            __nanosleep(200);
+        }
+        if (!got) { s_ok = 0; atomicExch(&g_xchg_timeout_flag, 4); }
+        __threadfence_system();
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    const int64_t w = blockIdx.x;
+    const float* parts = reinterpret_cast<const float*>(box) + (size_t)par * xchg_data_floats(world, npairs);
+    float mg = NEG_SENTINEL;
+    for (int s = 0; s < world; s++) mg = fmaxf(mg, __ldcg(parts + ((size_t)s * npairs + w) * PART));
+    float lg = 0.f;
+    for (int s = 0; s < world; s++) {
+        const float* pp = parts + ((size_t)s * npairs + w) * PART;
+        const float ms = __ldcg(pp);
+        if (ms != NEG_SENTINEL) lg += __ldcg(pp + 1) * expf(ms - mg);
+    }
+    const float inv = lg > 0.f ? 1.0f / lg : 0.f;
+    for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+        float a = 0.f;
+        for (int s = 0; s < world; s++) {
+            const float* pp = parts + ((size_t)s * npairs + w) * PART;
+            const float ms = __ldcg(pp);
+            if (ms != NEG_SENTINEL) a += __ldcg(pp + 2 + d) * expf(ms - mg);
+        }
+        out[(size_t)w * HD + d] = a * inv;
+    }
+}
+
+} // namespace
+
+size_t xchg_mailbox_bytes(int world, int64_t npairs) {
+    return xchg_counter_offset(world, npairs) + 256;
+}
+
+int launch_merge_pushed(const void* box, int world, int64_t npairs, uint32_t epoch, float* out,
+                        cudaStream_t st) {
+    k_merge_pushed<<<(unsigned)npairs, 256, 0, st>>>(static_cast<const uint8_t*>(box), world, npairs,
+                                                     epoch, out);
+    Q27_CUDA_TRY(cudaGetLastError());
+    return Q27_OK;
+}
+
+int read_xchg_timeout_flag(int* out) {
+    Q27_CUDA_TRY(cudaMemcpyFromSymbol(out, g_xchg_timeout_flag, sizeof(int)));
+    return Q27_OK;
+}
+
+} // namespace q27b

@@ -15,7 +15,8 @@ import torch
 import torch.distributed as dist
 
 from . import _lib as L
-from .attn import FD_ST, attn_decode_partial, attn_merge_partials
+from .attn import (FD_ST, attn_decode_partial, attn_decode_partial_push, attn_merge_partials,
+                   attn_merge_pushed)
 
 KV_PAGE = L.KV_PAGE
 
@@ -88,3 +89,65 @@ def sharded_decode(slots, ex: PartialExchange, out: torch.Tensor, q_stride: int,
     all_gather_partials(ex, group)
     attn_merge_partials(ex.gathered, ex.world, ex.npairs, out, st=st)
     return out
+
+
+class PeerMailboxes:
+    """Peer-memory exchange of partials: one mailbox per rank in that rank's HBM, mapped into
+    every other rank's process with CUDA IPC (the ranks are the processes of one node, one
+    GPU each). A step is `attn_decode_partial_push` (partials + combine, then peer stores of
+    the 258-float rows into every mailbox and a release flag) followed by `attn_merge_pushed`
+    (device-side bounded wait for all flags, then the merge): no collective call, no host
+    synchronisation. The handles are exchanged once, with `all_gather_object`."""
+
+    def __init__(self, nslots: int, lanes: int, n_q: int, group=None):
+        import ctypes as C
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world > L.MAX_RANKS:
+            raise ValueError(f"at most {L.MAX_RANKS} ranks share a split")
+        self.nslots, self.lanes, self.n_q = nslots, lanes, n_q
+        self.npairs = nslots * lanes * n_q
+        self.epoch = 0
+        nbytes = L.lib().q27_xchg_mailbox_bytes(self.world, self.npairs)
+        own, handle = C.c_void_p(), C.create_string_buffer(L.XCHG_HANDLE_BYTES)
+        L.check(L.lib().q27_xchg_alloc(nbytes, C.byref(own), handle), "q27_xchg_alloc")
+        self.own = own.value
+        handles = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(handles, handle.raw, group=group)
+        self.boxes, self._opened = [], []
+        for r in range(self.world):
+            if r == self.rank:
+                self.boxes.append(self.own)
+                continue
+            ptr = C.c_void_p()
+            L.check(L.lib().q27_xchg_open(C.create_string_buffer(handles[r], L.XCHG_HANDLE_BYTES),
+                                          C.byref(ptr)), "q27_xchg_open")
+            self.boxes.append(ptr.value)
+            self._opened.append(ptr.value)
+        if self.world > 1:
+            dist.barrier(group=group)         # every mailbox is mapped before anyone pushes
+
+    def bytes_per_rank(self) -> int:
+        return self.npairs * FD_ST * 4
+
+    def decode(self, slots, out: torch.Tensor, q_stride: int, n_kv_heads: int, scale: float,
+               kvk: int, st=None) -> torch.Tensor:
+        """One sharded decode / verify step; `out` [npairs][256] normalised on every rank."""
+        self.epoch += 1
+        attn_decode_partial_push(slots, self.lanes, q_stride, self.n_q, n_kv_heads, L.HEAD_DIM,
+                                 scale, self.boxes, self.rank, self.epoch, st=st, kvk=kvk)
+        attn_merge_pushed(self.own, self.world, self.npairs, self.epoch, out, st=st)
+        return out
+
+    def close(self, group=None):
+        """Unmap the peers' mailboxes, then (after a barrier) free the own one."""
+        torch.cuda.synchronize()
+        for ptr in self._opened:
+            L.check(L.lib().q27_xchg_close(ptr), "q27_xchg_close")
+        self._opened = []
+        if self.world > 1:
+            dist.barrier(group=group)
+        if self.own:
+            L.check(L.lib().q27_xchg_free(self.own), "q27_xchg_free")
+            self.own = None

@@ -153,6 +153,51 @@ def test_kv_split_partials_merge(oracle, cuda, kvk, nshards):
     assert synth.tolerance_ok(got, full)[0]
 
 
+@pytest.mark.parametrize("kvk", KINDS)
+def test_kv_split_through_mailboxes(oracle, cuda, kvk):
+    """The peer-memory exchange with both 'ranks' on this one GPU: two mailboxes, each rank's
+    push lands in both (plain stores here, peer stores across GPUs), flags carry the epoch,
+    and each rank's merge equals attention over the whole cache. Pushes and merges are
+    separate launches in stream order, so no kernel ever waits on one that has not run.
+    Three steps exercise both parities and the reuse of a parity."""
+    import ctypes as C
+    lib = Q._lib.lib()
+    world, lanes_stride = 2, 4
+    rows = 64 * 6
+    npairs = lanes_stride * 24
+    boxes = []
+    for _ in range(world):
+        ptr = C.c_void_p()
+        Q._lib.check(lib.q27_xchg_alloc(lib.q27_xchg_mailbox_bytes(world, npairs), C.byref(ptr), None),
+                     "q27_xchg_alloc")
+        boxes.append(ptr.value)
+    try:
+        for epoch in (1, 2, 3):
+            pos = [rows - 1, rows // 2 + epoch, 5 * epoch]
+            c = synth.make_case(oracle, kvk, rows=rows, pos=pos, seed=90 + epoch,
+                                outlier_frac=OUTLIERS[kvk])
+            full = synth.scale_out(c, oracle.attn_decode(c.q, c.k, c.v, kvk, c.pos))
+            keep = []
+            for r in range(world):
+                dc = DeviceCase(c, cuda, row_lo=r * rows // 2, row_hi=(r + 1) * rows // 2)
+                keep.append(dc)
+                Q.attn_decode_partial_push([dc.slot()], lanes_stride, synth.Q_STRIDE, 24, 4, 256,
+                                           SCALE, boxes, r, epoch, kvk=kvk)
+            for r in range(world):
+                out = torch.empty((npairs, 256), device=cuda)
+                Q.attn_merge_pushed(boxes[r], world, npairs, epoch, out)
+                torch.cuda.synchronize()
+                got = synth.scale_out(c, out.cpu().numpy().reshape(lanes_stride, -1)[: len(pos)])
+                assert synth.tolerance_ok(got, full)[0]
+        flag = C.c_int(-1)
+        Q._lib.check(lib.q27_wait_timeout_flag(C.byref(flag)), "q27_wait_timeout_flag")
+        assert flag.value == 0
+    finally:
+        torch.cuda.synchronize()
+        for b in boxes:
+            Q._lib.check(lib.q27_xchg_free(b), "q27_xchg_free")
+
+
 @pytest.mark.skipif(not REF_GPU_SO.exists(), reason="oracle/_ref not built")
 @pytest.mark.parametrize("kvk", KINDS)
 def test_against_reference_kernels_on_this_gpu(oracle, cuda, kvk):

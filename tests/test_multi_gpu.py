@@ -1,6 +1,7 @@
 """KV-sequence sharding across real GPUs (skipped on a single-GPU box): two NCCL ranks, each
-holding a page-aligned half of every slot's cache, exchange their 258-float partials with
-one all-gather and merge; the result must equal attention over the whole cache (oracle).
+holding a page-aligned half of every slot's cache, exchange their 258-float partials -- once with an NCCL
+all-gather, once through peer-memory mailboxes -- and merge; the result must equal attention
+over the whole cache (oracle).
 Run with `pytest -m gpu` on a box with >= 2 GPUs."""
 import os
 import socket
@@ -48,7 +49,18 @@ def _rank(rank, world, port, kvk, q, k, v, pos, ranges, ret):
     for _ in range(2):
         qd.sharded_decode([slot], ex, out, 512, 4, 1.0 / 16.0, kvk)
     torch.cuda.synchronize()
-    ret.put((rank, out.cpu().numpy()))
+    # the same steps through peer memory: partials pushed into every rank's mailbox over
+    # NVLink, flags, device-side wait, merge (no collective call per step)
+    boxes = qd.PeerMailboxes(1, lanes, 24)
+    out2 = torch.zeros((lanes * 24, 256), device=dev)
+    for _ in range(3):
+        boxes.decode([slot], out2, 512, 4, 1.0 / 16.0, kvk)
+    torch.cuda.synchronize()
+    import ctypes as C
+    flag = C.c_int(-1)
+    Q._lib.check(Q._lib.lib().q27_wait_timeout_flag(C.byref(flag)), "q27_wait_timeout_flag")
+    ret.put((rank, out.cpu().numpy(), out2.cpu().numpy(), flag.value))
+    boxes.close()
     dist.barrier()
     dist.destroy_process_group()
 
@@ -72,9 +84,12 @@ def test_two_gpu_kv_split_matches_full_attention(oracle, kvk):
              for r in range(2)]
     for p in procs:
         p.start()
-    outs = dict(ret.get(timeout=300) for _ in range(2))
+    got = [ret.get(timeout=300) for _ in range(2)]
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for r in range(2):      # every rank ends up with the merged result
-        assert synth.tolerance_ok(outs[r].reshape(len(pos), -1), full)[0]
+    for rank, via_nccl, via_peers, flag in got:      # every rank ends up with the merged result
+        assert synth.tolerance_ok(via_nccl.reshape(len(pos), -1), full)[0]
+        assert flag == 0                             # no device-side wait ran out
+        # same partials, same merge arithmetic: the two exchanges agree to the last bit
+        assert np.array_equal(via_nccl, via_peers)
