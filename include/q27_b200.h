@@ -245,6 +245,24 @@ int q27_kv_store_T_t3(const float* kT, const float* vT, void* const* ktab, void*
 int q27_wht_T(float* x, int n_heads, int head_dim, int head_stride, int row_stride, int T, int inv,
               void* stream);
 
+/* Lane forms of the three calls above, for the draft tokens of a decode / verify round:
+ * lane t's rows come from k->p[t] / v->p[t] (fp32 [n_kv_heads*256]) and go to cache row
+ * *pos->p[t] (read on the device), or x->p[t] is rotated in place.
+ * Replaces q27k::kv_store3 (src/spec3.cuh:87-88, src/spec3.cu:512-535). */
+int q27_kv_store3(const q27_CP3* k, const q27_CP3* v, void* const* ktab, void* const* vtab,
+                  const q27_IP3* pos, int rowlen, void* stream, int ntok, int fp8);
+/* Replaces q27k::kv_store_t3 (src/spec3.cuh:98-99, src/spec3.cu:556-588) for Q27_KV_T3; the
+ * other K legs (turbo3v, turbo5k, int8-g64) are refused. Blocks byte-identical to the
+ * reference's serial CPU codec, as for q27_kv_store_T_t3. */
+int q27_kv_store_t3(const q27_CP3* k, const q27_CP3* v, void* const* ktab, void* const* vtab,
+                    const q27_IP3* pos, int n_kv_heads, int head_dim, void* stream, int ntok,
+                    int kvk);
+/* Replaces q27k::wht3 (src/spec3.cuh:106-107, src/spec3.cu:595-614): per-128-group rotation
+ * of the first head_dim floats of each of n_heads heads (stride floats apart), bitwise equal
+ * to the CPU t3_fwht / t3_fwht_inv. */
+int q27_wht3(const q27_P3* x, int n_heads, int head_dim, int stride, int inv, void* stream,
+             int ntok);
+
 /* mk_tab (src/test_kernels.cu:27-36): fill a DEVICE table of ceil(rows/64) entries with
  * identity page pointers over a contiguous buffer. d_tab is caller-allocated. */
 int q27_mk_tab(const void* base, size_t row_bytes, int rows, void** d_tab, void* stream);

@@ -10,6 +10,9 @@
 //   q27k::kv_store_T       src/blocks.cuh:56-57     -> q27_kv_store_T
 //   q27k::kv_store_T_t3    src/blocks.cuh:63-65     -> q27_kv_store_T_t3
 //   q27k::wht_T            src/blocks.cuh:76-81     -> q27_wht_T
+//   q27k::kv_store3        src/spec3.cuh:87-88      -> q27_kv_store3
+//   q27k::kv_store_t3      src/spec3.cuh:98-99      -> q27_kv_store_t3
+//   q27k::wht3             src/spec3.cuh:106-107    -> q27_wht3
 //
 // Error behaviour is the reference's: these functions return void and a failure is fatal
 // (message + exit(1), CUDA_CHECK in src/cuda_common.h:8-16). Kinds the engine does not read
@@ -115,6 +118,32 @@ inline void wht_T(float* x, int n_heads, int head_dim, int head_stride, int row_
                   bool inv, cudaStream_t st) {
     q27_shim_check(q27_wht_T(x, n_heads, head_dim, head_stride, row_stride, T, inv ? 1 : 0, st),
                    "wht_T");
+}
+
+inline void kv_store3(CP3 k, CP3 v, void* const* ktab, void* const* vtab, IP3 pos, int rowlen,
+                      cudaStream_t st = 0, int ntok = 3, bool fp8 = false) {
+    q27_shim_check(q27_kv_store3(reinterpret_cast<const q27_CP3*>(&k),
+                                 reinterpret_cast<const q27_CP3*>(&v), ktab, vtab,
+                                 reinterpret_cast<const q27_IP3*>(&pos), rowlen, st, ntok,
+                                 fp8 ? 1 : 0),
+                   "kv_store3");
+}
+
+inline void kv_store_t3(CP3 k, CP3 v, void* const* ktab, void* const* vtab, IP3 pos,
+                        int n_kv_heads, int head_dim, cudaStream_t st = 0, int ntok = 3,
+                        int kvk = KV_T3) {
+    q27_shim_check(q27_kv_store_t3(reinterpret_cast<const q27_CP3*>(&k),
+                                   reinterpret_cast<const q27_CP3*>(&v), ktab, vtab,
+                                   reinterpret_cast<const q27_IP3*>(&pos), n_kv_heads, head_dim, st,
+                                   ntok, kvk),
+                   "kv_store_t3");
+}
+
+inline void wht3(P3 x, int n_heads, int head_dim, int stride, bool inv, cudaStream_t st = 0,
+                 int ntok = 3) {
+    q27_shim_check(q27_wht3(reinterpret_cast<const q27_P3*>(&x), n_heads, head_dim, stride,
+                            inv ? 1 : 0, st, ntok),
+                   "wht3");
 }
 
 } // namespace q27k

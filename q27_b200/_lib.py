@@ -81,6 +81,10 @@ SIGNATURES = {
     "q27_kv_store_T": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _i]),
     "q27_kv_store_T_t3": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _i]),
     "q27_wht_T": (_i, [_vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "q27_kv_store3": (_i, [C.POINTER(P3), C.POINTER(P3), _vp, _vp, C.POINTER(P3), _i, _vp, _i, _i]),
+    "q27_kv_store_t3": (_i, [C.POINTER(P3), C.POINTER(P3), _vp, _vp, C.POINTER(P3), _i, _i, _vp, _i,
+                             _i]),
+    "q27_wht3": (_i, [C.POINTER(P3), _i, _i, _i, _i, _vp, _i]),
     "q27_mk_tab": (_i, [_vp, _sz, _i, _vp, _vp]),
     "q27_kvpool_create": (_vp, [_sz, _sz, _sz, _sz]),
     "q27_kvpool_destroy": (None, [_vp]),

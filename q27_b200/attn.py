@@ -181,3 +181,29 @@ def wht_T(x, n_heads, head_dim, head_stride, row_stride, T, inv, st=None):
     """Per-128-group WHT rotate in place over a flat [T][row_stride] buffer."""
     L.check(L.lib().q27_wht_T(x.data_ptr(), n_heads, head_dim, head_stride, row_stride, T,
                               int(inv), stream_ptr(st)), "q27_wht_T")
+
+
+def kv_store3(k_lanes, v_lanes, ktab, vtab, pos_lanes, rowlen, st=None, fp8=False):
+    """Lane form of kv_store_T: lane t's fp32 K / V row to cache row *pos_lanes[t]."""
+    import ctypes as C
+    k, v, p = _p3(k_lanes), _p3(v_lanes), _p3(pos_lanes)
+    L.check(L.lib().q27_kv_store3(C.byref(k), C.byref(v), ktab.data_ptr(), vtab.data_ptr(),
+                                  C.byref(p), rowlen, stream_ptr(st), len(k_lanes), int(fp8)),
+            "q27_kv_store3")
+
+
+def kv_store_t3(k_lanes, v_lanes, ktab, vtab, pos_lanes, n_kv_heads, head_dim, st=None, kvk=2):
+    """Lane form of kv_store_T_t3 (turbo3 encoder)."""
+    import ctypes as C
+    k, v, p = _p3(k_lanes), _p3(v_lanes), _p3(pos_lanes)
+    L.check(L.lib().q27_kv_store_t3(C.byref(k), C.byref(v), ktab.data_ptr(), vtab.data_ptr(),
+                                    C.byref(p), n_kv_heads, head_dim, stream_ptr(st),
+                                    len(k_lanes), kvk), "q27_kv_store_t3")
+
+
+def wht3(x_lanes, n_heads, head_dim, stride, inv, st=None):
+    """Lane form of wht_T: rotate each lane's heads in place."""
+    import ctypes as C
+    x = _p3(x_lanes)
+    L.check(L.lib().q27_wht3(C.byref(x), n_heads, head_dim, stride, int(inv), stream_ptr(st),
+                             len(x_lanes)), "q27_wht3")

@@ -429,6 +429,40 @@ int q27_wht_T(float* x, int n_heads, int head_dim, int head_stride, int row_stri
                         static_cast<cudaStream_t>(stream));
 }
 
+int q27_kv_store3(const q27_CP3* k, const q27_CP3* v, void* const* ktab, void* const* vtab,
+                  const q27_IP3* pos, int rowlen, void* stream, int ntok, int fp8) {
+    if (!k || !v || !pos || !ktab || !vtab || ntok < 0 || ntok > Q27_MAX_LANES || rowlen < HD ||
+        rowlen % HD)
+        return Q27_ERR_INVALID_ARG;
+    for (int t = 0; t < ntok; t++)
+        if (!k->p[t] || !v->p[t] || !pos->p[t]) return Q27_ERR_INVALID_ARG;
+    return launch_kv_store3(k->p, v->p, pos->p, ktab, vtab, rowlen / HD, ntok,
+                            static_cast<cudaStream_t>(stream), fp8 ? Q27_KV_FP8 : Q27_KV_F16);
+}
+
+int q27_kv_store_t3(const q27_CP3* k, const q27_CP3* v, void* const* ktab, void* const* vtab,
+                    const q27_IP3* pos, int n_kv_heads, int head_dim, void* stream, int ntok,
+                    int kvk) {
+    if (kvk != Q27_KV_T3) return Q27_ERR_UNSUPPORTED_KIND; // turbo3v / turbo5k K legs: refused
+    if (head_dim != HD || n_kv_heads < 1) return Q27_ERR_UNSUPPORTED_WIDTH;
+    if (!k || !v || !pos || !ktab || !vtab || ntok < 0 || ntok > Q27_MAX_LANES)
+        return Q27_ERR_INVALID_ARG;
+    for (int t = 0; t < ntok; t++)
+        if (!k->p[t] || !v->p[t] || !pos->p[t]) return Q27_ERR_INVALID_ARG;
+    return launch_kv_store3(k->p, v->p, pos->p, ktab, vtab, n_kv_heads, ntok,
+                            static_cast<cudaStream_t>(stream), Q27_KV_T3);
+}
+
+int q27_wht3(const q27_P3* x, int n_heads, int head_dim, int stride, int inv, void* stream,
+             int ntok) {
+    if (head_dim != HD) return Q27_ERR_UNSUPPORTED_WIDTH;
+    if (!x || n_heads < 0 || ntok < 0 || ntok > Q27_MAX_LANES || stride < HD)
+        return Q27_ERR_INVALID_ARG;
+    for (int t = 0; t < ntok; t++)
+        if (!x->p[t]) return Q27_ERR_INVALID_ARG;
+    return launch_wht3(x->p, n_heads, stride, ntok, inv != 0, static_cast<cudaStream_t>(stream));
+}
+
 int q27_mk_tab(const void* base, size_t row_bytes, int rows, void** d_tab, void* stream) {
     if (!base || !d_tab || row_bytes == 0 || rows < 0) return Q27_ERR_INVALID_ARG;
     return launch_mk_tab(base, row_bytes, rows, d_tab, static_cast<cudaStream_t>(stream));

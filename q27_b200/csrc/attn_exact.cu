@@ -129,6 +129,7 @@ k_exact_partial(const __grid_constant__ DevBatch b) {
 template <bool NORMALISE>
 __global__ void __launch_bounds__(256)
 k_combine(const __grid_constant__ DevBatch b, float* __restrict__ partial_out, int lanes_stride) {
+    pdl_wait();                  // the partials come from the kernel before this one
     const int h = blockIdx.x, t = blockIdx.y, slot = blockIdx.z;
     const DevSlot& S = b.s[slot];
     if (t >= S.ntok) {
@@ -187,6 +188,8 @@ k_combine(const __grid_constant__ DevBatch b, float* __restrict__ partial_out, i
 __global__ void __launch_bounds__(256)
 k_combine_push(const __grid_constant__ DevBatch b, const __grid_constant__ Peers peers,
                int lanes_stride) {
+    pdl_trigger();               // the merge kernel may be scheduled; it waits for this grid
+    pdl_wait();                  // the partials come from the kernel before this one
     const int h = blockIdx.x, t = blockIdx.y, slot = blockIdx.z;
     const DevSlot& S = b.s[slot];
     const size_t row = peers.slot_floats() + (((size_t)slot * lanes_stride + t) * b.n_q + h) * PART;
@@ -332,10 +335,10 @@ int launch_exact_partials(const DevBatch& b, int kvk, cudaStream_t st) {
 int launch_combine(const DevBatch& b, float* partial_out, int lanes_stride, cudaStream_t st) {
     if (partial_out) {
         dim3 grid(b.n_q, lanes_stride, b.nslots);
-        k_combine<false><<<grid, 256, 0, st>>>(b, partial_out, lanes_stride);
+        Q27_CUDA_TRY(launch_pdl(k_combine<false>, grid, dim3(256), 0, st, b, partial_out, lanes_stride));
     } else {
         dim3 grid(b.n_q, b.max_ntok, b.nslots);
-        k_combine<true><<<grid, 256, 0, st>>>(b, nullptr, b.max_ntok);
+        Q27_CUDA_TRY(launch_pdl(k_combine<true>, grid, dim3(256), 0, st, b, (float*)nullptr, b.max_ntok));
     }
     Q27_CUDA_TRY(cudaGetLastError());
     return Q27_OK;
@@ -343,7 +346,7 @@ int launch_combine(const DevBatch& b, float* partial_out, int lanes_stride, cuda
 
 int launch_combine_push(const DevBatch& b, const Peers& peers, int lanes_stride, cudaStream_t st) {
     dim3 grid(b.n_q, lanes_stride, b.nslots);
-    k_combine_push<<<grid, 256, 0, st>>>(b, peers, lanes_stride);
+    Q27_CUDA_TRY(launch_pdl(k_combine_push, grid, dim3(256), 0, st, b, peers, lanes_stride));
     Q27_CUDA_TRY(cudaGetLastError());
     return Q27_OK;
 }

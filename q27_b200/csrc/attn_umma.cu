@@ -760,6 +760,7 @@ template <int KVK>
 __global__ void __launch_bounds__(UMMA_THREADS, 1)
 k_verify_umma(const __grid_constant__ DevBatch b) {
     extern __shared__ uint8_t smem_raw[];
+    pdl_trigger();               // the combine kernel may be scheduled; it waits for this grid
     const DevSlot& S = b.s[blockIdx.z];
     int max_len = 0;
     for (int u = 0; u < S.ntok; u++)

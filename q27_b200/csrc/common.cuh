@@ -130,6 +130,28 @@ __host__ __device__ __forceinline__ int row_bytes_of(int kvk, int n_kv) {
 // ---- launch entry points implemented per translation unit -----------------------------
 // exact (fp32 scalar) family
 int launch_exact_partials(const DevBatch& b, int kvk, cudaStream_t st);
+// Programmatic dependent launch: the kernel may be scheduled while the kernel before it in
+// the stream is still running (once all of that one's CTAs have called pdl_trigger or
+// exited); it must call pdl_wait before it touches anything the earlier kernel writes.
+// Hides the launch latency of the short combine / merge kernels behind the partial kernel.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 int launch_combine(const DevBatch& b, float* partial_out, int lanes_stride, cudaStream_t st);
 int launch_merge(const float* parts, int nparts, int64_t npairs, float* out, cudaStream_t st);
 // peer-memory exchange of partials (p2p_exchange.cu)
@@ -147,6 +169,10 @@ int launch_kv_dequant(const void* const* tab, int kvk, int row0, int nrows, int 
                       cudaStream_t st);
 int launch_kv_store_T(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
                       int base_pos, int n_kv, int T, cudaStream_t st, int kvk);
+int launch_kv_store3(const float* const* k, const float* const* v, const int* const* pos,
+                     void* const* ktab, void* const* vtab, int n_kv, int ntok, cudaStream_t st,
+                     int kvk);
+int launch_wht3(float* const* x, int n_heads, int stride, int ntok, bool inv, cudaStream_t st);
 int launch_wht_T(float* x, int n_heads, int head_stride, int row_stride, int T, bool inv,
                  cudaStream_t st);
 int launch_mk_tab(const void* base, size_t row_bytes, int rows, void** d_tab, cudaStream_t st);

@@ -469,6 +469,7 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
     uint8_t* ring = smem + 256;
 
     DTRACE_MIN(0);
+    pdl_trigger();               // the combine kernel may be scheduled; it waits for this grid
     const int t = blockIdx.x, sp = blockIdx.y;
     const int slot = blockIdx.z / (b.n_kv / F::KVH), kvg = blockIdx.z % (b.n_kv / F::KVH);
     const DevSlot& S = b.s[slot];

@@ -181,6 +181,64 @@ k_wht_T(float* __restrict__ x, int n_heads, int head_stride, int row_stride, int
     }
 }
 
+// ---- lane forms: one row per draft lane, source rows and positions behind lane bundles ----
+struct LaneRows {
+    const float* k[Q27_MAX_LANES];
+    const float* v[Q27_MAX_LANES];
+    const int* pos[Q27_MAX_LANES];
+};
+struct LaneVecs {
+    float* x[Q27_MAX_LANES];
+};
+
+// grid (groups per row x 2 sides / ST_WARPS, ntok): lane t's K and V rows into cache row *pos[t]
+__global__ void __launch_bounds__(ST_WARPS * 32)
+k_kv_store3_t3(const __grid_constant__ LaneRows L, void* const* ktab, void* const* vtab, int n_kv) {
+    __shared__ float xs[ST_WARPS][128];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.y, gpr = n_kv * 2;
+    const int w = blockIdx.x * ST_WARPS + warp;          // (group, side)
+    if (w >= gpr * 2) return;
+    const int side = w & 1, gi = w >> 1;
+    const int p = __ldg(L.pos[t]);
+    uint8_t* page = static_cast<uint8_t*>((side ? vtab : ktab)[p >> PAGE_SHIFT]);
+    uint8_t* blk = page + ((size_t)(p & (PAGE - 1)) * gpr + gi) * T3_BLK;
+    t3_encode_group((side ? L.v[t] : L.k[t]) + (size_t)gi * 128, blk, xs[warp], lane);
+}
+
+template <bool FP8>
+__global__ void __launch_bounds__(256)
+k_kv_store3(const __grid_constant__ LaneRows L, void* const* ktab, void* const* vtab, int rowlen) {
+    const int e = blockIdx.x * blockDim.x + threadIdx.x, t = blockIdx.y;
+    if (e >= rowlen) return;
+    const int p = __ldg(L.pos[t]);
+    const size_t off = (size_t)(p & (PAGE - 1)) * rowlen + e;
+    if (FP8) {
+        static_cast<__nv_fp8_e4m3*>(ktab[p >> PAGE_SHIFT])[off] = __nv_fp8_e4m3(L.k[t][e]);
+        static_cast<__nv_fp8_e4m3*>(vtab[p >> PAGE_SHIFT])[off] = __nv_fp8_e4m3(L.v[t][e]);
+    } else {
+        static_cast<__half*>(ktab[p >> PAGE_SHIFT])[off] = __float2half_rn(L.k[t][e]);
+        static_cast<__half*>(vtab[p >> PAGE_SHIFT])[off] = __float2half_rn(L.v[t][e]);
+    }
+}
+
+// grid (heads x 2 groups / ST_WARPS, ntok): rotate the first 256 floats of every head in place
+template <bool INV>
+__global__ void __launch_bounds__(ST_WARPS * 32)
+k_wht3(const __grid_constant__ LaneVecs V, int n_heads, int stride) {
+    __shared__ float xs[ST_WARPS][128];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int w = blockIdx.x * ST_WARPS + warp;
+    if (w >= n_heads * 2) return;
+    float* g = V.x[blockIdx.y] + (size_t)(w >> 1) * stride + (w & 1) * 128;
+#pragma unroll
+    for (int i = 0; i < 4; i++) xs[warp][lane + 32 * i] = g[lane + 32 * i];
+    __syncwarp();
+    wht_group<INV>(xs[warp], lane);
+#pragma unroll
+    for (int i = 0; i < 4; i++) g[lane + 32 * i] = xs[warp][lane + 32 * i];
+}
+
 unsigned blocks_for(int64_t units, int per_block) {
     int64_t b = (units + per_block - 1) / per_block;
     return (unsigned)(b < 1 ? 1 : b > 148 * 16 ? 148 * 16 : b);
@@ -203,6 +261,42 @@ int launch_kv_store_T(const float* kT, const float* vT, void* const* ktab, void*
     } else {
         return Q27_ERR_UNSUPPORTED_KIND;
     }
+    Q27_CUDA_TRY(cudaGetLastError());
+    return Q27_OK;
+}
+
+int launch_kv_store3(const float* const* k, const float* const* v, const int* const* pos,
+                     void* const* ktab, void* const* vtab, int n_kv, int ntok, cudaStream_t st,
+                     int kvk) {
+    if (ntok == 0) return Q27_OK;
+    LaneRows L{};
+    for (int t = 0; t < ntok; t++) {
+        L.k[t] = k[t];
+        L.v[t] = v[t];
+        L.pos[t] = pos[t];
+    }
+    if (kvk == Q27_KV_T3) {
+        dim3 grid((n_kv * 4 + ST_WARPS - 1) / ST_WARPS, ntok);
+        k_kv_store3_t3<<<grid, ST_WARPS * 32, 0, st>>>(L, ktab, vtab, n_kv);
+    } else if (kvk == Q27_KV_FP8 || kvk == Q27_KV_F16) {
+        const int rowlen = n_kv * HD;
+        dim3 grid((rowlen + 255) / 256, ntok);
+        if (kvk == Q27_KV_FP8) k_kv_store3<true><<<grid, 256, 0, st>>>(L, ktab, vtab, rowlen);
+        else k_kv_store3<false><<<grid, 256, 0, st>>>(L, ktab, vtab, rowlen);
+    } else {
+        return Q27_ERR_UNSUPPORTED_KIND;
+    }
+    Q27_CUDA_TRY(cudaGetLastError());
+    return Q27_OK;
+}
+
+int launch_wht3(float* const* x, int n_heads, int stride, int ntok, bool inv, cudaStream_t st) {
+    if (ntok == 0 || n_heads == 0) return Q27_OK;
+    LaneVecs V{};
+    for (int t = 0; t < ntok; t++) V.x[t] = x[t];
+    dim3 grid((n_heads * 2 + ST_WARPS - 1) / ST_WARPS, ntok);
+    if (inv) k_wht3<true><<<grid, ST_WARPS * 32, 0, st>>>(V, n_heads, stride);
+    else k_wht3<false><<<grid, ST_WARPS * 32, 0, st>>>(V, n_heads, stride);
     Q27_CUDA_TRY(cudaGetLastError());
     return Q27_OK;
 }

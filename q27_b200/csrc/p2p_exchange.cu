@@ -22,6 +22,7 @@ __device__ int g_xchg_timeout_flag = 0;
 __global__ void __launch_bounds__(256)
 k_merge_pushed(const uint8_t* __restrict__ box, int world, int64_t npairs, uint32_t epoch,
                float* __restrict__ out) {
+    pdl_wait();                  // this rank's own rows come from the kernel before this one
     const int par = epoch & 1;
     __shared__ int s_ok;
     if (threadIdx.x == 0) s_ok = 1;
@@ -69,9 +70,8 @@ size_t xchg_mailbox_bytes(int world, int64_t npairs) {
 
 int launch_merge_pushed(const void* box, int world, int64_t npairs, uint32_t epoch, float* out,
                         cudaStream_t st) {
-    k_merge_pushed<<<(unsigned)npairs, 256, 0, st>>>(static_cast<const uint8_t*>(box), world, npairs,
-                                                     epoch, out);
-    Q27_CUDA_TRY(cudaGetLastError());
+    Q27_CUDA_TRY(launch_pdl(k_merge_pushed, dim3((unsigned)npairs), dim3(256), 0, st,
+                            static_cast<const uint8_t*>(box), world, npairs, epoch, out));
     return Q27_OK;
 }
 

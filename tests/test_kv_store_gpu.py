@@ -151,3 +151,55 @@ def test_store_vs_reference_device_encoder(oracle, cuda):
             hi = np.stack([(sg >> i) & 1 for i in range(8)], -1).reshape(len(x), 128)
             return low | (hi << 2)
         assert (idx(a) != idx(b)).mean() <= 0.002
+
+
+@pytest.mark.parametrize("kvk", [KV_F16, KV_FP8, KV_T3])
+def test_lane_form_stores_match_cpu_codec_bytewise(oracle, cuda, kvk):
+    """kv_store3 / kv_store_t3 (src/spec3.cu:512-588): one row per draft lane, row index
+    read on the device from the lane's position pointer; rows land at scattered positions
+    and every other row of the cache stays untouched."""
+    rows = 300
+    pos = [299, 3, 64, 127, 128, 250]
+    n = len(pos)
+    kf, vf = synth.make_kv(oracle, n, kvk, seed=29, outlier_frac=0.02 if kvk == KV_T3 else 0.0)
+    if kvk == KV_FP8:
+        kf *= 40.0
+    ks, vs, perm = empty_cache(cuda, kvk, rows, scatter=6)
+    kd = [torch.from_numpy(kf[t].reshape(-1).copy()).to(cuda) for t in range(n)]
+    vd = [torch.from_numpy(vf[t].reshape(-1).copy()).to(cuda) for t in range(n)]
+    pd = [torch.tensor([p], dtype=torch.int32, device=cuda) for p in pos]
+    if kvk == KV_T3:
+        Q.kv_store_t3(kd, vd, ks.tab, vs.tab, pd, 4, 256)
+    else:
+        Q.kv_store3(kd, vd, ks.tab, vs.tab, pd, 1024, fp8=kvk == KV_FP8)
+    torch.cuda.synchronize()
+    for side, src in ((ks, kf), (vs, vf)):
+        got = read_rows(side, kvk, rows, perm)
+        if kvk == KV_T3:
+            want = oracle.t3_quant(src.reshape(-1, 128)).reshape(n, 400)
+        elif kvk == KV_FP8:
+            want = oracle.to_e4m3(src).reshape(n, -1)
+        else:
+            want = oracle.to_half_bits(src).view(np.uint8).reshape(n, -1)
+        for t, p in enumerate(pos):
+            assert (got[p] == want[t]).all()
+        untouched = np.ones(rows, bool)
+        untouched[pos] = False
+        assert (got[untouched] == 0).all()
+
+
+def test_lane_form_wht_bitwise(oracle, cuda):
+    """wht3 (src/spec3.cu:595-614) on q||gate rows: bitwise the CPU rotation, gate half kept."""
+    n = 5
+    x = oracle.randn(n * synth.Q_ROW, 31).reshape(n, 24, synth.Q_STRIDE)
+    lanes = [torch.from_numpy(x[t].reshape(-1).copy()).to(cuda) for t in range(n)]
+    Q.wht3(lanes, 24, 256, synth.Q_STRIDE, False)
+    torch.cuda.synchronize()
+    got = np.stack([l.cpu().numpy().reshape(24, synth.Q_STRIDE) for l in lanes])
+    want = oracle.wht(np.ascontiguousarray(x[:, :, :256]))
+    assert (got[:, :, :256].view(np.uint32) == want.view(np.uint32)).all()
+    assert (got[:, :, 256:] == x[:, :, 256:]).all()
+    Q.wht3(lanes, 24, 256, synth.Q_STRIDE, True)
+    torch.cuda.synchronize()
+    back = np.stack([l.cpu().numpy().reshape(24, synth.Q_STRIDE) for l in lanes])
+    assert np.abs(back[:, :, :256] - x[:, :, :256]).max() < 1e-5
