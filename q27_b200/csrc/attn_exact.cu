@@ -124,10 +124,67 @@ k_exact_partial(const __grid_constant__ DevBatch b) {
     }
 }
 
+// Log-sum-exp merge of the nsplit partials {m, l, acc[256]} at pp (stride PART) by a block of
+// COMBINE_THREADS threads. Every load of a phase is issued before any is used, so the
+// kernel costs a few L2 round trips rather than one per split: (1) thread sp fetches m and
+// l of split sp; (2) warp 0 forms the global max, the weights e^{m_s - M} and l; (3) four
+// groups of 128 threads each sum every fourth split, two dims per thread, and the groups
+// are added in a fixed order (same result every run). Splits with weight 0 (sentinels)
+// hold undefined accumulators: selected, never multiplied. On return threads 0..255 hold
+// the merged accumulator of dim threadIdx.x; mg / lg are valid in every thread.
+constexpr int COMBINE_THREADS = 512;
+__device__ __forceinline__ float combine_core(const float* __restrict__ pp, int nsplit, float& mg,
+                                              float& lg) {
+    __shared__ float s_mv[Q27_MAX_SPLITS], s_lv[Q27_MAX_SPLITS], s_w[Q27_MAX_SPLITS];
+    __shared__ float s_ml[2];
+    __shared__ float s_red[4][HD];
+    const int tid = threadIdx.x;
+    if (tid < nsplit) {
+        const float2 ml = *reinterpret_cast<const float2*>(pp + (size_t)tid * PART);
+        s_mv[tid] = ml.x;
+        s_lv[tid] = ml.y;
+    }
+    __syncthreads();
+    if (tid < 32) {
+        float m = NEG_SENTINEL;
+        for (int sp = tid; sp < nsplit; sp += 32) m = fmaxf(m, s_mv[sp]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        float l = 0.f;
+        for (int sp = tid; sp < nsplit; sp += 32) {
+            const float ms = s_mv[sp];
+            const float w = ms == NEG_SENTINEL ? 0.f : expf(ms - m);
+            s_w[sp] = w;
+            l += s_lv[sp] * w;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+        if (tid == 0) { s_ml[0] = m; s_ml[1] = l; }
+    }
+    __syncthreads();
+    mg = s_ml[0];
+    lg = s_ml[1];
+    const int grp = tid >> 7, c = tid & 127;
+    float ax = 0.f, ay = 0.f;
+#pragma unroll 8
+    for (int sp = grp; sp < nsplit; sp += 4) {
+        const float w = s_w[sp];
+        const float2 v = *reinterpret_cast<const float2*>(pp + (size_t)sp * PART + 2 + 2 * c);
+        ax += w != 0.f ? v.x * w : 0.f;
+        ay += w != 0.f ? v.y * w : 0.f;
+    }
+    s_red[grp][2 * c] = ax;
+    s_red[grp][2 * c + 1] = ay;
+    __syncthreads();
+    float a = 0.f;
+    if (tid < HD) a = ((s_red[0][tid] + s_red[1][tid]) + s_red[2][tid]) + s_red[3][tid];
+    return a;
+}
+
 // Merge the nsplit partials of one (slot, lane, head). NORMALISE: write out = acc / l to the
 // lane's output row; otherwise write the merged {m, l, acc} for a cross-GPU merge.
 template <bool NORMALISE>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(COMBINE_THREADS)
 k_combine(const __grid_constant__ DevBatch b, float* __restrict__ partial_out, int lanes_stride) {
     pdl_wait();                  // the partials come from the kernel before this one
     const int h = blockIdx.x, t = blockIdx.y, slot = blockIdx.z;
@@ -140,52 +197,23 @@ k_combine(const __grid_constant__ DevBatch b, float* __restrict__ partial_out, i
         }
         return;
     }
-    const float* pp = S.scratch + ((size_t)t * b.n_q + h) * b.nsplit * PART;
-    __shared__ float s_m, s_l;
-    __shared__ float s_w[Q27_MAX_SPLITS];
-    if (threadIdx.x < 32) {
-        float mg = NEG_SENTINEL;
-        for (int sp = threadIdx.x; sp < b.nsplit; sp += 32) mg = fmaxf(mg, pp[(size_t)sp * PART]);
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, off));
-        float lg = 0.f;
-        for (int sp = threadIdx.x; sp < b.nsplit; sp += 32) {
-            const float ms = pp[(size_t)sp * PART];
-            const float w = ms == NEG_SENTINEL ? 0.f : expf(ms - mg);
-            s_w[sp] = w;
-            lg += pp[(size_t)sp * PART + 1] * w;
+    float mg, lg;
+    const float a = combine_core(S.scratch + ((size_t)t * b.n_q + h) * b.nsplit * PART, b.nsplit, mg, lg);
+    if (threadIdx.x < HD) {
+        if (NORMALISE) {
+            S.out[t][(size_t)h * HD + threadIdx.x] = a * (lg > 0.f ? 1.0f / lg : 0.f);
+        } else {
+            float* d = partial_out + (((size_t)slot * lanes_stride + t) * b.n_q + h) * PART;
+            d[2 + threadIdx.x] = a;
+            if (threadIdx.x == 0) { d[0] = mg; d[1] = lg; }
         }
-        // fixed-shape tree: the same order every run
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) lg += __shfl_xor_sync(0xffffffffu, lg, off);
-        if (threadIdx.x == 0) { s_m = mg; s_l = lg; }
-    }
-    __syncthreads();
-    const float lg = s_l;
-    const float inv = lg > 0.f ? 1.0f / lg : 0.f;
-    for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-        float a = 0.f;
-        // splits with weight 0 (sentinels) hold undefined accumulators: select, never multiply
-#pragma unroll 8
-        for (int sp = 0; sp < b.nsplit; sp++) {
-            const float w = s_w[sp];
-            const float v = pp[(size_t)sp * PART + 2 + d];
-            a += w != 0.f ? v * w : 0.f;
-        }
-        if (NORMALISE) S.out[t][(size_t)h * HD + d] = a * inv;
-        else partial_out[(((size_t)slot * lanes_stride + t) * b.n_q + h) * PART + 2 + d] = a;
-    }
-    if (!NORMALISE && threadIdx.x == 0) {
-        float* d = partial_out + (((size_t)slot * lanes_stride + t) * b.n_q + h) * PART;
-        d[0] = s_m;
-        d[1] = lg;
     }
 }
 
 // k_combine<false> with the exchange fused in: the merged {m, l, acc} row of (slot, lane,
 // head) goes straight into slot `rank` of EVERY rank's mailbox (peer stores over NVLink),
 // and the last block publishes the epoch. Padded lanes get sentinel rows like everyone else.
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(COMBINE_THREADS)
 k_combine_push(const __grid_constant__ DevBatch b, const __grid_constant__ Peers peers,
                int lanes_stride) {
     pdl_trigger();               // the merge kernel may be scheduled; it waits for this grid
@@ -193,46 +221,20 @@ k_combine_push(const __grid_constant__ DevBatch b, const __grid_constant__ Peers
     const int h = blockIdx.x, t = blockIdx.y, slot = blockIdx.z;
     const DevSlot& S = b.s[slot];
     const size_t row = peers.slot_floats() + (((size_t)slot * lanes_stride + t) * b.n_q + h) * PART;
-    __shared__ float s_m, s_l;
-    __shared__ float s_w[Q27_MAX_SPLITS];
     if (t >= S.ntok) {
         for (int i = threadIdx.x; i < PART; i += blockDim.x) {
             const float v = i == 0 ? NEG_SENTINEL : 0.f;
             for (int r = 0; r < peers.world; r++) reinterpret_cast<float*>(peers.box[r])[row + i] = v;
         }
     } else {
-        const float* pp = S.scratch + ((size_t)t * b.n_q + h) * b.nsplit * PART;
-        if (threadIdx.x < 32) {
-            float mg = NEG_SENTINEL;
-            for (int sp = threadIdx.x; sp < b.nsplit; sp += 32) mg = fmaxf(mg, pp[(size_t)sp * PART]);
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, off));
-            float lg = 0.f;
-            for (int sp = threadIdx.x; sp < b.nsplit; sp += 32) {
-                const float ms = pp[(size_t)sp * PART];
-                const float w = ms == NEG_SENTINEL ? 0.f : expf(ms - mg);
-                s_w[sp] = w;
-                lg += pp[(size_t)sp * PART + 1] * w;
-            }
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) lg += __shfl_xor_sync(0xffffffffu, lg, off);
-            if (threadIdx.x == 0) { s_m = mg; s_l = lg; }
-        }
-        __syncthreads();
-        for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-            float a = 0.f;
-#pragma unroll 8
-            for (int sp = 0; sp < b.nsplit; sp++) {
-                const float w = s_w[sp];
-                const float v = pp[(size_t)sp * PART + 2 + d];
-                a += w != 0.f ? v * w : 0.f;
-            }
-            for (int r = 0; r < peers.world; r++) reinterpret_cast<float*>(peers.box[r])[row + 2 + d] = a;
-        }
-        if (threadIdx.x == 0)
+        float mg, lg;
+        const float a = combine_core(S.scratch + ((size_t)t * b.n_q + h) * b.nsplit * PART, b.nsplit,
+                                     mg, lg);
+        if (threadIdx.x < HD)
             for (int r = 0; r < peers.world; r++) {
-                reinterpret_cast<float*>(peers.box[r])[row] = s_m;
-                reinterpret_cast<float*>(peers.box[r])[row + 1] = s_l;
+                float* d = reinterpret_cast<float*>(peers.box[r]) + row;
+                d[2 + threadIdx.x] = a;
+                if (threadIdx.x == 0) { d[0] = mg; d[1] = lg; }
             }
     }
     xchg_publish(peers, gridDim.x * gridDim.y * gridDim.z);
@@ -335,10 +337,10 @@ int launch_exact_partials(const DevBatch& b, int kvk, cudaStream_t st) {
 int launch_combine(const DevBatch& b, float* partial_out, int lanes_stride, cudaStream_t st) {
     if (partial_out) {
         dim3 grid(b.n_q, lanes_stride, b.nslots);
-        Q27_CUDA_TRY(launch_pdl(k_combine<false>, grid, dim3(256), 0, st, b, partial_out, lanes_stride));
+        Q27_CUDA_TRY(launch_pdl(k_combine<false>, grid, dim3(COMBINE_THREADS), 0, st, b, partial_out, lanes_stride));
     } else {
         dim3 grid(b.n_q, b.max_ntok, b.nslots);
-        Q27_CUDA_TRY(launch_pdl(k_combine<true>, grid, dim3(256), 0, st, b, (float*)nullptr, b.max_ntok));
+        Q27_CUDA_TRY(launch_pdl(k_combine<true>, grid, dim3(COMBINE_THREADS), 0, st, b, (float*)nullptr, b.max_ntok));
     }
     Q27_CUDA_TRY(cudaGetLastError());
     return Q27_OK;
@@ -346,7 +348,7 @@ int launch_combine(const DevBatch& b, float* partial_out, int lanes_stride, cuda
 
 int launch_combine_push(const DevBatch& b, const Peers& peers, int lanes_stride, cudaStream_t st) {
     dim3 grid(b.n_q, lanes_stride, b.nslots);
-    Q27_CUDA_TRY(launch_pdl(k_combine_push, grid, dim3(256), 0, st, b, peers, lanes_stride));
+    Q27_CUDA_TRY(launch_pdl(k_combine_push, grid, dim3(COMBINE_THREADS), 0, st, b, peers, lanes_stride));
     Q27_CUDA_TRY(cudaGetLastError());
     return Q27_OK;
 }

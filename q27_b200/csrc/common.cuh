@@ -2,6 +2,7 @@
 // element decoders (bit-exact to the reference codec) and the per-launch argument bundles.
 #pragma once
 #include <cuda_fp16.h>
+#include <stdlib.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <float.h>
@@ -146,7 +147,8 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    static const bool off = getenv("Q27_NO_PDL") != nullptr;   // measurement switch
+    cfg.numAttrs = off ? 0 : 1;
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
