@@ -7,7 +7,7 @@ this package is the thin host-side mirror of the reference's launch functions.""
 from . import _lib
 from .kv import (KV_F16, KV_FP8, KV_T3, KV_PAGE, KvPool, PagedSide, kv_k_rotated, mk_tab,
                  paged_from_rows, row_bytes)
-from .attn import (SlotArgs, attn_decode, attn_decode3, attn_decode3_noalloc, attn_decode_batched,
+from .attn import (BatchedDecode, SlotArgs, marshal_slots, attn_decode, attn_decode3, attn_decode3_noalloc, attn_decode_batched,
                    attn_decode_partial, attn_decode_partial_push, attn_merge_partials,
                    attn_merge_pushed, attn_prefill_T,
                    decode_scratch_floats, kv_dequant, kv_store3, kv_store_T, kv_store_T_t3,

@@ -91,6 +91,12 @@ class SlotArgs:
     row_count: int = INT_MAX
 
 
+def marshal_slots(slots) -> C.Array:
+    """The q27_slot array of a list of SlotArgs, for callers that reuse it across steps (the
+    caller keeps the SlotArgs alive)."""
+    return _slots(slots)
+
+
 def _slots(slots) -> C.Array:
     arr = (L.Slot * len(slots))()
     for i, s in enumerate(slots):
@@ -115,6 +121,26 @@ def attn_decode_batched(slots, q_stride, n_q_heads, n_kv_heads, head_dim, scale,
                kvk), "q27_attn_decode_batched")
 
 
+class BatchedDecode:
+    """attn_decode_batched with its argument block marshalled once. A decode loop calls the
+    same slots every step (table, lane and scratch pointers are fixed for the life of the
+    engine's captured graph; positions and Q change behind them), so the per-step cost on the
+    host is one foreign call."""
+
+    def __init__(self, slots, q_stride, n_q_heads, n_kv_heads, head_dim, scale, kvk=0,
+                 exact=False):
+        self._keep = list(slots)                 # the tensors behind the raw pointers
+        self._arr = _slots(self._keep)
+        self._fn = (L.lib().q27_attn_decode_batched_exact if exact
+                    else L.lib().q27_attn_decode_batched)
+        self._args = (q_stride, n_q_heads, n_kv_heads, head_dim, scale)
+        self._kvk = kvk
+
+    def __call__(self, st=None):
+        L.check(self._fn(self._arr, len(self._keep), *self._args, stream_ptr(st), self._kvk),
+                "q27_attn_decode_batched")
+
+
 def attn_decode_partial(slots, lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim, scale,
                         partial_out, st=None, kvk=0):
     """Un-normalised {m, l, acc} per (slot, lane, head) over each slot's row window."""
@@ -129,9 +155,9 @@ def attn_decode_partial_push(slots, lanes_stride, q_stride, n_q_heads, n_kv_head
     """attn_decode_partial whose result lands in slot ``rank`` of every rank's mailbox
     (``mailboxes``: device addresses, one per rank, as mapped in this process)."""
     import ctypes as C
-    arr = _slots(slots)
+    arr = slots if isinstance(slots, C.Array) else _slots(slots)
     boxes = (C.c_void_p * len(mailboxes))(*mailboxes)
-    L.check(L.lib().q27_attn_decode_partial_push(arr, len(slots), lanes_stride, q_stride, n_q_heads,
+    L.check(L.lib().q27_attn_decode_partial_push(arr, len(arr), lanes_stride, q_stride, n_q_heads,
                                                  n_kv_heads, head_dim, scale, boxes,
                                                  len(mailboxes), rank, epoch, stream_ptr(st), kvk),
             "q27_attn_decode_partial_push")
