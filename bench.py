@@ -227,7 +227,7 @@ def run_ours(args):
     scratch = [torch.empty(Q.decode_scratch_floats(lanes), device=dev) for _ in range(nslots)]
     ex = boxes = None
     if world > 1 and args.exchange == "peer":
-        boxes = qd.PeerMailboxes(nslots, lanes, N_Q)
+        boxes = qd.PeerMailboxes(nslots, lanes, N_Q, device_epoch=not args.no_graph)
     elif world > 1:
         ex = qd.PartialExchange.create(nslots, lanes, N_Q, world, dev)
     merged = torch.zeros((nslots * lanes * N_Q, HD), device=dev)
@@ -260,9 +260,37 @@ def run_ours(args):
             dist.barrier()
             torch.cuda.synchronize()
 
+    # One CUDA graph holds a round of `copies` consecutive steps (every launch of the library
+    # is capturable and, with device-counted exchange epochs, has constant arguments), as the
+    # engine this path drops into replays its decode step from a graph. Steps that do not
+    # fill a round are launched directly.
+    use_graph = not args.no_graph and (world == 1 or boxes is not None)
+
+    def make_graph(fn):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        return graph
+
+    round_graph = make_graph(lambda: [step(c) for c in range(copies)]) if use_graph else None
+
+    def run_steps(first, n):
+        i = first
+        while n > 0:
+            if round_graph is not None and i % copies == 0 and n >= copies:
+                round_graph.replay()
+                i, n = i + copies, n - copies
+            else:
+                step(i)
+                i, n = i + 1, n - 1
+
     # ---- device-resident timing ---------------------------------------------------------
-    for i in range(args.warmup):
-        step(i)
+    run_steps(0, args.warmup)
     barrier()
     sampler = ClockSampler(local_rank)
     if rank == 0:
@@ -271,8 +299,7 @@ def run_ours(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     e0.record()
-    for i in range(args.steps):
-        step(args.warmup + i)
+    run_steps(0, args.steps)
     e1.record()
     barrier()
     ms = e0.elapsed_time(e1)
@@ -295,11 +322,19 @@ def run_ours(args):
     kernel_ms = sum(kms) / len(kms)
 
     # ---- end to end through the public call with host buffers ---------------------------
-    def e2e_step(i):
+    def e2e_body(i):
         in_dev.copy_(in_host, non_blocking=True)
         step(i)
         src = merged.view(nslots, lanes, N_Q * HD) if world > 1 else out_dev
         out_host.copy_(src, non_blocking=True)
+
+    e2e_graphs = [make_graph(lambda c=c: e2e_body(c)) for c in range(copies)] if use_graph else None
+
+    def e2e_step(i):
+        if e2e_graphs is not None:
+            e2e_graphs[i % copies].replay()
+        else:
+            e2e_body(i)
         torch.cuda.current_stream().synchronize()
 
     for i in range(args.warmup):
@@ -338,6 +373,8 @@ def run_ours(args):
                    "lanes": lanes, "context_rows_per_slot": rows_total,
                    "rows_per_gpu_per_slot": local_rows, "heads": "24q/4kv", "head_dim": HD,
                    "parallelism": f"kv-split x{world}" if world > 1 else "single gpu",
+                   "launch": (f"cuda graph per round of {copies} steps" if use_graph
+                              else "direct launches"),
                    "exchange": ("none" if world == 1 else
                                 "peer-memory mailboxes (P2P stores + flags, no collective)"
                                 if boxes is not None else "nccl all-gather"),
@@ -590,6 +627,8 @@ def main():
     ap.add_argument("--workload", default="c3", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch every step directly instead of replaying CUDA graphs")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="N > 1: how the ranks' partials meet (peer-memory mailboxes or NCCL)")
     args = ap.parse_args()

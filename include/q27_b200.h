@@ -184,7 +184,10 @@ size_t q27_xchg_mailbox_bytes(int world, int64_t npairs);
 /* q27_attn_decode_partial whose result goes to slot `rank` of EVERY rank's mailbox
  * (mailboxes[r] = rank r's mailbox as mapped here; mailboxes[rank] = the own one) with peer
  * stores, followed by a release flag carrying `epoch`. epoch starts at 1 and grows by one
- * per exchange on every rank; npairs = nslots * lanes_stride * n_q_heads. */
+ * per exchange on every rank; or pass 0 in every push and merge on a mailbox and the device
+ * counts the exchanges itself (the merge advances a step word in the mailbox), so that a
+ * step's launches have constant arguments and can be captured in a CUDA graph.
+ * npairs = nslots * lanes_stride * n_q_heads. */
 int q27_attn_decode_partial_push(const q27_slot* slots, int nslots, int lanes_stride, int q_stride,
                                  int n_q_heads, int n_kv_heads, int head_dim, float scale,
                                  void* const* mailboxes, int world, int rank, unsigned epoch,
@@ -193,8 +196,8 @@ int q27_attn_decode_partial_push(const q27_slot* slots, int nslots, int lanes_st
 /* Waits on the device (bounded; a timeout sets the flag q27_wait_timeout_flag reads and
  * leaves `out` untouched) until all `world` ranks have pushed `epoch` into this rank's own
  * mailbox, then log-sum-exp merges them: out [npairs][256] normalised. */
-int q27_attn_merge_pushed(const void* mailbox, int world, int64_t npairs, unsigned epoch,
-                          float* out, void* stream);
+int q27_attn_merge_pushed(void* mailbox, int world, int64_t npairs, unsigned epoch, float* out,
+                          void* stream);
 
 /* ---- prefill ----------------------------------------------------------------------- */
 

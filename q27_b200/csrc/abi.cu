@@ -371,7 +371,7 @@ int q27_attn_decode_partial_push(const q27_slot* slots, int nslots, int lanes_st
                                  int n_q_heads, int n_kv_heads, int head_dim, float scale,
                                  void* const* mailboxes, int world, int rank, unsigned epoch,
                                  void* stream, int kvk) {
-    if (!mailboxes || world < 1 || world > Q27_MAX_RANKS || rank < 0 || rank >= world || epoch == 0)
+    if (!mailboxes || world < 1 || world > Q27_MAX_RANKS || rank < 0 || rank >= world)
         return Q27_ERR_INVALID_ARG;
     for (int r = 0; r < world; r++)
         if (!mailboxes[r] || ((uintptr_t)mailboxes[r] & 255)) return Q27_ERR_INVALID_ARG;
@@ -387,10 +387,9 @@ int q27_attn_decode_partial_push(const q27_slot* slots, int nslots, int lanes_st
                       nullptr, stream, kvk, FAM_AUTO, &p);
 }
 
-int q27_attn_merge_pushed(const void* mailbox, int world, int64_t npairs, unsigned epoch,
-                          float* out, void* stream) {
-    if (!mailbox || !out || world < 1 || world > Q27_MAX_RANKS || npairs < 1 || (npairs & 1) ||
-        epoch == 0)
+int q27_attn_merge_pushed(void* mailbox, int world, int64_t npairs, unsigned epoch, float* out,
+                          void* stream) {
+    if (!mailbox || !out || world < 1 || world > Q27_MAX_RANKS || npairs < 1 || (npairs & 1))
         return Q27_ERR_INVALID_ARG;
     if (npairs > INT_MAX) return Q27_ERR_TOO_LARGE;
     return launch_merge_pushed(mailbox, world, npairs, epoch, out, static_cast<cudaStream_t>(stream));

@@ -214,10 +214,12 @@ k_combine(const __grid_constant__ DevBatch b, float* __restrict__ partial_out, i
 // head) goes straight into slot `rank` of EVERY rank's mailbox (peer stores over NVLink),
 // and the last block publishes the epoch. Padded lanes get sentinel rows like everyone else.
 __global__ void __launch_bounds__(COMBINE_THREADS)
-k_combine_push(const __grid_constant__ DevBatch b, const __grid_constant__ Peers peers,
+k_combine_push(const __grid_constant__ DevBatch b, const __grid_constant__ Peers peers_in,
                int lanes_stride) {
     pdl_trigger();               // the merge kernel may be scheduled; it waits for this grid
     pdl_wait();                  // the partials come from the kernel before this one
+    Peers peers = peers_in;
+    peers.epoch = xchg_epoch(peers.box[peers.rank], peers.world, peers.npairs, peers_in.epoch);
     const int h = blockIdx.x, t = blockIdx.y, slot = blockIdx.z;
     const DevSlot& S = b.s[slot];
     const size_t row = peers.slot_floats() + (((size_t)slot * lanes_stride + t) * b.n_q + h) * PART;

@@ -30,14 +30,14 @@ namespace q27b {
 __device__ int g_umma_timeout_flag = 0;
 #ifdef Q27_TRACE
 // timing experiments only: cycles spent waiting, summed over CTAs, by (role, barrier)
-__device__ unsigned long long g_umma_trace[16];
+__device__ unsigned long long g_umma_trace[24];
 __device__ long long g_umma_ev[12][64];   // per-event timestamps of CTA (0,0,0), first 64 tiles
 #define TRACE_EV(e, i) do { if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (i) < 64) g_umma_ev[e][i] = clock64(); } while (0)
 #define TRACE_EVMAX(e, i) do { if ((threadIdx.x & 31) == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (i) < 64) atomicMax(&g_umma_ev[e][i], clock64()); } while (0)
 #define TRACE_T0() const long long t0__ = clock64()
 #define TRACE_ADD(slot, cond) do { if (cond) tr_acc__[slot] += (unsigned long long)(clock64() - t0__); } while (0)
-#define TRACE_DECL() unsigned long long tr_acc__[16] = {0}
-#define TRACE_FLUSH() do { for (int q__ = 0; q__ < 16; q__++) if (tr_acc__[q__]) atomicAdd(&g_umma_trace[q__], tr_acc__[q__]); } while (0)
+#define TRACE_DECL() unsigned long long tr_acc__[24] = {0}
+#define TRACE_FLUSH() do { for (int q__ = 0; q__ < 24; q__++) if (tr_acc__[q__]) atomicAdd(&g_umma_trace[q__], tr_acc__[q__]); } while (0)
 #else
 #define TRACE_T0()
 #define TRACE_ADD(slot, cond)
@@ -279,19 +279,7 @@ template <> struct RawHalf<Q27_KV_T3> { uint32_t w[14]; };
 template <int KVK>
 __device__ __forceinline__ void half_load(RawHalf<KVK>& t, const uint8_t* page, int nkeys, int n_kv,
                                           int kvh, int p) {
-    if constexpr (KVK == Q27_KV_T3) {
-        // one thread = one 50-byte block: (key, block). Block 1 starts 2 bytes past a word
-        // boundary, so 14 words from the aligned address below it cover either block.
-        const int key = p & 63, blk = p >> 6;
-#pragma unroll
-        for (int i = 0; i < 14; i++) t.w[i] = 0;
-        if (key < nkeys) {
-            const uint32_t* src = reinterpret_cast<const uint32_t*>(
-                page + ((size_t)key * n_kv + kvh) * (2 * T3_BLK)) + 12 * blk;
-#pragma unroll
-            for (int i = 0; i < 13; i++) t.w[i] = __ldg(src + i);
-        }
-    } else if constexpr (KVK == Q27_KV_FP8) {
+    if constexpr (KVK == Q27_KV_FP8) {
 #pragma unroll
         for (int n = 0; n < 16; n++) {
             const int q = p + NPROD * n;
@@ -304,7 +292,8 @@ __device__ __forceinline__ void half_load(RawHalf<KVK>& t, const uint8_t* page, 
     }
 }
 
-template <int KVK>
+// BLK (turbo3 only): which of the two blocks of a (key, kv head) the thread decodes; warp-uniform
+template <int KVK, int BLK = 0>
 __device__ __forceinline__ void half_store(const RawHalf<KVK>& t, uint8_t* dst, int nkeys, int p) {
     if constexpr (KVK == Q27_KV_FP8) {
 #pragma unroll
@@ -320,17 +309,16 @@ __device__ __forceinline__ void half_store(const RawHalf<KVK>& t, uint8_t* dst, 
                 cv(t.d[n].x & 0xffffu), cv(t.d[n].x >> 16), cv(t.d[n].y & 0xffffu), cv(t.d[n].y >> 16));
         }
     } else if constexpr (KVK == Q27_KV_T3) {
-        const int key = p & 63, blk = p >> 6;
+        const int key = p & 63;
         const uint32_t* w = t.w;
         const T3Tab tab = t3_tables();
         // 32-bit little-endian word at byte `o` of the block (o even, compile time); block 1
-        // sits 2 bytes into the loaded words, block 0 at byte 0 (blk is warp-uniform)
+        // sits 2 bytes into the loaded words, block 0 at byte 0
         auto word_at = [&](int o) {
-            const uint32_t a0 = (o & 3) ? __funnelshift_r(w[o >> 2], w[(o >> 2) + 1], 16) : w[o >> 2];
-            const int o1 = o + 2;
-            const uint32_t a1 = (o1 & 3) ? __funnelshift_r(w[o1 >> 2], w[(o1 >> 2) + 1], 16) : w[o1 >> 2];
-            return blk ? a1 : a0;
+            const int ob = o + 2 * BLK;
+            return (ob & 3) ? __funnelshift_r(w[ob >> 2], w[(ob >> 2) + 1], 16) : w[ob >> 2];
         };
+        constexpr int blk = BLK;
         const __half nh = __ushort_as_half((unsigned short)(word_at(0) & 0xffffu));
         const __half2 n2 = key < nkeys ? __half2half2(nh) : __float2half2_rn(0.f);
 #pragma unroll
@@ -371,12 +359,16 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     uint8_t* q_sm = base + SMEM_BAR;
     uint8_t* k_sm = q_sm + Q_BYTES;
     uint8_t* v_sm = k_sm + K_SLOTS * KT_BYTES;
+    // turbo3 gives its third V slot to a raw staging area: the packed rows of a tile are
+    // fetched with coalesced asynchronous copies and decoded from shared memory
+    constexpr int VSL = KVK == Q27_KV_T3 ? 2 : V_SLOTS;
+    uint8_t* raw_sm = v_sm + 2 * KT_BYTES;
     // A K slot is released as soon as its S MMAs have run, a V slot after its PV MMAs.
     // pvb[b] completes when the PV MMAs of a tile that used S/P buffer b have run: it frees
     // the buffer for the S MMAs four tiles on and tells the softmax warps that O may be touched.
     const uint32_t k_full = s32(&bars[0]), k_empty = s32(&bars[4]), v_full = s32(&bars[8]),
                    v_empty = s32(&bars[12]), s_full = s32(&bars[16]), pvb = s32(&bars[20]),
-                   p_full = s32(&bars[24]);
+                   p_full = s32(&bars[24]), raw_full = s32(&bars[28]), raw_empty = s32(&bars[32]);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = (pb.hi - pb.lo + BN - 1) / BN;
     TRACE_DECL();
@@ -386,9 +378,13 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             bar_init(k_full + 8 * s, NPROD);
             bar_init(k_empty + 8 * s, 1);
         }
-        for (int s = 0; s < V_SLOTS; s++) {
+        for (int s = 0; s < VSL; s++) {
             bar_init(v_full + 8 * s, NPROD);
             bar_init(v_empty + 8 * s, 1);
+        }
+        for (int s = 0; s < 4; s++) {
+            bar_init(raw_full + 8 * s, NPROD);
+            bar_init(raw_empty + 8 * s, NPROD);
         }
         for (int s = 0; s < S_BUFS; s++) {
             bar_init(s_full + 8 * s, 1);
@@ -456,6 +452,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         const float sc2 = scale * LOG2E_F;      // > 0: the row max may be taken before scaling
         float m_ref = -INFINITY, l = 0.f;
         bool ok = true;
+        const bool warp_has_rows = __any_sync(0xffffffffu, ri.q != nullptr);
 #ifdef Q27_TRACE
         const long long tloop = clock64();
 #endif
@@ -467,6 +464,14 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
               TRACE_ADD(0, threadIdx.x == 0); }
             if (!ok) break;
             if (threadIdx.x == 0) TRACE_EV(4, i);
+            if (!warp_has_rows) {
+                // a warp of padding rows only (verify tiles use 6 rows per lane): it keeps
+                // step with the barriers and leaves its issue slots to the staging warps;
+                // whatever its S columns hold is multiplied into O rows nobody reads
+                tc_fence_before();
+                bar_arrive(p_full + 8 * b);
+                continue;
+            }
             TRACE_T0();
             tc_fence_after();
             float s[BN];
@@ -652,7 +657,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 __syncwarp();
                 if (lane == 0) TRACE_EV(3, i);
                 TRACE_ADD(10, lane == 0);
-                if (++vs_ == V_SLOTS) { vs_ = 0; vpar ^= 1; }
+                if (++vs_ == VSL) { vs_ = 0; vpar ^= 1; }
                 if (++b == S_BUFS) { b = 0; bpar ^= 1; }
             }
         }
@@ -662,7 +667,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         // exactly one cache page
         const int side = (warp - FIRST_LOAD_WARP) >> 2;                 // 0 = K, 1 = V
         const int p = threadIdx.x - (FIRST_LOAD_WARP + 4 * side) * 32;  // 0..127 within the side
-        const int nslots = side ? V_SLOTS : K_SLOTS;
+        const int nslots = side ? VSL : K_SLOTS;
         const uint32_t full = side ? v_full : k_full, empty = side ? v_empty : k_empty;
         uint8_t* ring = side ? v_sm : k_sm;
         const void* const* tab = side ? vtab : ktab;
@@ -702,6 +707,69 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
                              ::"r"(full + 8 * st) : "memory");
                 if (p == 0 && side == 0) TRACE_EV(11, i);
+            }
+            asm volatile("cp.async.wait_all;" ::: "memory");
+        } else if constexpr (KVK == Q27_KV_T3) {
+            // A tile's packed rows of this kv head (64 keys x 100 B, 400 B apart in the page)
+            // come in with 4-byte asynchronous copies, consecutive lanes on consecutive words
+            // (a block per thread straight from global memory costs one L1 wavefront per lane
+            // per load and bounded this path); two raw buffers per side, each with a "landed"
+            // and a "read" mbarrier. Each thread then decodes one 50-byte block from shared
+            // memory (lanes 25 words apart: conflict-free).
+            constexpr int RAW_BYTES = BN * 2 * T3_BLK;
+            uint8_t* raw = raw_sm + side * 2 * RAW_BYTES;
+            const uint32_t rfull = raw_full + 8 * (2 * side), rempty = raw_empty + 8 * (2 * side);
+            auto issue_raw = [&](int i) {
+                const int buf = i & 1, nk = nkeys_of(i);
+                const uint8_t* page = page_of(i);
+                const uint32_t dst = s32(raw + buf * RAW_BYTES);
+#pragma unroll
+                for (int n = 0; n < 13; n++) {
+                    const int w = p + NPROD * n;          // word 0..1599 of the tile's rows
+                    const int key = w / 25, j = w - 25 * key;
+                    if (w < BN * 25 && key < nk)
+                        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;"
+                                     ::"r"(dst + 4 * w),
+                                       "l"(page + ((size_t)key * n_kv + pb.kvh) * (2 * T3_BLK) + 4 * j)
+                                     : "memory");
+                }
+                asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
+                             ::"r"(rfull + 8 * buf) : "memory");
+            };
+            if (ntiles > 0) issue_raw(0);
+            if (ntiles > 1) issue_raw(1);
+            for (int i = 0; i < ntiles; i++) {
+                const int buf = i & 1;
+                const uint32_t par = (uint32_t)((i >> 1) & 1);
+                { TRACE_T0();
+                  if (!bar_wait(rfull + 8 * buf, par)) break;
+                  TRACE_ADD(16, p == 0 && side == 0); }
+                RawHalf<KVK> rw;
+                {
+                    const int key = p & 63, blk = p >> 6;
+                    const uint32_t* src = reinterpret_cast<const uint32_t*>(
+                        raw + buf * RAW_BYTES + key * (2 * T3_BLK) + 48 * blk);
+#pragma unroll
+                    for (int k = 0; k < 13; k++) rw.w[k] = src[k];
+                    rw.w[13] = 0;
+                }
+                bar_arrive(rempty + 8 * buf);
+                if (i + 2 < ntiles) {
+                    { TRACE_T0();
+                      if (!bar_wait(rempty + 8 * buf, par)) break;
+                      TRACE_ADD(17, p == 0 && side == 0); }
+                    { TRACE_T0();
+                      issue_raw(i + 2);
+                      TRACE_ADD(18, p == 0 && side == 0); }
+                }
+                if (!wait_slot(i)) break;
+                const int st = i % nslots;
+                { TRACE_T0();
+                  if (p >> 6) half_store<KVK, 1>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
+                  else half_store<KVK, 0>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
+                  fence_async_smem();
+                  TRACE_ADD(19, p == 0 && side == 0); }
+                bar_arrive(full + 8 * st);
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
         } else {
@@ -832,8 +900,8 @@ int launch_prefill_umma(const float* qT, int q_stride, int q_row, const void* co
 
 #ifdef Q27_TRACE
 extern "C" int q27_debug_umma_trace(unsigned long long* out, int reset) {
-    cudaMemcpyFromSymbol(out, g_umma_trace, sizeof(unsigned long long) * 16);
-    if (reset) { unsigned long long z[16] = {0}; cudaMemcpyToSymbol(g_umma_trace, z, sizeof(z)); }
+    cudaMemcpyFromSymbol(out, g_umma_trace, sizeof(unsigned long long) * 24);
+    if (reset) { unsigned long long z[24] = {0}; cudaMemcpyToSymbol(g_umma_trace, z, sizeof(z)); }
     return 0;
 }
 extern "C" int q27_debug_umma_events(long long* out) {

@@ -160,7 +160,7 @@ int launch_merge(const float* parts, int nparts, int64_t npairs, float* out, cud
 size_t xchg_mailbox_bytes(int world, int64_t npairs);
 struct Peers;
 int launch_combine_push(const DevBatch& b, const Peers& peers, int lanes_stride, cudaStream_t st);
-int launch_merge_pushed(const void* box, int world, int64_t npairs, uint32_t epoch, float* out,
+int launch_merge_pushed(void* box, int world, int64_t npairs, uint32_t epoch, float* out,
                         cudaStream_t st);
 int read_xchg_timeout_flag(int* out);
 int read_umma_timeout_flag(int* out);

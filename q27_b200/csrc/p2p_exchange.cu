@@ -20,23 +20,23 @@ __device__ int g_xchg_timeout_flag = 0;
 
 // box: this rank's own mailbox. out [npairs][256] normalised.
 __global__ void __launch_bounds__(256)
-k_merge_pushed(const uint8_t* __restrict__ box, int world, int64_t npairs, uint32_t epoch,
+k_merge_pushed(uint8_t* __restrict__ box, int world, int64_t npairs, uint32_t epoch_given,
                float* __restrict__ out) {
     pdl_wait();                  // this rank's own rows come from the kernel before this one
+    const uint32_t epoch = xchg_epoch(box, world, npairs, epoch_given);
     const int par = epoch & 1;
     __shared__ int s_ok;
     if (threadIdx.x == 0) s_ok = 1;
     __syncthreads();
     if (threadIdx.x < world) {
-        const volatile uint32_t* f = reinterpret_cast<const volatile uint32_t*>(
-            box + xchg_flags_offset(world, npairs) + ((size_t)par * world + threadIdx.x) * XCHG_FLAG_STRIDE);
+        const uint8_t* f =
+            box + xchg_flags_offset(world, npairs) + ((size_t)par * world + threadIdx.x) * XCHG_FLAG_STRIDE;
         bool got = false;
         for (int i = 0; i < (1 << 21); i++) {          // about half a second, then give up
-            if (*f == epoch) { got = true; break; }
+            if (xchg_flag_acquire(f) == epoch) { got = true; break; }
             __nanosleep(200);
         }
         if (!got) { s_ok = 0; atomicExch(&g_xchg_timeout_flag, 4); }
-        __threadfence_system();
     }
     __syncthreads();
     if (!s_ok) return;
@@ -60,6 +60,17 @@ k_merge_pushed(const uint8_t* __restrict__ box, int world, int64_t npairs, uint3
         }
         out[(size_t)w * HD + d] = a * inv;
     }
+    // the last block to finish records the exchange as completed (every block has read the
+    // step word by then)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned* ctr = reinterpret_cast<unsigned*>(box + xchg_counter_offset(world, npairs) + XCHG_MERGE_CTR);
+        __threadfence();
+        if (atomicAdd(ctr, 1u) == gridDim.x - 1) {
+            *ctr = 0;
+            *reinterpret_cast<volatile uint32_t*>(box + xchg_counter_offset(world, npairs) + XCHG_STEP) = epoch;
+        }
+    }
 }
 
 } // namespace
@@ -68,10 +79,10 @@ size_t xchg_mailbox_bytes(int world, int64_t npairs) {
     return xchg_counter_offset(world, npairs) + 256;
 }
 
-int launch_merge_pushed(const void* box, int world, int64_t npairs, uint32_t epoch, float* out,
+int launch_merge_pushed(void* box, int world, int64_t npairs, uint32_t epoch, float* out,
                         cudaStream_t st) {
     Q27_CUDA_TRY(launch_pdl(k_merge_pushed, dim3((unsigned)npairs), dim3(256), 0, st,
-                            static_cast<const uint8_t*>(box), world, npairs, epoch, out));
+                            static_cast<uint8_t*>(box), world, npairs, epoch, out));
     return Q27_OK;
 }
 

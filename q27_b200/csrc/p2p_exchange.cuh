@@ -1,5 +1,8 @@
 // Layout of a partial-exchange mailbox and what a kernel needs to publish into every rank's:
-// [2 parities][world][npairs][258] floats, [2][world] release flags, one block counter.
+// [2 parities][world][npairs][258] floats, [2][world] release flags, two block counters and the
+// step word (the number of exchanges completed on this rank, for callers that let the device
+// count the epochs so that a step's launches have constant arguments and can sit in a CUDA
+// graph).
 #pragma once
 #include "common.cuh"
 
@@ -18,36 +21,59 @@ __host__ __device__ inline size_t xchg_counter_offset(int world, int64_t npairs)
     return xchg_flags_offset(world, npairs) + (size_t)2 * world * XCHG_FLAG_STRIDE;
 }
 
+// byte offsets from the first counter: push counter 0, merge counter 64, step word 128
+constexpr int XCHG_MERGE_CTR = 64, XCHG_STEP = 128;
+
 struct Peers {
     uint8_t* box[Q27_MAX_RANKS];   // every rank's mailbox as mapped in this process
     int world, rank;
     int64_t npairs;
-    uint32_t epoch;
+    uint32_t epoch;                // 0: take it from the own mailbox's step word (+1)
     // float offset of this rank's slot for this epoch (the same in every mailbox)
     __host__ __device__ size_t slot_floats() const {
         return ((size_t)(epoch & 1) * world + rank) * (size_t)npairs * PART;
     }
 };
 
+// The epoch of the exchange a kernel belongs to: given by the host, or one past the number
+// of exchanges this rank has completed (the merge kernel advances that word when its last
+// block is done, and launches are stream-ordered behind it).
+__device__ __forceinline__ uint32_t xchg_epoch(const uint8_t* own_box, int world, int64_t npairs,
+                                               uint32_t given) {
+    if (given) return given;
+    return *reinterpret_cast<const volatile uint32_t*>(
+               own_box + xchg_counter_offset(world, npairs) + XCHG_STEP) + 1u;
+}
+
 // Called by every block of a kernel that has just stored its share of this rank's rows into
-// all mailboxes: the last block to arrive publishes the epoch in every mailbox. The stores
-// of each block are fenced system-wide before its count, and the publishing block fences
-// again before the flags, so a rank that sees the flag sees the rows.
+// all mailboxes: the last block to arrive publishes the epoch in every mailbox. Blocks count
+// themselves with a release/acquire atomic at GPU scope (after the block barrier, so it
+// covers every thread's stores); only the publishing block pays for a system-scope fence,
+// once, before the flags. The chain rows -> block count -> last block -> fence -> flag ->
+// the peer's acquire load orders the rows before whatever the peer reads after its flag.
 __device__ __forceinline__ void xchg_publish(const Peers& p, unsigned nblocks) {
-    __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
         unsigned* counter = reinterpret_cast<unsigned*>(
             p.box[p.rank] + xchg_counter_offset(p.world, p.npairs));
-        if (atomicAdd(counter, 1u) == nblocks - 1) {
+        unsigned old;
+        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+        if (old == nblocks - 1) {
             *counter = 0;
-            __threadfence_system();
+            asm volatile("fence.acq_rel.sys;" ::: "memory");
             for (int r = 0; r < p.world; r++)
-                *reinterpret_cast<volatile uint32_t*>(
-                    p.box[r] + xchg_flags_offset(p.world, p.npairs) +
-                    ((size_t)(p.epoch & 1) * p.world + p.rank) * XCHG_FLAG_STRIDE) = p.epoch;
+                asm volatile("st.relaxed.sys.global.u32 [%0], %1;"
+                             ::"l"(p.box[r] + xchg_flags_offset(p.world, p.npairs) +
+                                   ((size_t)(p.epoch & 1) * p.world + p.rank) * XCHG_FLAG_STRIDE),
+                               "r"(p.epoch) : "memory");
         }
     }
+}
+// acquire load of a flag (pairs with the release store above)
+__device__ __forceinline__ uint32_t xchg_flag_acquire(const uint8_t* addr) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+    return v;
 }
 
 } // namespace q27b

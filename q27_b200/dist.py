@@ -99,8 +99,11 @@ class PeerMailboxes:
     (device-side bounded wait for all flags, then the merge): no collective call, no host
     synchronisation. The handles are exchanged once, with `all_gather_object`."""
 
-    def __init__(self, nslots: int, lanes: int, n_q: int, group=None):
+    def __init__(self, nslots: int, lanes: int, n_q: int, group=None, device_epoch: bool = False):
         import ctypes as C
+        # device_epoch: the mailbox counts the exchanges itself, so every step's launches have
+        # the same arguments and a step (or several) can be captured in a CUDA graph
+        self.device_epoch = device_epoch
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         if self.world > L.MAX_RANKS:
@@ -135,9 +138,10 @@ class PeerMailboxes:
                kvk: int, st=None) -> torch.Tensor:
         """One sharded decode / verify step; `out` [npairs][256] normalised on every rank."""
         self.epoch += 1
+        epoch = 0 if self.device_epoch else self.epoch
         attn_decode_partial_push(slots, self.lanes, q_stride, self.n_q, n_kv_heads, L.HEAD_DIM,
-                                 scale, self.boxes, self.rank, self.epoch, st=st, kvk=kvk)
-        attn_merge_pushed(self.own, self.world, self.npairs, self.epoch, out, st=st)
+                                 scale, self.boxes, self.rank, epoch, st=st, kvk=kvk)
+        attn_merge_pushed(self.own, self.world, self.npairs, epoch, out, st=st)
         return out
 
     def close(self, group=None):
