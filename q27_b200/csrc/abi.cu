@@ -297,9 +297,9 @@ int q27_attn_prefill_T(const float* qT, int q_stride, int q_row, const void* con
         return Q27_ERR_INVALID_ARG;
     if (SB == 0) return Q27_OK;
     bool done = false;
-    rc = launch_prefill_umma(qT, q_stride, q_row, ktab, vtab, outT, out_row, base_pos, t0, SB,
-                             n_q_heads, n_kv_heads, scale, static_cast<cudaStream_t>(stream), kvk,
-                             &done);
+    rc = launch_prefill_umma(qT, q_stride, q_row, ktab, vtab, outT, out_row, part, base_pos, t0, SB,
+                             n_q_heads, n_kv_heads, scale, sm_count(),
+                             static_cast<cudaStream_t>(stream), kvk, &done);
     if (rc || done) return rc;
     return q27_attn_prefill_T_exact(qT, q_stride, q_row, ktab, vtab, outT, out_row, part, base_pos,
                                     t0, SB, n_q_heads, n_kv_heads, head_dim, scale, stream, kvk);

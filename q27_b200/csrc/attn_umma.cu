@@ -224,7 +224,13 @@ struct TileArgs {
     int base_pos, t0, t_end;
     int n_kv;
     float scale;
+    // split of the items (Q tile x kv head) that do not fill a wave: items [0, n_full) run
+    // whole; every later item is cut into `pieces` key ranges whose un-normalised results go
+    // to part[((head * part_rows + (t - t0)) * PF_SPLIT_MAX + piece) * 258] for the fix-up
+    float* part;
+    int part_rows, nx, n_full, pieces;
 };
+constexpr int PF_SPLIT_MAX = 8;   // pieces a row's scratch has room for (src/prefill.cuh:88)
 
 struct RowInfo {        // one Q row of the tile, owned by one softmax thread
     const float* q;     // 256 floats, or nullptr for a padding row
@@ -240,6 +246,7 @@ struct Problem {
     const DevBatch* vb;
     const DevSlot* slot;
     int kvh, tile_t0, lo, hi, sp;
+    int piece = -1;     // prefill: >= 0 when this CTA holds one key range of a split item
 
     __device__ __forceinline__ RowInfo row(int r) const {
         // a padding row (no q) sees everything: its lanes stay on the unmasked path of their
@@ -252,7 +259,11 @@ struct Problem {
                 const int h = kvh * GQA + j;
                 ri.q = ta->qT + (size_t)t * ta->q_row + (size_t)h * ta->q_stride;
                 ri.bound = ta->base_pos + t + 1;
-                ri.out = ta->outT + (size_t)t * ta->out_row + (size_t)h * HD;
+                if (piece < 0)
+                    ri.out = ta->outT + (size_t)t * ta->out_row + (size_t)h * HD;
+                else
+                    ri.part = ta->part + (((size_t)h * ta->part_rows + (t - ta->t0)) * PF_SPLIT_MAX +
+                                          piece) * PART;
             }
         } else {
             if (tok < slot->ntok) {
@@ -398,51 +409,61 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                      ::"r"(s32(tmem_slot)), "n"(TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    if (warp < N_SOFTMAX_WARPS) {
-        // Q tile, fp32 -> fp16: dims 128..255 of row r into row r of two [128][128 B] blocks
-        const RowInfo rq = pb.row(threadIdx.x);
-#pragma unroll 4
-        for (int ch = Q_TMEM_DIMS / 8; ch < HD / 8; ch++) {
-            float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-            if (rq.q) {
-                a = __ldg(reinterpret_cast<const float4*>(rq.q + 8 * ch));
-                b = __ldg(reinterpret_cast<const float4*>(rq.q + 8 * ch + 4));
+    {
+        // Q tile, fp32 -> fp16, by ALL threads with coalesced loads: consecutive threads take
+        // consecutive 16-byte pieces of a row (a thread walking its own row costs a dependent
+        // chain of uncoalesced loads, ~20 us per CTA). Dims 128..255 go straight into row r
+        // of two [128][128 B] swizzled blocks; dims 0..127 wait in the (still idle) K ring
+        // for the thread that owns TMEM lane r.
+        constexpr int QT_PITCH = 264;                       // bytes per row of the waiting half
+        for (int base_i = 0; base_i < BM * (HD / 4); base_i += UMMA_THREADS * 4) {
+            float4 v[4];
+            int idx[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                idx[u] = base_i + u * UMMA_THREADS + threadIdx.x;
+                v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (idx[u] < BM * (HD / 4)) {
+                    const RowInfo rq = pb.row(idx[u] >> 6);
+                    if (rq.q) v[u] = __ldg(reinterpret_cast<const float4*>(rq.q) + (idx[u] & 63));
+                }
             }
-            __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
-            __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
-            const int c2 = ch - Q_TMEM_DIMS / 8;
-            *reinterpret_cast<uint4*>(q_sm + (c2 >> 3) * (BM * 128) + sw128(threadIdx.x, c2 & 7)) =
-                make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
-                           *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                if (idx[u] >= BM * (HD / 4)) continue;
+                const int row = idx[u] >> 6, d = (idx[u] & 63) * 4;
+                __half2 h0 = __floats2half2_rn(v[u].x, v[u].y), h1 = __floats2half2_rn(v[u].z, v[u].w);
+                const uint2 w = make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+                if (d >= Q_TMEM_DIMS) {
+                    const int c2 = (d - Q_TMEM_DIMS) >> 3;
+                    *reinterpret_cast<uint2*>(q_sm + (c2 >> 3) * (BM * 128) + sw128(row, c2 & 7) + (d & 7) * 2) = w;
+                } else {
+                    *reinterpret_cast<uint2*>(k_sm + row * QT_PITCH + d * 2) = w;
+                }
+            }
         }
         fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (warp < N_SOFTMAX_WARPS) {
+            // dims 0..127 of row r into TMEM lane r, dims 2c, 2c+1 into column COL_Q + c
+            const uint32_t qaddr = (*tmem_slot) + ((uint32_t)(warp * 32) << 16) + COL_Q;
+            const uint32_t* src = reinterpret_cast<const uint32_t*>(k_sm + threadIdx.x * QT_PITCH);
+#pragma unroll 1
+            for (int c = 0; c < Q_TMEM_DIMS / 2; c += 32) {
+                float packed[32];
+#pragma unroll
+                for (int e = 0; e < 32; e++) packed[e] = __uint_as_float(src[c + e]);
+                tc_st32(qaddr + c, packed);
+            }
+            tc_wait_st();
+        }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    if (warp < N_SOFTMAX_WARPS) {
-        // dims 0..127 of row r into TMEM lane r, dims 2c, 2c+1 into column COL_Q + c
-        const RowInfo rq = pb.row(threadIdx.x);
-        const uint32_t qaddr = tmem + ((uint32_t)(warp * 32) << 16) + COL_Q;
-#pragma unroll 1
-        for (int c = 0; c < Q_TMEM_DIMS / 2; c += 32) {
-            float packed[32];
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-                float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (rq.q) a = __ldg(reinterpret_cast<const float4*>(rq.q + 2 * (c + e)));
-                __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
-                packed[e] = __uint_as_float(*reinterpret_cast<uint32_t*>(&h0));
-                packed[e + 1] = __uint_as_float(*reinterpret_cast<uint32_t*>(&h1));
-            }
-            tc_st32(qaddr + c, packed);
-        }
-        tc_wait_st();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
 
     if (warp < N_SOFTMAX_WARPS) {
         // ------------------------------ softmax: thread = row ------------------------------
@@ -551,20 +572,25 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 ri.part[1] = l;
             }
             // the TMEM loads are warp-collective: every lane runs them, padding rows just
-            // drop what they read
+            // drop what they read (the stores are fire-and-forget: a row per thread is
+            // uncoalesced, but going through shared memory for whole-line stores measured
+            // slower -- it puts a dependent chain where the direct stores overlap)
+            if (warp_has_rows) {
 #pragma unroll 1
-            for (int c = 0; c < HD; c += 32) {
-                float o[32];
-                tc_ld32(lane_base + COL_O + c, o);
-                tc_wait_ld();
-                if (ri.out) {
+                for (int c = 0; c < HD; c += 32) {
+                    float o[32];
+                    tc_ld32(lane_base + COL_O + c, o);
+                    tc_wait_ld();
+                    if (ri.out) {
 #pragma unroll
-                    for (int e = 0; e < 32; e += 4)
-                        *reinterpret_cast<float4*>(ri.out + c + e) =
-                            make_float4(o[e] * inv, o[e + 1] * inv, o[e + 2] * inv, o[e + 3] * inv);
-                } else if (ri.part) {
+                        for (int e = 0; e < 32; e += 4)
+                            *reinterpret_cast<float4*>(ri.out + c + e) =
+                                make_float4(o[e] * inv, o[e + 1] * inv, o[e + 2] * inv, o[e + 3] * inv);
+                    } else if (ri.part) {
 #pragma unroll
-                    for (int e = 0; e < 32; e++) ri.part[2 + c + e] = o[e];
+                        for (int e = 0; e < 32; e += 2)
+                            *reinterpret_cast<float2*>(ri.part + 2 + c + e) = make_float2(o[e], o[e + 1]);
+                    }
                 }
             }
         }
@@ -816,12 +842,59 @@ k_prefill_umma(const __grid_constant__ TileArgs a) {
     pb.ta = &a;
     pb.vb = nullptr;
     pb.slot = nullptr;
-    pb.kvh = blockIdx.y;
-    pb.tile_t0 = a.t0 + blockIdx.x * TOK_PER_TILE;
-    pb.lo = 0;
-    pb.hi = a.base_pos + min(pb.tile_t0 + TOK_PER_TILE, a.t_end);
     pb.sp = 0;
+    // items in launch order: Q tile fastest, then kv head; whole items first, then the pieces
+    const int id = blockIdx.x;
+    int item = id;
+    if (id >= a.n_full) {
+        const int j = id - a.n_full;
+        item = a.n_full + j / a.pieces;
+        pb.piece = j % a.pieces;
+    }
+    pb.kvh = item / a.nx;
+    pb.tile_t0 = a.t0 + (item % a.nx) * TOK_PER_TILE;
+    const int item_hi = a.base_pos + min(pb.tile_t0 + TOK_PER_TILE, a.t_end);
+    pb.lo = 0;
+    pb.hi = item_hi;
+    if (pb.piece >= 0) {               // tile-aligned key range of this piece
+        const int tiles = (item_hi + BN - 1) / BN;
+        pb.lo = (int)((int64_t)pb.piece * tiles / a.pieces) * BN;
+        pb.hi = min(item_hi, (int)((int64_t)(pb.piece + 1) * tiles / a.pieces) * BN);
+        if (pb.lo >= pb.hi) {           // fewer tiles than pieces: an empty range
+            for (int r = threadIdx.x; r < BM; r += blockDim.x) {
+                const RowInfo ri = pb.row(r);
+                if (ri.part) { ri.part[0] = NEG_SENTINEL; ri.part[1] = 0.f; }
+            }
+            return;
+        }
+    }
     attn_tile<KVK, 0>(pb, a.ktab, a.vtab, a.n_kv, a.scale, smem_raw);
+}
+
+// Merge the pieces of the split items: one block per (item, token), thread = dim, six heads.
+__global__ void __launch_bounds__(HD)
+k_prefill_fixup(const __grid_constant__ TileArgs a) {
+    pdl_wait();
+    const int item = a.n_full + blockIdx.y;
+    const int kvh = item / a.nx;
+    const int t = a.t0 + (item % a.nx) * TOK_PER_TILE + blockIdx.x;
+    if (t >= a.t_end) return;
+#pragma unroll
+    for (int j = 0; j < GQA; j++) {
+        const int h = kvh * GQA + j;
+        const float* pp = a.part + (((size_t)h * a.part_rows + (t - a.t0)) * PF_SPLIT_MAX) * PART;
+        float mg = NEG_SENTINEL;
+        for (int p = 0; p < a.pieces; p++) mg = fmaxf(mg, pp[(size_t)p * PART]);
+        float lg = 0.f, acc = 0.f;
+        for (int p = 0; p < a.pieces; p++) {
+            const float ms = pp[(size_t)p * PART];
+            if (ms == NEG_SENTINEL) continue;          // its accumulator was never written
+            const float w = expf(ms - mg);
+            lg += pp[(size_t)p * PART + 1] * w;
+            acc += pp[(size_t)p * PART + 2 + threadIdx.x] * w;
+        }
+        a.outT[(size_t)t * a.out_row + (size_t)h * HD + threadIdx.x] = lg > 0.f ? acc / lg : 0.f;
+    }
 }
 
 template <int KVK>
@@ -870,30 +943,53 @@ int set_attrs() {
 } // namespace
 
 int launch_prefill_umma(const float* qT, int q_stride, int q_row, const void* const* ktab,
-                        const void* const* vtab, float* outT, int out_row, int base_pos, int t0,
-                        int SB, int n_q, int n_kv, float scale, cudaStream_t st, int kvk,
-                        bool* done) {
+                        const void* const* vtab, float* outT, int out_row, float* part,
+                        int base_pos, int t0, int SB, int n_q, int n_kv, float scale,
+                        int sm_count, cudaStream_t st, int kvk, bool* done) {
     *done = false;
     (void)n_q;
     // float4 loads of Q rows and float4 stores of output rows
     if ((q_stride & 3) || (q_row & 3) || (out_row & 3) || ((uintptr_t)qT & 15) || ((uintptr_t)outT & 15))
         return Q27_OK;
-    TileArgs a{qT, ktab, vtab, outT, q_stride, q_row, out_row, base_pos, t0, t0 + SB, n_kv, scale};
-    dim3 grid((SB + TOK_PER_TILE - 1) / TOK_PER_TILE, n_kv);
+    TileArgs a{qT, ktab, vtab, outT, q_stride, q_row, out_row, base_pos, t0, t0 + SB, n_kv, scale,
+               part, (SB + 15) / 16 * 16, (SB + TOK_PER_TILE - 1) / TOK_PER_TILE, 0, 1};
+    // One CTA per SM: the items beyond the last full wave would hold the machine for a whole
+    // item time at partial occupancy. They are cut into P key ranges each, P chosen so the
+    // pieces pack into the fewest piece-times (a row's scratch has room for 8 pieces).
+    const int items = a.nx * n_kv;
+    a.n_full = items;
+    const int tail = items % sm_count;
+    if (part && ((uintptr_t)part & 15) == 0 && tail > 0) {
+        const int min_tiles = (base_pos + min(t0 + TOK_PER_TILE, t0 + SB) + BN - 1) / BN;
+        int best = 1;
+        double best_time = 1.0;
+        for (int P = 2; P <= PF_SPLIT_MAX && P <= min_tiles; P++) {
+            const double tm = (double)((tail * P + sm_count - 1) / sm_count) / P;
+            if (tm < best_time - 0.05) { best_time = tm; best = P; }
+        }
+        if (best > 1) {
+            a.n_full = items - tail;
+            a.pieces = best;
+        }
+    }
+    const int ncta = a.n_full + (items - a.n_full) * a.pieces;
     int rc;
     if (kvk == Q27_KV_F16) {
         if ((rc = set_attrs<Q27_KV_F16>())) return rc;
-        k_prefill_umma<Q27_KV_F16><<<grid, UMMA_THREADS, UMMA_SMEM, st>>>(a);
+        k_prefill_umma<Q27_KV_F16><<<ncta, UMMA_THREADS, UMMA_SMEM, st>>>(a);
     } else if (kvk == Q27_KV_FP8) {
         if ((rc = set_attrs<Q27_KV_FP8>())) return rc;
-        k_prefill_umma<Q27_KV_FP8><<<grid, UMMA_THREADS, UMMA_SMEM, st>>>(a);
+        k_prefill_umma<Q27_KV_FP8><<<ncta, UMMA_THREADS, UMMA_SMEM, st>>>(a);
     } else if (kvk == Q27_KV_T3) {
         if ((rc = set_attrs<Q27_KV_T3>())) return rc;
-        k_prefill_umma<Q27_KV_T3><<<grid, UMMA_THREADS, UMMA_SMEM, st>>>(a);
+        k_prefill_umma<Q27_KV_T3><<<ncta, UMMA_THREADS, UMMA_SMEM, st>>>(a);
     } else {
         return Q27_ERR_UNSUPPORTED_KIND;
     }
     Q27_CUDA_TRY(cudaGetLastError());
+    if (a.pieces > 1)
+        Q27_CUDA_TRY(launch_pdl(k_prefill_fixup, dim3(TOK_PER_TILE, items - a.n_full), dim3(HD),
+                                0, st, a));
     *done = true;
     return Q27_OK;
 }

@@ -5,10 +5,11 @@
 
 namespace q27b {
 
+// part: the caller's prefill scratch (24 * roundup16(SB) * 8 * 258 floats) or NULL.
 int launch_prefill_umma(const float* qT, int q_stride, int q_row, const void* const* ktab,
-                        const void* const* vtab, float* outT, int out_row, int base_pos, int t0,
-                        int SB, int n_q, int n_kv, float scale, cudaStream_t st, int kvk,
-                        bool* done);
+                        const void* const* vtab, float* outT, int out_row, float* part,
+                        int base_pos, int t0, int SB, int n_q, int n_kv, float scale,
+                        int sm_count, cudaStream_t st, int kvk, bool* done);
 
 // Writes split-KV partials for every lane of every slot in ONE pass over the cache per
 // (slot, kv head, split); fills b.nsplit / b.unit for the combine.
