@@ -745,20 +745,26 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             constexpr int RAW_BYTES = BN * 2 * T3_BLK;
             uint8_t* raw = raw_sm + side * 2 * RAW_BYTES;
             const uint32_t rfull = raw_full + 8 * (2 * side), rempty = raw_empty + 8 * (2 * side);
+            // this thread's 13 words of a tile: source offset inside the page and key index are
+            // the same for every tile
+            uint32_t soff[13];
+            int wkey[13];
+#pragma unroll
+            for (int n = 0; n < 13; n++) {
+                const int w = p + NPROD * n;              // word 0..1599 of the tile's rows
+                const int key = w / 25, j = w - 25 * key;
+                wkey[n] = w < BN * 25 ? key : BN;         // BN: never below the tile's key count
+                soff[n] = (uint32_t)((key * n_kv + pb.kvh) * (2 * T3_BLK) + 4 * j);
+            }
             auto issue_raw = [&](int i) {
                 const int buf = i & 1, nk = nkeys_of(i);
                 const uint8_t* page = page_of(i);
-                const uint32_t dst = s32(raw + buf * RAW_BYTES);
+                const uint32_t dst = s32(raw + buf * RAW_BYTES) + 4 * p;
 #pragma unroll
-                for (int n = 0; n < 13; n++) {
-                    const int w = p + NPROD * n;          // word 0..1599 of the tile's rows
-                    const int key = w / 25, j = w - 25 * key;
-                    if (w < BN * 25 && key < nk)
+                for (int n = 0; n < 13; n++)
+                    if (wkey[n] < nk)
                         asm volatile("cp.async.ca.shared.global [%0], [%1], 4;"
-                                     ::"r"(dst + 4 * w),
-                                       "l"(page + ((size_t)key * n_kv + pb.kvh) * (2 * T3_BLK) + 4 * j)
-                                     : "memory");
-                }
+                                     ::"r"(dst + 4 * NPROD * n), "l"(page + soff[n]) : "memory");
                 asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
                              ::"r"(rfull + 8 * buf) : "memory");
             };
@@ -954,18 +960,22 @@ int launch_prefill_umma(const float* qT, int q_stride, int q_row, const void* co
     TileArgs a{qT, ktab, vtab, outT, q_stride, q_row, out_row, base_pos, t0, t0 + SB, n_kv, scale,
                part, (SB + 15) / 16 * 16, (SB + TOK_PER_TILE - 1) / TOK_PER_TILE, 0, 1};
     // One CTA per SM: the items beyond the last full wave would hold the machine for a whole
-    // item time at partial occupancy. They are cut into P key ranges each, P chosen so the
-    // pieces pack into the fewest piece-times (a row's scratch has room for 8 pieces).
+    // item time at partial occupancy. They are cut into P key ranges each when that pays: a
+    // piece costs its share of the item's tiles plus a fixed ~32 tile-times (measured: pipeline
+    // fill and drain, Q staging, scattered partial stores), the fix-up kernel ~10 more, against one
+    // item time for leaving the tail whole (a row's scratch has room for 8 pieces).
     const int items = a.nx * n_kv;
     a.n_full = items;
     const int tail = items % sm_count;
     if (part && ((uintptr_t)part & 15) == 0 && tail > 0) {
-        const int min_tiles = (base_pos + min(t0 + TOK_PER_TILE, t0 + SB) + BN - 1) / BN;
+        const int min_tiles = (base_pos + t0 + min(TOK_PER_TILE, SB) + BN - 1) / BN;
+        const double item_tiles = (base_pos + t0 + 0.5 * SB) / BN;
         int best = 1;
-        double best_time = 1.0;
+        double best_cost = 0.95 * (item_tiles + 6.0);
         for (int P = 2; P <= PF_SPLIT_MAX && P <= min_tiles; P++) {
-            const double tm = (double)((tail * P + sm_count - 1) / sm_count) / P;
-            if (tm < best_time - 0.05) { best_time = tm; best = P; }
+            const int rounds = (tail * P + sm_count - 1) / sm_count;
+            const double cost = rounds * (item_tiles / P + 32.0) + 10.0;
+            if (cost < best_cost) { best_cost = cost; best = P; }
         }
         if (best > 1) {
             a.n_full = items - tail;

@@ -14,7 +14,7 @@ pytestmark = pytest.mark.gpu
 
 
 def run_prefill(oracle, cuda, kvk, base, T, t0=0, SB=None, seed=1, exact=False, scatter=None,
-                bf16=False):
+                bf16=False, with_part=True):
     SB = T - t0 if SB is None else SB
     c = synth.make_case(oracle, kvk, rows=base + T, pos=[0] * T, seed=seed, bf16=bf16)
     ref = synth.scale_out(c, oracle.attn_prefill(c.q, c.k, c.v, kvk, base, t0, SB))
@@ -26,8 +26,9 @@ def run_prefill(oracle, cuda, kvk, base, T, t0=0, SB=None, seed=1, exact=False, 
     qT = torch.from_numpy(c.q.reshape(T, -1).copy()).to(cuda)
     outT = torch.zeros((T, synth.OUT_ROW), device=cuda)
     part = torch.full((Q.prefill_part_floats(SB),), float("nan"), device=cuda)
-    Q.attn_prefill_T(qT, synth.Q_STRIDE, synth.Q_ROW, ks.tab, vs.tab, outT, synth.OUT_ROW, part,
-                     base, t0, SB, 24, 4, 256, SCALE, kvk=kvk, exact=exact)
+    Q.attn_prefill_T(qT, synth.Q_STRIDE, synth.Q_ROW, ks.tab, vs.tab, outT, synth.OUT_ROW,
+                     part if with_part else None, base, t0, SB, 24, 4, 256, SCALE, kvk=kvk,
+                     exact=exact)
     torch.cuda.synchronize()
     return synth.scale_out(c, outT.cpu().numpy()), ref
 
@@ -65,3 +66,26 @@ def test_prefill_deep_prefix_bf16_values(oracle, cuda):
 def test_prefill_no_prefix_first_row_is_v0(oracle, cuda):
     got, ref = run_prefill(oracle, cuda, KV_F16, base=0, T=70, seed=9)
     assert synth.tolerance_ok(got, ref)[0]
+
+
+@pytest.mark.parametrize("kvk", [KV_F16, KV_T3])
+def test_prefill_tail_items_split_into_key_ranges(oracle, cuda, kvk):
+    """With scratch given, the items that do not fill a wave of SMs are cut into key-range
+    pieces whose partials a fix-up kernel merges (here: 32 items, four pieces each; the
+    scratch starts as NaN, so a piece that was skipped or read early would show). Without
+    scratch the same call runs every item whole; both match the oracle and each other."""
+    base, T = 4096 + 37, 160
+    split, ref = run_prefill(oracle, cuda, kvk, base=base, T=T, seed=12, scatter=7)
+    whole, _ = run_prefill(oracle, cuda, kvk, base=base, T=T, seed=12, scatter=7, with_part=False)
+    assert np.isfinite(split).all()
+    assert synth.tolerance_ok(split, ref)[0]
+    assert synth.tolerance_ok(whole, ref)[0]
+    # same tiles, same operands; the pieces round P against their own running maxima
+    assert np.abs(split - whole).max() <= 1e-3 * np.abs(ref).max()
+
+
+def test_prefill_tail_split_sub_batch(oracle, cuda):
+    """A sub-batch (t0 > 0) through the split path: rows outside [t0, t0 + SB) stay untouched."""
+    got, ref = run_prefill(oracle, cuda, KV_F16, base=6000, T=200, t0=30, SB=150, seed=13)
+    assert synth.tolerance_ok(got[30:180], ref[30:180])[0]
+    assert (got[:30] == 0).all() and (got[180:] == 0).all()
