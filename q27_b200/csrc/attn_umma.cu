@@ -278,30 +278,14 @@ struct Problem {
 };
 
 // Staging of one 64-key tile of ONE side (K or V) as fp16 into the swizzled operand layout
-// by that side's 128 threads: `half_load` pulls the raw bytes into registers (issued before
-// the ring slot is free, so the global latency hides behind the tiles in flight),
-// `half_store` converts and writes them once the slot has been released. fp16 rows need
-// neither: they go from global to shared memory with cp.async.
+// by that side's 128 threads. fp16 rows go from global to shared memory with cp.async,
+// straight into that layout. fp8 and turbo3 rows come in packed (coalesced asynchronous
+// copies into raw shared-memory buffers); each thread then takes its share into registers
+// (`RawHalf`) and `half_store` converts and writes it once the ring slot has been released.
 template <int KVK> struct RawHalf;
 template <> struct RawHalf<Q27_KV_F16> { };
 template <> struct RawHalf<Q27_KV_FP8> { uint2 d[16]; };
 template <> struct RawHalf<Q27_KV_T3> { uint32_t w[14]; };
-
-template <int KVK>
-__device__ __forceinline__ void half_load(RawHalf<KVK>& t, const uint8_t* page, int nkeys, int n_kv,
-                                          int kvh, int p) {
-    if constexpr (KVK == Q27_KV_FP8) {
-#pragma unroll
-        for (int n = 0; n < 16; n++) {
-            const int q = p + NPROD * n;
-            const int key = q >> 5, ch = q & 31;
-            t.d[n] = make_uint2(0, 0);                  // rows past the range: exact zeros
-            if (key < nkeys)
-                t.d[n] = __ldg(reinterpret_cast<const uint2*>(
-                    page + ((size_t)key * n_kv + kvh) * HD + (size_t)ch * 8));
-        }
-    }
-}
 
 // BLK (turbo3 only): which of the two blocks of a (key, kv head) the thread decodes; warp-uniform
 template <int KVK, int BLK = 0>
@@ -372,7 +356,9 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     uint8_t* v_sm = k_sm + K_SLOTS * KT_BYTES;
     // turbo3 gives its third V slot to a raw staging area: the packed rows of a tile are
     // fetched with coalesced asynchronous copies and decoded from shared memory
-    constexpr int VSL = KVK == Q27_KV_T3 ? 2 : V_SLOTS;
+    // (fp8: the third K slot and the third V slot each hold a side's two raw buffers)
+    constexpr int VSL = KVK == Q27_KV_F16 ? V_SLOTS : 2;
+    constexpr int KSL = KVK == Q27_KV_FP8 ? 2 : K_SLOTS;
     uint8_t* raw_sm = v_sm + 2 * KT_BYTES;
     // A K slot is released as soon as its S MMAs have run, a V slot after its PV MMAs.
     // pvb[b] completes when the PV MMAs of a tile that used S/P buffer b have run: it frees
@@ -385,7 +371,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     TRACE_DECL();
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < K_SLOTS; s++) {
+        for (int s = 0; s < KSL; s++) {
             bar_init(k_full + 8 * s, NPROD);
             bar_init(k_empty + 8 * s, 1);
         }
@@ -607,8 +593,8 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             const uint64_t kd_base = make_desc(s32(k_sm), 0, 1024);
             bool ok = true;
             for (int i = warp - MMA_WARP; i < ntiles && ok; i += N_S_WARPS) {
-                const int ks_ = i % K_SLOTS, b = i % S_BUFS;
-                const uint32_t kpar = (uint32_t)((i / K_SLOTS) & 1);
+                const int ks_ = i % KSL, b = i % S_BUFS;
+                const uint32_t kpar = (uint32_t)((i / KSL) & 1);
                 const uint32_t bpar = (uint32_t)(((i / S_BUFS) - 1) & 1);   // previous use of buffer b
                 { TRACE_T0();
                   ok = bar_wait(k_full + 8 * ks_, kpar);
@@ -693,7 +679,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         // exactly one cache page
         const int side = (warp - FIRST_LOAD_WARP) >> 2;                 // 0 = K, 1 = V
         const int p = threadIdx.x - (FIRST_LOAD_WARP + 4 * side) * 32;  // 0..127 within the side
-        const int nslots = side ? VSL : K_SLOTS;
+        const int nslots = side ? VSL : KSL;
         const uint32_t full = side ? v_full : k_full, empty = side ? v_empty : k_empty;
         uint8_t* ring = side ? v_sm : k_sm;
         const void* const* tab = side ? vtab : ktab;
@@ -730,6 +716,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                         *reinterpret_cast<uint4*>(dst + off) = make_uint4(0, 0, 0, 0);
                     }
                 }
+                if (nk < BN) __threadfence_block();        // the zeros, before the arrival below
                 asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
                              ::"r"(full + 8 * st) : "memory");
                 if (p == 0 && side == 0) TRACE_EV(11, i);
@@ -805,30 +792,58 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
         } else {
-            RawHalf<KVK> raw0, raw1;
-            auto load = [&](RawHalf<KVK>& rw, int i) {
-                if (i < ntiles) half_load<KVK>(rw, page_of(i), nkeys_of(i), n_kv, pb.kvh, p);
+            // fp8: a tile's rows of this kv head (64 keys x 256 B) come in with coalesced
+            // 16-byte asynchronous copies into one of two raw buffers per side, and each
+            // thread converts its sixteen 8-byte pieces from shared memory. (Holding two
+            // tiles of raw bytes in registers instead spilled and made this path the
+            // bottleneck of the fp8 kernels.)
+            constexpr int RAW_BYTES = BN * HD;            // 16384
+            uint8_t* raw = (side ? v_sm : k_sm) + 2 * KT_BYTES;
+            const uint32_t rfull = raw_full + 8 * (2 * side), rempty = raw_empty + 8 * (2 * side);
+            auto issue_raw = [&](int i) {
+                const int buf = i & 1, nk = nkeys_of(i);
+                const uint8_t* page = page_of(i);
+                uint8_t* dst = raw + buf * RAW_BYTES;
+#pragma unroll
+                for (int n = 0; n < 8; n++) {
+                    const int q = p + NPROD * n;          // 16-byte chunk 0..1023
+                    const int key = q >> 4, c16 = q & 15;
+                    if (key < nk)
+                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                                     ::"r"(s32(dst + q * 16)),
+                                       "l"(page + ((size_t)key * n_kv + pb.kvh) * HD + c16 * 16)
+                                     : "memory");
+                    else                                   // rows past the range: exact zeros
+                        *reinterpret_cast<uint4*>(dst + q * 16) = make_uint4(0, 0, 0, 0);
+                }
+                if (nk < BN) __threadfence_block();        // the zeros, before the arrival below
+                asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
+                             ::"r"(rfull + 8 * buf) : "memory");
             };
-            auto store = [&](const RawHalf<KVK>& rw, int i) -> bool {
-                if (!wait_slot(i)) return false;
+            if (ntiles > 0) issue_raw(0);
+            if (ntiles > 1) issue_raw(1);
+            for (int i = 0; i < ntiles; i++) {
+                const int buf = i & 1;
+                const uint32_t par = (uint32_t)((i >> 1) & 1);
+                if (!bar_wait(rfull + 8 * buf, par)) break;
+                RawHalf<KVK> rw;
+#pragma unroll
+                for (int n = 0; n < 16; n++)
+                    rw.d[n] = *reinterpret_cast<const uint2*>(raw + buf * RAW_BYTES + (p + NPROD * n) * 8);
+                bar_arrive(rempty + 8 * buf);
+                if (i + 2 < ntiles) {
+                    if (!bar_wait(rempty + 8 * buf, par)) break;
+                    issue_raw(i + 2);
+                }
+                if (!wait_slot(i)) break;
                 const int st = i % nslots;
                 { TRACE_T0();
                   half_store<KVK>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
                   fence_async_smem();
                   TRACE_ADD(6, p == 0 && side == 0); }
                 bar_arrive(full + 8 * st);
-                return true;
-            };
-            load(raw0, 0);
-            load(raw1, 1);
-            for (int i = 0; i < ntiles; i += 2) {
-                if (!store(raw0, i)) break;
-                load(raw0, i + 2);
-                if (i + 1 < ntiles) {
-                    if (!store(raw1, i + 1)) break;
-                    load(raw1, i + 3);
-                }
             }
+            asm volatile("cp.async.wait_all;" ::: "memory");
         }
     }
     TRACE_FLUSH();
