@@ -324,22 +324,23 @@ __device__ __forceinline__ void half_store(const RawHalf<KVK>& t, uint8_t* dst, 
             t3_selectors(Qw, S16, ze, zo);
             t3_lookup(tab, ze, e);                // (0,2) (4,6) (8,10) (12,14)
             t3_lookup(tab, zo, o);                // (1,3) (5,7) (9,11) (13,15)
-            uint32_t nat[8];
+            // The lookups give (even dims) and (odd dims) of the group. They are stored as they
+            // are: positions 0..7 of a 16-dim group hold its even dims, 8..15 its odd dims.
+            // Q is staged with the same permutation (a dot product does not care) and the
+            // output columns are put back in order in the epilogue, so the eight PRMTs per
+            // group that would interleave them are never spent.
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                nat[2 * i] = prmt(e[i], o[i], 0x5410u);      // dims 4i, 4i+1
-                nat[2 * i + 1] = prmt(e[i], o[i], 0x7632u);  // dims 4i+2, 4i+3
+            for (int i = 0; i < 4; i++) {   // fp16 centroid x fp16 norm, rounded once
+                __half2 he = __hmul2(*reinterpret_cast<__half2*>(&e[i]), n2);
+                __half2 ho = __hmul2(*reinterpret_cast<__half2*>(&o[i]), n2);
+                e[i] = *reinterpret_cast<uint32_t*>(&he);
+                o[i] = *reinterpret_cast<uint32_t*>(&ho);
             }
-#pragma unroll
-            for (int i = 0; i < 8; i++) {   // fp16 centroid x fp16 norm, rounded once
-                __half2 h = __hmul2(*reinterpret_cast<__half2*>(&nat[i]), n2);
-                nat[i] = *reinterpret_cast<uint32_t*>(&h);
-            }
-            const int ch = 16 * blk + 2 * g8;    // 8-dim chunk index within the head
+            const int ch = 16 * blk + 2 * g8;    // 8-position chunk index within the head
             *reinterpret_cast<uint4*>(dst + (ch >> 3) * (BN * 128) + sw128(key, ch & 7)) =
-                make_uint4(nat[0], nat[1], nat[2], nat[3]);
+                make_uint4(e[0], e[1], e[2], e[3]);
             *reinterpret_cast<uint4*>(dst + ((ch + 1) >> 3) * (BN * 128) + sw128(key, (ch + 1) & 7)) =
-                make_uint4(nat[4], nat[5], nat[6], nat[7]);
+                make_uint4(o[0], o[1], o[2], o[3]);
         }
     }
 }
@@ -418,13 +419,24 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             for (int u = 0; u < 4; u++) {
                 if (idx[u] >= BM * (HD / 4)) continue;
                 const int row = idx[u] >> 6, d = (idx[u] & 63) * 4;
-                __half2 h0 = __floats2half2_rn(v[u].x, v[u].y), h1 = __floats2half2_rn(v[u].z, v[u].w);
-                const uint2 w = make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
-                if (d >= Q_TMEM_DIMS) {
-                    const int c2 = (d - Q_TMEM_DIMS) >> 3;
-                    *reinterpret_cast<uint2*>(q_sm + (c2 >> 3) * (BM * 128) + sw128(row, c2 & 7) + (d & 7) * 2) = w;
+                // where the 16-bit value of operand position X of this row lives
+                auto q_loc = [&](int X) -> uint8_t* {
+                    if (X >= Q_TMEM_DIMS) {
+                        const int c2 = (X - Q_TMEM_DIMS) >> 3;
+                        return q_sm + (c2 >> 3) * (BM * 128) + sw128(row, c2 & 7) + (X & 7) * 2;
+                    }
+                    return k_sm + row * QT_PITCH + X * 2;
+                };
+                if constexpr (KVK == Q27_KV_T3) {
+                    // turbo3 operand order (see half_store): evens of a 16-dim group, then odds
+                    __half2 he = __floats2half2_rn(v[u].x, v[u].z), ho = __floats2half2_rn(v[u].y, v[u].w);
+                    const int X = (d & ~15) + ((d & 15) >> 1);
+                    *reinterpret_cast<uint32_t*>(q_loc(X)) = *reinterpret_cast<uint32_t*>(&he);
+                    *reinterpret_cast<uint32_t*>(q_loc(X + 8)) = *reinterpret_cast<uint32_t*>(&ho);
                 } else {
-                    *reinterpret_cast<uint2*>(k_sm + row * QT_PITCH + d * 2) = w;
+                    __half2 h0 = __floats2half2_rn(v[u].x, v[u].y), h1 = __floats2half2_rn(v[u].z, v[u].w);
+                    *reinterpret_cast<uint2*>(q_loc(d)) =
+                        make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
                 }
             }
         }
@@ -567,15 +579,22 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                     float o[32];
                     tc_ld32(lane_base + COL_O + c, o);
                     tc_wait_ld();
+                    // register that holds natural column n of this 32-column chunk (turbo3
+                    // operand order: evens of a 16-dim group, then odds)
+                    auto reg = [](int n) {
+                        return KVK == Q27_KV_T3 ? (n & 16) + ((n & 1) ? 8 + ((n & 15) >> 1) : ((n & 15) >> 1)) : n;
+                    };
                     if (ri.out) {
 #pragma unroll
                         for (int e = 0; e < 32; e += 4)
                             *reinterpret_cast<float4*>(ri.out + c + e) =
-                                make_float4(o[e] * inv, o[e + 1] * inv, o[e + 2] * inv, o[e + 3] * inv);
+                                make_float4(o[reg(e)] * inv, o[reg(e + 1)] * inv, o[reg(e + 2)] * inv,
+                                            o[reg(e + 3)] * inv);
                     } else if (ri.part) {
 #pragma unroll
                         for (int e = 0; e < 32; e += 2)
-                            *reinterpret_cast<float2*>(ri.part + 2 + c + e) = make_float2(o[e], o[e + 1]);
+                            *reinterpret_cast<float2*>(ri.part + 2 + c + e) =
+                                make_float2(o[reg(e)], o[reg(e + 1)]);
                     }
                 }
             }
