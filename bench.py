@@ -54,7 +54,8 @@ FP8_DEQ_SCALE = 6.0 / 448.0
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from the
 # ncu captures summarised under profiles/ (None until a capture exists for the workload)
-NCU_TRAFFIC = {"c3": 215.6e6}   # profiles/decode_mma_turbo3_c3.md
+NCU_TRAFFIC = {"c3": 215.6e6,   # profiles/decode_mma_turbo3_c3.md
+               "c2": 68.9e6}    # profiles/verify_umma_fp8_c2.md
 
 
 def measured_peak_gbs() -> tuple[float, str]:
