@@ -265,6 +265,40 @@ __device__ __forceinline__ void softmax_tile(WarpAcc& A, const float (&s)[4], fl
     A.l[1] += p[1] + p[3];
 }
 
+// The same for two tiles (32 keys) in one step: one max, one rescale.
+__device__ __forceinline__ void softmax_pair(WarpAcc& A, const float (&s)[4], const float (&t)[4],
+                                             float (&p)[4], float (&q)[4]) {
+    float mx0 = fmaxf(fmaxf(s[0], s[2]), fmaxf(t[0], t[2]));
+    float mx1 = fmaxf(fmaxf(s[1], s[3]), fmaxf(t[1], t[3]));
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float mn0 = fmaxf(A.m[0], mx0), mn1 = fmaxf(A.m[1], mx1);
+    if (mn0 > A.m[0] || mn1 > A.m[1]) { // rescale (every thread of a column group agrees)
+        const float a0 = ex2(A.m[0] - mn0), a1 = ex2(A.m[1] - mn1);
+        A.l[0] *= a0;
+        A.l[1] *= a1;
+#pragma unroll
+        for (int mt = 0; mt < 16; mt++) {
+            A.o[mt][0] *= a0; A.o[mt][1] *= a1; A.o[mt][2] *= a0; A.o[mt][3] *= a1;
+        }
+        A.m[0] = mn0;
+        A.m[1] = mn1;
+    }
+    p[0] = ex2(s[0] - A.m[0]);
+    p[1] = ex2(s[1] - A.m[1]);
+    p[2] = ex2(s[2] - A.m[0]);
+    p[3] = ex2(s[3] - A.m[1]);
+    q[0] = ex2(t[0] - A.m[0]);
+    q[1] = ex2(t[1] - A.m[1]);
+    q[2] = ex2(t[2] - A.m[0]);
+    q[3] = ex2(t[3] - A.m[1]);
+    A.l[0] += (p[0] + p[2]) + (q[0] + q[2]);
+    A.l[1] += (p[1] + p[3]) + (q[1] + q[3]);
+}
+
 // ---- tile processors ------------------------------------------------------------------
 // Each consumes one 16-key tile of one kv head from the ring stage. `valid` = number of
 // real keys in the tile (rows >= valid are masked). qf = Q^T fragments, 2 regs per step.
@@ -360,12 +394,14 @@ __device__ __forceinline__ void tile_fp8(WarpAcc& A, uint32_t ks, uint32_t vs,
     }
 }
 
-__device__ __forceinline__ void tile_t3(WarpAcc& A, uint32_t ks, uint32_t vs, int kvh,
-                                        const uint32_t (&qf)[16][2], int valid, float sc2,
-                                        int lane, const T3Tab& tab) {
+// turbo3, one 16-key tile, K side: centroid dot products per 128-dim block recombined with the
+// block norms; s[4] = scores in the log2 domain for rows g, g+8 and columns 2c, 2c+1
+// (masked rows -inf).
+__device__ __forceinline__ void t3_scores(uint32_t ks, int kvh, const uint32_t (&qf)[16][2],
+                                          int valid, float sc2, int lane, const T3Tab& tab,
+                                          float (&sv)[4]) {
     constexpr int P = Fmt<Q27_KV_T3>::PITCH;
     const int g = lane >> 2, c = lane & 3;
-    // ---- scores: per 128-dim block an accumulator of centroid dot products ----
     float dk[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
     const uint32_t kr0 = ks + g * P + kvh * 100;
     const uint32_t kr1 = kr0 + 8 * P;
@@ -383,15 +419,10 @@ __device__ __forceinline__ void tile_t3(WarpAcc& A, uint32_t ks, uint32_t vs, in
             uint32_t ze0, zo0, ze1, zo1, h0[8], h1[8];
             t3_selectors(lds32_a2(q0 + 4 * w, al), w ? s0 >> 16 : s0 & 0xffffu, ze0, zo0);
             t3_selectors(lds32_a2(q1 + 4 * w, al), w ? s1 >> 16 : s1 & 0xffffu, ze1, zo1);
-            if (Q27_ABLATE & 1) {
-#pragma unroll
-                for (int x = 0; x < 8; x++) { h0[x] = ze0 + x; h1[x] = zo1 ^ x; }
-            } else {
-                t3_lookup(tab, ze0, h0);
-                t3_lookup(tab, zo0, h0 + 4);
-                t3_lookup(tab, ze1, h1);
-                t3_lookup(tab, zo1, h1 + 4);
-            }
+            t3_lookup(tab, ze0, h0);
+            t3_lookup(tab, zo0, h0 + 4);
+            t3_lookup(tab, ze1, h1);
+            t3_lookup(tab, zo1, h1 + 4);
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 const int s = 8 * b + 4 * w + i;
@@ -400,15 +431,19 @@ __device__ __forceinline__ void tile_t3(WarpAcc& A, uint32_t ks, uint32_t vs, in
             }
         }
     }
-    // norms: K for the score recombination, V folded into P
     const float nk00 = lds_half(kr0), nk01 = lds_half(kr0 + 50);
     const float nk10 = lds_half(kr1), nk11 = lds_half(kr1 + 50);
-    float sv[4], p[4];
     sv[0] = g < valid ? (dk[0][0] * nk00 + dk[1][0] * nk01) * sc2 : -INFINITY;
     sv[1] = g < valid ? (dk[0][1] * nk00 + dk[1][1] * nk01) * sc2 : -INFINITY;
     sv[2] = g + 8 < valid ? (dk[0][2] * nk10 + dk[1][2] * nk11) * sc2 : -INFINITY;
     sv[3] = g + 8 < valid ? (dk[0][3] * nk10 + dk[1][3] * nk11) * sc2 : -INFINITY;
-    softmax_tile(A, sv, p);
+}
+
+// turbo3, one 16-key tile, V side: O^T += V^T . P^T with the V norms folded into P.
+__device__ __forceinline__ void t3_values(WarpAcc& A, uint32_t vs, int kvh, const float (&p)[4],
+                                          int valid, int lane, const T3Tab& tab) {
+    constexpr int P = Fmt<Q27_KV_T3>::PITCH;
+    const int g = lane >> 2, c = lane & 3;
     const uint32_t vr0 = vs + g * P + kvh * 100;
     const uint32_t vr1 = vr0 + 8 * P;
     uint32_t pb[2][2]; // [block][key half] P^T fragments with the V norm folded in
@@ -420,8 +455,8 @@ __device__ __forceinline__ void tile_t3(WarpAcc& A, uint32_t ks, uint32_t vs, in
         pb[b][0] = movmatrix_t(pack_h2(p[0] * n0, p[1] * n0));
         pb[b][1] = movmatrix_t(pack_h2(p[2] * n1, p[3] * n1));
     }
-    // ---- V: this thread's keys are 2c, 2c+1 (pair 0) and 2c+8, 2c+9 (pair 1); its dims
-    // are [16g, 16g+16) of each block: one qs word + 16 sign bits per (key, block) ----
+    // this thread's keys are 2c, 2c+1 (pair 0) and 2c+8, 2c+9 (pair 1); its dims are
+    // [16g, 16g+16) of each block: one qs word + 16 sign bits per (key, block)
 #pragma unroll
     for (int b = 0; b < 2; b++) {
         const bool al = (b == 1);
@@ -440,21 +475,41 @@ __device__ __forceinline__ void tile_t3(WarpAcc& A, uint32_t ks, uint32_t vs, in
             const uint32_t ze_hi = ((ea >> 4) & 0x0F0F0F0Fu) | (eb & 0xF0F0F0F0u);
             const uint32_t zo_lo = (oa & 0x0F0F0F0Fu) | ((ob << 4) & 0xF0F0F0F0u);
             const uint32_t zo_hi = ((oa >> 4) & 0x0F0F0F0Fu) | (ob & 0xF0F0F0F0u);
-            if (Q27_ABLATE & 2) {
-#pragma unroll
-                for (int x = 0; x < 16; x++) hp[pr][x] = (ze_lo + x) ^ zo_hi ^ (ze_hi + zo_lo);
-            } else {
-                t3_lookup(tab, ze_lo, hp[pr]);       // dims e16 = 0, 4, 8, 12
-                t3_lookup(tab, ze_hi, hp[pr] + 4);   // 2, 6, 10, 14
-                t3_lookup(tab, zo_lo, hp[pr] + 8);   // 1, 5, 9, 13
-                t3_lookup(tab, zo_hi, hp[pr] + 12);  // 3, 7, 11, 15
-            }
+            t3_lookup(tab, ze_lo, hp[pr]);       // dims e16 = 0, 4, 8, 12
+            t3_lookup(tab, ze_hi, hp[pr] + 4);   // 2, 6, 10, 14
+            t3_lookup(tab, zo_lo, hp[pr] + 8);   // 1, 5, 9, 13
+            t3_lookup(tab, zo_hi, hp[pr] + 12);  // 3, 7, 11, 15
         }
 #pragma unroll
         for (int j = 0; j < 8; j++)
             mma16816(A.o[8 * b + j], hp[0][2 * j], hp[0][2 * j + 1], hp[1][2 * j],
                      hp[1][2 * j + 1], pb[b][0], pb[b][1]);
     }
+}
+
+__device__ __forceinline__ void tile_t3(WarpAcc& A, uint32_t ks, uint32_t vs, int kvh,
+                                        const uint32_t (&qf)[16][2], int valid, float sc2,
+                                        int lane, const T3Tab& tab) {
+    float sv[4], p[4];
+    t3_scores(ks, kvh, qf, valid, sc2, lane, tab, sv);
+    softmax_tile(A, sv, p);
+    t3_values(A, vs, kvh, p, valid, lane, tab);
+}
+
+// Both 16-key tiles of a ring stage at once: the two score computations are independent
+// instruction streams (a lone tile is a chain of dependent PRMT / LOP3 / MMA results and its
+// warp spends most cycles waiting on fixed latencies), and one online-softmax step covers the
+// 32 keys. valid = real keys among the 32 (17..32).
+__device__ __forceinline__ void tile_t3_pair(WarpAcc& A, uint32_t ks, uint32_t vs, int kvh,
+                                             const uint32_t (&qf)[16][2], int valid, float sc2,
+                                             int lane, const T3Tab& tab) {
+    constexpr int P = Fmt<Q27_KV_T3>::PITCH;
+    float s0[4], s1[4], p0[4], p1[4];
+    t3_scores(ks, kvh, qf, TILE, sc2, lane, tab, s0);
+    t3_scores(ks + TILE * P, kvh, qf, valid - TILE, sc2, lane, tab, s1);
+    softmax_pair(A, s0, s1, p0, p1);
+    t3_values(A, vs, kvh, p0, TILE, lane, tab);
+    t3_values(A, vs + TILE * P, kvh, p1, valid - TILE, lane, tab);
 }
 
 // ---- the kernel -------------------------------------------------------------------------
@@ -593,6 +648,11 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
             const int s = i % F::STAGES;
             const uint32_t ph = (uint32_t)((i / F::STAGES) & 1);
             if (!mbar_wait(&full[s], ph)) break;
+            if (KVK == Q27_KV_T3 && i % WAYS == way && hi - lo - i * STAGE_ROWS > TILE) {
+                const uint32_t ks = ring_s + s * stage_bytes<KVK>();
+                tile_t3_pair(A, ks, ks + STAGE_ROWS * F::PITCH, hq, qf,
+                             min(STAGE_ROWS, hi - lo - i * STAGE_ROWS), sc2, lane, tab);
+            } else
 #pragma unroll
             for (int half = 0; half < 2; half++) {
                 const int tile = 2 * i + half;
