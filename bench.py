@@ -228,8 +228,12 @@ def run_ours(args):
     scratch = [torch.empty(Q.decode_scratch_floats(lanes), device=dev) for _ in range(nslots)]
     ex = boxes = None
     if world > 1 and args.exchange == "peer":
-        boxes = qd.PeerMailboxes(nslots, lanes, N_Q, device_epoch=not args.no_graph)
-    elif world > 1:
+        try:
+            boxes = qd.PeerMailboxes(nslots, lanes, N_Q, device_epoch=not args.no_graph)
+        except RuntimeError as e:     # raised on every rank together: fall back together
+            if rank == 0:
+                print(f"bench: {e}; using the NCCL exchange", file=sys.stderr)
+    if world > 1 and boxes is None:
         ex = qd.PartialExchange.create(nslots, lanes, N_Q, world, dev)
     merged = torch.zeros((nslots * lanes * N_Q, HD), device=dev)
 

@@ -112,24 +112,38 @@ class PeerMailboxes:
         self.npairs = nslots * lanes * n_q
         self.epoch = 0
         nbytes = L.lib().q27_xchg_mailbox_bytes(self.world, self.npairs)
+        # Set-up is collective: a rank whose allocation or mapping fails still takes part in
+        # every exchange below, and all ranks then raise together (a caller can fall back to
+        # the NCCL exchange on every rank instead of hanging the others).
         own, handle = C.c_void_p(), C.create_string_buffer(L.XCHG_HANDLE_BYTES)
-        L.check(L.lib().q27_xchg_alloc(nbytes, C.byref(own), handle), "q27_xchg_alloc")
-        self.own = own.value
-        handles = [None] * self.world
-        if self.world > 1:
-            dist.all_gather_object(handles, handle.raw, group=group)
+        rc = L.lib().q27_xchg_alloc(nbytes, C.byref(own), handle)
+        self.own = own.value if rc == 0 else None
         self.boxes, self._opened = [], []
-        for r in range(self.world):
-            if r == self.rank:
-                self.boxes.append(self.own)
-                continue
-            ptr = C.c_void_p()
-            L.check(L.lib().q27_xchg_open(C.create_string_buffer(handles[r], L.XCHG_HANDLE_BYTES),
-                                          C.byref(ptr)), "q27_xchg_open")
-            self.boxes.append(ptr.value)
-            self._opened.append(ptr.value)
+        mine = handle.raw if rc == 0 else None
+        handles = [mine] * self.world
         if self.world > 1:
-            dist.barrier(group=group)         # every mailbox is mapped before anyone pushes
+            dist.all_gather_object(handles, mine, group=group)
+        ok = all(h is not None for h in handles)
+        if ok:
+            for r in range(self.world):
+                if r == self.rank:
+                    self.boxes.append(self.own)
+                    continue
+                ptr = C.c_void_p()
+                if L.lib().q27_xchg_open(C.create_string_buffer(handles[r], L.XCHG_HANDLE_BYTES),
+                                         C.byref(ptr)) != 0:
+                    ok = False
+                    break
+                self.boxes.append(ptr.value)
+                self._opened.append(ptr.value)
+        if self.world > 1:
+            oks = [ok] * self.world
+            dist.all_gather_object(oks, ok, group=group)   # also: every mailbox is mapped
+            ok = all(oks)
+        if not ok:
+            self.close(group)
+            raise RuntimeError("peer-memory mailboxes could not be set up on every rank "
+                               "(CUDA IPC allocation or mapping failed)")
 
     def bytes_per_rank(self) -> int:
         return self.npairs * FD_ST * 4
@@ -148,7 +162,7 @@ class PeerMailboxes:
         """Unmap the peers' mailboxes, then (after a barrier) free the own one."""
         torch.cuda.synchronize()
         for ptr in self._opened:
-            L.check(L.lib().q27_xchg_close(ptr), "q27_xchg_close")
+            L.lib().q27_xchg_close(ptr)
         self._opened = []
         if self.world > 1:
             dist.barrier(group=group)
