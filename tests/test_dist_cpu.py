@@ -93,3 +93,35 @@ def test_partial_exchange_geometry():
     assert ex.npairs == 8 * 6 * 24
     assert ex.bytes_per_rank() == 8 * 6 * 24 * 258 * 4      # 1.19 MB at BASELINE config 5
     assert tuple(ex.gathered.shape) == (8, 8, 6, 24, 258)
+
+
+def _mailbox_rank(rank, world, port, ret):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        qd.PeerMailboxes(1, 2, 24)
+        ret.put((rank, "constructed"))
+    except RuntimeError as e:
+        ret.put((rank, "raised: " + str(e)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_mailbox_setup_fails_on_every_rank_together():
+    """Without a GPU the mailbox allocation fails; the set-up is collective, so both ranks
+    must come out of the constructor with the same error instead of one of them hanging in
+    an exchange the other never joins (the caller then falls back to the NCCL form)."""
+    if torch.cuda.is_available():
+        pytest.skip("needs a box without a GPU")
+    ctx = mp.get_context("spawn")
+    ret = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_mailbox_rank, args=(r, 2, port, ret)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(ret.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(v.startswith("raised: peer-memory mailboxes could not be set up") for v in got.values())
