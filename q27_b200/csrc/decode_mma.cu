@@ -560,7 +560,7 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
     }
     if (threadIdx.x == 0) {
         for (int s = 0; s < F::STAGES; s++) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], KVK == Q27_KV_T3 ? 1 : 32);   // tx bytes, or 32 lane arrivals
             mbar_init(&empty[s], NCW);        // every consumer warp releases every stage
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -598,20 +598,29 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
                              bytes, &full[s]);
                 }
             } else {
-                if (lane == 0) mbar_expect_tx(&full[s], (uint32_t)nrows * 2 * F::SLICE);
-                __syncwarp();
-                if (lane < nrows) {
-                    const int r = row0 + lane;
-                    const size_t off = ((size_t)(r & (PAGE - 1)) * b.n_kv + kvh0) * F::SLICE;
-                    bulk_g2s(kdst + lane * F::PITCH,
-                             static_cast<const uint8_t*>(S.ktab[r >> PAGE_SHIFT]) + off, F::SLICE,
-                             &full[s]);
-                    bulk_g2s(vdst + lane * F::PITCH,
-                             static_cast<const uint8_t*>(S.vtab[r >> PAGE_SHIFT]) + off, F::SLICE,
-                             &full[s]);
+                // fp16 / fp8: the rows of one kv head are 512 / 256-byte slices 2048 / 1024 B
+                // apart, and each goes to a padded pitch, so there is no single large copy.
+                // One bulk copy per slice is bound by the copy rate (about one per 70 cycles:
+                // a third of the HBM rate at 131K rows); 16-byte asynchronous copies by the
+                // whole warp are not. Each lane's arrival is counted when its copies land.
+                constexpr int CPR = F::SLICE / 16;        // 16-byte chunks per row slice
+                constexpr int RPI = 32 / CPR;             // row slices per warp instruction
+                const size_t off = ((size_t)(row0 & (PAGE - 1)) * b.n_kv + kvh0) * F::SLICE;
+                const uint8_t* kp = static_cast<const uint8_t*>(S.ktab[row0 >> PAGE_SHIFT]) + off;
+                const uint8_t* vp = static_cast<const uint8_t*>(S.vtab[row0 >> PAGE_SHIFT]) + off;
+                const int c16 = (lane % CPR) * 16;
+                for (int r = lane / CPR; r < nrows; r += RPI) {
+                    const size_t src = (size_t)r * b.n_kv * F::SLICE + c16;
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                                 ::"r"(smem_u32(kdst + r * F::PITCH + c16)), "l"(kp + src) : "memory");
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                                 ::"r"(smem_u32(vdst + r * F::PITCH + c16)), "l"(vp + src) : "memory");
                 }
+                asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
+                             ::"r"(smem_u32(&full[s])) : "memory");
             }
         }
+        if (KVK != Q27_KV_T3) asm volatile("cp.async.wait_all;" ::: "memory");
     } else {
         // ---------------- consumers ----------------
         const int hq = warp % F::KVH, way = warp / F::KVH;
