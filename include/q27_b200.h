@@ -7,7 +7,12 @@
  * DEVICE pointers owned by the caller; small descriptor structs are HOST memory read
  * during the call. All work is enqueued on the caller's stream; nothing is allocated and
  * nothing synchronises, so every entry point may be called under stream capture (the
- * reference captures its rounds into CUDA graphs, src/engine.cuh:2515).
+ * reference captures its rounds into CUDA graphs, src/engine.cuh:2515) -- with one proviso:
+ * the first call that reaches a kernel family on a device opts that kernel into its
+ * shared-memory size (cudaFuncSetAttribute) and loads its module, so make one call per entry
+ * point and KV kind on each device before the first capture (the reference's own launchers
+ * latch the same attribute the same way, src/fdmma.cuh:795-800). The per-device caches behind
+ * this are filled with atomics: first calls may race across host threads.
  *
  * Fixed geometry of the path (src/engine.cuh:45, docs/SPEC.md:17): head_dim 256,
  * n_q_heads = 6 * n_kv_heads (24 / 4), 64-row KV pages (src/cuda_common.h:70-105).
@@ -59,6 +64,9 @@ const char* q27_status_string(int status);
 int q27_last_cuda_error(void);
 /* compiled-for architecture, e.g. 1000 for sm_100a; 0 if the image cannot run here */
 int q27_device_arch(void);
+/* Diagnostics: how many kernels this library has launched from the calling thread so far
+ * (a difference of two readings counts the launches of the calls in between). */
+long long q27_launch_count(void);
 
 /* Diagnostics: every device-side wait in this library is bounded; a kernel whose wait ran
  * out sets a device flag and returns early. This reads the flag (synchronous copy; do
@@ -101,6 +109,20 @@ int q27_attn_decode3(const q27_CP3* q, int q_stride, const void* const* ktab,
                      const void* const* vtab, const q27_P3* out, float* scratch,
                      const q27_IP3* pos, int max_ctx, int n_q_heads, int n_kv_heads,
                      int head_dim, float scale, void* stream, int ntok, int kvk);
+
+/* Replaces fdmma::launch_fdmma and fdmma::launch_fdmma_h16 (src/fdmma.cuh:460-463,808-810), the
+ * reference's shared-KV verify step WITHOUT its combine: ntok lanes against one pass over the
+ * cache, un-normalised split partials {m, l, acc[256]} written at
+ * part + ((t*n_q + h)*ns + sp)*258 with exactly the ns splits the caller names (its own
+ * k_attn_fd_combine then merges them with the same ns, src/spec3.cu:1224-1235). Splits that
+ * hold no row are stamped {-FLT_MAX, 0}, which that combine skips (src/spec3.cu:722). gqa must
+ * be 6, ns 1..128. Q27_ERR_UNSUPPORTED_WIDTH is the reference's `false`: the caller must fall
+ * through to another path (src/fdmma.cuh:497). Operands are fp16 with fp32 accumulation for
+ * every kind (the class of launch_fdmma_h16; tighter than launch_fdmma's e4m3). */
+int q27_attn_verify_partials(const q27_CP3* q, int q_stride, const void* const* ktab,
+                             const void* const* vtab, float* part, const q27_IP3* pos,
+                             int n_kv_heads, int gqa, int head_dim, float scale, int ns, int ntok,
+                             void* stream, int kvk);
 
 /* Has no counterpart in the reference. For callers that are not able to hand over scratch
  * memory: code running where device allocation is off limits (a CUDA graph being captured in
@@ -195,7 +217,9 @@ int q27_attn_decode_partial_push(const q27_slot* slots, int nslots, int lanes_st
 
 /* Waits on the device (bounded; a timeout sets the flag q27_wait_timeout_flag reads and
  * leaves `out` untouched) until all `world` ranks have pushed `epoch` into this rank's own
- * mailbox, then log-sum-exp merges them: out [npairs][256] normalised. */
+ * mailbox, then log-sum-exp merges them: out [npairs][256] normalised. After a timeout the
+ * mailbox stays usable: the exchange is not recorded as completed, so the same epoch may be
+ * merged again once the missing ranks have pushed. npairs <= 65535. */
 int q27_attn_merge_pushed(void* mailbox, int world, int64_t npairs, unsigned epoch, float* out,
                           void* stream);
 

@@ -13,9 +13,14 @@
 //   q27k::kv_store3        src/spec3.cuh:87-88      -> q27_kv_store3
 //   q27k::kv_store_t3      src/spec3.cuh:98-99      -> q27_kv_store_t3
 //   q27k::wht3             src/spec3.cuh:106-107    -> q27_wht3
+//   q27k::kv_store         src/blocks.cuh:45-46     -> q27_kv_store3 (one lane)
+//   fdmma::launch_fdmma     src/fdmma.cuh:460-463   -> q27_attn_verify_partials
+//   fdmma::launch_fdmma_h16 src/fdmma.cuh:808-810   -> q27_attn_verify_partials
 //
-// Error behaviour is the reference's: these functions return void and a failure is fatal
-// (message + exit(1), CUDA_CHECK in src/cuda_common.h:8-16). Kinds the engine does not read
+// Error behaviour is the reference's: the q27k:: functions return void and a failure is fatal
+// (message + exit(1), CUDA_CHECK in src/cuda_common.h:8-16); the two fdmma:: launchers return
+// `false` for a width they do not cover, and the caller must then fall through to another path
+// (src/fdmma.cuh:497), any other failure being fatal as well. Kinds the engine does not read
 // (turbo3v, turbo5k, int8-g64) are therefore fatal here rather than silently mis-read.
 #pragma once
 #include <cuda_runtime.h>
@@ -146,4 +151,58 @@ inline void wht3(P3 x, int n_heads, int head_dim, int stride, bool inv, cudaStre
                    "wht3");
 }
 
+// the single-token store of the plain decode step: row *d_pos of the pair's tables
+inline void kv_store(const float* kbuf, const float* vbuf, void* const* ktab, void* const* vtab,
+                     const int* d_pos, int rowlen, cudaStream_t st = 0, bool fp8 = false) {
+    q27_CP3 k{}, v{};
+    q27_IP3 p{};
+    k.p[0] = kbuf;
+    v.p[0] = vbuf;
+    p.p[0] = d_pos;
+    q27_shim_check(q27_kv_store3(&k, &v, ktab, vtab, &p, rowlen, st, 1, fp8 ? 1 : 0), "kv_store");
+}
+
 } // namespace q27k
+
+// The reference's shared-KV verify launchers (src/fdmma.cuh): partials only, the caller runs
+// its own combine with the same `ns`. `stages` is a staging choice of the reference's kernel
+// and has no meaning here.
+namespace fdmma {
+#ifndef Q27K_SHIM_NO_TYPES
+struct FCP3 { const float* p[16]; };
+struct FIP3 { const int* p[16]; };
+#endif
+
+inline bool q27_shim_partials(FCP3 qp, int q_stride, const void* const* ktab,
+                              const void* const* vtab, float* part, FIP3 pos, int n_kv_heads,
+                              int gqa, int head_dim, float scale, int ns, int ntok, cudaStream_t st,
+                              int kvk, const char* what) {
+    static_assert(sizeof(FCP3) == sizeof(q27_CP3) && sizeof(FIP3) == sizeof(q27_IP3),
+                  "lane bundles must stay layout-compatible with the C ABI");
+    const int rc = q27_attn_verify_partials(reinterpret_cast<const q27_CP3*>(&qp), q_stride, ktab,
+                                            vtab, part, reinterpret_cast<const q27_IP3*>(&pos),
+                                            n_kv_heads, gqa, head_dim, scale, ns, ntok, st, kvk);
+    if (rc == Q27_ERR_UNSUPPORTED_WIDTH) return false;
+    q27k::q27_shim_check(rc, what);
+    return true;
+}
+
+inline bool launch_fdmma(FCP3 qp, int q_stride, const void* const* ktab, const void* const* vtab,
+                         float* part, FIP3 pos, int n_kv_heads, int gqa, int head_dim, float scale,
+                         int ns, int ntok, cudaStream_t st, int stages = 2, bool t3 = false) {
+    (void)stages;
+    if (ntok < 4 || ntok > 16) return false;       // the widths the reference instantiates
+    return q27_shim_partials(qp, q_stride, ktab, vtab, part, pos, n_kv_heads, gqa, head_dim, scale,
+                             ns, ntok, st, t3 ? KV_T3 : KV_FP8, "launch_fdmma");
+}
+
+// fmt 0 = fp16, 1 = fp8, 2 = turbo3 rows (3 = turbo5k: not read by this engine -> false)
+inline bool launch_fdmma_h16(FCP3 qp, int q_stride, const void* const* ktab,
+                             const void* const* vtab, float* part, FIP3 pos, int n_kv_heads,
+                             int gqa, int head_dim, float scale, int ns, int ntok, int fmt,
+                             cudaStream_t st) {
+    if (ntok < 4 || ntok > 8 || fmt < 0 || fmt > 2) return false;
+    return q27_shim_partials(qp, q_stride, ktab, vtab, part, pos, n_kv_heads, gqa, head_dim, scale,
+                             ns, ntok, st, fmt, "launch_fdmma_h16");
+}
+} // namespace fdmma

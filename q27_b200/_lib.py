@@ -51,6 +51,7 @@ SIGNATURES = {
     "q27_status_string": (C.c_char_p, [_i]),
     "q27_last_cuda_error": (_i, []),
     "q27_device_arch": (_i, []),
+    "q27_launch_count": (C.c_longlong, []),
     "q27_wait_timeout_flag": (_i, [C.POINTER(_i)]),
     "q27_set_kernel_events": (_i, [_vp, _vp]),
     "q27_kv_row_bytes": (_i64, [_i, _i]),
@@ -59,6 +60,8 @@ SIGNATURES = {
     "q27_attn_decode": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp, _i]),
     "q27_attn_decode3": (_i, [C.POINTER(P3), _i, _vp, _vp, C.POINTER(P3), _vp, C.POINTER(P3),
                               _i, _i, _i, _i, _f, _vp, _i, _i]),
+    "q27_attn_verify_partials": (_i, [C.POINTER(P3), _i, _vp, _vp, _vp, C.POINTER(P3), _i, _i, _i,
+                                      _f, _i, _i, _vp, _i]),
     "q27_attn_decode3_noalloc": (_i, [C.POINTER(P3), _i, _vp, _vp, C.POINTER(P3), C.POINTER(P3),
                                       _i, _i, _i, _f, _vp, _i, _i]),
     "q27_attn_decode_batched": (_i, [C.POINTER(Slot), _i, _i, _i, _i, _i, _f, _vp, _i]),

@@ -62,6 +62,28 @@ def attn_decode3(q_lanes, q_stride, ktab, vtab, out_lanes, scratch, pos_lanes, m
             "q27_attn_decode3")
 
 
+def attn_verify_partials(q_lanes, q_stride, ktab, vtab, part, pos_lanes, n_kv_heads, gqa, head_dim,
+                         scale, ns, st=None, kvk=0) -> bool:
+    """The reference's fdmma::launch_fdmma / launch_fdmma_h16 (src/fdmma.cuh:460,808): ntok lanes
+    against one pass over the cache, un-normalised partials at part[((t*n_q + h)*ns + sp)*258]
+    for the caller's own combine. Returns False for a width that is not covered (the caller
+    falls through), as the reference does."""
+    ntok = len(q_lanes)
+    q, p = _p3(q_lanes), _p3(pos_lanes)
+    rc = L.lib().q27_attn_verify_partials(C.byref(q), q_stride, ktab.data_ptr(), vtab.data_ptr(),
+                                          part.data_ptr(), C.byref(p), n_kv_heads, gqa, head_dim,
+                                          scale, ns, ntok, stream_ptr(st), kvk)
+    if rc == L.ERR_UNSUPPORTED_WIDTH:
+        return False
+    L.check(rc, "q27_attn_verify_partials")
+    return True
+
+
+def launch_count() -> int:
+    """Kernels the library has launched from this thread so far."""
+    return int(L.lib().q27_launch_count())
+
+
 def attn_decode3_noalloc(q_lanes, q_stride, ktab, vtab, out_lanes, pos_lanes, n_q_heads,
                          n_kv_heads, head_dim, scale, st=None, ntok=1, kvk=0):
     """attn_decode3 for callers with no scratch buffer to give (no device allocator at

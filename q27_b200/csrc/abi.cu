@@ -11,20 +11,23 @@
 
 namespace q27b {
 thread_local int g_last_cuda_error = 0;
+thread_local long long g_launch_count = 0;
 
 namespace {
 
+// Per-device caches below are filled on first use; threads that race on a device's first call
+// compute and publish the same value (relaxed atomics), so concurrent first calls are safe.
 int sm_count() {
-    static int cached[64] = {0};
+    static std::atomic<int> cached[MAX_DEVICES];
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-    if (cached[dev] == 0) {
-        int v = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return 148;
+    int v = cached[dev].load(std::memory_order_relaxed);
+    if (v == 0) {
         if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
             v = 148;
-        cached[dev] = v;
+        cached[dev].store(v, std::memory_order_relaxed);
     }
-    return cached[dev];
+    return v;
 }
 
 int check_geometry(int q_stride, int n_q, int n_kv, int head_dim, int kvk) {
@@ -74,6 +77,7 @@ int build_batch(const q27_slot* slots, int nslots, int q_stride, int n_q, int n_
     b.n_kv = n_kv;
     b.scale = scale;
     b.unit = 32;
+    b.fuse = 0;
     (void)total_lanes;
     return Q27_OK;
 }
@@ -102,7 +106,8 @@ int run_decode(const q27_slot* slots, int nslots, int lanes_stride, int q_stride
         // a single lane: the mma.sync streaming kernel
         if (b.max_ntok >= 2) rc = launch_verify_umma(b, kvk, sms, st, &done);
         if (rc) return rc;
-        if (!done) rc = launch_decode_mma(b, kvk, sms, st, &done);
+        if (!done) rc = launch_decode_mma(b, kvk, sms, partial_out == nullptr && peers == nullptr,
+                                          st, &done);
         if (rc) return rc;
     }
     if (!done) {
@@ -116,6 +121,7 @@ int run_decode(const q27_slot* slots, int nslots, int lanes_stride, int q_stride
     }
     if (g_ev_stop) Q27_CUDA_TRY(cudaEventRecord(g_ev_stop, st));
     if (peers) return launch_combine_push(b, *peers, lanes_stride, st);
+    if (b.fuse) return Q27_OK;       // the partial kernel has merged and normalised already
     return launch_combine(b, partial_out, partial_out ? lanes_stride : b.max_ntok, st);
 }
 
@@ -145,16 +151,16 @@ static __device__ __align__(256) float g_noalloc_scratch[NOALLOC_FLOATS];
 
 // Device address of the static scratch on the current device (set up on first use).
 int noalloc_scratch_ptr(float** out) {
-    static float* by_device[64] = {nullptr};
+    static std::atomic<float*> by_device[MAX_DEVICES];
     int dev = 0;
     Q27_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return Q27_ERR_INVALID_ARG;
-    if (!by_device[dev]) {
-        float* p = nullptr;
+    if (dev < 0 || dev >= MAX_DEVICES) return Q27_ERR_INVALID_ARG;
+    float* p = by_device[dev].load(std::memory_order_relaxed);
+    if (!p) {
         Q27_CUDA_TRY(cudaGetSymbolAddress((void**)&p, g_noalloc_scratch));
-        by_device[dev] = p;
+        by_device[dev].store(p, std::memory_order_relaxed);
     }
-    *out = by_device[dev];
+    *out = p;
     return Q27_OK;
 }
 
@@ -178,6 +184,8 @@ const char* q27_status_string(int status) {
 }
 
 int q27_last_cuda_error(void) { return g_last_cuda_error; }
+
+long long q27_launch_count(void) { return g_launch_count; }
 
 int q27_device_arch(void) {
     int dev = 0, mj = 0, mn = 0;
@@ -224,6 +232,23 @@ int q27_attn_decode(const float* q, int q_stride, const void* const* ktab,
     pp.p[0] = d_pos;
     return q27_attn_decode3(&qp, q_stride, ktab, vtab, &op, scratch, &pp, max_ctx, n_q_heads,
                             n_kv_heads, head_dim, scale, stream, 1, kvk);
+}
+
+int q27_attn_verify_partials(const q27_CP3* q, int q_stride, const void* const* ktab,
+                             const void* const* vtab, float* part, const q27_IP3* pos,
+                             int n_kv_heads, int gqa, int head_dim, float scale, int ns, int ntok,
+                             void* stream, int kvk) {
+    if (!q || !pos || !part) return Q27_ERR_INVALID_ARG;
+    if (gqa != GQA || ntok < 1 || ntok > Q27_MAX_LANES || ns < 1 || ns > Q27_MAX_SPLITS)
+        return Q27_ERR_UNSUPPORTED_WIDTH;
+    q27_slot s = single_slot(q, ktab, vtab, nullptr, part, pos, ntok);
+    DevBatch b;
+    int rc = build_batch(&s, 1, q_stride, gqa * n_kv_heads, n_kv_heads, head_dim, scale, kvk, false, b);
+    if (rc) return rc;
+    bool done = false;
+    rc = launch_verify_umma(b, kvk, sm_count(), static_cast<cudaStream_t>(stream), &done, ns);
+    if (rc) return rc;
+    return done ? Q27_OK : Q27_ERR_UNSUPPORTED_WIDTH;
 }
 
 int q27_attn_decode3_noalloc(const q27_CP3* q, int q_stride, const void* const* ktab,

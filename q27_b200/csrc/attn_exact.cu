@@ -1,5 +1,5 @@
-// Exact (fp32 scalar) attention family: split-KV partials, the log-sum-exp combine / merge
-// kernels, and a scalar causal prefill. These kernels decode every cache element with the
+// Exact (fp32 scalar) attention family: tiled split-KV partials, the log-sum-exp combine /
+// merge kernels, and a scalar causal prefill. These kernels decode every cache element with the
 // bit-exact decoders of common.cuh and do all arithmetic in fp32 with expf, so they are the
 // engine's tight-tolerance path (the class of the reference's k_attn_fd2, src/spec3.cu:804-921,
 // and k_attn_prefill_T, src/prefill.cu:2293-2388). The tensor-core kernels are checked
@@ -11,18 +11,49 @@ namespace q27b {
 
 namespace {
 
-constexpr int EX_WARPS = 4;
+// Split-KV partial of one (split, kv head, slot-lane), fp32 throughout, as a tiled two-phase
+// loop over blocks of 32 keys that lives in shared memory:
+//   phase 1  the block's K rows are decoded (bit-exact element decoders) into shared memory;
+//            thread (head j, key k) -- warp j holds the 32 keys of head j -- forms one whole
+//            dot product in dimension order, the warp takes the block maximum and sum with
+//            shuffles, and the block's probabilities go to shared memory;
+//   phase 2  the block's V rows take the K rows' place; thread d owns output dimension d of
+//            all six heads and adds the 32 weighted rows in key order.
+// The running (m, l) of head j live in the registers of warp j, the accumulators of dimension
+// d in thread d: one state per CTA, nothing to merge at the end, and every sum has a fixed
+// order, so results are run-to-run identical. Tolerance class of the reference's scalar decode
+// (src/spec3.cu:804-921): exact element decode, fp32 FMA, expf.
+constexpr int EXK = 32;                  // keys per block
+constexpr int EX_THREADS = 256;          // = head_dim: one output dimension per thread
+constexpr int EX_PITCH = HD + 1;         // odd pitch: rows read by 32 keys at once hit 32 banks
 
-// Partial over one (split, kv head, slot-lane). Warp w walks rows lo+w, lo+w+4, ...; lane
-// owns dims [8*lane, 8*lane+8); the six query heads of the KV head share every row read.
 template <int KVK>
-__global__ void __launch_bounds__(EX_WARPS * 32)
+__device__ __forceinline__ void stage_rows(float (*tile)[EX_PITCH], const void* const* tab,
+                                           int row0, int nrows, int n_kv, int kvh) {
+    for (int i = threadIdx.x; i < EXK * (HD / 8); i += EX_THREADS) {
+        const int k = i / (HD / 8), d0 = (i % (HD / 8)) * 8;
+        float v[8];
+        if (k < nrows) {
+            const int p = row0 + k;
+            load8_exact<KVK>(static_cast<const uint8_t*>(tab[p >> PAGE_SHIFT]), p & (PAGE - 1), n_kv,
+                             kvh, d0, v);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = 0.f;   // past the window: weight 0, value finite
+        }
+#pragma unroll
+        for (int e = 0; e < 8; e++) tile[k][d0 + e] = v[e];
+    }
+}
+
+template <int KVK>
+__global__ void __launch_bounds__(EX_THREADS)
 k_exact_partial(const __grid_constant__ DevBatch b) {
     const int sp = blockIdx.x, kvh = blockIdx.y;
     const int slot = blockIdx.z / b.max_ntok, t = blockIdx.z % b.max_ntok;
     const DevSlot& S = b.s[slot];
     if (t >= S.ntok) return;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     // slot-wide chunking from the longest lane (all lanes share split boundaries)
     int max_len = 0;
@@ -34,8 +65,8 @@ k_exact_partial(const __grid_constant__ DevBatch b) {
 
     float* dst0 = S.scratch + (((size_t)t * b.n_q + kvh * GQA) * b.nsplit + sp) * PART;
     if (lo >= hi) { // empty window: stamp the sentinel so the combine can skip it
-        if (threadIdx.x < GQA) {
-            float* d = dst0 + (size_t)threadIdx.x * b.nsplit * PART;
+        if (tid < GQA) {
+            float* d = dst0 + (size_t)tid * b.nsplit * PART;
             d[0] = NEG_SENTINEL;
             d[1] = 0.f;
         }
@@ -43,84 +74,58 @@ k_exact_partial(const __grid_constant__ DevBatch b) {
     }
 
     __shared__ float s_q[GQA][HD];
-    __shared__ float s_acc[GQA][HD];
-    __shared__ float s_ml[EX_WARPS][GQA][2];
-    for (int i = threadIdx.x; i < GQA * HD; i += blockDim.x) {
+    __shared__ float s_tile[EXK][EX_PITCH];
+    __shared__ float s_p[GQA][EXK];
+    __shared__ float s_shrink[GQA];
+    for (int i = tid; i < GQA * HD; i += EX_THREADS)
         s_q[i / HD][i % HD] = S.q[t][(size_t)(kvh * GQA + i / HD) * b.q_stride + (i % HD)];
-        s_acc[i / HD][i % HD] = 0.f;
-    }
-    __syncthreads();
 
-    float qr[GQA][8];
+    float m_run = NEG_SENTINEL, l_run = 0.f;      // head `warp` (warps 0..5), same in every lane
+    float acc[GQA];                               // dimension `tid` of every head
 #pragma unroll
-    for (int j = 0; j < GQA; j++)
-#pragma unroll
-        for (int i = 0; i < 8; i++) qr[j][i] = s_q[j][8 * lane + i];
+    for (int j = 0; j < GQA; j++) acc[j] = 0.f;
 
-    float m[GQA], l[GQA], acc[GQA][8];
-#pragma unroll
-    for (int j = 0; j < GQA; j++) {
-        m[j] = NEG_SENTINEL;
-        l[j] = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; i++) acc[j][i] = 0.f;
-    }
-
-    for (int p = lo + warp; p < hi;) {
-        const int pg = p >> PAGE_SHIFT;
-        const int pend = min(hi, (pg + 1) << PAGE_SHIFT);
-        const uint8_t* kpage = static_cast<const uint8_t*>(S.ktab[pg]);
-        const uint8_t* vpage = static_cast<const uint8_t*>(S.vtab[pg]);
-        for (; p < pend; p += EX_WARPS) {
-            float kv[8], vv[8];
-            load8_exact<KVK>(kpage, p & (PAGE - 1), b.n_kv, kvh, 8 * lane, kv);
-            load8_exact<KVK>(vpage, p & (PAGE - 1), b.n_kv, kvh, 8 * lane, vv);
-#pragma unroll
-            for (int j = 0; j < GQA; j++) {
-                float d = 0.f;
-#pragma unroll
-                for (int i = 0; i < 8; i++) d = fmaf(qr[j][i], kv[i], d);
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
-                d *= b.scale;
-                const float mn = fmaxf(m[j], d);
-                const float so = expf(m[j] - mn), w = expf(d - mn);
-                l[j] = l[j] * so + w;
-                m[j] = mn;
-#pragma unroll
-                for (int i = 0; i < 8; i++) acc[j][i] = acc[j][i] * so + w * vv[i];
-            }
-        }
-    }
-
-    if (lane == 0)
-#pragma unroll
-        for (int j = 0; j < GQA; j++) { s_ml[warp][j][0] = m[j]; s_ml[warp][j][1] = l[j]; }
-    __syncthreads();
-    // warps add their rescaled accumulators in warp order: run-to-run bitwise stable
-    for (int w = 0; w < EX_WARPS; w++) {
-        if (warp == w) {
-#pragma unroll
-            for (int j = 0; j < GQA; j++) {
-                float mb = NEG_SENTINEL;
-#pragma unroll
-                for (int u = 0; u < EX_WARPS; u++) mb = fmaxf(mb, s_ml[u][j][0]);
-                const float sc = m[j] == NEG_SENTINEL ? 0.f : expf(m[j] - mb);
-#pragma unroll
-                for (int i = 0; i < 8; i++) s_acc[j][8 * lane + i] += acc[j][i] * sc;
-            }
-        }
+    for (int r0 = lo; r0 < hi; r0 += EXK) {
+        const int nrows = min(EXK, hi - r0);
+        __syncthreads();                          // the tile's previous user is done (and s_q is in)
+        stage_rows<KVK>(s_tile, S.ktab, r0, nrows, b.n_kv, kvh);
         __syncthreads();
+        if (warp < GQA) {
+            float dot = 0.f;
+#pragma unroll 8
+            for (int d = 0; d < HD; d++) dot = fmaf(s_q[warp][d], s_tile[lane][d], dot);
+            const float sc = lane < nrows ? dot * b.scale : NEG_SENTINEL;
+            float bm = sc;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, off));
+            const float m_new = fmaxf(m_run, bm);             // finite: the block has a live key
+            const float pk = lane < nrows ? expf(sc - m_new) : 0.f;
+            float ps = pk;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+            const float shrink = m_run == NEG_SENTINEL ? 0.f : expf(m_run - m_new);
+            l_run = l_run * shrink + ps;
+            m_run = m_new;
+            s_p[warp][lane] = pk;
+            if (lane == 0) s_shrink[warp] = shrink;
+        }
+        __syncthreads();                          // scores are out of the tile
+        stage_rows<KVK>(s_tile, S.vtab, r0, nrows, b.n_kv, kvh);
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < GQA; j++) {
+            float a = acc[j] * s_shrink[j];
+#pragma unroll 8
+            for (int k = 0; k < EXK; k++) a = fmaf(s_p[j][k], s_tile[k][tid], a);
+            acc[j] = a;
+        }
     }
-    for (int j = warp; j < GQA; j += EX_WARPS) {
-        float mb = NEG_SENTINEL;
-        for (int u = 0; u < EX_WARPS; u++) mb = fmaxf(mb, s_ml[u][j][0]);
-        float lb = 0.f;
-        for (int u = 0; u < EX_WARPS; u++)
-            lb += s_ml[u][j][0] == NEG_SENTINEL ? 0.f : s_ml[u][j][1] * expf(s_ml[u][j][0] - mb);
-        float* d = dst0 + (size_t)j * b.nsplit * PART;
-        if (lane == 0) { d[0] = mb; d[1] = lb; }
-        for (int i = lane; i < HD; i += 32) d[2 + i] = s_acc[j][i];
+#pragma unroll
+    for (int j = 0; j < GQA; j++) dst0[(size_t)j * b.nsplit * PART + 2 + tid] = acc[j];
+    if (warp < GQA && lane == 0) {
+        float* d = dst0 + (size_t)warp * b.nsplit * PART;
+        d[0] = m_run;
+        d[1] = l_run;
     }
 }
 
@@ -328,11 +333,12 @@ k_prefill_exact(const float* __restrict__ qT, int q_stride, int q_row,
 
 int launch_exact_partials(const DevBatch& b, int kvk, cudaStream_t st) {
     dim3 grid(b.nsplit, b.n_kv, b.nslots * b.max_ntok);
-    if (kvk == Q27_KV_F16) k_exact_partial<Q27_KV_F16><<<grid, EX_WARPS * 32, 0, st>>>(b);
-    else if (kvk == Q27_KV_FP8) k_exact_partial<Q27_KV_FP8><<<grid, EX_WARPS * 32, 0, st>>>(b);
-    else if (kvk == Q27_KV_T3) k_exact_partial<Q27_KV_T3><<<grid, EX_WARPS * 32, 0, st>>>(b);
+    if (kvk == Q27_KV_F16) k_exact_partial<Q27_KV_F16><<<grid, EX_THREADS, 0, st>>>(b);
+    else if (kvk == Q27_KV_FP8) k_exact_partial<Q27_KV_FP8><<<grid, EX_THREADS, 0, st>>>(b);
+    else if (kvk == Q27_KV_T3) k_exact_partial<Q27_KV_T3><<<grid, EX_THREADS, 0, st>>>(b);
     else return Q27_ERR_UNSUPPORTED_KIND;
     Q27_CUDA_TRY(cudaGetLastError());
+    Q27_COUNT_LAUNCH();
     return Q27_OK;
 }
 
@@ -358,6 +364,7 @@ int launch_combine_push(const DevBatch& b, const Peers& peers, int lanes_stride,
 int launch_merge(const float* parts, int nparts, int64_t npairs, float* out, cudaStream_t st) {
     k_merge<<<(unsigned)npairs, 256, 0, st>>>(parts, nparts, npairs, out);
     Q27_CUDA_TRY(cudaGetLastError());
+    Q27_COUNT_LAUNCH();
     return Q27_OK;
 }
 
@@ -378,6 +385,7 @@ int launch_prefill_exact(const float* qT, int q_stride, int q_row, const void* c
             qT, q_stride, q_row, ktab, vtab, outT, out_row, base_pos, t0, te, n_kv, scale);
     else return Q27_ERR_UNSUPPORTED_KIND;
     Q27_CUDA_TRY(cudaGetLastError());
+    Q27_COUNT_LAUNCH();
     return Q27_OK;
 }
 

@@ -28,24 +28,6 @@ namespace q27b {
 // without relocatable device code a __device__ variable is private to its translation unit:
 // this file keeps its own timeout flag and the library's reader ORs them together
 __device__ int g_umma_timeout_flag = 0;
-#ifdef Q27_TRACE
-// timing experiments only: cycles spent waiting, summed over CTAs, by (role, barrier)
-__device__ unsigned long long g_umma_trace[24];
-__device__ long long g_umma_ev[12][64];   // per-event timestamps of CTA (0,0,0), first 64 tiles
-#define TRACE_EV(e, i) do { if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (i) < 64) g_umma_ev[e][i] = clock64(); } while (0)
-#define TRACE_EVMAX(e, i) do { if ((threadIdx.x & 31) == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (i) < 64) atomicMax(&g_umma_ev[e][i], clock64()); } while (0)
-#define TRACE_T0() const long long t0__ = clock64()
-#define TRACE_ADD(slot, cond) do { if (cond) tr_acc__[slot] += (unsigned long long)(clock64() - t0__); } while (0)
-#define TRACE_DECL() unsigned long long tr_acc__[24] = {0}
-#define TRACE_FLUSH() do { for (int q__ = 0; q__ < 24; q__++) if (tr_acc__[q__]) atomicAdd(&g_umma_trace[q__], tr_acc__[q__]); } while (0)
-#else
-#define TRACE_T0()
-#define TRACE_ADD(slot, cond)
-#define TRACE_EV(e, i)
-#define TRACE_EVMAX(e, i)
-#define TRACE_DECL()
-#define TRACE_FLUSH()
-#endif
 
 namespace {
 
@@ -369,7 +351,6 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                    p_full = s32(&bars[24]), raw_full = s32(&bars[28]), raw_empty = s32(&bars[32]);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = (pb.hi - pb.lo + BN - 1) / BN;
-    TRACE_DECL();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < KSL; s++) {
@@ -472,17 +453,11 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         float m_ref = -INFINITY, l = 0.f;
         bool ok = true;
         const bool warp_has_rows = __any_sync(0xffffffffu, ri.q != nullptr);
-#ifdef Q27_TRACE
-        const long long tloop = clock64();
-#endif
         for (int i = 0; i < ntiles && ok; i++) {
             const int b = i % S_BUFS;
             const uint32_t s_col = lane_base + COL_S + b * BN;
-            { TRACE_T0();
-              ok = __all_sync(0xffffffffu, bar_wait(s_full + 8 * b, (uint32_t)((i / S_BUFS) & 1)));
-              TRACE_ADD(0, threadIdx.x == 0); }
+            ok = __all_sync(0xffffffffu, bar_wait(s_full + 8 * b, (uint32_t)((i / S_BUFS) & 1)));
             if (!ok) break;
-            if (threadIdx.x == 0) TRACE_EV(4, i);
             if (!warp_has_rows) {
                 // a warp of padding rows only (verify tiles use 6 rows per lane): it keeps
                 // step with the barriers and leaves its issue slots to the staging warps;
@@ -491,7 +466,6 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 bar_arrive(p_full + 8 * b);
                 continue;
             }
-            TRACE_T0();
             tc_fence_after();
             float s[BN];
             tc_ld32(s_col, s);
@@ -526,13 +500,10 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 ph[j >> 1] = *reinterpret_cast<uint32_t*>(&h);
             }
             l = l * alpha + (sum0 + sum1);
-            if (threadIdx.x == 0) TRACE_EV(5, i);
             if (__any_sync(0xffffffffu, need)) {       // warp-collective TMEM round trip on O
                 const int pi = i - 1;
-                { TRACE_T0();
-                  ok = __all_sync(0xffffffffu,
-                                  bar_wait(pvb + 8 * (pi % S_BUFS), (uint32_t)((pi / S_BUFS) & 1)));
-                  TRACE_ADD(1, threadIdx.x == 0); }
+                ok = __all_sync(0xffffffffu,
+                                bar_wait(pvb + 8 * (pi % S_BUFS), (uint32_t)((pi / S_BUFS) & 1)));
                 if (!ok) break;
                 tc_fence_after();
 #pragma unroll 1
@@ -551,17 +522,9 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             tc_wait_st();
             tc_fence_before();
             bar_arrive(p_full + 8 * b);
-            TRACE_EVMAX(6, i);
-            TRACE_ADD(warp == 3 ? 6 : 13 + warp, lane == 0);
         }
         if (ok) ok = bar_wait(pvb + 8 * ((ntiles - 1) % S_BUFS), (uint32_t)(((ntiles - 1) / S_BUFS) & 1));
         ok = __all_sync(0xffffffffu, ok);
-#ifdef Q27_TRACE
-        if (threadIdx.x == 0) {
-            tr_acc__[7] += (unsigned long long)(clock64() - tloop);
-            tr_acc__[8] += (unsigned long long)ntiles;
-        }
-#endif
         tc_fence_after();
         if (ok) {
             const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -615,21 +578,13 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 const int ks_ = i % KSL, b = i % S_BUFS;
                 const uint32_t kpar = (uint32_t)((i / KSL) & 1);
                 const uint32_t bpar = (uint32_t)(((i / S_BUFS) - 1) & 1);   // previous use of buffer b
-                { TRACE_T0();
-                  ok = bar_wait(k_full + 8 * ks_, kpar);
-                  TRACE_ADD(2, lane == 0); }
-                if (lane == 0) TRACE_EV(8, i);
-                { TRACE_T0();
-                  if (ok && i >= S_BUFS) ok = bar_wait(pvb + 8 * b, bpar);
-                  TRACE_ADD(3, lane == 0); }
-                if (lane == 0) TRACE_EV(9, i);
+                ok = bar_wait(k_full + 8 * ks_, kpar);
+                if (ok && i >= S_BUFS) ok = bar_wait(pvb + 8 * b, bpar);
                 if (!ok) break;
                 fence_async_smem();
                 tc_fence_after();
                 const uint64_t kd0 = kd_base + (uint64_t)((ks_ * KT_BYTES) >> 4);
                 const uint32_t d = tmem + COL_S + b * BN;
-                if (lane == 0) TRACE_EV(0, i);
-                TRACE_T0();
                 if (elect_one()) {
 #pragma unroll
                     for (int ks = 0; ks < HD / 16; ks++) {
@@ -648,8 +603,6 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                     tc_commit(k_empty + 8 * ks_);
                 }
                 __syncwarp();
-                if (lane == 0) TRACE_EV(1, i);
-                TRACE_ADD(9, lane == 0);
             }
         }
     } else if (warp == PV_WARP) {
@@ -661,21 +614,14 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             int vs_ = 0, b = 0;
             uint32_t vpar = 0, bpar = 0;
             for (int i = 0; i < ntiles && ok; i++) {
-                { TRACE_T0();
-                  ok = bar_wait(p_full + 8 * b, bpar);
-                  TRACE_ADD(4, lane == 0); }
-                if (lane == 0) TRACE_EV(7, i);
+                ok = bar_wait(p_full + 8 * b, bpar);
                 if (!ok) break;
-                { TRACE_T0();
-                  ok = bar_wait(v_full + 8 * vs_, vpar);
-                  TRACE_ADD(12, lane == 0); }
+                ok = bar_wait(v_full + 8 * vs_, vpar);
                 if (!ok) break;
                 fence_async_smem();
                 tc_fence_after();
                 const uint64_t vd0 = vd_base + (uint64_t)((vs_ * KT_BYTES) >> 4);
                 const uint32_t pa = tmem + COL_S + b * BN;
-                if (lane == 0) TRACE_EV(2, i);
-                TRACE_T0();
                 if (elect_one()) {
                     if (i > 0) tc_mma_f16_ta_c<1>(tmem + COL_O, pa, vd0, IDESC_O);
                     else tc_mma_f16_ta_c<0>(tmem + COL_O, pa, vd0, IDESC_O);
@@ -686,8 +632,6 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                     tc_commit(v_empty + 8 * vs_);
                 }
                 __syncwarp();
-                if (lane == 0) TRACE_EV(3, i);
-                TRACE_ADD(10, lane == 0);
                 if (++vs_ == VSL) { vs_ = 0; vpar ^= 1; }
                 if (++b == S_BUFS) { b = 0; bpar ^= 1; }
             }
@@ -708,9 +652,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         auto nkeys_of = [&](int i) { return min(BN, pb.hi - (pb.lo + i * BN)); };
         auto wait_slot = [&](int i) -> bool {
             bool okw = true;
-            TRACE_T0();
             if (i >= nslots) okw = bar_wait(empty + 8 * (i % nslots), (uint32_t)(((i / nslots) - 1) & 1));
-            TRACE_ADD(5, p == 0 && side == 0);
             return okw;
         };
         if constexpr (KVK == Q27_KV_F16) {
@@ -718,7 +660,6 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             // operand layout and the slot's barrier is arrived when the copies have landed
             for (int i = 0; i < ntiles; i++) {
                 if (!wait_slot(i)) break;
-                if (p == 0 && side == 0) TRACE_EV(10, i);
                 const int st = i % nslots, nk = nkeys_of(i);
                 const uint8_t* page = page_of(i);
                 uint8_t* dst = ring + st * KT_BYTES;
@@ -738,7 +679,6 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 if (nk < BN) __threadfence_block();        // the zeros, before the arrival below
                 asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
                              ::"r"(full + 8 * st) : "memory");
-                if (p == 0 && side == 0) TRACE_EV(11, i);
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
         } else if constexpr (KVK == Q27_KV_T3) {
@@ -779,9 +719,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             for (int i = 0; i < ntiles; i++) {
                 const int buf = i & 1;
                 const uint32_t par = (uint32_t)((i >> 1) & 1);
-                { TRACE_T0();
-                  if (!bar_wait(rfull + 8 * buf, par)) break;
-                  TRACE_ADD(16, p == 0 && side == 0); }
+                if (!bar_wait(rfull + 8 * buf, par)) break;
                 RawHalf<KVK> rw;
                 {
                     const int key = p & 63, blk = p >> 6;
@@ -793,20 +731,14 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 }
                 bar_arrive(rempty + 8 * buf);
                 if (i + 2 < ntiles) {
-                    { TRACE_T0();
-                      if (!bar_wait(rempty + 8 * buf, par)) break;
-                      TRACE_ADD(17, p == 0 && side == 0); }
-                    { TRACE_T0();
-                      issue_raw(i + 2);
-                      TRACE_ADD(18, p == 0 && side == 0); }
+                    if (!bar_wait(rempty + 8 * buf, par)) break;
+                    issue_raw(i + 2);
                 }
                 if (!wait_slot(i)) break;
                 const int st = i % nslots;
-                { TRACE_T0();
-                  if (p >> 6) half_store<KVK, 1>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
-                  else half_store<KVK, 0>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
-                  fence_async_smem();
-                  TRACE_ADD(19, p == 0 && side == 0); }
+                if (p >> 6) half_store<KVK, 1>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
+                else half_store<KVK, 0>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
+                fence_async_smem();
                 bar_arrive(full + 8 * st);
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
@@ -856,16 +788,13 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 }
                 if (!wait_slot(i)) break;
                 const int st = i % nslots;
-                { TRACE_T0();
-                  half_store<KVK>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
-                  fence_async_smem();
-                  TRACE_ADD(6, p == 0 && side == 0); }
+                half_store<KVK>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
+                fence_async_smem();
                 bar_arrive(full + 8 * st);
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
         }
     }
-    TRACE_FLUSH();
     __syncthreads();
     if (warp == MMA_WARP) {
         tc_fence_after();
@@ -969,15 +898,14 @@ k_verify_umma(const __grid_constant__ DevBatch b) {
 
 template <int KVK>
 int set_attrs() {
-    static bool done = false;
-    if (!done) {
+    static DeviceOnce once;      // the attribute belongs to a device, not to the process
+    return device_once(once, []() -> int {
         Q27_CUDA_TRY(cudaFuncSetAttribute(k_prefill_umma<KVK>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, UMMA_SMEM));
         Q27_CUDA_TRY(cudaFuncSetAttribute(k_verify_umma<KVK>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, UMMA_SMEM));
-        done = true;
-    }
-    return Q27_OK;
+        return Q27_OK;
+    });
 }
 
 } // namespace
@@ -1031,6 +959,7 @@ int launch_prefill_umma(const float* qT, int q_stride, int q_row, const void* co
         return Q27_ERR_UNSUPPORTED_KIND;
     }
     Q27_CUDA_TRY(cudaGetLastError());
+    Q27_COUNT_LAUNCH();
     if (a.pieces > 1)
         Q27_CUDA_TRY(launch_pdl(k_prefill_fixup, dim3(TOK_PER_TILE, items - a.n_full), dim3(HD),
                                 0, st, a));
@@ -1038,32 +967,20 @@ int launch_prefill_umma(const float* qT, int q_stride, int q_row, const void* co
     return Q27_OK;
 }
 
-#ifdef Q27_TRACE
-extern "C" int q27_debug_umma_trace(unsigned long long* out, int reset) {
-    cudaMemcpyFromSymbol(out, g_umma_trace, sizeof(unsigned long long) * 24);
-    if (reset) { unsigned long long z[24] = {0}; cudaMemcpyToSymbol(g_umma_trace, z, sizeof(z)); }
-    return 0;
-}
-extern "C" int q27_debug_umma_events(long long* out) {
-    cudaMemcpyFromSymbol(out, g_umma_ev, sizeof(long long) * 12 * 64);
-    static long long z[12 * 64];
-    cudaMemcpyToSymbol(g_umma_ev, z, sizeof(z));
-    return 0;
-}
-#endif
 
 int read_umma_timeout_flag(int* out) {
     Q27_CUDA_TRY(cudaMemcpyFromSymbol(out, g_umma_timeout_flag, sizeof(int)));
     return Q27_OK;
 }
 
-int launch_verify_umma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool* done) {
+int launch_verify_umma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool* done,
+                       int force_nsplit) {
     *done = false;
     if (b.q_stride & 3) return Q27_OK;
     for (int i = 0; i < b.nslots; i++)
         for (int t = 0; t < b.s[i].ntok; t++)
             if ((uintptr_t)b.s[i].q[t] & 15) return Q27_OK;
-    int ns = sm_count / (b.nslots * b.n_kv);
+    int ns = force_nsplit > 0 ? force_nsplit : sm_count / (b.nslots * b.n_kv);
     b.nsplit = ns < 1 ? 1 : ns > Q27_MAX_SPLITS ? Q27_MAX_SPLITS : ns;
     b.unit = BN;
     dim3 grid(b.nsplit, b.n_kv, b.nslots);
@@ -1081,6 +998,7 @@ int launch_verify_umma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool
         return Q27_ERR_UNSUPPORTED_KIND;
     }
     Q27_CUDA_TRY(cudaGetLastError());
+    Q27_COUNT_LAUNCH();
     *done = true;
     return Q27_OK;
 }

@@ -12,7 +12,9 @@ int launch_prefill_umma(const float* qT, int q_stride, int q_row, const void* co
                         int sm_count, cudaStream_t st, int kvk, bool* done);
 
 // Writes split-KV partials for every lane of every slot in ONE pass over the cache per
-// (slot, kv head, split); fills b.nsplit / b.unit for the combine.
-int launch_verify_umma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool* done);
+// (slot, kv head, split); fills b.nsplit / b.unit for the combine. force_nsplit > 0 fixes the
+// split count (a caller that merges the partials itself chose the stride).
+int launch_verify_umma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool* done,
+                       int force_nsplit = 0);
 
 } // namespace q27b

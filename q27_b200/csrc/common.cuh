@@ -2,13 +2,15 @@
 // element decoders (bit-exact to the reference codec) and the per-launch argument bundles.
 #pragma once
 #include <cuda_fp16.h>
-#include <stdlib.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <float.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/q27_b200.h"
+#include "t3_tables.cuh"
 
 namespace q27b {
 
@@ -22,6 +24,9 @@ constexpr float NEG_SENTINEL = -FLT_MAX; // "empty partial" marker (src/prefill.
 
 // Per-thread record of the last failing CUDA call (read by q27_last_cuda_error()).
 extern thread_local int g_last_cuda_error;
+// Kernels this library has launched from this thread (read by q27_launch_count()).
+extern thread_local long long g_launch_count;
+#define Q27_COUNT_LAUNCH() (++q27b::g_launch_count)
 
 #define Q27_CUDA_TRY(expr)                                  \
     do {                                                    \
@@ -31,6 +36,24 @@ extern thread_local int g_last_cuda_error;
             return Q27_ERR_CUDA;                            \
         }                                                   \
     } while (0)
+
+// Per-device one-shot set-up (cudaFuncSetAttribute belongs to ONE device, so a process that
+// drives several GPUs must repeat it on each). Threads that race on a device's first call all
+// run `f`, which is idempotent, and publish the same flag: safe without a lock.
+constexpr int MAX_DEVICES = 64;
+struct DeviceOnce {
+    std::atomic<unsigned char> done[MAX_DEVICES];
+};
+template <typename F>
+inline int device_once(DeviceOnce& once, F&& f) {
+    int dev = 0;
+    Q27_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= MAX_DEVICES) return Q27_ERR_INVALID_ARG;
+    if (once.done[dev].load(std::memory_order_acquire)) return Q27_OK;
+    const int rc = f();
+    if (rc == Q27_OK) once.done[dev].store(1, std::memory_order_release);
+    return rc;
+}
 
 // One slot as the kernels see it (device-visible copy of q27_slot, passed by value as a
 // __grid_constant__ parameter so no descriptor memory has to be allocated or copied).
@@ -56,6 +79,7 @@ struct DevBatch {
     int n_kv;
     float scale;
     int unit;       // split granularity in rows (chunk is a multiple of it)
+    int fuse;       // the partial kernel also merges the splits and writes the output rows
 };
 static_assert(sizeof(DevBatch) <= 4000, "DevBatch must fit the kernel parameter space");
 
@@ -76,12 +100,27 @@ __host__ __device__ __forceinline__ int split_chunk(int max_len, int nsplit, int
     return c < unit ? unit : c;
 }
 
-// ---- element decoders ---------------------------------------------------------------
+// "Am I the last of n CTAs to get here?" on a 64-bit word of caller scratch that nobody has
+// to clear first: the word carries a 48-bit tag above a 16-bit count. ticket_arm (any time
+// before the first arrival, by every CTA that will arrive) gives a word without the tag a
+// zero count; ticket_take counts an arrival, and the n-th one re-arms the word for the next
+// launch. Call from ONE thread, ticket_take after a block barrier; its fences make every
+// earlier arrival's global writes visible to the last one.
+constexpr unsigned long long TICKET_TAG = 0xD15C0A77E5B2ull;      // 48 bits
+__device__ __forceinline__ void ticket_arm(unsigned long long* word) {
+    const unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(word);
+    if ((old >> 16) != TICKET_TAG) atomicCAS(word, old, TICKET_TAG << 16);   // losers change nothing
+}
+__device__ __forceinline__ bool ticket_take(unsigned long long* word, unsigned n) {
+    __threadfence();
+    const unsigned long long prev = atomicAdd(word, 1ull);
+    const bool last = (unsigned)(prev & 0xffffu) + 1 >= n;
+    if (last) atomicExch(word, TICKET_TAG << 16);
+    __threadfence();
+    return last;
+}
 
-// fp32 turbo3 centroids (src/turbo3.cuh:38-40); idx = low2 | hi << 2
-static __device__ __constant__ float kT3Centroid[8] = {-0.190207f, -0.118786f, -0.066822f,
-                                                      -0.021663f, 0.021663f,  0.066822f,
-                                                      0.118786f,  0.190207f};
+// ---- element decoders ---------------------------------------------------------------
 
 __device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
     __half_raw hr = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3);
@@ -147,8 +186,8 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    static const bool off = getenv("Q27_NO_PDL") != nullptr;   // measurement switch
-    cfg.numAttrs = off ? 0 : 1;
+    cfg.numAttrs = 1;
+    Q27_COUNT_LAUNCH();
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

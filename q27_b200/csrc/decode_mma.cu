@@ -1,9 +1,10 @@
 // Tensor-core split-KV decode for sm_100a.
 //
 // One CTA = (slot, lane, position split [, kv head]). A producer warp streams the split's
-// K and V rows into a shared-memory ring with bulk async copies (cp.async.bulk, completion
-// on an mbarrier); eight consumer warps turn ring rows straight into mma.sync fragments in
-// registers -- no dequantised tile is ever written back to shared memory -- and run
+// K and V rows into a shared-memory ring with asynchronous copies (cp.async.bulk for whole
+// turbo3 rows, 16-byte cp.async for fp16 / fp8 slices; completion on an mbarrier); consumer
+// warps turn ring rows straight into mma.sync fragments in registers -- no dequantised tile
+// is ever written back to shared memory -- and run
 //     S^T = K . Q^T        (16 keys x 8 query columns per MMA, fp16 operands, fp32 accum)
 //     O^T += V^T . P^T     (16 dims x 8 query columns, contraction over 16 keys)
 // with an online softmax per query column. The six GQA heads of a KV head are the columns
@@ -15,52 +16,35 @@
 // operands are the eight centroid constants, looked up 4 elements per PRMT. The bit-exact
 // centroid*norm product lives in the exact family and q27_kv_dequant.
 //
+// turbo3 is bound by the integer pipe (selector assembly and lookups: about 2.4 PRMT / LOP3 /
+// SHF lane-operations per cache element against 64 per clock and SM). A consumer warp takes
+// BOTH 16-key tiles of a ring stage at once: two independent score streams keep the pipe fed
+// while one waits on a lookup or an MMA, and one online-softmax step covers the 32 keys.
+//
 // Dimension and key indices inside a tile are permuted per format so that every thread's
 // fragment registers come from contiguous packed bytes; Q^T fragments and the output rows
 // use the same maps (kdim_* / vdim_* below), so the permutation cancels.
+//
+// Small launches finish in the same kernel: when the partials of a (slot, lane, kv group)
+// fit one SM's appetite, the CTA that completes a group last merges its splits and writes the
+// normalised output rows, so a short decode is ONE launch (q27b::arrive_last).
+#include <limits.h>
+
 #include "decode_mma.cuh"
 #include "t3_lut.cuh"
 
 namespace q27b {
 
 __device__ int g_wait_timeout_flag = 0; // set when a bounded mbarrier wait ran out
-#ifdef Q27_TRACE
-// timing experiments only: [0] earliest CTA start, [1] latest CTA end, [2] latest end of the
-// prologue, [3] latest end of the stage loop (globaltimer ns)
-__device__ unsigned long long g_dec_trace[4] = {~0ull, 0, 0, 0};
-__device__ __forceinline__ unsigned long long gtime() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-#define DTRACE_MIN(i) do { if (threadIdx.x == 0) atomicMin(&g_dec_trace[i], gtime()); } while (0)
-#define DTRACE_MAX(i) do { if (threadIdx.x == 0) atomicMax(&g_dec_trace[i], gtime()); } while (0)
-extern "C" int q27_debug_dec_trace(unsigned long long* out) {
-    cudaMemcpyFromSymbol(out, g_dec_trace, sizeof(unsigned long long) * 4);
-    unsigned long long z[4] = {~0ull, 0, 0, 0};
-    cudaMemcpyToSymbol(g_dec_trace, z, sizeof(z));
-    return 0;
-}
-#else
-#define DTRACE_MIN(i)
-#define DTRACE_MAX(i)
-#endif
 
 namespace {
 
-#ifndef Q27_NCW
-#define Q27_NCW 8
-#endif
-constexpr int NCW = Q27_NCW;      // consumer warps
 constexpr int STAGE_ROWS = 32;    // rows per ring stage (= 2 key tiles; never crosses a page)
 constexpr int TILE = 16;          // keys per MMA tile
 constexpr float LOG2E = 1.4426950408889634f;
-#ifndef Q27_KERNEL_ATTR
-#define Q27_KERNEL_ATTR __launch_bounds__((NCW + 1) * 32, 1)
-#endif
-#ifndef Q27_ABLATE
-#define Q27_ABLATE 0   // timing experiments only: 1 skip K lookups, 2 skip V lookups, 4 skip MMAs
-#endif
+constexpr float LN2 = 0.6931471805599453f;
+constexpr int FUSE_MAX_SPLITS = 64;               // the ticket words live behind split 64
+constexpr int FUSE_MAX_BYTES = 288 * 1024;        // partial bytes one finishing CTA may merge
 
 template <int KVK> struct Fmt;
 template <> struct Fmt<Q27_KV_F16> {
@@ -75,22 +59,24 @@ template <> struct Fmt<Q27_KV_FP8> {
     static constexpr int SLICE = 256;
     static constexpr int STAGES = 8;
 };
-#ifndef Q27_T3_STAGES
-#define Q27_T3_STAGES 5
-#endif
 template <> struct Fmt<Q27_KV_T3> {
     static constexpr int KVH = 4;               // whole 400-byte rows: all four kv heads
     static constexpr int PITCH = 400;
     static constexpr int SLICE = 400;
-    static constexpr int STAGES = Q27_T3_STAGES;
+    static constexpr int STAGES = 5;
 };
+constexpr int NCW = 8;                            // consumer warps
+constexpr int N_THREADS = (NCW + 1) * 32;         // + the producer warp
+constexpr int HEADER_BYTES = 256;                 // ring barriers
 template <int KVK> constexpr int stage_bytes() { return 2 * STAGE_ROWS * Fmt<KVK>::PITCH; }
 template <int KVK> constexpr int ring_bytes() { return stage_bytes<KVK>() * Fmt<KVK>::STAGES; }
 constexpr int MERGE_BYTES = NCW * GQA * PART * 4; // per-warp partials for the final merge
+template <int KVK> constexpr int work_bytes() {
+    return ring_bytes<KVK>() > MERGE_BYTES ? ring_bytes<KVK>() : MERGE_BYTES;
+}
 template <int KVK> constexpr int qstage_bytes() { return Fmt<KVK>::KVH * GQA * HD * 4; }
 template <int KVK> constexpr int smem_bytes() {
-    return 256 + (ring_bytes<KVK>() > MERGE_BYTES ? ring_bytes<KVK>() : MERGE_BYTES) +
-           qstage_bytes<KVK>();
+    return HEADER_BYTES + work_bytes<KVK>() + qstage_bytes<KVK>();
 }
 
 // ---- PTX helpers ----------------------------------------------------------------------
@@ -132,11 +118,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 }
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
-    if (Q27_ABLATE & 4) {
-        c[0] += __uint_as_float(a0 ^ b0); c[1] += __uint_as_float(a1 ^ b1);
-        c[2] += __uint_as_float(a2); c[3] += __uint_as_float(a3);
-        return;
-    }
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%0,%1,%2,%3};"
@@ -157,6 +138,13 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
     uint32_t d;
     asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(x));
     return d;
+}
+// a pointer held by lane `src` of the warp
+__device__ __forceinline__ const void* shfl_ptr(const void* p, int src) {
+    const unsigned long long v = (unsigned long long)(uintptr_t)p;
+    const uint32_t lo = __shfl_sync(0xffffffffu, (uint32_t)v, src);
+    const uint32_t hi = __shfl_sync(0xffffffffu, (uint32_t)(v >> 32), src);
+    return reinterpret_cast<const void*>((uintptr_t)(((unsigned long long)hi << 32) | lo));
 }
 __device__ __forceinline__ float ex2(float x) {
     float y;
@@ -184,11 +172,15 @@ __device__ __forceinline__ uint4 lds128(uint32_t a) {
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
     return v;
 }
-// 32 bits starting at a 2-byte-aligned shared address
+// 32 bits starting at a 2-byte-aligned shared address. The unaligned form glues two 16-bit
+// loads with a multiply-add: that instruction runs on the FMA pipe, which this kernel leaves
+// idle, where a funnel shift would compete with the lookups for the integer pipe.
 __device__ __forceinline__ uint32_t lds32_a2(uint32_t a, bool aligned4) {
     if (aligned4) return lds32(a);
-    const uint32_t lo = lds32(a - 2), hi = lds32(a + 2);
-    return __funnelshift_r(lo, hi, 16);
+    const uint32_t lo = lds16(a), hi = lds16(a + 2);
+    uint32_t r;
+    asm("mad.lo.u32 %0, %1, 65536, %2;" : "=r"(r) : "r"(hi), "r"(lo));
+    return r;
 }
 __device__ __forceinline__ float lds_half(uint32_t a) {
     return __half2float(__ushort_as_half((unsigned short)lds16(a)));
@@ -440,8 +432,9 @@ __device__ __forceinline__ void t3_scores(uint32_t ks, int kvh, const uint32_t (
 }
 
 // turbo3, one 16-key tile, V side: O^T += V^T . P^T with the V norms folded into P.
-__device__ __forceinline__ void t3_values(WarpAcc& A, uint32_t vs, int kvh, const float (&p)[4],
-                                          int valid, int lane, const T3Tab& tab) {
+__device__ __forceinline__ void t3_values(float (&o)[16][4], uint32_t vs, int kvh,
+                                          const float (&p)[4], int valid, int lane,
+                                          const T3Tab& tab) {
     constexpr int P = Fmt<Q27_KV_T3>::PITCH;
     const int g = lane >> 2, c = lane & 3;
     const uint32_t vr0 = vs + g * P + kvh * 100;
@@ -482,55 +475,151 @@ __device__ __forceinline__ void t3_values(WarpAcc& A, uint32_t vs, int kvh, cons
         }
 #pragma unroll
         for (int j = 0; j < 8; j++)
-            mma16816(A.o[8 * b + j], hp[0][2 * j], hp[0][2 * j + 1], hp[1][2 * j],
+            mma16816(o[8 * b + j], hp[0][2 * j], hp[0][2 * j + 1], hp[1][2 * j],
                      hp[1][2 * j + 1], pb[b][0], pb[b][1]);
     }
 }
 
-__device__ __forceinline__ void tile_t3(WarpAcc& A, uint32_t ks, uint32_t vs, int kvh,
-                                        const uint32_t (&qf)[16][2], int valid, float sc2,
-                                        int lane, const T3Tab& tab) {
-    float sv[4], p[4];
-    t3_scores(ks, kvh, qf, valid, sc2, lane, tab, sv);
-    softmax_tile(A, sv, p);
-    t3_values(A, vs, kvh, p, valid, lane, tab);
-}
-
-// Both 16-key tiles of a ring stage at once: the two score computations are independent
-// instruction streams (a lone tile is a chain of dependent PRMT / LOP3 / MMA results and its
-// warp spends most cycles waiting on fixed latencies), and one online-softmax step covers the
-// 32 keys. valid = real keys among the 32 (17..32).
-__device__ __forceinline__ void tile_t3_pair(WarpAcc& A, uint32_t ks, uint32_t vs, int kvh,
-                                             const uint32_t (&qf)[16][2], int valid, float sc2,
-                                             int lane, const T3Tab& tab) {
+// turbo3: both 16-key tiles of a ring stage at once. rows = real keys among the 32 (1..32);
+// a missing second tile costs nothing.
+__device__ __forceinline__ void stage_t3(WarpAcc& A, uint32_t ks, uint32_t vs, int kvh,
+                                         const uint32_t (&qf)[16][2], int rows, float sc2,
+                                         int lane, const T3Tab& tab) {
     constexpr int P = Fmt<Q27_KV_T3>::PITCH;
     float s0[4], s1[4], p0[4], p1[4];
-    t3_scores(ks, kvh, qf, TILE, sc2, lane, tab, s0);
-    t3_scores(ks + TILE * P, kvh, qf, valid - TILE, sc2, lane, tab, s1);
-    softmax_pair(A, s0, s1, p0, p1);
-    t3_values(A, vs, kvh, p0, TILE, lane, tab);
-    t3_values(A, vs + TILE * P, kvh, p1, valid - TILE, lane, tab);
+    if (rows > TILE) {
+        t3_scores(ks, kvh, qf, TILE, sc2, lane, tab, s0);
+        t3_scores(ks + TILE * P, kvh, qf, rows - TILE, sc2, lane, tab, s1);
+        softmax_pair(A, s0, s1, p0, p1);
+        t3_values(A.o, vs, kvh, p0, TILE, lane, tab);
+        t3_values(A.o, vs + TILE * P, kvh, p1, rows - TILE, lane, tab);
+    } else {
+        t3_scores(ks, kvh, qf, rows, sc2, lane, tab, s0);
+        softmax_tile(A, s0, p0);
+        t3_values(A.o, vs, kvh, p0, rows, lane, tab);
+    }
+}
+
+// ---- the finishing step of a fused launch -------------------------------------------------
+// Log-sum-exp merge (k_attn_fd_combine, src/spec3.cu:706-739) of the first `used` splits of NH
+// heads of one lane by the CTA that completed the group last. A head's partials are `used`
+// consecutive 258-float records; bulk copies bring them into the idle ring, up to NBUF heads
+// ahead (one SM pulls a few hundred KB out of L2 in a couple of microseconds this way; plain
+// loads would take several times longer). Sums run in split order with four interleaved
+// accumulators added in a fixed order: the result is the same every run.
+template <int NH, int WORK_BYTES>
+__device__ void finish_group(const float* __restrict__ base, int nsplit, int used,
+                             float* __restrict__ out, uint8_t* ring, uint64_t* bars) {
+    __shared__ float s_w[FUSE_MAX_SPLITS];
+    __shared__ float s_inv;
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (used == 0) {             // nothing attended (an empty shard): zeros, like the combine
+        for (int i = tid; i < NH * HD; i += blockDim.x) out[i] = 0.f;
+        return;
+    }
+    const uint32_t rec_bytes = (uint32_t)used * PART * 4;
+    const uint32_t buf_bytes = (rec_bytes + 16 + 15) & ~15u;        // slack for the alignment shift
+    const int nbuf = min(NH, (int)(WORK_BYTES / buf_bytes));
+    if (tid == 0) {
+        for (int i = 0; i < nbuf; i++) mbar_init(&bars[i], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // ring: generic reads/writes -> bulk writes
+    __syncthreads();
+    auto issue = [&](int h) {
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(base + (size_t)h * nsplit * PART);
+        const uint32_t off = (uint32_t)((uintptr_t)src & 15);
+        const uint32_t bytes = (off + rec_bytes + 15) & ~15u;
+        mbar_expect_tx(&bars[h % nbuf], bytes);
+        bulk_g2s(ring + (size_t)(h % nbuf) * buf_bytes, src - off, bytes, &bars[h % nbuf]);
+    };
+    if (tid == 0)
+        for (int h = 0; h < nbuf; h++) issue(h);
+    bool ok = true;
+    for (int h = 0; h < NH; h++) {
+        ok = ok && mbar_wait(&bars[h % nbuf], (uint32_t)((h / nbuf) & 1));
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(base + (size_t)h * nsplit * PART);
+        const float* rec = reinterpret_cast<const float*>(ring + (size_t)(h % nbuf) * buf_bytes +
+                                                          ((uintptr_t)src & 15));
+        if (tid < 32) {
+            // used <= 64: lane owns splits lane and lane + 32 (clamped loads, masked weights)
+            const int s0 = min(lane, used - 1), s1 = min(lane + 32, used - 1);
+            const float m0 = rec[s0 * PART], m1 = rec[s1 * PART];
+            const float l0 = rec[s0 * PART + 1], l1 = rec[s1 * PART + 1];
+            const bool v0 = lane < used && m0 != NEG_SENTINEL, v1 = lane + 32 < used && m1 != NEG_SENTINEL;
+            float m = fmaxf(v0 ? m0 : NEG_SENTINEL, v1 ? m1 : NEG_SENTINEL);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+            const float w0 = v0 ? expf(m0 - m) : 0.f, w1 = v1 ? expf(m1 - m) : 0.f;
+            s_w[lane] = w0;
+            s_w[lane + 32] = w1;
+            float l = (v0 ? l0 * w0 : 0.f) + (v1 ? l1 * w1 : 0.f);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+            if (lane == 0) s_inv = l > 0.f ? 1.0f / l : 0.f;
+        }
+        __syncthreads();
+        if (tid < HD && ok) {
+            float a[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int s0 = 0; s0 < used; s0 += 8) {
+                float v[8], w[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) {     // every load is issued before any is used
+                    const int sp = min(s0 + u, used - 1);
+                    v[u] = rec[sp * PART + 2 + tid];
+                    w[u] = s0 + u < used ? s_w[sp] : 0.f;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    // sentinel splits hold undefined accumulators: selected, never added
+                    const float x = v[u] * w[u];
+                    a[u & 3] += w[u] != 0.f ? x : 0.f;
+                }
+            }
+            out[(size_t)h * HD + tid] = ((a[0] + a[1]) + (a[2] + a[3])) * s_inv;
+        }
+        __syncthreads();         // every thread is done reading this buffer
+        if (tid == 0 && h + nbuf < NH && ok) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // reads before the overwrite
+            issue(h + nbuf);
+        }
+    }
+    if (!ok) atomicExch(&g_wait_timeout_flag, 1);
 }
 
 // ---- the kernel -------------------------------------------------------------------------
 template <int KVK>
-__global__ void Q27_KERNEL_ATTR
+__global__ void __launch_bounds__(N_THREADS, 1)
 k_decode_mma(const __grid_constant__ DevBatch b) {
     using F = Fmt<KVK>;
     constexpr int WAYS = NCW / F::KVH;             // consumer warps per kv head
+    constexpr int NHEADS = F::KVH * GQA;           // query heads this CTA serves
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + 16;
-    uint8_t* ring = smem + 256;
+    uint8_t* ring = smem + HEADER_BYTES;
+    float* q_stage = reinterpret_cast<float*>(ring + work_bytes<KVK>());
+    __shared__ int s_fail, s_last;
+    __shared__ float s_wt[NHEADS][WAYS], s_mb[NHEADS], s_lb[NHEADS];
 
-    DTRACE_MIN(0);
-    pdl_trigger();               // the combine kernel may be scheduled; it waits for this grid
+    pdl_trigger();               // a combine kernel may be scheduled; it waits for this grid
     const int t = blockIdx.x, sp = blockIdx.y;
-    const int slot = blockIdx.z / (b.n_kv / F::KVH), kvg = blockIdx.z % (b.n_kv / F::KVH);
+    const int groups = b.n_kv / F::KVH;
+    const int slot = blockIdx.z / groups, kvg = blockIdx.z % groups;
     const DevSlot& S = b.s[slot];
     if (t >= S.ntok) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+    unsigned long long* ticket = nullptr;
+    if (b.fuse) {
+        // the ticket word of this (lane, kv group), behind split 64 of the slot's scratch; a
+        // word that does not carry the tag yet (first use of this scratch) is armed here, long
+        // before anybody arrives on it
+        ticket = reinterpret_cast<unsigned long long*>(
+                     S.scratch + (size_t)S.ntok * b.n_q * FUSE_MAX_SPLITS * PART) +
+                 (size_t)t * groups + kvg;
+        if (threadIdx.x == 0) ticket_arm(ticket);
+    }
     int max_len = 0;
     for (int u = 0; u < S.ntok; u++)
         max_len = max(max_len, local_len(__ldg(S.pos[u]), S.row_base, S.row_count));
@@ -539,231 +628,309 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
     const int lo = sp * chunk, hi = min(my_len, lo + chunk);
     const int kvh0 = kvg * F::KVH;
     float* dst0 = S.scratch + (((size_t)t * b.n_q + kvh0 * GQA) * b.nsplit + sp) * PART;
+
     if (lo >= hi) {
-        if (threadIdx.x < F::KVH * GQA) {
+        // empty window: stamp the sentinel so that whoever merges can skip it
+        if (threadIdx.x < NHEADS) {
             float* d = dst0 + (size_t)threadIdx.x * b.nsplit * PART;
             d[0] = NEG_SENTINEL;
             d[1] = 0.f;
         }
-        DTRACE_MAX(1);
-        return;
-    }
-    const int nstages = (hi - lo + STAGE_ROWS - 1) / STAGE_ROWS;
-
-    // the CTA's query heads, fp32, staged once with coalesced loads
-    float* q_stage = reinterpret_cast<float*>(ring + (ring_bytes<KVK>() > MERGE_BYTES
-                                                          ? ring_bytes<KVK>() : MERGE_BYTES));
-    for (int i = threadIdx.x; i < F::KVH * GQA * (HD / 4); i += blockDim.x) {
-        const int h = i / (HD / 4), d4 = i % (HD / 4);
-        reinterpret_cast<float4*>(q_stage)[i] = __ldg(reinterpret_cast<const float4*>(
-            S.q[t] + (size_t)(kvh0 * GQA + h) * b.q_stride) + d4);
-    }
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < F::STAGES; s++) {
-            mbar_init(&full[s], KVK == Q27_KV_T3 ? 1 : 32);   // tx bytes, or 32 lane arrivals
-            mbar_init(&empty[s], NCW);        // every consumer warp releases every stage
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    // Rows past the end of a ragged last stage are never copied; their weights are exact
-    // zeros, so the stale bytes only have to decode to finite numbers. Any turbo3 byte
-    // pattern decodes to a centroid (its norms are masked); fp16 / fp8 patterns may be
-    // NaN or Inf, so those rings are cleared once.
-    if (KVK != Q27_KV_T3) {
-        for (int i = threadIdx.x; i < ring_bytes<KVK>() / 16; i += blockDim.x)
-            reinterpret_cast<uint4*>(ring)[i] = make_uint4(0, 0, 0, 0);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    }
-    __syncthreads();
-    DTRACE_MAX(2);
-
-    if (warp == NCW) {
-        // ---------------- producer ----------------
-        for (int i = 0; i < nstages; i++) {
-            const int s = i % F::STAGES;
-            const uint32_t ph = (uint32_t)((i / F::STAGES) & 1);
-            if (i >= F::STAGES && !mbar_wait(&empty[s], ph ^ 1)) break;
-            const int row0 = lo + i * STAGE_ROWS;
-            const int nrows = min(STAGE_ROWS, hi - row0);
-            uint8_t* kdst = ring + (size_t)s * stage_bytes<KVK>();
-            uint8_t* vdst = kdst + STAGE_ROWS * F::PITCH;
-            if (KVK == Q27_KV_T3) {
-                if (lane == 0) {
-                    const uint32_t bytes = (uint32_t)nrows * F::SLICE;
-                    const size_t off = (size_t)(row0 & (PAGE - 1)) * F::SLICE;
-                    mbar_expect_tx(&full[s], 2 * bytes);
-                    bulk_g2s(kdst, static_cast<const uint8_t*>(S.ktab[row0 >> PAGE_SHIFT]) + off,
-                             bytes, &full[s]);
-                    bulk_g2s(vdst, static_cast<const uint8_t*>(S.vtab[row0 >> PAGE_SHIFT]) + off,
-                             bytes, &full[s]);
-                }
-            } else {
-                // fp16 / fp8: the rows of one kv head are 512 / 256-byte slices 2048 / 1024 B
-                // apart, and each goes to a padded pitch, so there is no single large copy.
-                // One bulk copy per slice is bound by the copy rate (about one per 70 cycles:
-                // a third of the HBM rate at 131K rows); 16-byte asynchronous copies by the
-                // whole warp are not. Each lane's arrival is counted when its copies land.
-                constexpr int CPR = F::SLICE / 16;        // 16-byte chunks per row slice
-                constexpr int RPI = 32 / CPR;             // row slices per warp instruction
-                const size_t off = ((size_t)(row0 & (PAGE - 1)) * b.n_kv + kvh0) * F::SLICE;
-                const uint8_t* kp = static_cast<const uint8_t*>(S.ktab[row0 >> PAGE_SHIFT]) + off;
-                const uint8_t* vp = static_cast<const uint8_t*>(S.vtab[row0 >> PAGE_SHIFT]) + off;
-                const int c16 = (lane % CPR) * 16;
-                for (int r = lane / CPR; r < nrows; r += RPI) {
-                    const size_t src = (size_t)r * b.n_kv * F::SLICE + c16;
-                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-                                 ::"r"(smem_u32(kdst + r * F::PITCH + c16)), "l"(kp + src) : "memory");
-                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-                                 ::"r"(smem_u32(vdst + r * F::PITCH + c16)), "l"(vp + src) : "memory");
-                }
-                asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
-                             ::"r"(smem_u32(&full[s])) : "memory");
-            }
-        }
-        if (KVK != Q27_KV_T3) asm volatile("cp.async.wait_all;" ::: "memory");
     } else {
-        // ---------------- consumers ----------------
-        const int hq = warp % F::KVH, way = warp / F::KVH;
-        const int kvh = kvh0 + hq;
-        const int g = lane >> 2, c = lane & 3;
-        // Q^T fragments: column n = g is head kvh*6 + g (columns 6, 7 are zero padding)
-        uint32_t qf[16][2];
-        {
-            const float* qh = q_stage + (size_t)(hq * GQA + (g < GQA ? g : 0)) * HD;
-#pragma unroll
-            for (int s = 0; s < 16; s++)
-#pragma unroll
-                for (int r = 0; r < 2; r++) {
-                    const float x0 = g < GQA ? qh[kdim<KVK>(s, c, r, 0)] : 0.f;
-                    const float x1 = g < GQA ? qh[kdim<KVK>(s, c, r, 1)] : 0.f;
-                    qf[s][r] = pack_h2(x0, x1);
-                }
+        const int nstages = (hi - lo + STAGE_ROWS - 1) / STAGE_ROWS;
+        if (threadIdx.x == 0) {
+            s_fail = 0;
+            for (int s = 0; s < F::STAGES; s++) {
+                mbar_init(&full[s], KVK == Q27_KV_T3 ? 1 : 32);   // tx bytes, or 32 lane arrivals
+                mbar_init(&empty[s], NCW);        // every consumer warp releases every stage
+            }
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         }
-        WarpAcc A;
-#pragma unroll
-        for (int mt = 0; mt < 16; mt++) A.o[mt][0] = A.o[mt][1] = A.o[mt][2] = A.o[mt][3] = 0.f;
-        A.m[0] = A.m[1] = -INFINITY;
-        A.l[0] = A.l[1] = 0.f;
+        __syncthreads();         // barriers are live: the producer starts while Q is staged
+
         const float sc2 = b.scale * LOG2E;
-        T3Tab tab = t3_tables();
-        (void)tab;
-
-        const int ntiles = (hi - lo + TILE - 1) / TILE;
         const uint32_t ring_s = smem_u32(ring);
-        // Every consumer warp observes every phase of every ring slot, in order (waits on
-        // `full`, arrives on `empty`), whether or not it owns a tile of that stage: a warp
-        // that skipped phases could not tell them apart by parity.
-        for (int i = 0; i < nstages; i++) {
-            const int s = i % F::STAGES;
-            const uint32_t ph = (uint32_t)((i / F::STAGES) & 1);
-            if (!mbar_wait(&full[s], ph)) break;
-            if (KVK == Q27_KV_T3 && i % WAYS == way && hi - lo - i * STAGE_ROWS > TILE) {
-                const uint32_t ks = ring_s + s * stage_bytes<KVK>();
-                tile_t3_pair(A, ks, ks + STAGE_ROWS * F::PITCH, hq, qf,
-                             min(STAGE_ROWS, hi - lo - i * STAGE_ROWS), sc2, lane, tab);
-            } else
-#pragma unroll
-            for (int half = 0; half < 2; half++) {
-                const int tile = 2 * i + half;
-                if (i % WAYS == way && tile < ntiles) {
-                    const int valid = min(TILE, hi - lo - tile * TILE);
-                    const uint32_t ks = ring_s + s * stage_bytes<KVK>() + half * TILE * F::PITCH;
-                    const uint32_t vs = ks + STAGE_ROWS * F::PITCH;
-                    if (KVK == Q27_KV_F16) tile_f16<KVK>(A, ks, vs, qf, valid, sc2, lane);
-                    else if (KVK == Q27_KV_FP8) tile_fp8(A, ks, vs, qf, valid, sc2, lane);
-                    else tile_t3(A, ks, vs, hq, qf, valid, sc2, lane, tab);
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-        }
+        const int g = lane >> 2, c = lane & 3;
+        float* ring_f = reinterpret_cast<float*>(ring);
 
-        // every consumer is past its last ring read once all of them reach this barrier
-        asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32));
-        DTRACE_MAX(3);
-        // column sums: add the shares of the 8 threads of a column group
-#pragma unroll
-        for (int off = 4; off < 32; off <<= 1) {
-            A.l[0] += __shfl_xor_sync(0xffffffffu, A.l[0], off);
-            A.l[1] += __shfl_xor_sync(0xffffffffu, A.l[1], off);
-        }
-        // per-warp partial [head j][258] into the (now idle) ring; natural-log domain for m
-        float* wp = reinterpret_cast<float*>(ring) + (size_t)warp * GQA * PART;
-        const float LN2 = 0.6931471805599453f;
-#pragma unroll
-        for (int e = 0; e < 2; e++) {
-            const int j = 2 * c + e;
-            if (j < GQA) {
-                if (g == 0) {
-                    wp[j * PART] = A.m[e] == -INFINITY ? NEG_SENTINEL : A.m[e] * LN2;
-                    wp[j * PART + 1] = A.l[e];
+        if (warp == NCW) {
+            // ---------------- producer ----------------
+            // page pointers are fetched 32 pages at a time, one per lane, so that no stage
+            // waits on a dependent table load
+            const int last_page = (hi - 1) >> PAGE_SHIFT;
+            const void* kpl = nullptr;
+            const void* vpl = nullptr;
+            int pbase = INT_MIN / 2;
+            int issued = 0;
+            for (int i = 0; i < nstages; i++) {
+                const int s = i % F::STAGES;
+                const uint32_t ph = (uint32_t)((i / F::STAGES) & 1);
+                const int row0 = lo + i * STAGE_ROWS;
+                const int pg = row0 >> PAGE_SHIFT;
+                if (pg - pbase >= 32) {
+                    pbase = pg;
+                    if (pg + lane <= last_page) {
+                        kpl = S.ktab[pg + lane];
+                        vpl = S.vtab[pg + lane];
+                    }
                 }
+                const uint8_t* kpage = static_cast<const uint8_t*>(shfl_ptr(kpl, pg - pbase));
+                const uint8_t* vpage = static_cast<const uint8_t*>(shfl_ptr(vpl, pg - pbase));
+                if (i >= F::STAGES && !mbar_wait(&empty[s], ph ^ 1)) { s_fail = 1; break; }
+                const int nrows = min(STAGE_ROWS, hi - row0);
+                uint8_t* kdst = ring + (size_t)s * stage_bytes<KVK>();
+                uint8_t* vdst = kdst + STAGE_ROWS * F::PITCH;
+                if (KVK == Q27_KV_T3) {
+                    if (lane == 0) {
+                        const uint32_t bytes = (uint32_t)nrows * F::SLICE;
+                        const size_t off = (size_t)(row0 & (PAGE - 1)) * F::SLICE;
+                        mbar_expect_tx(&full[s], 2 * bytes);
+                        bulk_g2s(kdst, kpage + off, bytes, &full[s]);
+                        bulk_g2s(vdst, vpage + off, bytes, &full[s]);
+                    }
+                } else {
+                    // fp16 / fp8: the rows of one kv head are 512 / 256-byte slices 2048 / 1024 B
+                    // apart, and each goes to a padded pitch, so there is no single large copy.
+                    // One bulk copy per slice is bound by the copy rate (about one per 70 cycles:
+                    // a third of the HBM rate at 131K rows); 16-byte asynchronous copies by the
+                    // whole warp are not. Each lane's arrival is counted when its copies land.
+                    constexpr int CPR = F::SLICE / 16;        // 16-byte chunks per row slice
+                    constexpr int RPI = 32 / CPR;             // row slices per warp instruction
+                    const size_t off = ((size_t)(row0 & (PAGE - 1)) * b.n_kv + kvh0) * F::SLICE;
+                    const uint8_t* kp = kpage + off;
+                    const uint8_t* vp = vpage + off;
+                    const int c16 = (lane % CPR) * 16;
+                    for (int r = lane / CPR; r < nrows; r += RPI) {
+                        const size_t src = (size_t)r * b.n_kv * F::SLICE + c16;
+                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                                     ::"r"(smem_u32(kdst + r * F::PITCH + c16)), "l"(kp + src) : "memory");
+                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                                     ::"r"(smem_u32(vdst + r * F::PITCH + c16)), "l"(vp + src) : "memory");
+                    }
+                    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
+                                 ::"r"(smem_u32(&full[s])) : "memory");
+                }
+                issued = i + 1;
+            }
+            // No copy may still be in flight when the CTA hands its shared memory back (or reuses
+            // it below), also when a consumer gave up early: wait, bounded, for what was issued.
+            if (KVK != Q27_KV_T3) {
+                asm volatile("cp.async.wait_all;" ::: "memory");
+            } else {
+                for (int i = max(0, issued - F::STAGES); i < issued; i++)
+                    if (!mbar_wait(&full[i % F::STAGES], (uint32_t)((i / F::STAGES) & 1))) s_fail = 1;
+            }
+        } else {
+            // ---------------- consumers ----------------
+            const int ctid = threadIdx.x;         // 0 .. NCW*32-1
+            // the CTA's query heads, fp32, staged once with coalesced loads
+            for (int i = ctid; i < NHEADS * (HD / 4); i += NCW * 32) {
+                const int h = i / (HD / 4), d4 = i % (HD / 4);
+                reinterpret_cast<float4*>(q_stage)[i] = __ldg(reinterpret_cast<const float4*>(
+                    S.q[t] + (size_t)(kvh0 * GQA + h) * b.q_stride) + d4);
+            }
+            // Rows past the end of a ragged last stage are never copied; their weights are exact
+            // zeros, so what the ring holds there only has to decode to finite numbers. Any
+            // turbo3 byte pattern decodes to a centroid (its norms are masked). fp16 / fp8
+            // patterns may be NaN or Inf: if the last stage's slot was never filled before, the
+            // rows the copies will not touch are cleared (bytes the copies do not write).
+            if (KVK != Q27_KV_T3 && nstages <= F::STAGES) {
+                const int il = nstages - 1, nlast = hi - lo - il * STAGE_ROWS;
+                uint8_t* kdst = ring + (size_t)(il % F::STAGES) * stage_bytes<KVK>();
+                const int per_row = F::PITCH / 16;
+                for (int i = ctid; i < (STAGE_ROWS - nlast) * per_row * 2; i += NCW * 32) {
+                    const int side = i / ((STAGE_ROWS - nlast) * per_row);
+                    const int j = i % ((STAGE_ROWS - nlast) * per_row);
+                    reinterpret_cast<uint4*>(kdst + side * STAGE_ROWS * F::PITCH +
+                                             (size_t)(nlast + j / per_row) * F::PITCH)[j % per_row] =
+                        make_uint4(0, 0, 0, 0);
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32));
+
+            const int hq = warp % F::KVH, way = warp / F::KVH;
+            // Q^T fragments: column n = g is head (kvh0 + hq)*6 + g (columns 6, 7 are zero padding)
+            uint32_t qf[16][2];
+            {
+                const float* qh = q_stage + (size_t)(hq * GQA + (g < GQA ? g : 0)) * HD;
 #pragma unroll
-                for (int mt = 0; mt < 16; mt++) {
-                    wp[j * PART + 2 + vdim<KVK>(mt, g)] = A.o[mt][e];
-                    wp[j * PART + 2 + vdim<KVK>(mt, g + 8)] = A.o[mt][2 + e];
+                for (int s = 0; s < 16; s++)
+#pragma unroll
+                    for (int r = 0; r < 2; r++) {
+                        const float x0 = g < GQA ? qh[kdim<KVK>(s, c, r, 0)] : 0.f;
+                        const float x1 = g < GQA ? qh[kdim<KVK>(s, c, r, 1)] : 0.f;
+                        qf[s][r] = pack_h2(x0, x1);
+                    }
+            }
+            WarpAcc A;
+#pragma unroll
+            for (int mt = 0; mt < 16; mt++) A.o[mt][0] = A.o[mt][1] = A.o[mt][2] = A.o[mt][3] = 0.f;
+            A.m[0] = A.m[1] = -INFINITY;
+            A.l[0] = A.l[1] = 0.f;
+            const T3Tab tab = t3_tables();
+            (void)tab;
+            const int ntiles = (hi - lo + TILE - 1) / TILE;
+            // Every consumer warp observes every phase of every ring slot, in order (waits on
+            // `full`, arrives on `empty`), whether or not it owns a tile of that stage: a warp
+            // that skipped phases could not tell them apart by parity.
+            for (int i = 0; i < nstages; i++) {
+                const int s = i % F::STAGES;
+                const uint32_t ph = (uint32_t)((i / F::STAGES) & 1);
+                if (!mbar_wait(&full[s], ph)) { s_fail = 1; break; }
+                if (KVK == Q27_KV_T3) {
+                    if (i % WAYS == way) {
+                        const uint32_t ks = ring_s + s * stage_bytes<KVK>();
+                        stage_t3(A, ks, ks + STAGE_ROWS * F::PITCH, hq, qf,
+                                 min(STAGE_ROWS, hi - lo - i * STAGE_ROWS), sc2, lane, tab);
+                    }
+                } else {
+#pragma unroll
+                    for (int half = 0; half < 2; half++) {
+                        const int tile = 2 * i + half;
+                        if (i % WAYS == way && tile < ntiles) {
+                            const int valid = min(TILE, hi - lo - tile * TILE);
+                            const uint32_t ks = ring_s + s * stage_bytes<KVK>() + half * TILE * F::PITCH;
+                            const uint32_t vs = ks + STAGE_ROWS * F::PITCH;
+                            if (KVK == Q27_KV_F16) tile_f16<KVK>(A, ks, vs, qf, valid, sc2, lane);
+                            else tile_fp8(A, ks, vs, qf, valid, sc2, lane);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+            }
+            // every consumer is past its last ring read once all of them reach this barrier
+            asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32));
+            // column sums: add the shares of the 8 threads of a column group
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                A.l[0] += __shfl_xor_sync(0xffffffffu, A.l[0], off);
+                A.l[1] += __shfl_xor_sync(0xffffffffu, A.l[1], off);
+            }
+            // per-warp partial [head j][258] into the (now idle) ring; natural-log domain for m
+            float* wp = ring_f + (size_t)warp * GQA * PART;
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int j = 2 * c + e;
+                if (j < GQA) {
+                    if (g == 0) {
+                        wp[j * PART] = A.m[e] == -INFINITY ? NEG_SENTINEL : A.m[e] * LN2;
+                        wp[j * PART + 1] = A.l[e];
+                    }
+#pragma unroll
+                    for (int mt = 0; mt < 16; mt++) {
+                        wp[j * PART + 2 + vdim<KVK>(mt, g)] = A.o[mt][e];
+                        wp[j * PART + 2 + vdim<KVK>(mt, g + 8)] = A.o[mt][2 + e];
+                    }
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32));
+            // Merge the WAYS partial sets of each head in a fixed order. One thread per head
+            // forms the weights e^{m_w - M} once; then every thread owns one dim of all heads.
+            // A CTA that gave up on a wait publishes empty partials instead.
+            const bool failed = s_fail != 0;
+            if (ctid < NHEADS) {
+                const int h = ctid / GQA, j = ctid % GQA;
+                const float* src = ring_f + (size_t)h * GQA * PART + j * PART;
+                float mb = NEG_SENTINEL;
+#pragma unroll
+                for (int w = 0; w < WAYS; w++) mb = fmaxf(mb, src[(size_t)w * NHEADS * PART]);
+                float lb = 0.f;
+#pragma unroll
+                for (int w = 0; w < WAYS; w++) {
+                    const float* pw = src + (size_t)w * NHEADS * PART;
+                    const float e = pw[0] == NEG_SENTINEL ? 0.f : expf(pw[0] - mb);
+                    s_wt[ctid][w] = e;
+                    lb += pw[1] * e;
+                }
+                s_mb[ctid] = failed ? NEG_SENTINEL : mb;
+                s_lb[ctid] = failed ? 0.f : lb;
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32));
+            if (ctid < HD) {
+#pragma unroll 6
+                for (int hj = 0; hj < NHEADS; hj++) {
+                    const float* src = ring_f + (size_t)(hj / GQA) * GQA * PART + (hj % GQA) * PART;
+                    float acc = 0.f, v[WAYS];
+#pragma unroll
+                    for (int w = 0; w < WAYS; w++) v[w] = src[(size_t)w * NHEADS * PART + 2 + ctid];
+#pragma unroll
+                    for (int w = 0; w < WAYS; w++) {
+                        // a set that saw no key has weight 0: selected, never added
+                        const float e = s_wt[hj][w], x = v[w] * e;
+                        acc += e != 0.f ? x : 0.f;
+                    }
+                    float* d = dst0 + (size_t)hj * b.nsplit * PART;
+                    if (ctid == 0) { d[0] = s_mb[hj]; d[1] = s_lb[hj]; }
+                    d[2 + ctid] = acc;
                 }
             }
         }
-        asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32));
-        // merge the WAYS warps of each kv head in a fixed order and write the CTA partial
-        const int tid = threadIdx.x;
-        for (int hj = 0; tid < HD && hj < F::KVH * GQA; hj++) {
-            const int h = hj / GQA, j = hj % GQA;
-            const float* src = reinterpret_cast<float*>(ring) + (size_t)h * GQA * PART + j * PART;
-            float mb = NEG_SENTINEL;
-#pragma unroll
-            for (int w = 0; w < WAYS; w++) mb = fmaxf(mb, src[(size_t)w * F::KVH * GQA * PART]);
-            float lb = 0.f, acc = 0.f;
-#pragma unroll
-            for (int w = 0; w < WAYS; w++) {
-                const float* pw = src + (size_t)w * F::KVH * GQA * PART;
-                const float e = pw[0] == NEG_SENTINEL ? 0.f : expf(pw[0] - mb);
-                lb += pw[1] * e;
-                acc += pw[2 + tid] * e;
-            }
-            float* d = dst0 + (size_t)hj * b.nsplit * PART;
-            if (tid == 0) { d[0] = mb; d[1] = lb; }
-            d[2 + tid] = acc;
+        __syncthreads();         // the producer has drained: shared memory is quiet from here on
+    }
+
+    if (b.fuse) {
+        // the CTA that completes this (slot, lane, kv group) last merges its splits
+        __syncthreads();
+        if (threadIdx.x == 0) s_last = ticket_take(ticket, (unsigned)b.nsplit) ? 1 : 0;
+        __syncthreads();
+        if (s_last) {
+            const int used = min(b.nsplit, (max_len + chunk - 1) / chunk);
+            finish_group<NHEADS, work_bytes<KVK>()>(
+                S.scratch + ((size_t)t * b.n_q + kvh0 * GQA) * b.nsplit * PART, b.nsplit, used,
+                S.out[t] + (size_t)kvh0 * GQA * HD, ring, full);
         }
-        DTRACE_MAX(1);
     }
 }
 
 template <int KVK>
-int launch_one(DevBatch& b, int sm_count, cudaStream_t st) {
+int launch_one(DevBatch& b, int sm_count, bool may_fuse, cudaStream_t st) {
     using F = Fmt<KVK>;
-    static bool attr_set = false;
-    if (!attr_set) {
+    static DeviceOnce once;      // the attribute belongs to a device, not to the process
+    int rc = device_once(once, []() -> int {
         Q27_CUDA_TRY(cudaFuncSetAttribute(k_decode_mma<KVK>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           smem_bytes<KVK>()));
-        attr_set = true;
-    }
+        return Q27_OK;
+    });
+    if (rc) return rc;
     const int groups = b.n_kv / F::KVH;
     const int per_split = b.nslots * b.max_ntok * groups;
     int ns = sm_count / per_split;
-    b.nsplit = ns < 1 ? 1 : ns > Q27_MAX_SPLITS ? Q27_MAX_SPLITS : ns;
+    ns = ns < 1 ? 1 : ns > Q27_MAX_SPLITS ? Q27_MAX_SPLITS : ns;
+    // Small launches finish in this kernel: the last CTA of a (slot, lane, kv group) merges
+    // the group's partials, if they are few enough for one SM to pull through in about the
+    // time a second launch would cost. The ticket words sit behind split 64 of the scratch.
+    b.fuse = 0;
+    if (may_fuse && ns <= FUSE_MAX_SPLITS && F::KVH * GQA * ns * PART * 4 <= FUSE_MAX_BYTES) {
+        b.fuse = 1;
+        for (int i = 0; i < b.nslots; i++)
+            if ((uintptr_t)b.s[i].scratch & 15) b.fuse = 0;   // bulk copies out of the scratch
+    }
+    b.nsplit = ns;
     b.unit = STAGE_ROWS;
     dim3 grid(b.max_ntok, b.nsplit, b.nslots * groups);
-    k_decode_mma<KVK><<<grid, (NCW + 1) * 32, smem_bytes<KVK>(), st>>>(b);
+    k_decode_mma<KVK><<<grid, N_THREADS, smem_bytes<KVK>(), st>>>(b);
     Q27_CUDA_TRY(cudaGetLastError());
+    Q27_COUNT_LAUNCH();
     return Q27_OK;
 }
 
 } // namespace
 
-int launch_decode_mma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool* done) {
+int launch_decode_mma(DevBatch& b, int kvk, int sm_count, bool may_fuse, cudaStream_t st,
+                      bool* done) {
     *done = false;
+    b.fuse = 0;
     if (b.n_kv != 4) return Q27_OK; // the ring layouts assume 4 kv heads per row
     if (b.q_stride & 3) return Q27_OK; // Q heads are staged with 16-byte loads
     for (int i = 0; i < b.nslots; i++)
         for (int t = 0; t < b.s[i].ntok; t++)
             if ((uintptr_t)b.s[i].q[t] & 15) return Q27_OK;
     int rc;
-    if (kvk == Q27_KV_F16) rc = launch_one<Q27_KV_F16>(b, sm_count, st);
-    else if (kvk == Q27_KV_FP8) rc = launch_one<Q27_KV_FP8>(b, sm_count, st);
-    else if (kvk == Q27_KV_T3) rc = launch_one<Q27_KV_T3>(b, sm_count, st);
+    if (kvk == Q27_KV_F16) rc = launch_one<Q27_KV_F16>(b, sm_count, may_fuse, st);
+    else if (kvk == Q27_KV_FP8) rc = launch_one<Q27_KV_FP8>(b, sm_count, may_fuse, st);
+    else if (kvk == Q27_KV_T3) rc = launch_one<Q27_KV_T3>(b, sm_count, may_fuse, st);
     else return Q27_ERR_UNSUPPORTED_KIND;
     if (rc == Q27_OK) *done = true;
     return rc;

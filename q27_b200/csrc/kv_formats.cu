@@ -42,6 +42,7 @@ int launch_kv_dequant(const void* const* tab, int kvk, int row0, int nrows, int 
     else if (kvk == Q27_KV_T3) k_kv_dequant<Q27_KV_T3><<<blocks, 256, 0, st>>>(tab, row0, nrows, n_kv, out);
     else return Q27_ERR_UNSUPPORTED_KIND;
     Q27_CUDA_TRY(cudaGetLastError());
+    Q27_COUNT_LAUNCH();
     return Q27_OK;
 }
 
@@ -51,6 +52,7 @@ int launch_mk_tab(const void* base, size_t row_bytes, int rows, void** d_tab, cu
     k_mk_tab<<<(np + 255) / 256, 256, 0, st>>>(static_cast<const char*>(base),
                                                (size_t)PAGE * row_bytes, np, d_tab);
     Q27_CUDA_TRY(cudaGetLastError());
+    Q27_COUNT_LAUNCH();
     return Q27_OK;
 }
 

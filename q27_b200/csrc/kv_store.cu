@@ -13,23 +13,15 @@ namespace q27b {
 namespace {
 
 constexpr float INV_SQRT_128 = 0.08838834764831845f;
-// WHT sign diagonals as bit masks: bit j set <=> element j is -1 (src/turbo3.cuh:42-43)
-__device__ __constant__ uint32_t kS1Neg[4] = {0xE46A0359u, 0x42F85949u, 0xA4C63BBBu, 0x49F250A9u};
-__device__ __constant__ uint32_t kS2Neg[4] = {0x16ACEE90u, 0x3F628FDCu, 0xB7A5357Au, 0xBEA56562u};
-
 __device__ __forceinline__ float sgn(const uint32_t* m, int j) {
     return (m[j >> 5] >> (j & 31)) & 1u ? -1.f : 1.f;
 }
 
 __device__ __forceinline__ int t3_nearest(float v) { // src/turbo3.cuh:57-66
-    if (v < -0.154496f) return 0;
-    if (v < -0.092804f) return 1;
-    if (v < -0.044243f) return 2;
-    if (v < 0.000000f) return 3;
-    if (v < 0.044243f) return 4;
-    if (v < 0.092804f) return 5;
-    if (v < 0.154496f) return 6;
-    return 7;
+    int idx = 0;
+#pragma unroll
+    for (int i = 0; i < 7; i++) idx += v < kT3Midpoint[i] ? 0 : 1;   // thresholds ascend
+    return idx;
 }
 
 // 128-point butterfly over a warp's shared buffer: element pairs (j, j^h), lo+hi / lo-hi.
@@ -262,6 +254,7 @@ int launch_kv_store_T(const float* kT, const float* vT, void* const* ktab, void*
         return Q27_ERR_UNSUPPORTED_KIND;
     }
     Q27_CUDA_TRY(cudaGetLastError());
+    Q27_COUNT_LAUNCH();
     return Q27_OK;
 }
 
@@ -287,6 +280,7 @@ int launch_kv_store3(const float* const* k, const float* const* v, const int* co
         return Q27_ERR_UNSUPPORTED_KIND;
     }
     Q27_CUDA_TRY(cudaGetLastError());
+    Q27_COUNT_LAUNCH();
     return Q27_OK;
 }
 
@@ -298,6 +292,7 @@ int launch_wht3(float* const* x, int n_heads, int stride, int ntok, bool inv, cu
     if (inv) k_wht3<true><<<grid, ST_WARPS * 32, 0, st>>>(V, n_heads, stride);
     else k_wht3<false><<<grid, ST_WARPS * 32, 0, st>>>(V, n_heads, stride);
     Q27_CUDA_TRY(cudaGetLastError());
+    Q27_COUNT_LAUNCH();
     return Q27_OK;
 }
 
@@ -308,6 +303,7 @@ int launch_wht_T(float* x, int n_heads, int head_stride, int row_stride, int T, 
     if (inv) k_wht_T<true><<<blocks, ST_WARPS * 32, 0, st>>>(x, n_heads, head_stride, row_stride, T);
     else k_wht_T<false><<<blocks, ST_WARPS * 32, 0, st>>>(x, n_heads, head_stride, row_stride, T);
     Q27_CUDA_TRY(cudaGetLastError());
+    Q27_COUNT_LAUNCH();
     return Q27_OK;
 }
 

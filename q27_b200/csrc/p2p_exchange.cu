@@ -39,36 +39,42 @@ k_merge_pushed(uint8_t* __restrict__ box, int world, int64_t npairs, uint32_t ep
         if (!got) { s_ok = 0; atomicExch(&g_xchg_timeout_flag, 4); }
     }
     __syncthreads();
-    if (!s_ok) return;
+    const bool ok = s_ok != 0;
     const int64_t w = blockIdx.x;
-    const float* parts = reinterpret_cast<const float*>(box) + (size_t)par * xchg_data_floats(world, npairs);
-    float mg = NEG_SENTINEL;
-    for (int s = 0; s < world; s++) mg = fmaxf(mg, __ldcg(parts + ((size_t)s * npairs + w) * PART));
-    float lg = 0.f;
-    for (int s = 0; s < world; s++) {
-        const float* pp = parts + ((size_t)s * npairs + w) * PART;
-        const float ms = __ldcg(pp);
-        if (ms != NEG_SENTINEL) lg += __ldcg(pp + 1) * expf(ms - mg);
-    }
-    const float inv = lg > 0.f ? 1.0f / lg : 0.f;
-    for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-        float a = 0.f;
+    if (ok) {
+        const float* parts = reinterpret_cast<const float*>(box) + (size_t)par * xchg_data_floats(world, npairs);
+        float mg = NEG_SENTINEL;
+        for (int s = 0; s < world; s++) mg = fmaxf(mg, __ldcg(parts + ((size_t)s * npairs + w) * PART));
+        float lg = 0.f;
         for (int s = 0; s < world; s++) {
             const float* pp = parts + ((size_t)s * npairs + w) * PART;
             const float ms = __ldcg(pp);
-            if (ms != NEG_SENTINEL) a += __ldcg(pp + 2 + d) * expf(ms - mg);
+            if (ms != NEG_SENTINEL) lg += __ldcg(pp + 1) * expf(ms - mg);
         }
-        out[(size_t)w * HD + d] = a * inv;
+        const float inv = lg > 0.f ? 1.0f / lg : 0.f;
+        for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+            float a = 0.f;
+            for (int s = 0; s < world; s++) {
+                const float* pp = parts + ((size_t)s * npairs + w) * PART;
+                const float ms = __ldcg(pp);
+                if (ms != NEG_SENTINEL) a += __ldcg(pp + 2 + d) * expf(ms - mg);
+            }
+            out[(size_t)w * HD + d] = a * inv;
+        }
     }
-    // the last block to finish records the exchange as completed (every block has read the
-    // step word by then)
+    // Every block, timed out or not, counts itself (a block that gave up adds a mark in the
+    // upper half), so the counter always returns to zero. The last block records the exchange
+    // as completed only if nobody gave up: after a timeout the step word stays where it was,
+    // `out` is untouched in the blocks that gave up, and the same epoch can be tried again.
     __syncthreads();
     if (threadIdx.x == 0) {
         unsigned* ctr = reinterpret_cast<unsigned*>(box + xchg_counter_offset(world, npairs) + XCHG_MERGE_CTR);
         __threadfence();
-        if (atomicAdd(ctr, 1u) == gridDim.x - 1) {
+        const unsigned seen = atomicAdd(ctr, ok ? 1u : 0x10001u) + (ok ? 1u : 0x10001u);
+        if ((seen & 0xffffu) == gridDim.x) {
             *ctr = 0;
-            *reinterpret_cast<volatile uint32_t*>(box + xchg_counter_offset(world, npairs) + XCHG_STEP) = epoch;
+            if ((seen >> 16) == 0)
+                *reinterpret_cast<volatile uint32_t*>(box + xchg_counter_offset(world, npairs) + XCHG_STEP) = epoch;
         }
     }
 }
@@ -81,6 +87,7 @@ size_t xchg_mailbox_bytes(int world, int64_t npairs) {
 
 int launch_merge_pushed(void* box, int world, int64_t npairs, uint32_t epoch, float* out,
                         cudaStream_t st) {
+    if (npairs > 0xffff) return Q27_ERR_TOO_LARGE;   // the block counter keeps 16 bits
     Q27_CUDA_TRY(launch_pdl(k_merge_pushed, dim3((unsigned)npairs), dim3(256), 0, st,
                             static_cast<uint8_t*>(box), world, npairs, epoch, out));
     return Q27_OK;

@@ -5,6 +5,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "t3_tables.cuh"
+
 namespace q27b {
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -19,8 +21,7 @@ struct T3Tab {
 };
 __device__ __forceinline__ T3Tab t3_tables() {
     uint32_t lo[2] = {0, 0}, hi[2] = {0, 0};
-    const float c[8] = {-0.190207f, -0.118786f, -0.066822f, -0.021663f,
-                        0.021663f,  0.066822f,  0.118786f,  0.190207f};
+    const float c[8] = {Q27_T3_CENTROID_LIST};
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const uint32_t bits = __half_as_ushort(__float2half_rn(c[i]));

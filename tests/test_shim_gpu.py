@@ -40,3 +40,26 @@ def test_shim_default_and_fd2_entries_agree(cuda):
     assert outs[0][1] > 1.0                                   # something was computed
     assert abs(outs[0][0] - outs[1][0]) < 5e-3 * outs[1][1]   # fp16-operand vs fp32 family
     assert abs(outs[0][1] - outs[1][1]) < 5e-3 * outs[1][1]
+
+
+@pytest.mark.gpu
+def test_shim_verify_launchers_and_single_token_store(cuda):
+    """fdmma::launch_fdmma_h16 by its reference signature: `false` for a width the reference
+    does not instantiate (the caller falls through), partials for ntok = 4 that a
+    k_attn_fd_combine-style merge turns into the attn_decode3 result; q27k::kv_store writes the
+    token's row (first K element of row 7 = fp16 of q[0])."""
+    if not BIN.exists():
+        build_shim_smoke()
+    r = subprocess.run([str(BIN), "fdmma"], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    m = re.search(r"narrow (\d) wide (\d) maxdiff ([\d.e+-]+) stored ([0-9a-f]{4})", r.stdout)
+    assert m, r.stdout
+    assert m.group(1) == "0" and m.group(2) == "1"
+    assert float(m.group(3)) < 2e-3
+    # q[0] of the smoke program's LCG stream, rounded to fp16 (the same generator as the .cu)
+    import numpy as np
+    s = 12345
+    for _ in range(300 * 4 * 256 + 1):
+        s = (s * 1664525 + 1013904223) & 0xFFFFFFFF
+    q0 = np.float32(((s >> 8) & 0xFFFF) / 65536.0 - 0.5)
+    assert int(m.group(4), 16) == int(np.float16(q0).view(np.uint16))
