@@ -130,13 +130,17 @@ k_exact_partial(const __grid_constant__ DevBatch b) {
 }
 
 // Log-sum-exp merge of the nsplit partials {m, l, acc[256]} at pp (stride PART) by a block of
-// COMBINE_THREADS threads. Every load of a phase is issued before any is used, so the
-// kernel costs a few L2 round trips rather than one per split: (1) thread sp fetches m and
-// l of split sp; (2) warp 0 forms the global max, the weights e^{m_s - M} and l; (3) four
-// groups of 128 threads each sum every fourth split, two dims per thread, and the groups
-// are added in a fixed order (same result every run). Splits with weight 0 (sentinels)
-// hold undefined accumulators: selected, never multiplied. On return threads 0..255 hold
-// the merged accumulator of dim threadIdx.x; mg / lg are valid in every thread.
+// COMBINE_THREADS threads. The kernel sits on the step's critical path behind the partial
+// kernel, so it is built around ONE round trip to L2: thread sp fetches {m, l} of split sp
+// and, in the same breath, every thread fetches the accumulator pieces it will weigh (four
+// groups of 128 threads each own every fourth split, two dims per thread; the first 80 splits
+// -- all of them in the usual one-CTA-per-SM launches -- are in flight together, which keeps the
+// block at 64 registers so that it fits beside a CTA of the partial kernel when it is launched
+// early); warp 0 then forms the global max, the weights
+// e^{m_s - M} and l; the groups' sums are added in a fixed order (same result every run).
+// Splits with weight 0 (sentinels) hold undefined accumulators: selected, never added. On
+// return threads 0..255 hold the merged accumulator of dim threadIdx.x; mg / lg are valid in
+// every thread.
 constexpr int COMBINE_THREADS = 512;
 __device__ __forceinline__ float combine_core(const float* __restrict__ pp, int nsplit, float& mg,
                                               float& lg) {
@@ -144,6 +148,15 @@ __device__ __forceinline__ float combine_core(const float* __restrict__ pp, int 
     __shared__ float s_ml[2];
     __shared__ float s_red[4][HD];
     const int tid = threadIdx.x;
+    const int grp = tid >> 7, c = tid & 127;
+    constexpr int EARLY = 20;            // loads per thread issued before the weights are known
+    float2 v[EARLY];
+#pragma unroll
+    for (int k = 0; k < EARLY; k++) {
+        const int sp = grp + 4 * k;
+        v[k] = sp < nsplit ? *reinterpret_cast<const float2*>(pp + (size_t)sp * PART + 2 + 2 * c)
+                           : make_float2(0.f, 0.f);
+    }
     if (tid < nsplit) {
         const float2 ml = *reinterpret_cast<const float2*>(pp + (size_t)tid * PART);
         s_mv[tid] = ml.x;
@@ -169,14 +182,21 @@ __device__ __forceinline__ float combine_core(const float* __restrict__ pp, int 
     __syncthreads();
     mg = s_ml[0];
     lg = s_ml[1];
-    const int grp = tid >> 7, c = tid & 127;
     float ax = 0.f, ay = 0.f;
-#pragma unroll 8
-    for (int sp = grp; sp < nsplit; sp += 4) {
+#pragma unroll
+    for (int k = 0; k < EARLY; k++) {
+        const int sp = grp + 4 * k;
+        const float w = sp < nsplit ? s_w[sp] : 0.f;
+        const float px = v[k].x * w, py = v[k].y * w;
+        ax += w != 0.f ? px : 0.f;
+        ay += w != 0.f ? py : 0.f;
+    }
+    for (int sp = grp + 4 * EARLY; sp < nsplit; sp += 4) {
         const float w = s_w[sp];
-        const float2 v = *reinterpret_cast<const float2*>(pp + (size_t)sp * PART + 2 + 2 * c);
-        ax += w != 0.f ? v.x * w : 0.f;
-        ay += w != 0.f ? v.y * w : 0.f;
+        const float2 u = *reinterpret_cast<const float2*>(pp + (size_t)sp * PART + 2 + 2 * c);
+        const float px = u.x * w, py = u.y * w;
+        ax += w != 0.f ? px : 0.f;
+        ay += w != 0.f ? py : 0.f;
     }
     s_red[grp][2 * c] = ax;
     s_red[grp][2 * c + 1] = ay;
@@ -189,7 +209,7 @@ __device__ __forceinline__ float combine_core(const float* __restrict__ pp, int 
 // Merge the nsplit partials of one (slot, lane, head). NORMALISE: write out = acc / l to the
 // lane's output row; otherwise write the merged {m, l, acc} for a cross-GPU merge.
 template <bool NORMALISE>
-__global__ void __launch_bounds__(COMBINE_THREADS)
+__global__ void __launch_bounds__(COMBINE_THREADS, 2)
 k_combine(const __grid_constant__ DevBatch b, float* __restrict__ partial_out, int lanes_stride) {
     pdl_wait();                  // the partials come from the kernel before this one
     const int h = blockIdx.x, t = blockIdx.y, slot = blockIdx.z;
@@ -218,7 +238,7 @@ k_combine(const __grid_constant__ DevBatch b, float* __restrict__ partial_out, i
 // k_combine<false> with the exchange fused in: the merged {m, l, acc} row of (slot, lane,
 // head) goes straight into slot `rank` of EVERY rank's mailbox (peer stores over NVLink),
 // and the last block publishes the epoch. Padded lanes get sentinel rows like everyone else.
-__global__ void __launch_bounds__(COMBINE_THREADS)
+__global__ void __launch_bounds__(COMBINE_THREADS, 2)
 k_combine_push(const __grid_constant__ DevBatch b, const __grid_constant__ Peers peers_in,
                int lanes_stride) {
     pdl_trigger();               // the merge kernel may be scheduled; it waits for this grid

@@ -980,7 +980,23 @@ int launch_verify_umma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool
     for (int i = 0; i < b.nslots; i++)
         for (int t = 0; t < b.s[i].ntok; t++)
             if ((uintptr_t)b.s[i].q[t] & 15) return Q27_OK;
-    int ns = force_nsplit > 0 ? force_nsplit : sm_count / (b.nslots * b.n_kv);
+    // One CTA per SM at a time. When the (slot, kv head) pairs do not divide the machine, a
+    // single wave leaves SMs idle (8 slots x 4 heads x 4 splits = 128 CTAs on 148 SMs); finer
+    // splits over several waves fill it: take the smallest split count whose last wave is
+    // nearly full.
+    const int pairs = b.nslots * b.n_kv;
+    int ns = force_nsplit;
+    if (ns <= 0) {
+        ns = sm_count / pairs;
+        if (ns < 1) ns = 1;
+        auto fill = [&](int n) {
+            const int ctas = pairs * n, waves = (ctas + sm_count - 1) / sm_count;
+            return (double)ctas / ((double)waves * sm_count);
+        };
+        double best = fill(ns);
+        for (int n = ns + 1; n <= Q27_MAX_SPLITS && n <= 4 * ns + 4 && best < 0.95; n++)
+            if (fill(n) > best + 0.02) { best = fill(n); ns = n; }
+    }
     b.nsplit = ns < 1 ? 1 : ns > Q27_MAX_SPLITS ? Q27_MAX_SPLITS : ns;
     b.unit = BN;
     dim3 grid(b.nsplit, b.n_kv, b.nslots);

@@ -52,27 +52,30 @@ template <> struct Fmt<Q27_KV_F16> {
     static constexpr int PITCH = 512 + 16;      // one (row, head) slice + pad: conflict-free ldmatrix
     static constexpr int SLICE = 512;
     static constexpr int STAGES = 5;
+    static constexpr int NCW = 8;               // consumer warps
 };
 template <> struct Fmt<Q27_KV_FP8> {
     static constexpr int KVH = 1;
     static constexpr int PITCH = 256 + 16;
     static constexpr int SLICE = 256;
     static constexpr int STAGES = 8;
+    static constexpr int NCW = 8;
 };
 template <> struct Fmt<Q27_KV_T3> {
     static constexpr int KVH = 4;               // whole 400-byte rows: all four kv heads
     static constexpr int PITCH = 400;
     static constexpr int SLICE = 400;
     static constexpr int STAGES = 5;
+    static constexpr int NCW = 8;
 };
-constexpr int NCW = 8;                            // consumer warps
-constexpr int N_THREADS = (NCW + 1) * 32;         // + the producer warp
+template <int KVK> constexpr int n_threads() { return (Fmt<KVK>::NCW + 1) * 32; }   // + the producer warp
 constexpr int HEADER_BYTES = 256;                 // ring barriers
 template <int KVK> constexpr int stage_bytes() { return 2 * STAGE_ROWS * Fmt<KVK>::PITCH; }
 template <int KVK> constexpr int ring_bytes() { return stage_bytes<KVK>() * Fmt<KVK>::STAGES; }
-constexpr int MERGE_BYTES = NCW * GQA * PART * 4; // per-warp partials for the final merge
+// per-warp partials for the final merge
+template <int KVK> constexpr int merge_bytes() { return Fmt<KVK>::NCW * GQA * PART * 4; }
 template <int KVK> constexpr int work_bytes() {
-    return ring_bytes<KVK>() > MERGE_BYTES ? ring_bytes<KVK>() : MERGE_BYTES;
+    return ring_bytes<KVK>() > merge_bytes<KVK>() ? ring_bytes<KVK>() : merge_bytes<KVK>();
 }
 template <int KVK> constexpr int qstage_bytes() { return Fmt<KVK>::KVH * GQA * HD * 4; }
 template <int KVK> constexpr int smem_bytes() {
@@ -589,9 +592,10 @@ __device__ void finish_group(const float* __restrict__ base, int nsplit, int use
 
 // ---- the kernel -------------------------------------------------------------------------
 template <int KVK>
-__global__ void __launch_bounds__(N_THREADS, 1)
+__global__ void __launch_bounds__(n_threads<KVK>(), 1)
 k_decode_mma(const __grid_constant__ DevBatch b) {
     using F = Fmt<KVK>;
+    constexpr int NCW = F::NCW;
     constexpr int WAYS = NCW / F::KVH;             // consumer warps per kv head
     constexpr int NHEADS = F::KVH * GQA;           // query heads this CTA serves
     extern __shared__ __align__(128) uint8_t smem[];
@@ -910,7 +914,7 @@ int launch_one(DevBatch& b, int sm_count, bool may_fuse, cudaStream_t st) {
     b.nsplit = ns;
     b.unit = STAGE_ROWS;
     dim3 grid(b.max_ntok, b.nsplit, b.nslots * groups);
-    k_decode_mma<KVK><<<grid, N_THREADS, smem_bytes<KVK>(), st>>>(b);
+    k_decode_mma<KVK><<<grid, n_threads<KVK>(), smem_bytes<KVK>(), st>>>(b);
     Q27_CUDA_TRY(cudaGetLastError());
     Q27_COUNT_LAUNCH();
     return Q27_OK;

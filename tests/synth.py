@@ -88,7 +88,7 @@ def scale_out(case: Case, out: np.ndarray) -> np.ndarray:
 
 
 def tolerance_ok(got: np.ndarray, ref: np.ndarray, atol=2e-3, rtol=1e-3):
-    """BASELINE parity bar: |a-b| <= 2e-3 + 1e-3*|b| element-wise; returns (ok, max excess,
+    """The parity bar of the headline metric: |a-b| <= 2e-3 + 1e-3*|b| element-wise; returns (ok, max excess,
     max-abs/RMS as the reference's own tests report it, src/test_kernels.cu:885-893)."""
     got = np.asarray(got, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)

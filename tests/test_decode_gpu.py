@@ -19,7 +19,7 @@ KINDS = [KV_F16, KV_FP8, KV_T3]
 # tight bar for the fp32 "exact" family: max-abs/RMS, the reference's own gate for fd2
 # (1e-4 fp16/fp8, 2e-4 turbo3: src/test_kernels.cu:981,1521)
 EXACT_TOL = {KV_F16: 1e-4, KV_FP8: 1e-4, KV_T3: 2e-4}
-# BASELINE draws plain N(0,1) for the fp16 / fp8 caches and adds x8 outlier channels (2 %)
+# the named workloads draw plain N(0,1) for the fp16 / fp8 caches and add x8 outlier channels (2 %)
 # only to the turbo3 configs, whose WHT rotation is there to spread them
 OUTLIERS = {KV_F16: 0.0, KV_FP8: 0.0, KV_T3: 0.02}
 
@@ -51,7 +51,7 @@ def test_decode_vs_oracle(oracle, cuda, kvk, ntok, seq):
     rms = np.sqrt((ref.astype(np.float64) ** 2).mean()) + 1e-12
     assert np.abs(exact - ref).max() / rms < EXACT_TOL[kvk]
     got = synth.scale_out(c, dc.run3())
-    ok, excess, rel = synth.tolerance_ok(got, ref)   # 2e-3 abs + 1e-3 rel (BASELINE)
+    ok, excess, rel = synth.tolerance_ok(got, ref)   # the parity bar: 2e-3 abs + 1e-3 rel
     assert ok, (excess, rel)
     assert rel < 1e-2                                 # the reference's fp16-MMA class bar
     again = synth.scale_out(c, dc.run3())
@@ -74,7 +74,7 @@ def test_scattered_pages_and_untouched_gate(oracle, cuda, kvk):
 
 
 def test_attn_decode_single_token_entry(oracle, cuda):
-    c = synth.make_case(oracle, KV_F16, rows=4096, pos=[4095], seed=1)
+    c = synth.make_case(oracle, KV_F16, rows=4096, pos=[4095], seed=1)   # the 4096-row fp16 single-token workload
     ref = oracle.attn_decode(c.q, c.k, c.v, KV_F16, c.pos)
     dc = DeviceCase(c, cuda)
     Q.attn_decode(dc.q[0], synth.Q_STRIDE, dc.kside.tab, dc.vside.tab, dc.out[0], dc.scratch,
@@ -142,7 +142,7 @@ def test_kv_split_partials_merge(oracle, cuda, kvk, nshards):
         b = want[live][:, 2:] / want[live][:, 1:2] * vs
         # a shard's own partial (as little as one key) is held to the reference's gate for
         # fp16-operand tensor-core paths (max-abs/RMS 1e-2, src/test_kernels.cu:1824-1962);
-        # the BASELINE bar applies to the merged output below
+        # the parity bar applies to the merged output below
         assert np.abs(a - b).max() / (np.sqrt((b.astype(np.float64) ** 2).mean()) + 1e-12) < 1e-2
         # padded lane (index 5) is a well-formed empty partial
         assert (parts[g, 0, 5, :, 0].cpu().numpy() < -1e38).all()
@@ -203,7 +203,7 @@ def test_kv_split_through_mailboxes(oracle, cuda, kvk):
 def test_against_reference_kernels_on_this_gpu(oracle, cuda, kvk):
     """The reference's own k_attn_fd2 + combine, recompiled for sm_100a from the reference
     tree, on the identical buffers: pins the oracle to the reference itself (<= 1e-4 / 2e-4
-    max-abs/RMS, its own gate) and the engine to the reference within the BASELINE bar."""
+    max-abs/RMS, its own gate) and the engine to the reference within the parity bar."""
     ref_gpu = RefGpu()
     for seq, ntok in ((47, 1), (1024, 5), (16384, 5)):
         c = synth.make_case(oracle, kvk, rows=seq, pos=lanes_for(seq, ntok), seed=300 + seq % 89)

@@ -28,7 +28,7 @@ def test_shard_ranges_are_page_aligned_and_cover():
             assert hi == lo2 and lo <= hi
         for lo, hi in r[:-1]:
             assert lo % 64 == 0 and (hi % 64 == 0 or hi == total)
-    # 262144 rows over 8 GPUs -> 32768 rows (512 pages) each
+    # the sharded verify workload: 262144 rows over 8 GPUs -> 32768 rows (512 pages) each
     assert qd.shard_ranges(262144, 8)[3] == (3 * 32768, 4 * 32768)
 
 
@@ -91,7 +91,7 @@ def test_two_rank_exchange_reproduces_full_attention(oracle):
 def test_partial_exchange_geometry():
     ex = qd.PartialExchange.create(8, 6, 24, 8, "cpu")
     assert ex.npairs == 8 * 6 * 24
-    assert ex.bytes_per_rank() == 8 * 6 * 24 * 258 * 4      # 1.19 MB at BASELINE config 5
+    assert ex.bytes_per_rank() == 8 * 6 * 24 * 258 * 4      # 1.19 MB for 8 slots x 6 lanes
     assert tuple(ex.gathered.shape) == (8, 8, 6, 24, 258)
 
 

@@ -112,7 +112,7 @@ def test_turbo3_pipeline_end_to_end(oracle, cuda):
     want = oracle.wht(rot.reshape(-1, 128), inverse=True).reshape(rot.shape)
     # after the inverse rotation every output mixes 128 rotated ones: judged with the
     # reference's own gate for its tensor-core paths (max-abs/RMS, src/test_kernels.cu:1521)
-    assert synth.tolerance_ok(rot_got, rot)[0]    # BASELINE bar on the attention output
+    assert synth.tolerance_ok(rot_got, rot)[0]    # the parity bar on the attention output
     rms = np.sqrt((want.astype(np.float64) ** 2).mean())
     assert np.abs(got - want).max() / rms < 3e-2  # x8 outlier channels, 900 keys, 3 lanes
     c16 = synth.make_case(oracle, KV_F16, rows=rows, pos=pos, seed=29, outlier_frac=0.02)

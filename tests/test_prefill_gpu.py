@@ -56,7 +56,7 @@ def test_prefill_turbo3_base100(oracle, cuda):
 
 
 def test_prefill_deep_prefix_bf16_values(oracle, cuda):
-    # BASELINE config 4 in miniature: bf16-rounded Q/K/V in an fp16 cache, a reused prefix
+    # the prefill workload in miniature: bf16-rounded Q/K/V in an fp16 cache, a reused prefix
     # fully visible, the chunk causal
     got, ref = run_prefill(oracle, cuda, KV_F16, base=2048 + 64, T=256, seed=8, bf16=True)
     ok, excess, rel = synth.tolerance_ok(got, ref)
