@@ -30,7 +30,7 @@ extern "C" {
 enum {
     Q27_OK = 0,
     Q27_ERR_INVALID_ARG = 1,      /* null pointer, bad stride, misaligned page, ... */
-    Q27_ERR_UNSUPPORTED_KIND = 2, /* a KvKind this engine does not read (refused, never
+    Q27_ERR_UNSUPPORTED_KIND = 2, /* a KvKind outside the enum below (refused, never
                                      mis-read: src/spec3.cu:1109-1122) */
     Q27_ERR_UNSUPPORTED_WIDTH = 3,/* ntok / geometry outside the instantiated range
                                      (the reference's `bool false`, src/fdmma.cuh:497) */
@@ -38,8 +38,15 @@ enum {
     Q27_ERR_TOO_LARGE = 5         /* exceeds a fixed capacity (no-allocation entry) */
 };
 
-/* KvKind, src/cuda_common.h:53. Kinds 3..5 (turbo3v, turbo5k, int8-g64) are refused. */
-enum { Q27_KV_F16 = 0, Q27_KV_FP8 = 1, Q27_KV_T3 = 2 };
+/* KvKind, src/cuda_common.h:53. From turbo3 up the V side is always turbo3 blocks and only
+ * the K side varies: turbo3v keeps K as fp16 rows, turbo5k as 82-byte 5-bit blocks
+ * (src/turbo5.cuh), int8-g64 as 132-byte int8 blocks with one fp16 scale per 64 dims
+ * (src/i8g64.cuh). Q must arrive rotated for turbo3 and turbo5k only (kv_k_rotated,
+ * src/cuda_common.h:59). Kinds 3..5 are served by the fp32 family of kernels (as the reference
+ * serves them with its scalar kernel, src/spec3.cu:1080-1088); the tensor-core kernels cover
+ * kinds 0..2. */
+enum { Q27_KV_F16 = 0, Q27_KV_FP8 = 1, Q27_KV_T3 = 2, Q27_KV_T3V = 3, Q27_KV_T5K = 4,
+       Q27_KV_I8G64 = 5 };
 
 #define Q27_KV_PAGE 64        /* rows per page, src/cuda_common.h:70 */
 #define Q27_HEAD_DIM 256
@@ -49,6 +56,8 @@ enum { Q27_KV_F16 = 0, Q27_KV_FP8 = 1, Q27_KV_T3 = 2 };
 #define Q27_PART_STRIDE 258   /* {m, l, acc[256]}: FD_ST src/spec3.cuh:127, PF_PART_STRIDE */
 #define Q27_PF_SPLIT_MAX 8    /* src/prefill.cuh:88 */
 #define Q27_T3_BLOCK_BYTES 50 /* sizeof(block_turbo3), src/turbo3.cuh:26-32 */
+#define Q27_T5_BLOCK_BYTES 82 /* sizeof(block_turbo5), src/turbo5.cuh:41-47 */
+#define Q27_I8_BLOCK_BYTES 132 /* sizeof(block_i8g64), src/i8g64.cuh:36-41 */
 #define Q27_MAX_SLOTS 8       /* slots per batched launch */
 #define Q27_MAX_RANKS 8       /* GPUs of one node that share a KV-sequence split */
 #define Q27_XCHG_HANDLE_BYTES 64
@@ -79,8 +88,12 @@ int q27_wait_timeout_flag(int* out);
  * combine. Pass NULLs to switch it off. Not for use under stream capture. */
 int q27_set_kernel_events(void* ev_start, void* ev_stop);
 
-/* bytes per cache row: fp16 n_kv*512, fp8 n_kv*256, turbo3 n_kv*100; -1 = refused kind */
+/* bytes per cache row: fp16 n_kv*512, fp8 n_kv*256, turbo3 n_kv*100; -1 = refused kind.
+ * For a kind whose sides differ this is the K side (turbo3v n_kv*512, turbo5k n_kv*164,
+ * int8-g64 n_kv*264); q27_kv_row_bytes_side gives either side (is_v != 0: the V side, turbo3
+ * for every kind from Q27_KV_T3 up). Engine::kv_bytes(is_v), src/engine.cuh:868-876. */
 int64_t q27_kv_row_bytes(int kvk, int n_kv_heads);
+int64_t q27_kv_row_bytes_side(int kvk, int n_kv_heads, int is_v);
 /* floats the caller must provide as `scratch` for ntok lanes:
  * ntok * n_q_heads * Q27_MAX_SPLITS * Q27_PART_STRIDE (src/spec3.cuh:109-111) */
 int64_t q27_decode_scratch_floats(int ntok, int n_q_heads);
@@ -247,9 +260,15 @@ int q27_attn_prefill_T_exact(const float* qT, int q_stride, int q_row,
 
 /* Bit-exact dequantisation of cache rows [row0, row0+nrows) through a page table to fp32
  * [nrows][n_kv_heads][256]: half2float / float(e4m3) / CENTROIDS[idx]*half2float(norm)
- * (kv2f src/cuda_common.h:113-114, turbo3_deq_elem src/turbo3.cuh:134-137). */
+ * (kv2f src/cuda_common.h:113-114, turbo3_deq_elem src/turbo3.cuh:134-137). For a kind whose
+ * sides differ this form reads the table as K rows. */
 int q27_kv_dequant(const void* const* tab, int kvk, int row0, int nrows, int n_kv_heads,
                    float* out, void* stream);
+/* The same for one side of a kind (is_v: 0 = the table holds K rows, 1 = V rows): turbo5
+ * CENTROIDS5[idx]*norm (turbo5_deq_elem, src/turbo5.cuh:163-166), int8-g64 code*scale
+ * (i8g64_deq_elem, src/i8g64.cuh:68-72). */
+int q27_kv_dequant_side(const void* const* tab, int kvk, int is_v, int row0, int nrows,
+                        int n_kv_heads, float* out, void* stream);
 
 /* Replaces q27k::kv_store_T (src/blocks.cuh:56-57, src/prefill.cu:1221-1243): store T
  * tokens' K and V rows (fp32 [T][rowlen], rowlen = n_kv_heads*256) into cache rows
@@ -257,10 +276,16 @@ int q27_kv_dequant(const void* const* tab, int kvk, int row0, int nrows, int n_k
 int q27_kv_store_T(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
                    int base_pos, int rowlen, int T, void* stream, int fp8);
 
-/* Replaces q27k::kv_store_T_t3 (src/blocks.cuh:63-65, src/prefill.cu:2556-2596) for
- * Q27_KV_T3: per 128-element group L2 norm -> forward WHT -> nearest of 8 centroids -> pack
- * -> corrected fp16 norm, written block-addressed. Byte-identical to the reference's
- * serial CPU codec (t3_quant, src/test_kernels.cu:1089-1103). K must already be rope'd. */
+/* Replaces q27k::kv_store_T_t3 (src/blocks.cuh:63-65, src/prefill.cu:2556-2596) for kinds
+ * Q27_KV_T3 .. Q27_KV_I8G64. turbo3 (V of every kind, K of Q27_KV_T3): per 128-element group
+ * L2 norm -> forward WHT -> nearest of 8 centroids -> pack -> corrected fp16 norm, written
+ * block-addressed; byte-identical to the reference's serial CPU codec (t3_quant,
+ * src/test_kernels.cu:1089-1103). K legs of the other kinds: turbo3v plain fp16 rows;
+ * turbo5k the same pipeline over 32 centroids with the two norms summed in the halving-tree
+ * order of the reference's device encoder (turbo5_quant_group, src/turbo5.cuh:129-162), so
+ * the blocks equal that encoder's and its CPU oracle's tree mode byte for byte; int8-g64
+ * per-64 absmax, fp16 scale, codes from the reciprocal of the ROUNDED scale
+ * (i8g64_quant_group, src/i8g64.cuh:48-64), exact. K must already be rope'd. */
 int q27_kv_store_T_t3(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
                       int base_pos, int n_kv_heads, int head_dim, int T, void* stream, int kvk);
 
@@ -278,9 +303,8 @@ int q27_wht_T(float* x, int n_heads, int head_dim, int head_stride, int row_stri
  * Replaces q27k::kv_store3 (src/spec3.cuh:87-88, src/spec3.cu:512-535). */
 int q27_kv_store3(const q27_CP3* k, const q27_CP3* v, void* const* ktab, void* const* vtab,
                   const q27_IP3* pos, int rowlen, void* stream, int ntok, int fp8);
-/* Replaces q27k::kv_store_t3 (src/spec3.cuh:98-99, src/spec3.cu:556-588) for Q27_KV_T3; the
- * other K legs (turbo3v, turbo5k, int8-g64) are refused. Blocks byte-identical to the
- * reference's serial CPU codec, as for q27_kv_store_T_t3. */
+/* Replaces q27k::kv_store_t3 (src/spec3.cuh:98-99, src/spec3.cu:556-588) for kinds
+ * Q27_KV_T3 .. Q27_KV_I8G64; encoders and byte-level guarantees as for q27_kv_store_T_t3. */
 int q27_kv_store_t3(const q27_CP3* k, const q27_CP3* v, void* const* ktab, void* const* vtab,
                     const q27_IP3* pos, int n_kv_heads, int head_dim, void* stream, int ntok,
                     int kvk);

@@ -20,8 +20,12 @@
 // Error behaviour is the reference's: the q27k:: functions return void and a failure is fatal
 // (message + exit(1), CUDA_CHECK in src/cuda_common.h:8-16); the two fdmma:: launchers return
 // `false` for a width they do not cover, and the caller must then fall through to another path
-// (src/fdmma.cuh:497), any other failure being fatal as well. Kinds the engine does not read
-// (turbo3v, turbo5k, int8-g64) are therefore fatal here rather than silently mis-read.
+// (src/fdmma.cuh:497), any other failure being fatal as well. All six KvKinds are read; a value
+// outside the enum is fatal here rather than silently mis-read. The kinds whose K side differs
+// (turbo3v, turbo5k, int8-g64) are served by the fp32 kernels behind the q27k:: entries, and
+// the fdmma:: launchers return `false` for them, which sends the caller to attn_decode3_fd2
+// as the reference does for the kinds its tensor-core verify does not cover
+// (src/spec3.cu:1118-1135).
 #pragma once
 #include <cuda_runtime.h>
 
@@ -196,7 +200,7 @@ inline bool launch_fdmma(FCP3 qp, int q_stride, const void* const* ktab, const v
                              ns, ntok, st, t3 ? KV_T3 : KV_FP8, "launch_fdmma");
 }
 
-// fmt 0 = fp16, 1 = fp8, 2 = turbo3 rows (3 = turbo5k: not read by this engine -> false)
+// fmt 0 = fp16, 1 = fp8, 2 = turbo3 rows (3 = turbo5k: no tensor-core verify here -> false)
 inline bool launch_fdmma_h16(FCP3 qp, int q_stride, const void* const* ktab,
                              const void* const* vtab, float* part, FIP3 pos, int n_kv_heads,
                              int gqa, int head_dim, float scale, int ns, int ntok, int fmt,

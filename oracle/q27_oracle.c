@@ -124,11 +124,33 @@ static const float T3_INV_SQRT_128 = 0.08838834764831845f;
 static float T3_S1[128], T3_S2[128];
 static int t3_tables_ready = 0;
 
+/* turbo5: the 32-level table and its 31 decision thresholds are odd-symmetric
+ * (c[31-i] = -c[i], T[30-i] = -T[i], T[15] = 0); the positive halves are stated here and
+ * mirrored at start-up (src/turbo5.cuh:63-80 lists all 63 numbers). */
+static const float T5_CENTROIDS_POS[16] = {
+    0.00582388f, 0.01750547f, 0.02928998f, 0.04125080f, 0.05346908f, 0.06603809f,
+    0.07906913f, 0.09270022f, 0.10710939f, 0.12253633f, 0.13932019f, 0.15797059f,
+    0.17931595f, 0.20486116f, 0.23786362f, 0.28821075f};
+static const float T5_THRESH_POS[15] = {
+    0.01166468f, 0.02339773f, 0.03527039f, 0.04735994f, 0.05975358f,
+    0.07255360f, 0.08588468f, 0.09990481f, 0.11482286f, 0.13092826f,
+    0.14864540f, 0.16864327f, 0.19208856f, 0.22136238f, 0.26303717f};
+static float T5_CENTROIDS[32], T5_THRESH[31];
+
 static void t3_init(void) {
     if (t3_tables_ready) return;
     for (int j = 0; j < 128; j++) {
         T3_S1[j] = (T3_S1_NEG[j >> 5] >> (j & 31)) & 1u ? -1.f : 1.f;
         T3_S2[j] = (T3_S2_NEG[j >> 5] >> (j & 31)) & 1u ? -1.f : 1.f;
+    }
+    for (int i = 0; i < 16; i++) {
+        T5_CENTROIDS[16 + i] = T5_CENTROIDS_POS[i];
+        T5_CENTROIDS[15 - i] = -T5_CENTROIDS_POS[i];
+    }
+    T5_THRESH[15] = 0.f;
+    for (int i = 0; i < 15; i++) {
+        T5_THRESH[16 + i] = T5_THRESH_POS[i];
+        T5_THRESH[14 - i] = -T5_THRESH_POS[i];
     }
     t3_tables_ready = 1;
 }
@@ -208,6 +230,96 @@ void q27o_t3_dequant(const uint8_t* blk, float* y) {
     }
 }
 
+/* ------------------------------------------------------------------- turbo5 -------- */
+
+const float* q27o_t5_centroids(void) { t3_init(); return T5_CENTROIDS; }
+const float* q27o_t5_thresholds(void) { t3_init(); return T5_THRESH; }
+
+int q27o_t5_nearest(float v) {
+    int idx = 0;
+    for (int i = 0; i < 31; i++) idx += v >= T5_THRESH[i];
+    return idx;
+}
+
+/* sum of 128 floats: serially, or as the halving tree r[j] += r[j+s], s = 64, 32 .. 1 */
+static float sum128(const float* v, int tree) {
+    if (!tree) {
+        float s = 0.f;
+        for (int j = 0; j < 128; j++) s += v[j];
+        return s;
+    }
+    float r[128];
+    memcpy(r, v, sizeof r);
+    for (int s = 64; s > 0; s >>= 1)
+        for (int j = 0; j < s; j++) r[j] += r[j + s];
+    return r[0];
+}
+
+void q27o_t5_quant(const float* x, uint8_t* blk, int tree) {
+    t3_init();
+    float buf[128], sq[128];
+    for (int j = 0; j < 128; j++) { buf[j] = x[j]; sq[j] = x[j] * x[j]; }
+    float gn = sqrtf(sum128(sq, tree)), inv = gn > 1e-10f ? 1.f / gn : 0.f;
+    for (int j = 0; j < 128; j++) buf[j] *= inv;
+    q27o_t3_fwht(buf);
+    uint8_t* qs = blk + 2;
+    uint8_t* hi = blk + 66;
+    memset(qs, 0, 64);
+    memset(hi, 0, 16);
+    for (int j = 0; j < 128; j++) {
+        int idx = q27o_t5_nearest(buf[j]);
+        qs[j / 2] |= (uint8_t)((idx & 15) << ((j % 2) * 4));
+        if (idx & 16) hi[j / 8] |= (uint8_t)(1 << (j % 8));
+        sq[j] = T5_CENTROIDS[idx] * T5_CENTROIDS[idx];
+    }
+    float rn = sqrtf(sum128(sq, tree)), corr = rn > 1e-10f ? gn / rn : gn;
+    uint16_t h = q27o_float_to_half(corr);
+    memcpy(blk, &h, 2);
+}
+
+void q27o_t5_dequant(const uint8_t* blk, float* y) {
+    t3_init();
+    uint16_t h;
+    memcpy(&h, blk, 2);
+    float norm = q27o_half_to_float(h);
+    const uint8_t* qs = blk + 2;
+    const uint8_t* hi = blk + 66;
+    for (int j = 0; j < 128; j++) {
+        uint8_t l = (qs[j / 2] >> ((j % 2) * 4)) & 15;
+        uint8_t hb = (hi[j / 8] >> (j % 8)) & 1;
+        y[j] = T5_CENTROIDS[l | (hb << 4)] * norm;
+    }
+}
+
+/* ------------------------------------------------------------------ int8-g64 ------- */
+
+void q27o_i8_quant(const float* x, uint8_t* blk) {
+    int8_t* qs = (int8_t*)blk;
+    for (int g = 0; g < 2; g++) {
+        float amax = 0.f;
+        for (int j = 0; j < 64; j++) amax = fmaxf(amax, fabsf(x[g * 64 + j]));
+        uint16_t sh = q27o_float_to_half(amax / 127.0f);
+        float sw = q27o_half_to_float(sh);                /* the ROUNDED scale */
+        float inv = sw > 0.f ? 1.0f / sw : 0.f;
+        memcpy(blk + 128 + 2 * g, &sh, 2);
+        for (int j = 0; j < 64; j++) {
+            int q = (int)rintf(x[g * 64 + j] * inv);      /* nearest even, as __float2int_rn */
+            q = q < -127 ? -127 : q > 127 ? 127 : q;
+            qs[g * 64 + j] = (int8_t)(sw > 0.f ? q : 0);
+        }
+    }
+}
+
+void q27o_i8_dequant(const uint8_t* blk, float* y) {
+    const int8_t* qs = (const int8_t*)blk;
+    for (int g = 0; g < 2; g++) {
+        uint16_t sh;
+        memcpy(&sh, blk + 128 + 2 * g, 2);
+        float sc = q27o_half_to_float(sh);
+        for (int j = 0; j < 64; j++) y[g * 64 + j] = (float)qs[g * 64 + j] * sc;
+    }
+}
+
 static int nthr(int n) {
 #ifdef _OPENMP
     if (n <= 0) n = omp_get_max_threads();
@@ -226,6 +338,23 @@ void q27o_t3_quant_groups(const float* x, int64_t ngroups, uint8_t* blocks, int 
     for (int64_t g = 0; g < ngroups; g++) q27o_t3_quant(x + g * 128, blocks + g * 50);
 }
 
+void q27o_t5_quant_groups(const float* x, int64_t ngroups, uint8_t* blocks, int tree,
+                          int nthreads) {
+    t3_init();
+    int nt = nthr(nthreads);
+    (void)nt;
+#pragma omp parallel for num_threads(nt) schedule(static)
+    for (int64_t g = 0; g < ngroups; g++)
+        q27o_t5_quant(x + g * 128, blocks + g * Q27O_T5_BLOCK, tree);
+}
+
+void q27o_i8_quant_groups(const float* x, int64_t ngroups, uint8_t* blocks, int nthreads) {
+    int nt = nthr(nthreads);
+    (void)nt;
+#pragma omp parallel for num_threads(nt) schedule(static)
+    for (int64_t g = 0; g < ngroups; g++) q27o_i8_quant(x + g * 128, blocks + g * Q27O_I8_BLOCK);
+}
+
 void q27o_wht_groups(float* x, int64_t ngroups, int inverse, int nthreads) {
     t3_init();
     int nt = nthr(nthreads);
@@ -237,42 +366,78 @@ void q27o_wht_groups(float* x, int64_t ngroups, int inverse, int nthreads) {
     }
 }
 
-int64_t q27o_row_bytes(int kvk, int n_kv) {
+/* storage format of one side of a kind: the K side varies, the V side of every kind from
+ * turbo3 up is turbo3 (src/cuda_common.h:47-53) */
+enum { RF_F16, RF_FP8, RF_T3, RF_T5, RF_I8, RF_BAD };
+static int side_fmt(int kvk, int is_v) {
     switch (kvk) {
-    case Q27O_KV_F16: return (int64_t)n_kv * Q27O_HD * 2;
-    case Q27O_KV_FP8: return (int64_t)n_kv * Q27O_HD;
-    case Q27O_KV_T3: return (int64_t)n_kv * 2 * Q27O_T3_BLOCK;
+    case Q27O_KV_F16: return RF_F16;
+    case Q27O_KV_FP8: return RF_FP8;
+    case Q27O_KV_T3: return RF_T3;
+    case Q27O_KV_T3V: return is_v ? RF_T3 : RF_F16;
+    case Q27O_KV_T5K: return is_v ? RF_T3 : RF_T5;
+    case Q27O_KV_I8G64: return is_v ? RF_T3 : RF_I8;
+    default: return RF_BAD;
+    }
+}
+
+static int64_t fmt_row_bytes(int fmt, int n_kv) {
+    switch (fmt) {
+    case RF_F16: return (int64_t)n_kv * Q27O_HD * 2;
+    case RF_FP8: return (int64_t)n_kv * Q27O_HD;
+    case RF_T3: return (int64_t)n_kv * 2 * Q27O_T3_BLOCK;
+    case RF_T5: return (int64_t)n_kv * 2 * Q27O_T5_BLOCK;
+    case RF_I8: return (int64_t)n_kv * 2 * Q27O_I8_BLOCK;
     default: return -1;
     }
 }
 
+int64_t q27o_row_bytes_side(int kvk, int n_kv, int is_v) {
+    return fmt_row_bytes(side_fmt(kvk, is_v), n_kv);
+}
+int64_t q27o_row_bytes(int kvk, int n_kv) { return q27o_row_bytes_side(kvk, n_kv, 0); }
+
 /* one (row, head) slice of 256 dims -> fp32 */
-static void deq_head(const uint8_t* cache, int kvk, int64_t row, int n_kv, int kvh, float* y) {
-    if (kvk == Q27O_KV_F16) {
+static void deq_head(const uint8_t* cache, int fmt, int64_t row, int n_kv, int kvh, float* y) {
+    if (fmt == RF_F16) {
         const uint16_t* p = (const uint16_t*)cache + ((size_t)row * n_kv + kvh) * Q27O_HD;
         for (int i = 0; i < Q27O_HD; i++) y[i] = q27o_half_to_float(p[i]);
-    } else if (kvk == Q27O_KV_FP8) {
+    } else if (fmt == RF_FP8) {
         const uint8_t* p = cache + ((size_t)row * n_kv + kvh) * Q27O_HD;
         for (int i = 0; i < Q27O_HD; i++) y[i] = q27o_e4m3_to_float(p[i]);
-    } else {
+    } else if (fmt == RF_T3) {
         const uint8_t* p = cache + ((size_t)row * n_kv + kvh) * 2 * Q27O_T3_BLOCK;
         q27o_t3_dequant(p, y);
         q27o_t3_dequant(p + Q27O_T3_BLOCK, y + 128);
+    } else if (fmt == RF_T5) {
+        const uint8_t* p = cache + ((size_t)row * n_kv + kvh) * 2 * Q27O_T5_BLOCK;
+        q27o_t5_dequant(p, y);
+        q27o_t5_dequant(p + Q27O_T5_BLOCK, y + 128);
+    } else {
+        const uint8_t* p = cache + ((size_t)row * n_kv + kvh) * 2 * Q27O_I8_BLOCK;
+        q27o_i8_dequant(p, y);
+        q27o_i8_dequant(p + Q27O_I8_BLOCK, y + 128);
     }
 }
 
-int q27o_kv_dequant(const void* cache, int kvk, int64_t rows, int n_kv, float* out,
-                    int nthreads) {
-    if (q27o_row_bytes(kvk, n_kv) < 0) return 1;
+int q27o_kv_dequant_side(const void* cache, int kvk, int is_v, int64_t rows, int n_kv,
+                         float* out, int nthreads) {
+    const int fmt = side_fmt(kvk, is_v);
+    if (fmt == RF_BAD) return 1;
     t3_init();
     int nt = nthr(nthreads);
     (void)nt;
 #pragma omp parallel for num_threads(nt) schedule(static)
     for (int64_t r = 0; r < rows; r++)
         for (int h = 0; h < n_kv; h++)
-            deq_head((const uint8_t*)cache, kvk, r, n_kv, h,
+            deq_head((const uint8_t*)cache, fmt, r, n_kv, h,
                      out + ((size_t)r * n_kv + h) * Q27O_HD);
     return 0;
+}
+
+int q27o_kv_dequant(const void* cache, int kvk, int64_t rows, int n_kv, float* out,
+                    int nthreads) {
+    return q27o_kv_dequant_side(cache, kvk, 0, rows, n_kv, out, nthreads);
 }
 
 /* ------------------------------------------------------------------ attention ------ */
@@ -289,7 +454,7 @@ static void attn_window(const float* qv, const uint8_t* kc, const uint8_t* vc, i
     float row[Q27O_HD];
     double mx = -1e300;
     for (int64_t p = lo; p < hi; p++) {
-        deq_head(kc, kvk, p, n_kv, kvh, row);
+        deq_head(kc, side_fmt(kvk, 0), p, n_kv, kvh, row);
         double d = 0;
         for (int i = 0; i < Q27O_HD; i++) d += (double)qv[i] * (double)row[i];
         d *= scale;
@@ -299,7 +464,7 @@ static void attn_window(const float* qv, const uint8_t* kc, const uint8_t* vc, i
     double lsum = 0;
     for (int64_t p = 0; p < n; p++) { sc[p] = exp(sc[p] - mx); lsum += sc[p]; }
     for (int64_t p = lo; p < hi; p++) {
-        deq_head(vc, kvk, p, n_kv, kvh, row);
+        deq_head(vc, side_fmt(kvk, 1), p, n_kv, kvh, row);
         double w = sc[p - lo];
         for (int i = 0; i < Q27O_HD; i++) acc[i] += w * (double)row[i];
     }

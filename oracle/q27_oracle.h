@@ -22,11 +22,16 @@
 extern "C" {
 #endif
 
-/* KvKind, src/cuda_common.h:53 */
-enum { Q27O_KV_F16 = 0, Q27O_KV_FP8 = 1, Q27O_KV_T3 = 2 };
+/* KvKind, src/cuda_common.h:53. From turbo3 up the V side is always turbo3 blocks; only the
+ * K side varies: turbo3v = fp16 rows, turbo5k = 82-byte 5-bit blocks, int8-g64 = 132-byte
+ * int8 blocks with one fp16 scale per 64 dims. */
+enum { Q27O_KV_F16 = 0, Q27O_KV_FP8 = 1, Q27O_KV_T3 = 2, Q27O_KV_T3V = 3, Q27O_KV_T5K = 4,
+       Q27O_KV_I8G64 = 5 };
 #define Q27O_HD 256      /* head_dim, src/engine.cuh:45 */
 #define Q27O_FD_ST 258   /* partial stride {m, l, acc[256]}, src/spec3.cuh:127 */
 #define Q27O_T3_BLOCK 50 /* sizeof(block_turbo3), src/turbo3.cuh:26-32 */
+#define Q27O_T5_BLOCK 82 /* sizeof(block_turbo5), src/turbo5.cuh:41-47 */
+#define Q27O_I8_BLOCK 132 /* sizeof(block_i8g64), src/i8g64.cuh:36-41 */
 
 /* ---- element conversions (src/cuda_common.h:110-121 use the CUDA intrinsics) ------- */
 /* __half2float */
@@ -54,17 +59,44 @@ void q27o_t3_fwht_inv(float* x128);            /* t3_fwht_inv, test_kernels.cu:1
 void q27o_t3_quant(const float* x128, uint8_t* blk50);   /* t3_quant,   :1089 */
 void q27o_t3_dequant(const uint8_t* blk50, float* y128); /* t3_dequant, :1105 */
 
+/* ---- turbo5 codec, the 5-bit K side (src/turbo5.cuh, tools/turbo5_test.cu:36-89) ---- */
+const float* q27o_t5_centroids(void);          /* 32 values, src/turbo5.cuh:63-71 */
+const float* q27o_t5_thresholds(void);         /* 31 values, src/turbo5.cuh:72-80 */
+int q27o_t5_nearest(float v);                  /* #{i : v >= T[i]}, src/turbo5.cuh:95-107 */
+/* cpu_quant5 (tools/turbo5_test.cu:67-84): turbo3's normalise -> rotate -> nearest -> norm
+ * correction with the 32-level table; low 4 bits two per byte at +2, fifth bit eight per
+ * byte at +66. tree != 0 sums the two norms in the order of the reference's device encoder
+ * (r[j] += r[j+s], s = 64..1; turbo5_quant_group, src/turbo5.cuh:129-162) and is bit-equal
+ * to it; tree == 0 sums serially (near-boundary ties against the device possible). */
+void q27o_t5_quant(const float* x128, uint8_t* blk82, int tree);
+void q27o_t5_dequant(const uint8_t* blk82, float* y128);   /* cpu_dequant5, :85-89 */
+/* ---- int8-g64 codec (src/i8g64.cuh:48-72, tools/i8g64_test.cu:29-50) ----------------- */
+/* oracle_quant: per 64 dims absmax; scale = fp16_rn(absmax / 127); codes = rint(x / the
+ * ROUNDED scale) clamped to +-127; a zero scale stores zero codes. No rotation. */
+void q27o_i8_quant(const float* x128, uint8_t* blk132);
+void q27o_i8_dequant(const uint8_t* blk132, float* y128);  /* code * scale, oracle_deq */
+
 /* rows helpers: ngroups consecutive 128-float groups <-> ngroups 50-byte blocks */
 void q27o_t3_quant_groups(const float* x, int64_t ngroups, uint8_t* blocks, int nthreads);
 void q27o_wht_groups(float* x, int64_t ngroups, int inverse, int nthreads);
+void q27o_t5_quant_groups(const float* x, int64_t ngroups, uint8_t* blocks, int tree,
+                          int nthreads);
+void q27o_i8_quant_groups(const float* x, int64_t ngroups, uint8_t* blocks, int nthreads);
 
 /* Dequantise `rows` cache rows of n_kv heads x 256 dims to fp32 [rows][n_kv][256].
  * fp16: half2float; fp8: float(e4m3); turbo3: CENTROIDS[idx] * half2float(norm) as an
  * fp32 product (src/turbo3.cuh:69-73) -- the bit-exact dequant target. */
 int q27o_kv_dequant(const void* cache, int kvk, int64_t rows, int n_kv, float* out,
                     int nthreads);
-/* bytes per cache row for a kind (fp16 2*n_kv*256, fp8 n_kv*256, turbo3 n_kv*2*50) */
+/* the same for one side of a kind whose K and V rows differ (is_v: 0 = K rows, 1 = V rows):
+ * turbo5 CENTROIDS5[idx]*norm (src/turbo5.cuh:111-115), int8-g64 code*scale
+ * (src/i8g64.cuh:68-72) */
+int q27o_kv_dequant_side(const void* cache, int kvk, int is_v, int64_t rows, int n_kv,
+                         float* out, int nthreads);
+/* bytes per cache row for a kind (fp16 2*n_kv*256, fp8 n_kv*256, turbo3 n_kv*2*50); the
+ * plain form gives the K side. Engine::kv_bytes, src/engine.cuh:868-876 */
 int64_t q27o_row_bytes(int kvk, int n_kv);
+int64_t q27o_row_bytes_side(int kvk, int n_kv, int is_v);
 
 /* ---- attention --------------------------------------------------------------------- */
 /* Exact decode/verify reference: host_ref (src/test_kernels.cu:898-928) and the inner

@@ -22,6 +22,8 @@ KV_PAGE = 64
 HEAD_DIM = 256
 GQA = 6
 T3_BLOCK_BYTES = 50
+T5_BLOCK_BYTES = 82
+I8_BLOCK_BYTES = 132
 
 OK, ERR_INVALID_ARG, ERR_UNSUPPORTED_KIND, ERR_UNSUPPORTED_WIDTH, ERR_CUDA, ERR_TOO_LARGE = range(6)
 
@@ -55,6 +57,7 @@ SIGNATURES = {
     "q27_wait_timeout_flag": (_i, [C.POINTER(_i)]),
     "q27_set_kernel_events": (_i, [_vp, _vp]),
     "q27_kv_row_bytes": (_i64, [_i, _i]),
+    "q27_kv_row_bytes_side": (_i64, [_i, _i, _i]),
     "q27_decode_scratch_floats": (_i64, [_i, _i]),
     "q27_prefill_part_floats": (_i64, [_i, _i]),
     "q27_attn_decode": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp, _i]),
@@ -81,6 +84,7 @@ SIGNATURES = {
     "q27_attn_prefill_T_exact": (_i, [_vp, _i, _i, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i,
                                       _f, _vp, _i]),
     "q27_kv_dequant": (_i, [_vp, _i, _i, _i, _i, _vp, _vp]),
+    "q27_kv_dequant_side": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp]),
     "q27_kv_store_T": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _i]),
     "q27_kv_store_T_t3": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _i]),
     "q27_wht_T": (_i, [_vp, _i, _i, _i, _i, _i, _i, _vp]),

@@ -206,10 +206,10 @@ def attn_prefill_T(qT, q_stride, q_row, ktab, vtab, outT, out_row, part, base_po
                n_q_heads, n_kv_heads, head_dim, scale, stream_ptr(st), kvk), "q27_attn_prefill_T")
 
 
-def kv_dequant(tab, kvk, row0, nrows, n_kv_heads, out, st=None):
-    """Bit-exact dequantisation of cache rows to fp32 [nrows][n_kv_heads][256]."""
-    L.check(L.lib().q27_kv_dequant(tab.data_ptr(), kvk, row0, nrows, n_kv_heads, out.data_ptr(),
-                                   stream_ptr(st)), "q27_kv_dequant")
+def kv_dequant(tab, kvk, row0, nrows, n_kv_heads, out, st=None, is_v=False):
+    """Bit-exact dequantisation of cache rows of one side to fp32 [nrows][n_kv_heads][256]."""
+    L.check(L.lib().q27_kv_dequant_side(tab.data_ptr(), kvk, int(is_v), row0, nrows, n_kv_heads,
+                                        out.data_ptr(), stream_ptr(st)), "q27_kv_dequant_side")
 
 
 def kv_store_T(kT, vT, ktab, vtab, base_pos, rowlen, T, st=None, fp8=False):
@@ -219,7 +219,8 @@ def kv_store_T(kT, vT, ktab, vtab, base_pos, rowlen, T, st=None, fp8=False):
 
 
 def kv_store_T_t3(kT, vT, ktab, vtab, base_pos, n_kv_heads, head_dim, T, st=None, kvk=2):
-    """turbo3 prefill store: cooperative per-128-group quantise of T tokens' K and V rows."""
+    """Prefill store of the kinds from turbo3 up: per-128-group quantise of T tokens' V rows
+    (turbo3) and K rows (the kind's K format)."""
     L.check(L.lib().q27_kv_store_T_t3(kT.data_ptr(), vT.data_ptr(), ktab.data_ptr(),
                                       vtab.data_ptr(), base_pos, n_kv_heads, head_dim, T,
                                       stream_ptr(st), kvk), "q27_kv_store_T_t3")

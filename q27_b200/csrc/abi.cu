@@ -31,7 +31,7 @@ int sm_count() {
 }
 
 int check_geometry(int q_stride, int n_q, int n_kv, int head_dim, int kvk) {
-    if (kvk != Q27_KV_F16 && kvk != Q27_KV_FP8 && kvk != Q27_KV_T3) return Q27_ERR_UNSUPPORTED_KIND;
+    if (!kind_known(kvk)) return Q27_ERR_UNSUPPORTED_KIND;
     if (head_dim != HD || n_kv < 1 || n_kv > 8 || n_q != GQA * n_kv) return Q27_ERR_UNSUPPORTED_WIDTH;
     if (q_stride < HD) return Q27_ERR_INVALID_ARG;
     return Q27_OK;
@@ -195,10 +195,12 @@ int q27_device_arch(void) {
     return (mj == 10 && mn == 0) ? 1000 : 0; // the image holds sm_100a code only
 }
 
-int64_t q27_kv_row_bytes(int kvk, int n_kv_heads) {
-    if (kvk != Q27_KV_F16 && kvk != Q27_KV_FP8 && kvk != Q27_KV_T3) return -1;
-    return row_bytes_of(kvk, n_kv_heads);
+int64_t q27_kv_row_bytes_side(int kvk, int n_kv_heads, int is_v) {
+    if (!kind_known(kvk)) return -1;
+    return row_bytes_of(side_fmt(kvk, is_v != 0), n_kv_heads);
 }
+
+int64_t q27_kv_row_bytes(int kvk, int n_kv_heads) { return q27_kv_row_bytes_side(kvk, n_kv_heads, 0); }
 
 int64_t q27_decode_scratch_floats(int ntok, int n_q_heads) {
     return (int64_t)ntok * n_q_heads * Q27_MAX_SPLITS * Q27_PART_STRIDE;
@@ -420,12 +422,17 @@ int q27_attn_merge_pushed(void* mailbox, int world, int64_t npairs, unsigned epo
     return launch_merge_pushed(mailbox, world, npairs, epoch, out, static_cast<cudaStream_t>(stream));
 }
 
+int q27_kv_dequant_side(const void* const* tab, int kvk, int is_v, int row0, int nrows,
+                        int n_kv_heads, float* out, void* stream) {
+    if (!kind_known(kvk)) return Q27_ERR_UNSUPPORTED_KIND;
+    if (!tab || !out || row0 < 0 || nrows < 0 || n_kv_heads < 1) return Q27_ERR_INVALID_ARG;
+    return launch_kv_dequant(tab, side_fmt(kvk, is_v != 0), row0, nrows, n_kv_heads, out,
+                             static_cast<cudaStream_t>(stream));
+}
+
 int q27_kv_dequant(const void* const* tab, int kvk, int row0, int nrows, int n_kv_heads,
                    float* out, void* stream) {
-    if (kvk != Q27_KV_F16 && kvk != Q27_KV_FP8 && kvk != Q27_KV_T3) return Q27_ERR_UNSUPPORTED_KIND;
-    if (!tab || !out || row0 < 0 || nrows < 0 || n_kv_heads < 1) return Q27_ERR_INVALID_ARG;
-    return launch_kv_dequant(tab, kvk, row0, nrows, n_kv_heads, out,
-                             static_cast<cudaStream_t>(stream));
+    return q27_kv_dequant_side(tab, kvk, 0, row0, nrows, n_kv_heads, out, stream);
 }
 
 int q27_kv_store_T(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
@@ -438,11 +445,11 @@ int q27_kv_store_T(const float* kT, const float* vT, void* const* ktab, void* co
 
 int q27_kv_store_T_t3(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
                       int base_pos, int n_kv_heads, int head_dim, int T, void* stream, int kvk) {
-    if (kvk != Q27_KV_T3) return Q27_ERR_UNSUPPORTED_KIND; // turbo3v / turbo5k K legs: refused
+    if (kvk < Q27_KV_T3 || !kind_known(kvk)) return Q27_ERR_UNSUPPORTED_KIND;
     if (head_dim != HD || n_kv_heads < 1) return Q27_ERR_UNSUPPORTED_WIDTH;
     if (!kT || !vT || !ktab || !vtab || base_pos < 0 || T < 0) return Q27_ERR_INVALID_ARG;
     return launch_kv_store_T(kT, vT, ktab, vtab, base_pos, n_kv_heads, T,
-                             static_cast<cudaStream_t>(stream), Q27_KV_T3);
+                             static_cast<cudaStream_t>(stream), kvk);
 }
 
 int q27_wht_T(float* x, int n_heads, int head_dim, int head_stride, int row_stride, int T, int inv,
@@ -467,14 +474,14 @@ int q27_kv_store3(const q27_CP3* k, const q27_CP3* v, void* const* ktab, void* c
 int q27_kv_store_t3(const q27_CP3* k, const q27_CP3* v, void* const* ktab, void* const* vtab,
                     const q27_IP3* pos, int n_kv_heads, int head_dim, void* stream, int ntok,
                     int kvk) {
-    if (kvk != Q27_KV_T3) return Q27_ERR_UNSUPPORTED_KIND; // turbo3v / turbo5k K legs: refused
+    if (kvk < Q27_KV_T3 || !kind_known(kvk)) return Q27_ERR_UNSUPPORTED_KIND;
     if (head_dim != HD || n_kv_heads < 1) return Q27_ERR_UNSUPPORTED_WIDTH;
     if (!k || !v || !pos || !ktab || !vtab || ntok < 0 || ntok > Q27_MAX_LANES)
         return Q27_ERR_INVALID_ARG;
     for (int t = 0; t < ntok; t++)
         if (!k->p[t] || !v->p[t] || !pos->p[t]) return Q27_ERR_INVALID_ARG;
     return launch_kv_store3(k->p, v->p, pos->p, ktab, vtab, n_kv_heads, ntok,
-                            static_cast<cudaStream_t>(stream), Q27_KV_T3);
+                            static_cast<cudaStream_t>(stream), kvk);
 }
 
 int q27_wht3(const q27_P3* x, int n_heads, int head_dim, int stride, int inv, void* stream,

@@ -27,7 +27,7 @@ constexpr int EXK = 32;                  // keys per block
 constexpr int EX_THREADS = 256;          // = head_dim: one output dimension per thread
 constexpr int EX_PITCH = HD + 1;         // odd pitch: rows read by 32 keys at once hit 32 banks
 
-template <int KVK>
+template <int FMT>
 __device__ __forceinline__ void stage_rows(float (*tile)[EX_PITCH], const void* const* tab,
                                            int row0, int nrows, int n_kv, int kvh) {
     for (int i = threadIdx.x; i < EXK * (HD / 8); i += EX_THREADS) {
@@ -35,7 +35,7 @@ __device__ __forceinline__ void stage_rows(float (*tile)[EX_PITCH], const void* 
         float v[8];
         if (k < nrows) {
             const int p = row0 + k;
-            load8_exact<KVK>(static_cast<const uint8_t*>(tab[p >> PAGE_SHIFT]), p & (PAGE - 1), n_kv,
+            load8_exact<FMT>(static_cast<const uint8_t*>(tab[p >> PAGE_SHIFT]), p & (PAGE - 1), n_kv,
                              kvh, d0, v);
         } else {
 #pragma unroll
@@ -46,7 +46,7 @@ __device__ __forceinline__ void stage_rows(float (*tile)[EX_PITCH], const void* 
     }
 }
 
-template <int KVK>
+template <int KF, int VF>   // storage formats of the K and V sides
 __global__ void __launch_bounds__(EX_THREADS)
 k_exact_partial(const __grid_constant__ DevBatch b) {
     const int sp = blockIdx.x, kvh = blockIdx.y;
@@ -88,7 +88,7 @@ k_exact_partial(const __grid_constant__ DevBatch b) {
     for (int r0 = lo; r0 < hi; r0 += EXK) {
         const int nrows = min(EXK, hi - r0);
         __syncthreads();                          // the tile's previous user is done (and s_q is in)
-        stage_rows<KVK>(s_tile, S.ktab, r0, nrows, b.n_kv, kvh);
+        stage_rows<KF>(s_tile, S.ktab, r0, nrows, b.n_kv, kvh);
         __syncthreads();
         if (warp < GQA) {
             float dot = 0.f;
@@ -110,7 +110,7 @@ k_exact_partial(const __grid_constant__ DevBatch b) {
             if (lane == 0) s_shrink[warp] = shrink;
         }
         __syncthreads();                          // scores are out of the tile
-        stage_rows<KVK>(s_tile, S.vtab, r0, nrows, b.n_kv, kvh);
+        stage_rows<VF>(s_tile, S.vtab, r0, nrows, b.n_kv, kvh);
         __syncthreads();
 #pragma unroll
         for (int j = 0; j < GQA; j++) {
@@ -292,7 +292,7 @@ k_merge(const float* __restrict__ parts, int nparts, int64_t npairs, float* __re
 // Scalar causal prefill: one warp per (token, kv head), six heads per warp, rows read
 // straight from the paged cache (neighbouring tokens share them through L1/L2).
 constexpr int PFX_WARPS = 8;
-template <int KVK>
+template <int KF, int VF>
 __global__ void __launch_bounds__(PFX_WARPS * 32)
 k_prefill_exact(const float* __restrict__ qT, int q_stride, int q_row,
                 const void* const* __restrict__ ktab, const void* const* __restrict__ vtab,
@@ -321,8 +321,8 @@ k_prefill_exact(const float* __restrict__ qT, int q_stride, int q_row,
         const uint8_t* vpage = static_cast<const uint8_t*>(vtab[pg]);
         for (; p < pend; p++) {
             float kv[8], vv[8];
-            load8_exact<KVK>(kpage, p & (PAGE - 1), n_kv, kvh, 8 * lane, kv);
-            load8_exact<KVK>(vpage, p & (PAGE - 1), n_kv, kvh, 8 * lane, vv);
+            load8_exact<KF>(kpage, p & (PAGE - 1), n_kv, kvh, 8 * lane, kv);
+            load8_exact<VF>(vpage, p & (PAGE - 1), n_kv, kvh, 8 * lane, vv);
 #pragma unroll
             for (int j = 0; j < GQA; j++) {
                 float d = 0.f;
@@ -353,10 +353,9 @@ k_prefill_exact(const float* __restrict__ qT, int q_stride, int q_row,
 
 int launch_exact_partials(const DevBatch& b, int kvk, cudaStream_t st) {
     dim3 grid(b.nsplit, b.n_kv, b.nslots * b.max_ntok);
-    if (kvk == Q27_KV_F16) k_exact_partial<Q27_KV_F16><<<grid, EX_THREADS, 0, st>>>(b);
-    else if (kvk == Q27_KV_FP8) k_exact_partial<Q27_KV_FP8><<<grid, EX_THREADS, 0, st>>>(b);
-    else if (kvk == Q27_KV_T3) k_exact_partial<Q27_KV_T3><<<grid, EX_THREADS, 0, st>>>(b);
-    else return Q27_ERR_UNSUPPORTED_KIND;
+#define Q27_LAUNCH(KF, VF) k_exact_partial<KF, VF><<<grid, EX_THREADS, 0, st>>>(b)
+    Q27_FOR_KIND(kvk, Q27_LAUNCH, return Q27_ERR_UNSUPPORTED_KIND)
+#undef Q27_LAUNCH
     Q27_CUDA_TRY(cudaGetLastError());
     Q27_COUNT_LAUNCH();
     return Q27_OK;
@@ -394,16 +393,11 @@ int launch_prefill_exact(const float* qT, int q_stride, int q_row, const void* c
     (void)n_q;
     dim3 grid(n_kv, (SB + PFX_WARPS - 1) / PFX_WARPS);
     const int te = t0 + SB;
-    if (kvk == Q27_KV_F16)
-        k_prefill_exact<Q27_KV_F16><<<grid, PFX_WARPS * 32, 0, st>>>(
-            qT, q_stride, q_row, ktab, vtab, outT, out_row, base_pos, t0, te, n_kv, scale);
-    else if (kvk == Q27_KV_FP8)
-        k_prefill_exact<Q27_KV_FP8><<<grid, PFX_WARPS * 32, 0, st>>>(
-            qT, q_stride, q_row, ktab, vtab, outT, out_row, base_pos, t0, te, n_kv, scale);
-    else if (kvk == Q27_KV_T3)
-        k_prefill_exact<Q27_KV_T3><<<grid, PFX_WARPS * 32, 0, st>>>(
-            qT, q_stride, q_row, ktab, vtab, outT, out_row, base_pos, t0, te, n_kv, scale);
-    else return Q27_ERR_UNSUPPORTED_KIND;
+#define Q27_LAUNCH(KF, VF)                                        \
+    k_prefill_exact<KF, VF><<<grid, PFX_WARPS * 32, 0, st>>>(     \
+        qT, q_stride, q_row, ktab, vtab, outT, out_row, base_pos, t0, te, n_kv, scale)
+    Q27_FOR_KIND(kvk, Q27_LAUNCH, return Q27_ERR_UNSUPPORTED_KIND)
+#undef Q27_LAUNCH
     Q27_CUDA_TRY(cudaGetLastError());
     Q27_COUNT_LAUNCH();
     return Q27_OK;

@@ -915,6 +915,7 @@ int launch_prefill_umma(const float* qT, int q_stride, int q_row, const void* co
                         int base_pos, int t0, int SB, int n_q, int n_kv, float scale,
                         int sm_count, cudaStream_t st, int kvk, bool* done) {
     *done = false;
+    if (kind_known(kvk) && !kind_has_tensor_path(kvk)) return Q27_OK;   // served by the fp32 family
     (void)n_q;
     // float4 loads of Q rows and float4 stores of output rows
     if ((q_stride & 3) || (q_row & 3) || (out_row & 3) || ((uintptr_t)qT & 15) || ((uintptr_t)outT & 15))
@@ -976,6 +977,7 @@ int read_umma_timeout_flag(int* out) {
 int launch_verify_umma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool* done,
                        int force_nsplit) {
     *done = false;
+    if (kind_known(kvk) && !kind_has_tensor_path(kvk)) return Q27_OK;   // served by the fp32 family
     if (b.q_stride & 3) return Q27_OK;
     for (int i = 0; i < b.nslots; i++)
         for (int t = 0; t < b.s[i].ntok; t++)

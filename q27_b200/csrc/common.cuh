@@ -20,6 +20,22 @@ constexpr int PAGE = Q27_KV_PAGE;      // 64 rows per page (src/cuda_common.h:70
 constexpr int PAGE_SHIFT = 6;
 constexpr int PART = Q27_PART_STRIDE;  // 258 floats: m, l, acc[256]
 constexpr int T3_BLK = Q27_T3_BLOCK_BYTES;
+constexpr int T5_BLK = Q27_T5_BLOCK_BYTES;
+constexpr int I8_BLK = Q27_I8_BLOCK_BYTES;
+
+// Storage format of one side of a cache. The first three coincide with the KvKinds whose two
+// sides are stored alike; from turbo3 up the V side is always turbo3 and only the K side
+// varies (src/cuda_common.h:47-53).
+enum RowFmt : int { RF_F16 = 0, RF_FP8 = 1, RF_T3 = 2, RF_T5 = 3, RF_I8 = 4 };
+static_assert(RF_F16 == Q27_KV_F16 && RF_FP8 == Q27_KV_FP8 && RF_T3 == Q27_KV_T3, "formats 0..2 are kinds 0..2");
+__host__ __device__ constexpr int k_fmt(int kvk) {
+    return kvk == Q27_KV_T3V ? RF_F16 : kvk == Q27_KV_T5K ? RF_T5 : kvk == Q27_KV_I8G64 ? RF_I8 : kvk;
+}
+__host__ __device__ constexpr int v_fmt(int kvk) { return kvk >= Q27_KV_T3 ? RF_T3 : kvk; }
+__host__ __device__ constexpr int side_fmt(int kvk, bool is_v) { return is_v ? v_fmt(kvk) : k_fmt(kvk); }
+inline bool kind_known(int kvk) { return kvk >= Q27_KV_F16 && kvk <= Q27_KV_I8G64; }
+// kinds the tensor-core kernels read (both sides in one of the first three formats)
+inline bool kind_has_tensor_path(int kvk) { return kvk >= Q27_KV_F16 && kvk <= Q27_KV_T3; }
 constexpr float NEG_SENTINEL = -FLT_MAX; // "empty partial" marker (src/prefill.cu:1353-1362)
 
 // Per-thread record of the last failing CUDA call (read by q27_last_cuda_error()).
@@ -128,11 +144,12 @@ __device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
 }
 
 // 8 consecutive elements (d0 multiple of 8) of one (row, kv head) slice as fp32.
-// Bit-exact to kv2f (src/cuda_common.h:113-114) and turbo3_deq_elem (src/turbo3.cuh:134).
-template <int KVK>
+// Bit-exact to kv2f (src/cuda_common.h:113-114), turbo3_deq_elem (src/turbo3.cuh:134),
+// turbo5_deq_elem (src/turbo5.cuh:163-166) and i8g64_deq_elem (src/i8g64.cuh:68-72).
+template <int FMT>
 __device__ __forceinline__ void load8_exact(const uint8_t* __restrict__ page, int r, int n_kv,
                                             int kvh, int d0, float* o) {
-    if constexpr (KVK == Q27_KV_F16) {
+    if constexpr (FMT == RF_F16) {
         const uint4 v = *reinterpret_cast<const uint4*>(
             page + ((size_t)(r * n_kv + kvh) * HD + d0) * 2);
         const __half2* h = reinterpret_cast<const __half2*>(&v);
@@ -142,13 +159,37 @@ __device__ __forceinline__ void load8_exact(const uint8_t* __restrict__ page, in
             o[2 * i] = f.x;
             o[2 * i + 1] = f.y;
         }
-    } else if constexpr (KVK == Q27_KV_FP8) {
+    } else if constexpr (FMT == RF_FP8) {
         const uint2 v =
             *reinterpret_cast<const uint2*>(page + (size_t)(r * n_kv + kvh) * HD + d0);
         const uint8_t* b = reinterpret_cast<const uint8_t*>(&v);
 #pragma unroll
         for (int i = 0; i < 8; i++) o[i] = e4m3_to_f32(b[i]);
+    } else if constexpr (FMT == RF_T5) {
+        // block = 82 B: fp16 norm @0, qs[64] @2 (low 4 bits, 2 per byte), hi[16] @66 (fifth bit)
+        const uint8_t* blk = page + ((size_t)(r * n_kv + kvh) * 2 + (d0 >> 7)) * T5_BLK;
+        const int j0 = d0 & 127;
+        const float norm = __half2float(*reinterpret_cast<const __half*>(blk));
+        const uint16_t* q16 = reinterpret_cast<const uint16_t*>(blk + 2 + (j0 >> 1));   // 2-aligned
+        const uint32_t qs = (uint32_t)q16[0] | ((uint32_t)q16[1] << 16);
+        const uint32_t hb = blk[66 + (j0 >> 3)];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            int idx = ((qs >> (4 * i)) & 15) | (((hb >> i) & 1) << 4);
+            o[i] = kT5Centroid[idx] * norm;
+        }
+    } else if constexpr (FMT == RF_I8) {
+        // block = 132 B: int8 codes[128] @0, fp16 scale per 64 dims @128
+        const uint8_t* blk = page + ((size_t)(r * n_kv + kvh) * 2 + (d0 >> 7)) * I8_BLK;
+        const int j0 = d0 & 127;
+        const float sc = __half2float(*reinterpret_cast<const __half*>(blk + 128 + 2 * (j0 >> 6)));
+        const uint2 v = make_uint2(*reinterpret_cast<const uint32_t*>(blk + j0),
+                                   *reinterpret_cast<const uint32_t*>(blk + j0 + 4));  // 4-aligned
+        const int8_t* c = reinterpret_cast<const int8_t*>(&v);
+#pragma unroll
+        for (int i = 0; i < 8; i++) o[i] = (float)c[i] * sc;
     } else {
+        static_assert(FMT == RF_T3, "unknown row format");
         // block = 50 B: fp16 norm @0, qs[32] @2 (2 bits/elem), signs[16] @34 (1 bit/elem)
         const uint8_t* blk = page + ((size_t)(r * n_kv + kvh) * 2 + (d0 >> 7)) * T3_BLK;
         const int j0 = d0 & 127;
@@ -163,9 +204,27 @@ __device__ __forceinline__ void load8_exact(const uint8_t* __restrict__ page, in
     }
 }
 
-__host__ __device__ __forceinline__ int row_bytes_of(int kvk, int n_kv) {
-    return kvk == Q27_KV_F16 ? n_kv * HD * 2 : kvk == Q27_KV_FP8 ? n_kv * HD : n_kv * 2 * T3_BLK;
+// bytes per cache row of a storage format
+__host__ __device__ __forceinline__ int row_bytes_of(int fmt, int n_kv) {
+    return fmt == RF_F16 ? n_kv * HD * 2
+         : fmt == RF_FP8 ? n_kv * HD
+         : fmt == RF_T3  ? n_kv * 2 * T3_BLK
+         : fmt == RF_T5  ? n_kv * 2 * T5_BLK
+                         : n_kv * 2 * I8_BLK;
 }
+
+// Run CALL(KF, VF) with the storage formats of the K and V sides of a kind as compile-time
+// constants; `otherwise` for a kind outside the enum.
+#define Q27_FOR_KIND(kvk, CALL, otherwise)                      \
+    switch (kvk) {                                              \
+    case Q27_KV_F16: CALL(RF_F16, RF_F16); break;               \
+    case Q27_KV_FP8: CALL(RF_FP8, RF_FP8); break;               \
+    case Q27_KV_T3: CALL(RF_T3, RF_T3); break;                  \
+    case Q27_KV_T3V: CALL(RF_F16, RF_T3); break;                \
+    case Q27_KV_T5K: CALL(RF_T5, RF_T3); break;                 \
+    case Q27_KV_I8G64: CALL(RF_I8, RF_T3); break;               \
+    default: otherwise;                                         \
+    }
 
 // ---- launch entry points implemented per translation unit -----------------------------
 // exact (fp32 scalar) family
@@ -206,7 +265,7 @@ int read_umma_timeout_flag(int* out);
 int launch_prefill_exact(const float* qT, int q_stride, int q_row, const void* const* ktab,
                          const void* const* vtab, float* outT, int out_row, int base_pos, int t0,
                          int SB, int n_q, int n_kv, float scale, cudaStream_t st, int kvk);
-int launch_kv_dequant(const void* const* tab, int kvk, int row0, int nrows, int n_kv, float* out,
+int launch_kv_dequant(const void* const* tab, int fmt, int row0, int nrows, int n_kv, float* out,
                       cudaStream_t st);
 int launch_kv_store_T(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
                       int base_pos, int n_kv, int T, cudaStream_t st, int kvk);

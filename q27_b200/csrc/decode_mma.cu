@@ -925,6 +925,7 @@ int launch_one(DevBatch& b, int sm_count, bool may_fuse, cudaStream_t st) {
 int launch_decode_mma(DevBatch& b, int kvk, int sm_count, bool may_fuse, cudaStream_t st,
                       bool* done) {
     *done = false;
+    if (kind_known(kvk) && !kind_has_tensor_path(kvk)) return Q27_OK;   // served by the fp32 family
     b.fuse = 0;
     if (b.n_kv != 4) return Q27_OK; // the ring layouts assume 4 kv heads per row
     if (b.q_stride & 3) return Q27_OK; // Q heads are staged with 16-byte loads

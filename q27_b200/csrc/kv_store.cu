@@ -7,6 +7,14 @@
 // order, separate multiply and add -- so its blocks are byte-identical to that codec. (The
 // reference's own device encoder reduces in a tree and is allowed <= 0.2 % index ties
 // against the same CPU codec, src/test_kernels.cu:1150-1316.)
+//
+// K legs of the kinds above turbo3 (src/spec3.cu:564-578, src/prefill.cu:2570-2584): turbo3v
+// stores plain fp16 rows; turbo5k runs the same normalise / rotate / nearest / norm-correction
+// pipeline over 32 centroids, with the two norms summed in the halving-tree order of the
+// reference's device encoder (turbo5_quant_group, src/turbo5.cuh:129-162), whose bit-for-bit
+// gate is its CPU oracle in tree mode (tools/turbo5_test.cu:58-84); int8-g64 takes the absmax
+// of each 64 dims, rounds absmax/127 to fp16 and quantises with the reciprocal of the ROUNDED
+// scale (i8g64_quant_group, src/i8g64.cuh:48-64) -- order-independent, hence exact.
 #include "common.cuh"
 
 namespace q27b {
@@ -111,10 +119,114 @@ __device__ __forceinline__ void t3_encode_group(const float* __restrict__ src, u
     __syncwarp();
 }
 
+__device__ __forceinline__ int t5_nearest(float v) { // src/turbo5.cuh:95-107
+    int idx = 0;
+#pragma unroll
+    for (int i = 0; i < 31; i++) idx += v >= kT5Threshold[i] ? 1 : 0;
+    return idx;
+}
+
+// Sum of a group's 128 values, lane holding elements lane + 32 i, in the order of the loop
+// `for (s = 64; s > 0; s >>= 1) r[j] += r[j + s]  (j < s)`: result valid in lane 0.
+__device__ __forceinline__ float tree_sum128(const float (&v)[4], int lane) {
+    float a = __fadd_rn(__fadd_rn(v[0], v[2]), __fadd_rn(v[1], v[3]));   // s = 64, then s = 32
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, s));
+    return a;
+}
+
+// One warp encodes one 128-element group into an 82-byte turbo5 block.
+__device__ __forceinline__ void t5_encode_group(const float* __restrict__ src, uint8_t* blk,
+                                                float* xs, int lane) {
+    float v[4], sq[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        v[i] = src[lane + 32 * i];
+        sq[i] = __fmul_rn(v[i], v[i]);
+    }
+    const float gn = __shfl_sync(0xffffffffu, sqrtf(tree_sum128(sq, lane)), 0);
+    const float inv = gn > 1e-10f ? __fdiv_rn(1.f, gn) : 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; i++) xs[lane + 32 * i] = __fmul_rn(v[i], inv);
+    __syncwarp();
+    wht_group<false>(xs, lane);
+    // lane owns elements 4*lane .. 4*lane+3: two qs bytes, half a hi byte
+    int idx[4];
+    uint32_t qs = 0, hb = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        idx[i] = t5_nearest(xs[4 * lane + i]);
+        qs |= (uint32_t)(idx[i] & 15) << (4 * i);
+        hb |= (uint32_t)((idx[i] >> 4) & 1) << i;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float cv = kT5Centroid[idx[i]];
+        xs[4 * lane + i] = __fmul_rn(cv, cv);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; i++) sq[i] = xs[lane + 32 * i];
+    const float rn = sqrtf(tree_sum128(sq, lane));
+    const uint32_t hb_hi = __shfl_down_sync(0xffffffffu, hb, 1);
+    *reinterpret_cast<uint16_t*>(blk + 2 + 2 * lane) = (uint16_t)qs;          // block is 2-aligned
+    if ((lane & 1) == 0) blk[66 + (lane >> 1)] = (uint8_t)(hb | (hb_hi << 4));
+    if (lane == 0) {
+        const float corr = rn > 1e-10f ? __fdiv_rn(gn, rn) : gn;
+        *reinterpret_cast<__half*>(blk) = __float2half_rn(corr);
+    }
+    __syncwarp();
+}
+
+// One warp encodes one 128-element group into a 132-byte int8-g64 block: lane holds elements
+// lane + 32 i, so i = 0, 1 belong to the first 64-group and i = 2, 3 to the second.
+__device__ __forceinline__ void i8_encode_group(const float* __restrict__ src, uint8_t* blk,
+                                                int lane) {
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) v[i] = src[lane + 32 * i];
+    float am[2] = {fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3]))};
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        am[0] = fmaxf(am[0], __shfl_xor_sync(0xffffffffu, am[0], off));
+        am[1] = fmaxf(am[1], __shfl_xor_sync(0xffffffffu, am[1], off));
+    }
+#pragma unroll
+    for (int g = 0; g < 2; g++) {
+        const __half sh = __float2half_rn(__fdiv_rn(am[g], 127.0f));
+        const float sw = __half2float(sh);                 // the ROUNDED scale
+        const float inv = sw > 0.f ? __fdiv_rn(1.0f, sw) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const int q = min(127, max(-127, __float2int_rn(__fmul_rn(v[2 * g + i], inv))));
+            reinterpret_cast<int8_t*>(blk)[64 * g + 32 * i + lane] = (int8_t)(sw > 0.f ? q : 0);
+        }
+        if (lane == 0) *reinterpret_cast<__half*>(blk + 128 + 2 * g) = sh;
+    }
+}
+
+// One (row, group) of a side in the side's storage format; `cell` = (row in page) * groups per
+// row + group. V sides and turbo3 K go through the turbo3 encoder.
+__device__ __forceinline__ void encode_group(int fmt, const float* __restrict__ src, uint8_t* page,
+                                             size_t cell, float* xs, int lane) {
+    if (fmt == RF_T3) {
+        t3_encode_group(src, page + cell * T3_BLK, xs, lane);
+    } else if (fmt == RF_T5) {
+        t5_encode_group(src, page + cell * T5_BLK, xs, lane);
+    } else if (fmt == RF_I8) {
+        i8_encode_group(src, page + cell * I8_BLK, lane);
+    } else {                                                // RF_F16: 128 plain halves
+        __half* d = reinterpret_cast<__half*>(page) + cell * 128;
+#pragma unroll
+        for (int i = 0; i < 4; i++) d[lane + 32 * i] = __float2half_rn(src[lane + 32 * i]);
+    }
+}
+
 // rows base_pos .. base_pos+T-1; kT/vT: [T][n_kv*256] fp32
 __global__ void __launch_bounds__(ST_WARPS * 32)
 k_kv_store_T_t3(const float* __restrict__ kT, const float* __restrict__ vT, void* const* ktab,
-                void* const* vtab, int base_pos, int n_kv, int T) {
+                void* const* vtab, int base_pos, int n_kv, int T, int kfmt) {
     __shared__ float xs[ST_WARPS][128];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gpr = n_kv * 2; // groups per row per side
@@ -126,9 +238,8 @@ k_kv_store_T_t3(const float* __restrict__ kT, const float* __restrict__ vT, void
         const int t = (int)(gidx / gpr), gi = (int)(gidx % gpr);
         const int p = base_pos + t;
         uint8_t* page = static_cast<uint8_t*>((side ? vtab : ktab)[p >> PAGE_SHIFT]);
-        uint8_t* blk = page + ((size_t)(p & (PAGE - 1)) * gpr + gi) * T3_BLK;
-        t3_encode_group((side ? vT : kT) + (size_t)t * gpr * 128 + (size_t)gi * 128, blk, xs[warp],
-                        lane);
+        encode_group(side ? RF_T3 : kfmt, (side ? vT : kT) + (size_t)t * gpr * 128 + (size_t)gi * 128,
+                     page, (size_t)(p & (PAGE - 1)) * gpr + gi, xs[warp], lane);
     }
 }
 
@@ -185,7 +296,8 @@ struct LaneVecs {
 
 // grid (groups per row x 2 sides / ST_WARPS, ntok): lane t's K and V rows into cache row *pos[t]
 __global__ void __launch_bounds__(ST_WARPS * 32)
-k_kv_store3_t3(const __grid_constant__ LaneRows L, void* const* ktab, void* const* vtab, int n_kv) {
+k_kv_store3_t3(const __grid_constant__ LaneRows L, void* const* ktab, void* const* vtab, int n_kv,
+               int kfmt) {
     __shared__ float xs[ST_WARPS][128];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.y, gpr = n_kv * 2;
@@ -194,8 +306,8 @@ k_kv_store3_t3(const __grid_constant__ LaneRows L, void* const* ktab, void* cons
     const int side = w & 1, gi = w >> 1;
     const int p = __ldg(L.pos[t]);
     uint8_t* page = static_cast<uint8_t*>((side ? vtab : ktab)[p >> PAGE_SHIFT]);
-    uint8_t* blk = page + ((size_t)(p & (PAGE - 1)) * gpr + gi) * T3_BLK;
-    t3_encode_group((side ? L.v[t] : L.k[t]) + (size_t)gi * 128, blk, xs[warp], lane);
+    encode_group(side ? RF_T3 : kfmt, (side ? L.v[t] : L.k[t]) + (size_t)gi * 128, page,
+                 (size_t)(p & (PAGE - 1)) * gpr + gi, xs[warp], lane);
 }
 
 template <bool FP8>
@@ -241,9 +353,9 @@ unsigned blocks_for(int64_t units, int per_block) {
 int launch_kv_store_T(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
                       int base_pos, int n_kv, int T, cudaStream_t st, int kvk) {
     if (T == 0) return Q27_OK;
-    if (kvk == Q27_KV_T3) {
+    if (kvk >= Q27_KV_T3 && kind_known(kvk)) {
         k_kv_store_T_t3<<<blocks_for((int64_t)T * n_kv * 4, ST_WARPS), ST_WARPS * 32, 0, st>>>(
-            kT, vT, ktab, vtab, base_pos, n_kv, T);
+            kT, vT, ktab, vtab, base_pos, n_kv, T, k_fmt(kvk));
     } else if (kvk == Q27_KV_FP8) {
         k_kv_store_T<true><<<blocks_for((int64_t)T * n_kv * HD, 256), 256, 0, st>>>(
             kT, vT, ktab, vtab, base_pos, n_kv * HD, T);
@@ -268,9 +380,9 @@ int launch_kv_store3(const float* const* k, const float* const* v, const int* co
         L.v[t] = v[t];
         L.pos[t] = pos[t];
     }
-    if (kvk == Q27_KV_T3) {
+    if (kvk >= Q27_KV_T3 && kind_known(kvk)) {
         dim3 grid((n_kv * 4 + ST_WARPS - 1) / ST_WARPS, ntok);
-        k_kv_store3_t3<<<grid, ST_WARPS * 32, 0, st>>>(L, ktab, vtab, n_kv);
+        k_kv_store3_t3<<<grid, ST_WARPS * 32, 0, st>>>(L, ktab, vtab, n_kv, k_fmt(kvk));
     } else if (kvk == Q27_KV_FP8 || kvk == Q27_KV_F16) {
         const int rowlen = n_kv * HD;
         dim3 grid((rowlen + 255) / 256, ntok);

@@ -14,9 +14,12 @@ import torch
 from . import _lib as L
 
 KV_F16, KV_FP8, KV_T3 = 0, 1, 2
-KV_T3V, KV_T5K, KV_I8G64 = 3, 4, 5  # refused by the engine (out of scope), never mis-read
+# From turbo3 up the V side is turbo3 blocks and only the K side varies: fp16 rows (turbo3v),
+# 5-bit blocks (turbo5k), int8 blocks with a scale per 64 dims (int8-g64)
+KV_T3V, KV_T5K, KV_I8G64 = 3, 4, 5
 KV_PAGE = L.KV_PAGE
-KIND_NAMES = {KV_F16: "fp16", KV_FP8: "fp8", KV_T3: "turbo3"}
+KIND_NAMES = {KV_F16: "fp16", KV_FP8: "fp8", KV_T3: "turbo3", KV_T3V: "turbo3v",
+              KV_T5K: "turbo5k", KV_I8G64: "int8g64"}
 
 
 def kv_k_rotated(kvk: int) -> bool:
@@ -24,8 +27,9 @@ def kv_k_rotated(kvk: int) -> bool:
     return kvk in (KV_T3, KV_T5K)
 
 
-def row_bytes(kvk: int, n_kv_heads: int = 4) -> int:
-    n = L.lib().q27_kv_row_bytes(kvk, n_kv_heads)
+def row_bytes(kvk: int, n_kv_heads: int = 4, is_v: bool = False) -> int:
+    """Bytes per cache row of one side of a kind (Engine::kv_bytes(is_v), src/engine.cuh:868)."""
+    n = L.lib().q27_kv_row_bytes_side(kvk, n_kv_heads, int(is_v))
     if n < 0:
         raise L.Q27Error(L.ERR_UNSUPPORTED_KIND, "row_bytes")
     return int(n)
@@ -54,13 +58,13 @@ class PagedSide:
 
 
 def paged_from_rows(rows_bytes: torch.Tensor, kvk: int, n_kv_heads: int = 4,
-                    page_perm: torch.Tensor | None = None) -> PagedSide:
-    """Place logical cache rows (uint8 [rows, row_bytes], device) into 64-row pages.
+                    page_perm: torch.Tensor | None = None, is_v: bool = False) -> PagedSide:
+    """Place logical cache rows (uint8 [rows, row_bytes], device) of one side into 64-row pages.
 
     With ``page_perm`` the pages are scattered: logical page j lives in physical page
     ``page_perm[j]`` (the reference's Q27_KV_SCATTER proof, src/engine.cuh:1294-1358).
     """
-    rb = row_bytes(kvk, n_kv_heads)
+    rb = row_bytes(kvk, n_kv_heads, is_v)
     assert rows_bytes.dtype == torch.uint8 and rows_bytes.dim() == 2 and rows_bytes.shape[1] == rb
     rows = rows_bytes.shape[0]
     npages = max((rows + KV_PAGE - 1) // KV_PAGE, 1)

@@ -1,6 +1,7 @@
-"""Generates tests/golden/turbo3_codec.npz from the REFERENCE's own code: the CPU turbo3
-codec in tools/turbo3_test.cu and the CUDA toolkit's host fp16/e4m3 converters, both built
-from the reference tree into oracle/_ref/libq27ref_codec.so by oracle/Makefile.
+"""Generates tests/golden/turbo3_codec.npz and tests/golden/k_codecs.npz from the REFERENCE's
+own code: the CPU turbo3 / turbo5 / int8-g64 codecs in tools/turbo3_test.cu,
+tools/turbo5_test.cu and tools/i8g64_test.cu and the CUDA toolkit's host fp16/e4m3 converters,
+all built from the reference tree into oracle/_ref/libq27ref_codec.so by oracle/Makefile.
 
 Run in a container that has the reference tree:  make -C oracle ref && python tests/golden/make_golden.py
 The inputs come from an LCG of the kind the reference's tools use
@@ -49,6 +50,28 @@ def main():
                         fwht=fw, conv_in=conv_in, half_bits=half_bits, e4m3_bits=e4m3_bits,
                         e4m3_table=e4m3_table)
     print("wrote turbo3_codec.npz", blocks.shape, conv_in.shape)
+
+    # K-side codecs of the turbo5k and int8-g64 kinds: same inputs plus scale extremes
+    xk = x.copy()
+    xk[9] *= 1e-6                        # tiny group: fp16 scale underflow territory for int8
+    xk[11, 64:] = 0.0                    # one all-zero 64-group inside a live block
+    b5_tree = np.zeros((ngroups, 82), np.uint8)
+    b5_serial = np.zeros((ngroups, 82), np.uint8)
+    d5 = np.zeros((ngroups, 128), np.float32)
+    b8 = np.zeros((ngroups, 132), np.uint8)
+    d8 = np.zeros((ngroups // 2, 256), np.float32)
+    vp = C.c_void_p
+    for i in range(ngroups):
+        ref.lib.q27ref_cpu_quant5(xk[i].ctypes.data_as(_fp), b5_tree[i].ctypes.data_as(vp), 1)
+        ref.lib.q27ref_cpu_quant5(xk[i].ctypes.data_as(_fp), b5_serial[i].ctypes.data_as(vp), 0)
+        ref.lib.q27ref_cpu_dequant5(b5_tree[i].ctypes.data_as(vp), d5[i].ctypes.data_as(_fp))
+        ref.lib.q27ref_i8_quant(xk[i].ctypes.data_as(_fp), b8[i].ctypes.data_as(vp))
+    b8 = np.ascontiguousarray(b8)
+    for r in range(ngroups // 2):
+        ref.lib.q27ref_i8_dequant_row(b8[2 * r:].ctypes.data_as(vp), d8[r].ctypes.data_as(_fp))
+    np.savez_compressed(Path(__file__).parent / "k_codecs.npz", x=xk, t5_tree=b5_tree,
+                        t5_serial=b5_serial, t5_dequant=d5, i8_blocks=b8, i8_dequant=d8)
+    print("wrote k_codecs.npz", b5_tree.shape, b8.shape, int((b5_tree != b5_serial).sum()))
 
 
 if __name__ == "__main__":

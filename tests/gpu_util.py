@@ -32,7 +32,7 @@ class DeviceCase:
             kb = torch.zeros((0, case.k.shape[1]), dtype=torch.uint8, device=device)
             vb = torch.zeros((0, case.v.shape[1]), dtype=torch.uint8, device=device)
         self.kside = Q.paged_from_rows(kb, case.kvk, page_perm=perm)
-        self.vside = Q.paged_from_rows(vb, case.kvk, page_perm=perm)
+        self.vside = Q.paged_from_rows(vb, case.kvk, page_perm=perm, is_v=True)
         ntok = len(case.pos)
         self.ntok = ntok
         self.q = [torch.from_numpy(case.q[t].copy()).to(device) for t in range(ntok)]

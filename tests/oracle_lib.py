@@ -16,8 +16,9 @@ ORACLE_SO = ROOT / "oracle" / "build" / "libq27_oracle.so"
 REF_CODEC_SO = ROOT / "oracle" / "_ref" / "libq27ref_codec.so"
 REF_GPU_SO = ROOT / "oracle" / "_ref" / "libq27ref_gpu.so"
 
-KV_F16, KV_FP8, KV_T3 = 0, 1, 2
-HD, FD_ST, T3_BLOCK = 256, 258, 50
+KV_F16, KV_FP8, KV_T3, KV_T3V, KV_T5K, KV_I8G64 = range(6)
+ALL_KINDS = (KV_F16, KV_FP8, KV_T3, KV_T3V, KV_T5K, KV_I8G64)
+HD, FD_ST, T3_BLOCK, T5_BLOCK, I8_BLOCK = 256, 258, 50, 82, 132
 
 _fp = C.POINTER(C.c_float)
 _vp = C.c_void_p
@@ -54,6 +55,13 @@ class Oracle:
             getattr(L, f).restype = _fp
         L.q27o_t3_nearest.argtypes = [C.c_float]
         L.q27o_row_bytes.restype = C.c_int64
+        L.q27o_row_bytes_side.restype = C.c_int64
+        for f in ("q27o_t5_centroids", "q27o_t5_thresholds"):
+            getattr(L, f).restype = _fp
+        L.q27o_t5_nearest.argtypes = [C.c_float]
+        L.q27o_t5_quant_groups.argtypes = [_fp, C.c_int64, _vp, C.c_int, C.c_int]
+        L.q27o_i8_quant_groups.argtypes = [_fp, C.c_int64, _vp, C.c_int]
+        L.q27o_kv_dequant_side.argtypes = [_vp, C.c_int, C.c_int, C.c_int64, C.c_int, _fp, C.c_int]
         L.q27o_splitmix64.restype = C.c_uint64
         L.q27o_splitmix64.argtypes = [C.c_uint64]
         L.q27o_randn.argtypes = [_fp, C.c_int64, C.c_uint64, C.c_int]
@@ -104,19 +112,37 @@ class Oracle:
         self.lib.q27o_t3_quant_groups(px, ng, out.ctypes.data_as(_vp), 0)
         return out
 
+    def t5_quant(self, x, tree: bool = True) -> np.ndarray:
+        """x [..., 128k] fp32 -> uint8 turbo5 blocks [ngroups, 82]; tree = the reduction order
+        of the reference's device encoder"""
+        x, px = _f32(x)
+        ng = x.size // 128
+        out = np.zeros((ng, T5_BLOCK), dtype=np.uint8)
+        self.lib.q27o_t5_quant_groups(px, ng, out.ctypes.data_as(_vp), int(tree), 0)
+        return out
+
+    def i8_quant(self, x) -> np.ndarray:
+        """x [..., 128k] fp32 -> uint8 int8-g64 blocks [ngroups, 132]"""
+        x, px = _f32(x)
+        ng = x.size // 128
+        out = np.zeros((ng, I8_BLOCK), dtype=np.uint8)
+        self.lib.q27o_i8_quant_groups(px, ng, out.ctypes.data_as(_vp), 0)
+        return out
+
     def wht(self, x, inverse: bool = False) -> np.ndarray:
         x = np.array(x, dtype=np.float32, copy=True, order="C")
         self.lib.q27o_wht_groups(x.ctypes.data_as(_fp), x.size // 128, int(inverse), 0)
         return x
 
-    def row_bytes(self, kvk: int, n_kv: int = 4) -> int:
-        return int(self.lib.q27o_row_bytes(kvk, n_kv))
+    def row_bytes(self, kvk: int, n_kv: int = 4, is_v: bool = False) -> int:
+        return int(self.lib.q27o_row_bytes_side(kvk, n_kv, int(is_v)))
 
-    def kv_dequant(self, cache: np.ndarray, kvk: int, rows: int, n_kv: int = 4) -> np.ndarray:
+    def kv_dequant(self, cache: np.ndarray, kvk: int, rows: int, n_kv: int = 4,
+                   is_v: bool = False) -> np.ndarray:
         cache = np.ascontiguousarray(cache)
         out = np.empty((rows, n_kv, HD), dtype=np.float32)
-        rc = self.lib.q27o_kv_dequant(cache.ctypes.data_as(_vp), kvk, rows, n_kv,
-                                      out.ctypes.data_as(_fp), 0)
+        rc = self.lib.q27o_kv_dequant_side(cache.ctypes.data_as(_vp), kvk, int(is_v), rows, n_kv,
+                                           out.ctypes.data_as(_fp), 0)
         assert rc == 0
         return out
 
@@ -195,3 +221,12 @@ class RefCodec:
         L.q27ref_cpu_dequant.argtypes = [_vp, _fp]
         L.q27ref_cpu_fwht.argtypes = [_fp]
         L.q27ref_cpu_fwht_inv.argtypes = [_fp]
+        # the 5-bit and int8-g64 K codecs (tools/turbo5_test.cu, tools/i8g64_test.cu)
+        for f in ("q27ref_hdr5_centroids", "q27ref_hdr5_thresholds"):
+            getattr(L, f).restype = _fp
+        L.q27ref_cpu5_nearest.argtypes = [C.c_float]
+        L.q27ref_hdr5_nearest.argtypes = [C.c_float]
+        L.q27ref_cpu_quant5.argtypes = [_fp, _vp, C.c_int]
+        L.q27ref_cpu_dequant5.argtypes = [_vp, _fp]
+        L.q27ref_i8_quant.argtypes = [_fp, _vp]
+        L.q27ref_i8_dequant_row.argtypes = [_vp, _fp]

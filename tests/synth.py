@@ -6,7 +6,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from tests.oracle_lib import KV_F16, KV_FP8, KV_T3, HD, Oracle
+from tests.oracle_lib import KV_F16, KV_FP8, KV_T3, KV_T3V, KV_T5K, KV_I8G64, HD, Oracle
 
 N_Q, N_KV, GQA = 24, 4, 6
 Q_STRIDE = 2 * HD          # interleaved [q | gate] per head (src/engine.cuh: q||gate layout)
@@ -29,9 +29,26 @@ class Case:
     vf: np.ndarray | None = None
 
 
-def encode_rows(o: Oracle, x: np.ndarray, kvk: int):
-    """x [rows, N_KV, HD] fp32 -> (uint8 [rows, row_bytes], per-head scale or None)."""
+def k_rotated(kvk: int) -> bool:
+    """Does the K side carry the rotation, so that Q must be rotated to match?
+    (kv_k_rotated, src/cuda_common.h:59)"""
+    return kvk in (KV_T3, KV_T5K)
+
+
+def encode_rows(o: Oracle, x: np.ndarray, kvk: int, is_v: bool = False):
+    """x [rows, N_KV, HD] fp32 -> (uint8 [rows, row_bytes], per-head scale or None). From
+    turbo3 up the V side is turbo3 blocks whatever the K side holds (src/cuda_common.h:47-53)."""
     rows = x.shape[0]
+    if kvk >= KV_T3:
+        if is_v or kvk == KV_T3:
+            return o.t3_quant(x.reshape(-1, 128)).reshape(rows, -1), None
+        if kvk == KV_T3V:
+            return o.to_half_bits(x).view(np.uint8).reshape(rows, -1), None
+        if kvk == KV_T5K:
+            return o.t5_quant(x.reshape(-1, 128)).reshape(rows, -1), None
+        if kvk == KV_I8G64:
+            return o.i8_quant(x.reshape(-1, 128)).reshape(rows, -1), None
+        raise ValueError(kvk)
     if kvk == KV_F16:
         return o.to_half_bits(x).view(np.uint8).reshape(rows, -1), None
     if kvk == KV_FP8:
@@ -41,8 +58,6 @@ def encode_rows(o: Oracle, x: np.ndarray, kvk: int):
         a = np.where(a > 0, a, 1.0).astype(np.float32)
         scaled = xh * (np.float32(448.0) / a)[None, :, None]
         return o.to_e4m3(scaled).reshape(rows, -1), (a / np.float32(448.0)).astype(np.float32)
-    if kvk == KV_T3:
-        return o.t3_quant(x.reshape(-1, 128)).reshape(rows, -1), None
     raise ValueError(kvk)
 
 
@@ -65,10 +80,10 @@ def make_case(o: Oracle, kvk: int, rows: int, pos: list, seed: int,
     q_raw = o.randn(ntok * N_Q * Q_STRIDE, seed * 2 + 1000003).reshape(ntok, N_Q, Q_STRIDE)
     if bf16:
         kf, vf, q_raw = o.round_bf16(kf), o.round_bf16(vf), o.round_bf16(q_raw)
-    k, ks = encode_rows(o, kf, kvk)
-    v, vs = encode_rows(o, vf, kvk)
+    k, ks = encode_rows(o, kf, kvk, is_v=False)
+    v, vs = encode_rows(o, vf, kvk, is_v=True)
     q = q_raw.copy()
-    if kvk == KV_T3:  # the engine receives Q already rotated (src/engine.cuh:1485-1488)
+    if k_rotated(kvk):  # the engine receives Q already rotated (src/engine.cuh:1485-1488)
         q[:, :, :HD] = o.wht(np.ascontiguousarray(q_raw[:, :, :HD]))
     if kvk == KV_FP8:
         # the reference's fp8 cache is scale-free (src/cuda_common.h:110-121): the per-head

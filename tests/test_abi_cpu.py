@@ -37,8 +37,13 @@ def test_sizes_and_status_strings():
     lib = L.lib()
     assert lib.q27_kv_row_bytes(0, 4) == 2048 and lib.q27_kv_row_bytes(1, 4) == 1024
     assert lib.q27_kv_row_bytes(2, 4) == 400
-    for refused in (3, 4, 5, -1):   # turbo3v, turbo5k, int8-g64: refused, never mis-read
-        assert lib.q27_kv_row_bytes(refused, 4) == -1
+    # kinds whose sides differ: K side by default (656 / 1056 B per row, src/server.cu:891-892),
+    # V side turbo3 (Engine::kv_bytes, src/engine.cuh:868-876)
+    assert [lib.q27_kv_row_bytes(k, 4) for k in (3, 4, 5)] == [2048, 656, 1056]
+    assert [lib.q27_kv_row_bytes_side(k, 4, 1) for k in (2, 3, 4, 5)] == [400] * 4
+    assert [lib.q27_kv_row_bytes_side(k, 4, 0) for k in (0, 1, 2)] == [2048, 1024, 400]
+    for refused in (6, -1):         # outside the enum: refused, never mis-read
+        assert lib.q27_kv_row_bytes(refused, 4) == -1 and lib.q27_kv_row_bytes_side(refused, 4, 1) == -1
     # ntok * n_q_heads * FD_MAXNS * FD_ST floats (src/spec3.cuh:109-127)
     assert q27_b200.decode_scratch_floats(12) == 12 * 24 * 128 * 258
     # n_q_heads * SB_rounded_to_16 * PF_SPLIT_MAX * 258 (src/prefill.cuh:86-88)
@@ -51,8 +56,8 @@ def test_validation_needs_no_gpu():
     one = 0x1000  # never dereferenced: validation fails first
     q = L.P3()
     q.p[0] = one
-    # refused kinds
-    for kvk in (3, 4, 5):
+    # kinds outside the enum
+    for kvk in (6, -1, 99):
         rc = lib.q27_attn_decode3(C.byref(q), 512, one, one, C.byref(q), one, C.byref(q), 0, 24, 4,
                                   256, 0.0625, None, 1, kvk)
         assert rc == L.ERR_UNSUPPORTED_KIND
@@ -72,8 +77,12 @@ def test_validation_needs_no_gpu():
     assert lib.q27_attn_prefill_T(None, 512, 12288, one, one, one, 6144, None, 0, 0, 8, 24, 4, 256,
                                   0.0625, None, 0) == L.ERR_INVALID_ARG
     assert lib.q27_attn_prefill_T(one, 512, 12288, one, one, one, 6144, None, 0, 0, 8, 24, 4, 256,
-                                  0.0625, None, 4) == L.ERR_UNSUPPORTED_KIND
-    assert lib.q27_kv_dequant(one, 5, 0, 1, 4, one, None) == L.ERR_UNSUPPORTED_KIND
+                                  0.0625, None, 6) == L.ERR_UNSUPPORTED_KIND
+    assert lib.q27_kv_dequant(one, 6, 0, 1, 4, one, None) == L.ERR_UNSUPPORTED_KIND
+    assert lib.q27_kv_dequant_side(one, -1, 1, 0, 1, 4, one, None) == L.ERR_UNSUPPORTED_KIND
+    # the block stores serve the kinds from turbo3 up; fp16 / fp8 have their own entry
+    assert lib.q27_kv_store_T_t3(one, one, one, one, 0, 4, 256, 1, None, 1) == L.ERR_UNSUPPORTED_KIND
+    assert lib.q27_kv_store_T_t3(one, one, one, one, 0, 4, 256, 1, None, 6) == L.ERR_UNSUPPORTED_KIND
     assert lib.q27_attn_merge_partials(None, 2, 10, one, None) == L.ERR_INVALID_ARG
 
 

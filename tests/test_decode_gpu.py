@@ -221,7 +221,7 @@ def test_errors_are_status_codes(cuda, oracle):
     dc = DeviceCase(c, cuda)
     with pytest.raises(Q._lib.Q27Error) as e:
         Q.attn_decode3(dc.q, synth.Q_STRIDE, dc.kside.tab, dc.vside.tab, dc.out, dc.scratch,
-                       dc.pos, 0, 24, 4, 256, SCALE, ntok=1, kvk=4)     # turbo5k: refused
+                       dc.pos, 0, 24, 4, 256, SCALE, ntok=1, kvk=6)     # outside the KvKind enum
     assert e.value.status == Q._lib.ERR_UNSUPPORTED_KIND
     assert torch.isnan(dc.out[0]).all()                                  # nothing was written
 

@@ -7,7 +7,8 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-from tests.oracle_lib import (KV_F16, KV_FP8, KV_T3, HD, REF_CODEC_SO, Oracle, RefCodec)
+from tests.oracle_lib import (ALL_KINDS, KV_F16, KV_FP8, KV_I8G64, KV_T3, KV_T3V, KV_T5K, HD,
+                              REF_CODEC_SO, Oracle, RefCodec)
 from tests import synth
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
@@ -28,7 +29,10 @@ def test_block_is_50_bytes_and_zero_vector_packs_index_4(oracle):
     assert blk.shape == (1, 50)
     assert (blk[0, 2:34] == 0).all() and (blk[0, 34:50] == 255).all()
     assert oracle.row_bytes(KV_T3) == 400 and oracle.row_bytes(KV_FP8) == 1024
-    assert oracle.row_bytes(KV_F16) == 2048 and oracle.row_bytes(3) == -1
+    assert oracle.row_bytes(KV_F16) == 2048 and oracle.row_bytes(6) == -1
+    # K rows of the kinds whose sides differ (656 / 1056 B: src/server.cu:891-892); V is turbo3
+    assert [oracle.row_bytes(k) for k in (KV_T3V, KV_T5K, KV_I8G64)] == [2048, 656, 1056]
+    assert all(oracle.row_bytes(k, is_v=True) == 400 for k in (KV_T3, KV_T3V, KV_T5K, KV_I8G64))
 
 
 def test_tables_match_reference_header(oracle, ref):
@@ -66,6 +70,58 @@ def test_codec_bitwise_vs_reference_cpu_codec(oracle, ref):
     assert (oracle.wht(oracle.wht(a), inverse=True).view(np.uint32) == b.view(np.uint32)).all()
 
 
+def test_turbo5_tables_and_codec_vs_reference_cpu_codec(oracle, ref):
+    c, t = oracle.lib.q27o_t5_centroids(), oracle.lib.q27o_t5_thresholds()
+    rc, rt = ref.lib.q27ref_hdr5_centroids(), ref.lib.q27ref_hdr5_thresholds()
+    assert [c[i] for i in range(32)] == [rc[i] for i in range(32)]
+    assert [t[i] for i in range(31)] == [rt[i] for i in range(31)]
+    assert ref.lib.q27ref_block5_bytes() == 82
+    probe = np.concatenate([np.linspace(-0.3, 0.3, 6001, dtype=np.float32),
+                            np.array([t[i] for i in range(31)], np.float32)])
+    for v in probe:
+        assert oracle.lib.q27o_t5_nearest(float(v)) == ref.lib.q27ref_hdr5_nearest(float(v)) \
+            == ref.lib.q27ref_cpu5_nearest(float(v))
+    rng = np.random.default_rng(17)
+    n = 3000
+    x = (rng.standard_normal((n, 128)) * rng.choice([1e-3, 1, 8, 50], size=(n, 1))).astype(np.float32)
+    x[0] = 0
+    vp = C.c_void_p
+    for tree in (True, False):
+        mine = oracle.t5_quant(x, tree=tree)
+        theirs = np.zeros_like(mine)
+        for i in range(n):
+            ref.lib.q27ref_cpu_quant5(x[i].ctypes.data_as(_fp), theirs[i].ctypes.data_as(vp), int(tree))
+        assert (mine == theirs).all()
+    mine = oracle.t5_quant(x)
+    deq = oracle.kv_dequant(mine.reshape(n // 8, 656), KV_T5K, n // 8).reshape(n, 128)
+    y = np.zeros(128, np.float32)
+    for i in range(0, n, 13):
+        ref.lib.q27ref_cpu_dequant5(mine[i].ctypes.data_as(vp), y.ctypes.data_as(_fp))
+        assert (deq[i].view(np.uint32) == y.view(np.uint32)).all()
+
+
+def test_int8_g64_codec_vs_reference_cpu_codec(oracle, ref):
+    assert ref.lib.q27ref_block_i8_bytes() == 132
+    rng = np.random.default_rng(19)
+    n = 3000
+    x = (rng.standard_normal((n, 128)) * rng.choice([1e-7, 1e-3, 1, 8, 300], size=(n, 1))).astype(np.float32)
+    x[0] = 0
+    x[1, :64] = 0
+    x[2] = np.float32(65504.0 * 127)      # scale at the top of fp16
+    vp = C.c_void_p
+    mine = oracle.i8_quant(x)
+    theirs = np.zeros_like(mine)
+    for i in range(n):
+        ref.lib.q27ref_i8_quant(x[i].ctypes.data_as(_fp), theirs[i].ctypes.data_as(vp))
+    assert (mine == theirs).all()          # order-independent codec: exact, no tie class
+    assert (mine[0] == 0).all() and (mine[1, :64] == 0).all() and (mine[1, 128:130] == 0).all()
+    deq = oracle.kv_dequant(mine.reshape(n // 8, 1056), KV_I8G64, n // 8).reshape(n // 2, 256)
+    y = np.zeros(256, np.float32)
+    for r in range(0, n // 2, 11):
+        ref.lib.q27ref_i8_dequant_row(mine[2 * r:].ctypes.data_as(vp), y.ctypes.data_as(_fp))
+        assert (deq[r].view(np.uint32) == y.view(np.uint32)).all()
+
+
 def test_converters_vs_cuda_host_converters(oracle, ref):
     for h in range(0, 65536, 3):
         a, b = oracle.lib.q27o_half_to_float(h), ref.lib.q27ref_half_to_float(h)
@@ -95,6 +151,36 @@ def test_golden_fixtures(oracle):
     assert (e.view(np.uint32)[~nan] == g["e4m3_table"].view(np.uint32)[~nan]).all()
 
 
+def test_golden_fixtures_of_the_k_side_codecs(oracle):
+    g = np.load(GOLDEN / "k_codecs.npz")
+    assert (oracle.t5_quant(g["x"], tree=True) == g["t5_tree"]).all()
+    assert (oracle.t5_quant(g["x"], tree=False) == g["t5_serial"]).all()
+    n = g["x"].shape[0]
+    d5 = oracle.kv_dequant(g["t5_tree"].reshape(n // 8, 656), KV_T5K, n // 8)
+    assert (d5.reshape(n, 128).view(np.uint32) == g["t5_dequant"].view(np.uint32)).all()
+    assert (oracle.i8_quant(g["x"]) == g["i8_blocks"]).all()
+    d8 = oracle.kv_dequant(g["i8_blocks"].reshape(n // 8, 1056), KV_I8G64, n // 8)
+    assert (d8.reshape(n // 2, 256).view(np.uint32) == g["i8_dequant"].view(np.uint32)).all()
+    # the V side of both kinds is turbo3: same bytes, same dequant as the turbo3 kind
+    t3 = np.load(GOLDEN / "turbo3_codec.npz")
+    for kvk in (KV_T3V, KV_T5K, KV_I8G64):
+        dv = oracle.kv_dequant(t3["blocks"].reshape(-1, 400), kvk, t3["blocks"].shape[0] // 8, is_v=True)
+        assert (dv.reshape(-1, 128).view(np.uint32) == t3["dequant"].view(np.uint32)).all()
+
+
+def test_k_side_codecs_round_trip_quality(oracle):
+    # turbo5 round-trip cosine >= 0.998 predicted from its distortion (src/turbo5.cuh:57-60);
+    # int8-g64 error <= half a step of each group's scale (src/i8g64.cuh:14-21)
+    x = oracle.randn(256 * 128, 15).reshape(256, 128)
+    d5 = oracle.kv_dequant(oracle.t5_quant(x).reshape(32, 656), KV_T5K, 32).reshape(256, 128)
+    rec = oracle.wht(d5, inverse=True)
+    assert (rec * x).sum() / np.sqrt((rec ** 2).sum() * (x ** 2).sum()) > 0.998
+    blk = oracle.i8_quant(x)
+    d8 = oracle.kv_dequant(blk.reshape(32, 1056), KV_I8G64, 32).reshape(512, 64)
+    scale = blk[:, 128:132].copy().view(np.float16).astype(np.float32).reshape(512, 1)
+    assert (np.abs(d8 - x.reshape(512, 64)) <= 0.5 * scale * (1 + 1e-6) + 1e-12).all()
+
+
 def test_wht_round_trip_and_dot_invariance(oracle):
     # WHT round trip (src/test_kernels.cu:1320-1357) and the read contract
     # WHT(q).deq(K) ~ q.K (tools/turbo3_test.cu:126-147: score cosine >= 0.97)
@@ -113,13 +199,13 @@ def test_wht_round_trip_and_dot_invariance(oracle):
     assert c2 > 0.97
 
 
-@pytest.mark.parametrize("kvk", [KV_F16, KV_FP8, KV_T3])
+@pytest.mark.parametrize("kvk", ALL_KINDS)
 def test_attention_vs_plain_numpy_softmax(oracle, kvk):
     # independent double-precision restatement in numpy over the oracle's own dequant
     c = synth.make_case(oracle, kvk, rows=97, pos=[96, 40, 0], seed=11)
     out = oracle.attn_decode(c.q, c.k, c.v, kvk, c.pos)
     kd = oracle.kv_dequant(c.k, kvk, c.rows).astype(np.float64)
-    vd = oracle.kv_dequant(c.v, kvk, c.rows).astype(np.float64)
+    vd = oracle.kv_dequant(c.v, kvk, c.rows, is_v=True).astype(np.float64)
     for t, p in enumerate(c.pos):
         for h in range(24):
             s = kd[: p + 1, h // 6] @ c.q[t, h, :HD].astype(np.float64) / 16.0
