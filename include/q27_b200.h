@@ -256,6 +256,44 @@ int q27_attn_prefill_T_exact(const float* qT, int q_stride, int q_row,
                              int n_q_heads, int n_kv_heads, int head_dim, float scale,
                              void* stream, int kvk);
 
+/* ---- attention with the rotation folded in ---------------------------------------------
+ * For the kinds from Q27_KV_T3 up the reference brackets every attention call with two
+ * launches of its own: wht3 / wht_T forward on Q where the K side is rotated (turbo3, turbo5k:
+ * kv_k_rotated, src/cuda_common.h:59) and wht3 / wht_T inverse on the output wherever V is
+ * turbo3 (src/engine.cuh:1482-1506, src/spec3.cu:595-614, src/prefill.cu:2598-2618). The
+ * entries below take the UN-rotated Q and write the UN-rotated output: the forward rotation
+ * runs on the Q heads as the attention kernel stages them (the caller's Q buffer, its gate
+ * half included, is left as it was), the inverse on each output head in the kernel that
+ * normalises it (combine, fused finish, merge, prefill epilogue / fix-up). Each rotation is
+ * the same sequence of rounded operations as q27_wht3 / q27_wht_T, so the result equals the
+ * three-launch sequence bit for bit. For Q27_KV_F16 / Q27_KV_FP8 they are the plain entries.
+ * Arguments as for the entry each one is named after. */
+int q27_attn_decode3_wht(const q27_CP3* q, int q_stride, const void* const* ktab,
+                         const void* const* vtab, const q27_P3* out, float* scratch,
+                         const q27_IP3* pos, int max_ctx, int n_q_heads, int n_kv_heads,
+                         int head_dim, float scale, void* stream, int ntok, int kvk);
+/* exact != 0: the fp32 family (q27_attn_decode_batched_exact) */
+int q27_attn_decode_batched_wht(const q27_slot* slots, int nslots, int q_stride, int n_q_heads,
+                                int n_kv_heads, int head_dim, float scale, void* stream, int kvk,
+                                int exact);
+/* exact != 0: the scalar fp32 prefill (q27_attn_prefill_T_exact) */
+int q27_attn_prefill_T_wht(const float* qT, int q_stride, int q_row, const void* const* ktab,
+                           const void* const* vtab, float* outT, int out_row, float* part,
+                           int base_pos, int t0, int SB, int n_q_heads, int n_kv_heads,
+                           int head_dim, float scale, void* stream, int kvk, int exact);
+/* KV-sequence split: the partial side rotates Q, the merge side un-rotates the output */
+int q27_attn_decode_partial_wht(const q27_slot* slots, int nslots, int lanes_stride, int q_stride,
+                                int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                                float* partial_out, void* stream, int kvk);
+int q27_attn_merge_partials_wht(const float* parts, int nparts, int64_t npairs, float* out,
+                                void* stream, int kvk);
+int q27_attn_decode_partial_push_wht(const q27_slot* slots, int nslots, int lanes_stride,
+                                     int q_stride, int n_q_heads, int n_kv_heads, int head_dim,
+                                     float scale, void* const* mailboxes, int world, int rank,
+                                     unsigned epoch, void* stream, int kvk);
+int q27_attn_merge_pushed_wht(void* mailbox, int world, int64_t npairs, unsigned epoch, float* out,
+                              void* stream, int kvk);
+
 /* ---- KV formats -------------------------------------------------------------------- */
 
 /* Bit-exact dequantisation of cache rows [row0, row0+nrows) through a page table to fp32

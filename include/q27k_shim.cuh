@@ -80,6 +80,31 @@ inline void attn_decode3(CP3 q, int q_stride, const void* const* ktab, const voi
                    "attn_decode3");
 }
 
+// Extensions (no counterpart in the reference): attn_decode3 / attn_prefill_T with the two
+// rotation launches around them folded in. A call site of the form
+//     if (kv_k_rotated(kvk)) wht3(q, ..., false);  attn_decode3(q, ...);  if (kvk >= KV_T3) wht3(out, ..., true);
+// (src/engine.cuh:1482-1506) becomes one call with the UN-rotated q;
+// the q||gate buffer is left untouched and the output is bit for bit what the three calls give.
+inline void attn_decode3_wht(CP3 q, int q_stride, const void* const* ktab, const void* const* vtab,
+                             P3 out, float* scratch, IP3 pos, int max_ctx, int n_q_heads,
+                             int n_kv_heads, int head_dim, float scale, cudaStream_t st = 0,
+                             int ntok = 3, int kvk = KV_T3) {
+    q27_shim_check(q27_attn_decode3_wht(reinterpret_cast<const q27_CP3*>(&q), q_stride, ktab, vtab,
+                                        reinterpret_cast<const q27_P3*>(&out), scratch,
+                                        reinterpret_cast<const q27_IP3*>(&pos), max_ctx, n_q_heads,
+                                        n_kv_heads, head_dim, scale, st, ntok, kvk),
+                   "attn_decode3_wht");
+}
+inline void attn_prefill_T_wht(const float* qT, int q_stride, int q_row, const void* const* ktab,
+                               const void* const* vtab, float* outT, int out_row, float* part,
+                               int base_pos, int t0, int SB, int n_q_heads, int n_kv_heads,
+                               int head_dim, float scale, cudaStream_t st, int kvk = KV_T3) {
+    q27_shim_check(q27_attn_prefill_T_wht(qT, q_stride, q_row, ktab, vtab, outT, out_row, part,
+                                          base_pos, t0, SB, n_q_heads, n_kv_heads, head_dim, scale,
+                                          st, kvk, 0),
+                   "attn_prefill_T_wht");
+}
+
 // the explicit fp32 entry the reference's unit gate compares the default dispatch against
 inline void attn_decode3_fd2(CP3 q, int q_stride, const void* const* ktab,
                              const void* const* vtab, P3 out, float* scratch, IP3 pos,

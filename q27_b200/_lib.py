@@ -83,6 +83,16 @@ SIGNATURES = {
                                 _vp, _i]),
     "q27_attn_prefill_T_exact": (_i, [_vp, _i, _i, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i,
                                       _f, _vp, _i]),
+    "q27_attn_decode3_wht": (_i, [C.POINTER(P3), _i, _vp, _vp, C.POINTER(P3), _vp, C.POINTER(P3),
+                                  _i, _i, _i, _i, _f, _vp, _i, _i]),
+    "q27_attn_decode_batched_wht": (_i, [C.POINTER(Slot), _i, _i, _i, _i, _i, _f, _vp, _i, _i]),
+    "q27_attn_prefill_T_wht": (_i, [_vp, _i, _i, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _f,
+                                    _vp, _i, _i]),
+    "q27_attn_decode_partial_wht": (_i, [C.POINTER(Slot), _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _i]),
+    "q27_attn_merge_partials_wht": (_i, [_vp, _i, _i64, _vp, _vp, _i]),
+    "q27_attn_decode_partial_push_wht": (_i, [C.POINTER(Slot), _i, _i, _i, _i, _i, _i, _f,
+                                              C.POINTER(_vp), _i, _i, C.c_uint, _vp, _i]),
+    "q27_attn_merge_pushed_wht": (_i, [_vp, _i, _i64, C.c_uint, _vp, _vp, _i]),
     "q27_kv_dequant": (_i, [_vp, _i, _i, _i, _i, _vp, _vp]),
     "q27_kv_dequant_side": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp]),
     "q27_kv_store_T": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _i]),

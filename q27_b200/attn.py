@@ -47,19 +47,19 @@ def attn_decode(q, q_stride, ktab, vtab, out, scratch, d_pos, max_ctx, n_q_heads
 
 
 def attn_decode3(q_lanes, q_stride, ktab, vtab, out_lanes, scratch, pos_lanes, max_ctx,
-                 n_q_heads, n_kv_heads, head_dim, scale, st=None, ntok=3, kvk=0):
+                 n_q_heads, n_kv_heads, head_dim, scale, st=None, ntok=3, kvk=0, wht=False):
     """ntok lanes against one pass over the cache; lane t attends cache[0 .. *pos_lanes[t]].
 
     q_lanes / out_lanes / pos_lanes: sequences of per-lane tensors (the reference's CP3 /
-    P3 / IP3 bundles); entries beyond ntok are ignored."""
+    P3 / IP3 bundles); entries beyond ntok are ignored. ``wht``: Q comes un-rotated and the
+    output leaves un-rotated, the two rotations of the turbo kinds run inside the call."""
     q = _p3(q_lanes[:ntok])
     o = _p3(out_lanes[:ntok])
     p = _p3(pos_lanes[:ntok])
-    L.check(L.lib().q27_attn_decode3(C.byref(q), q_stride, ktab.data_ptr(), vtab.data_ptr(),
-                                     C.byref(o), scratch.data_ptr(), C.byref(p), max_ctx,
-                                     n_q_heads, n_kv_heads, head_dim, scale, stream_ptr(st),
-                                     ntok, kvk),
-            "q27_attn_decode3")
+    fn = L.lib().q27_attn_decode3_wht if wht else L.lib().q27_attn_decode3
+    L.check(fn(C.byref(q), q_stride, ktab.data_ptr(), vtab.data_ptr(), C.byref(o),
+               scratch.data_ptr(), C.byref(p), max_ctx, n_q_heads, n_kv_heads, head_dim, scale,
+               stream_ptr(st), ntok, kvk), "q27_attn_decode3")
 
 
 def attn_verify_partials(q_lanes, q_stride, ktab, vtab, part, pos_lanes, n_kv_heads, gqa, head_dim,
@@ -135,9 +135,14 @@ def _slots(slots) -> C.Array:
 
 
 def attn_decode_batched(slots, q_stride, n_q_heads, n_kv_heads, head_dim, scale, st=None, kvk=0,
-                        exact=False):
+                        exact=False, wht=False):
     """All slots in one launch; per-slot semantics of attn_decode3."""
     arr = _slots(slots)
+    if wht:
+        L.check(L.lib().q27_attn_decode_batched_wht(arr, len(slots), q_stride, n_q_heads,
+                                                    n_kv_heads, head_dim, scale, stream_ptr(st),
+                                                    kvk, int(exact)), "q27_attn_decode_batched_wht")
+        return
     fn = L.lib().q27_attn_decode_batched_exact if exact else L.lib().q27_attn_decode_batched
     L.check(fn(arr, len(slots), q_stride, n_q_heads, n_kv_heads, head_dim, scale, stream_ptr(st),
                kvk), "q27_attn_decode_batched")
@@ -150,56 +155,72 @@ class BatchedDecode:
     host is one foreign call."""
 
     def __init__(self, slots, q_stride, n_q_heads, n_kv_heads, head_dim, scale, kvk=0,
-                 exact=False):
+                 exact=False, wht=False):
         self._keep = list(slots)                 # the tensors behind the raw pointers
         self._arr = _slots(self._keep)
-        self._fn = (L.lib().q27_attn_decode_batched_exact if exact
+        self._fn = (L.lib().q27_attn_decode_batched_wht if wht
+                    else L.lib().q27_attn_decode_batched_exact if exact
                     else L.lib().q27_attn_decode_batched)
         self._args = (q_stride, n_q_heads, n_kv_heads, head_dim, scale)
-        self._kvk = kvk
+        self._tail = (kvk, int(exact)) if wht else (kvk,)
 
     def __call__(self, st=None):
-        L.check(self._fn(self._arr, len(self._keep), *self._args, stream_ptr(st), self._kvk),
+        L.check(self._fn(self._arr, len(self._keep), *self._args, stream_ptr(st), *self._tail),
                 "q27_attn_decode_batched")
 
 
 def attn_decode_partial(slots, lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim, scale,
-                        partial_out, st=None, kvk=0):
+                        partial_out, st=None, kvk=0, wht=False):
     """Un-normalised {m, l, acc} per (slot, lane, head) over each slot's row window."""
     arr = _slots(slots)
-    L.check(L.lib().q27_attn_decode_partial(arr, len(slots), lanes_stride, q_stride, n_q_heads,
-                                            n_kv_heads, head_dim, scale, partial_out.data_ptr(),
-                                            stream_ptr(st), kvk), "q27_attn_decode_partial")
+    fn = L.lib().q27_attn_decode_partial_wht if wht else L.lib().q27_attn_decode_partial
+    L.check(fn(arr, len(slots), lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim, scale,
+               partial_out.data_ptr(), stream_ptr(st), kvk), "q27_attn_decode_partial")
 
 
 def attn_decode_partial_push(slots, lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim, scale,
-                             mailboxes, rank, epoch, st=None, kvk=0):
+                             mailboxes, rank, epoch, st=None, kvk=0, wht=False):
     """attn_decode_partial whose result lands in slot ``rank`` of every rank's mailbox
     (``mailboxes``: device addresses, one per rank, as mapped in this process)."""
     import ctypes as C
     arr = slots if isinstance(slots, C.Array) else _slots(slots)
     boxes = (C.c_void_p * len(mailboxes))(*mailboxes)
-    L.check(L.lib().q27_attn_decode_partial_push(arr, len(arr), lanes_stride, q_stride, n_q_heads,
-                                                 n_kv_heads, head_dim, scale, boxes,
-                                                 len(mailboxes), rank, epoch, stream_ptr(st), kvk),
-            "q27_attn_decode_partial_push")
+    fn = L.lib().q27_attn_decode_partial_push_wht if wht else L.lib().q27_attn_decode_partial_push
+    L.check(fn(arr, len(arr), lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim, scale, boxes,
+               len(mailboxes), rank, epoch, stream_ptr(st), kvk), "q27_attn_decode_partial_push")
 
 
-def attn_merge_pushed(mailbox, world, npairs, epoch, out, st=None):
-    """Device-side wait for every rank's push of ``epoch``, then the LSE merge into out."""
-    L.check(L.lib().q27_attn_merge_pushed(mailbox, world, npairs, epoch, out.data_ptr(),
-                                          stream_ptr(st)), "q27_attn_merge_pushed")
+def attn_merge_pushed(mailbox, world, npairs, epoch, out, st=None, wht_kvk=None):
+    """Device-side wait for every rank's push of ``epoch``, then the LSE merge into out.
+    ``wht_kvk``: the cache kind, when the output rotation of that kind is to run here."""
+    if wht_kvk is None:
+        L.check(L.lib().q27_attn_merge_pushed(mailbox, world, npairs, epoch, out.data_ptr(),
+                                              stream_ptr(st)), "q27_attn_merge_pushed")
+    else:
+        L.check(L.lib().q27_attn_merge_pushed_wht(mailbox, world, npairs, epoch, out.data_ptr(),
+                                                  stream_ptr(st), wht_kvk), "q27_attn_merge_pushed_wht")
 
 
-def attn_merge_partials(parts, nparts, npairs, out, st=None):
+def attn_merge_partials(parts, nparts, npairs, out, st=None, wht_kvk=None):
     """LSE merge of ``nparts`` partial sets [nparts][npairs][258] -> out [npairs][256]."""
-    L.check(L.lib().q27_attn_merge_partials(parts.data_ptr(), nparts, npairs, out.data_ptr(),
-                                            stream_ptr(st)), "q27_attn_merge_partials")
+    if wht_kvk is None:
+        L.check(L.lib().q27_attn_merge_partials(parts.data_ptr(), nparts, npairs, out.data_ptr(),
+                                                stream_ptr(st)), "q27_attn_merge_partials")
+    else:
+        L.check(L.lib().q27_attn_merge_partials_wht(parts.data_ptr(), nparts, npairs,
+                                                    out.data_ptr(), stream_ptr(st), wht_kvk),
+                "q27_attn_merge_partials_wht")
 
 
 def attn_prefill_T(qT, q_stride, q_row, ktab, vtab, outT, out_row, part, base_pos, t0, SB,
-                   n_q_heads, n_kv_heads, head_dim, scale, st=None, kvk=0, exact=False):
+                   n_q_heads, n_kv_heads, head_dim, scale, st=None, kvk=0, exact=False, wht=False):
     """Causal GQA prefill attention for SB tokens starting at base_pos + t0."""
+    if wht:
+        L.check(L.lib().q27_attn_prefill_T_wht(
+            qT.data_ptr(), q_stride, q_row, ktab.data_ptr(), vtab.data_ptr(), outT.data_ptr(),
+            out_row, part.data_ptr() if part is not None else None, base_pos, t0, SB, n_q_heads,
+            n_kv_heads, head_dim, scale, stream_ptr(st), kvk, int(exact)), "q27_attn_prefill_T_wht")
+        return
     fn = L.lib().q27_attn_prefill_T_exact if exact else L.lib().q27_attn_prefill_T
     L.check(fn(qT.data_ptr(), q_stride, q_row, ktab.data_ptr(), vtab.data_ptr(), outT.data_ptr(),
                out_row, part.data_ptr() if part is not None else None, base_pos, t0, SB,

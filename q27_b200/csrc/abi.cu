@@ -8,6 +8,7 @@
 #include "p2p_exchange.cuh"
 #include "attn_umma.cuh"
 #include "decode_mma.cuh"
+#include "wht.cuh"
 
 namespace q27b {
 thread_local int g_last_cuda_error = 0;
@@ -78,6 +79,7 @@ int build_batch(const q27_slot* slots, int nslots, int q_stride, int n_q, int n_
     b.scale = scale;
     b.unit = 32;
     b.fuse = 0;
+    b.wht = 0;
     (void)total_lanes;
     return Q27_OK;
 }
@@ -90,11 +92,12 @@ thread_local cudaEvent_t g_ev_start = nullptr, g_ev_stop = nullptr;
 
 int run_decode(const q27_slot* slots, int nslots, int lanes_stride, int q_stride, int n_q, int n_kv,
                int head_dim, float scale, float* partial_out, void* stream, int kvk, Family fam,
-               const Peers* peers = nullptr) {
+               const Peers* peers = nullptr, int wht = 0) {
     DevBatch b;
     int rc = build_batch(slots, nslots, q_stride, n_q, n_kv, head_dim, scale, kvk,
                          partial_out == nullptr && peers == nullptr, b);
     if (rc) return rc;
+    b.wht = wht;
     if ((partial_out || peers) && (lanes_stride < b.max_ntok || lanes_stride > Q27_MAX_LANES))
         return Q27_ERR_INVALID_ARG;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -210,16 +213,33 @@ int64_t q27_prefill_part_floats(int SB, int n_q_heads) {
     return (int64_t)n_q_heads * ((SB + 15) / 16 * 16) * Q27_PF_SPLIT_MAX * Q27_PART_STRIDE;
 }
 
+static int decode3(const q27_CP3* q, int q_stride, const void* const* ktab,
+                   const void* const* vtab, const q27_P3* out, float* scratch, const q27_IP3* pos,
+                   int n_q_heads, int n_kv_heads, int head_dim, float scale, void* stream, int ntok,
+                   int kvk, int wht) {
+    if (!q || !out || !pos) return Q27_ERR_INVALID_ARG;
+    if (ntok < 1 || ntok > Q27_MAX_LANES) return Q27_ERR_UNSUPPORTED_WIDTH;
+    q27_slot s = single_slot(q, ktab, vtab, out, scratch, pos, ntok);
+    return run_decode(&s, 1, 0, q_stride, n_q_heads, n_kv_heads, head_dim, scale, nullptr, stream,
+                      kvk, FAM_AUTO, nullptr, wht);
+}
+
 int q27_attn_decode3(const q27_CP3* q, int q_stride, const void* const* ktab,
                      const void* const* vtab, const q27_P3* out, float* scratch,
                      const q27_IP3* pos, int max_ctx, int n_q_heads, int n_kv_heads,
                      int head_dim, float scale, void* stream, int ntok, int kvk) {
     (void)max_ctx;
-    if (!q || !out || !pos) return Q27_ERR_INVALID_ARG;
-    if (ntok < 1 || ntok > Q27_MAX_LANES) return Q27_ERR_UNSUPPORTED_WIDTH;
-    q27_slot s = single_slot(q, ktab, vtab, out, scratch, pos, ntok);
-    return run_decode(&s, 1, 0, q_stride, n_q_heads, n_kv_heads, head_dim, scale, nullptr, stream,
-                      kvk, FAM_AUTO);
+    return decode3(q, q_stride, ktab, vtab, out, scratch, pos, n_q_heads, n_kv_heads, head_dim,
+                   scale, stream, ntok, kvk, 0);
+}
+
+int q27_attn_decode3_wht(const q27_CP3* q, int q_stride, const void* const* ktab,
+                         const void* const* vtab, const q27_P3* out, float* scratch,
+                         const q27_IP3* pos, int max_ctx, int n_q_heads, int n_kv_heads,
+                         int head_dim, float scale, void* stream, int ntok, int kvk) {
+    (void)max_ctx;
+    return decode3(q, q_stride, ktab, vtab, out, scratch, pos, n_q_heads, n_kv_heads, head_dim,
+                   scale, stream, ntok, kvk, wht_flags_for(kvk));
 }
 
 int q27_attn_decode(const float* q, int q_stride, const void* const* ktab,
@@ -274,6 +294,13 @@ int q27_attn_decode_batched(const q27_slot* slots, int nslots, int q_stride, int
                       stream, kvk, FAM_AUTO);
 }
 
+int q27_attn_decode_batched_wht(const q27_slot* slots, int nslots, int q_stride, int n_q_heads,
+                                int n_kv_heads, int head_dim, float scale, void* stream, int kvk,
+                                int exact) {
+    return run_decode(slots, nslots, 0, q_stride, n_q_heads, n_kv_heads, head_dim, scale, nullptr,
+                      stream, kvk, exact ? FAM_EXACT : FAM_AUTO, nullptr, wht_flags_for(kvk));
+}
+
 int q27_attn_decode_batched_exact(const q27_slot* slots, int nslots, int q_stride, int n_q_heads,
                                   int n_kv_heads, int head_dim, float scale, void* stream,
                                   int kvk) {
@@ -289,47 +316,78 @@ int q27_attn_decode_partial(const q27_slot* slots, int nslots, int lanes_stride,
                       partial_out, stream, kvk, FAM_AUTO);
 }
 
-int q27_attn_merge_partials(const float* parts, int nparts, int64_t npairs, float* out,
-                            void* stream) {
+int q27_attn_decode_partial_wht(const q27_slot* slots, int nslots, int lanes_stride, int q_stride,
+                                int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                                float* partial_out, void* stream, int kvk) {
+    if (!partial_out) return Q27_ERR_INVALID_ARG;
+    return run_decode(slots, nslots, lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim, scale,
+                      partial_out, stream, kvk, FAM_AUTO, nullptr, wht_flags_for(kvk) & WHT_Q);
+}
+
+static int merge_partials(const float* parts, int nparts, int64_t npairs, float* out, void* stream,
+                          int wht) {
     if (!parts || !out || nparts < 1 || npairs < 0) return Q27_ERR_INVALID_ARG;
     if (npairs == 0) return Q27_OK;
     if (npairs > INT_MAX) return Q27_ERR_TOO_LARGE;
-    return launch_merge(parts, nparts, npairs, out, static_cast<cudaStream_t>(stream));
+    return launch_merge(parts, nparts, npairs, out, wht, static_cast<cudaStream_t>(stream));
+}
+
+int q27_attn_merge_partials(const float* parts, int nparts, int64_t npairs, float* out,
+                            void* stream) {
+    return merge_partials(parts, nparts, npairs, out, stream, 0);
+}
+
+int q27_attn_merge_partials_wht(const float* parts, int nparts, int64_t npairs, float* out,
+                                void* stream, int kvk) {
+    if (!kind_known(kvk)) return Q27_ERR_UNSUPPORTED_KIND;
+    return merge_partials(parts, nparts, npairs, out, stream, wht_flags_for(kvk) & WHT_OUT);
+}
+
+static int prefill_T(const float* qT, int q_stride, int q_row, const void* const* ktab,
+                     const void* const* vtab, float* outT, int out_row, float* part, int base_pos,
+                     int t0, int SB, int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                     void* stream, int kvk, bool exact, int wht) {
+    int rc = check_geometry(q_stride, n_q_heads, n_kv_heads, head_dim, kvk);
+    if (rc) return rc;
+    if (!qT || !ktab || !vtab || !outT || base_pos < 0 || t0 < 0 || SB < 0 ||
+        q_row < n_q_heads * HD || out_row < n_q_heads * HD)
+        return Q27_ERR_INVALID_ARG;
+    if (SB == 0) return Q27_OK;
+    if (!exact) {
+        bool done = false;
+        rc = launch_prefill_umma(qT, q_stride, q_row, ktab, vtab, outT, out_row, part, base_pos, t0,
+                                 SB, n_q_heads, n_kv_heads, scale, sm_count(),
+                                 static_cast<cudaStream_t>(stream), kvk, wht, &done);
+        if (rc || done) return rc;
+    }
+    return launch_prefill_exact(qT, q_stride, q_row, ktab, vtab, outT, out_row, base_pos, t0, SB,
+                                n_q_heads, n_kv_heads, scale, static_cast<cudaStream_t>(stream),
+                                kvk, wht);
 }
 
 int q27_attn_prefill_T_exact(const float* qT, int q_stride, int q_row, const void* const* ktab,
                              const void* const* vtab, float* outT, int out_row, float* part,
                              int base_pos, int t0, int SB, int n_q_heads, int n_kv_heads,
                              int head_dim, float scale, void* stream, int kvk) {
-    (void)part;
-    int rc = check_geometry(q_stride, n_q_heads, n_kv_heads, head_dim, kvk);
-    if (rc) return rc;
-    if (!qT || !ktab || !vtab || !outT || base_pos < 0 || t0 < 0 || SB < 0 ||
-        q_row < n_q_heads * HD || out_row < n_q_heads * HD)
-        return Q27_ERR_INVALID_ARG;
-    if (SB == 0) return Q27_OK;
-    return launch_prefill_exact(qT, q_stride, q_row, ktab, vtab, outT, out_row, base_pos, t0, SB,
-                                n_q_heads, n_kv_heads, scale, static_cast<cudaStream_t>(stream),
-                                kvk);
+    return prefill_T(qT, q_stride, q_row, ktab, vtab, outT, out_row, part, base_pos, t0, SB,
+                     n_q_heads, n_kv_heads, head_dim, scale, stream, kvk, true, 0);
 }
 
 int q27_attn_prefill_T(const float* qT, int q_stride, int q_row, const void* const* ktab,
                        const void* const* vtab, float* outT, int out_row, float* part,
                        int base_pos, int t0, int SB, int n_q_heads, int n_kv_heads,
                        int head_dim, float scale, void* stream, int kvk) {
-    int rc = check_geometry(q_stride, n_q_heads, n_kv_heads, head_dim, kvk);
-    if (rc) return rc;
-    if (!qT || !ktab || !vtab || !outT || base_pos < 0 || t0 < 0 || SB < 0 ||
-        q_row < n_q_heads * HD || out_row < n_q_heads * HD)
-        return Q27_ERR_INVALID_ARG;
-    if (SB == 0) return Q27_OK;
-    bool done = false;
-    rc = launch_prefill_umma(qT, q_stride, q_row, ktab, vtab, outT, out_row, part, base_pos, t0, SB,
-                             n_q_heads, n_kv_heads, scale, sm_count(),
-                             static_cast<cudaStream_t>(stream), kvk, &done);
-    if (rc || done) return rc;
-    return q27_attn_prefill_T_exact(qT, q_stride, q_row, ktab, vtab, outT, out_row, part, base_pos,
-                                    t0, SB, n_q_heads, n_kv_heads, head_dim, scale, stream, kvk);
+    return prefill_T(qT, q_stride, q_row, ktab, vtab, outT, out_row, part, base_pos, t0, SB,
+                     n_q_heads, n_kv_heads, head_dim, scale, stream, kvk, false, 0);
+}
+
+int q27_attn_prefill_T_wht(const float* qT, int q_stride, int q_row, const void* const* ktab,
+                           const void* const* vtab, float* outT, int out_row, float* part,
+                           int base_pos, int t0, int SB, int n_q_heads, int n_kv_heads,
+                           int head_dim, float scale, void* stream, int kvk, int exact) {
+    return prefill_T(qT, q_stride, q_row, ktab, vtab, outT, out_row, part, base_pos, t0, SB,
+                     n_q_heads, n_kv_heads, head_dim, scale, stream, kvk, exact != 0,
+                     wht_flags_for(kvk));
 }
 
 int q27_set_kernel_events(void* ev_start, void* ev_stop) {
@@ -394,10 +452,10 @@ size_t q27_xchg_mailbox_bytes(int world, int64_t npairs) {
     return xchg_mailbox_bytes(world, npairs);
 }
 
-int q27_attn_decode_partial_push(const q27_slot* slots, int nslots, int lanes_stride, int q_stride,
-                                 int n_q_heads, int n_kv_heads, int head_dim, float scale,
-                                 void* const* mailboxes, int world, int rank, unsigned epoch,
-                                 void* stream, int kvk) {
+static int partial_push(const q27_slot* slots, int nslots, int lanes_stride, int q_stride,
+                        int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                        void* const* mailboxes, int world, int rank, unsigned epoch, void* stream,
+                        int kvk, int wht) {
     if (!mailboxes || world < 1 || world > Q27_MAX_RANKS || rank < 0 || rank >= world)
         return Q27_ERR_INVALID_ARG;
     for (int r = 0; r < world; r++)
@@ -411,15 +469,44 @@ int q27_attn_decode_partial_push(const q27_slot* slots, int nslots, int lanes_st
     p.npairs = (int64_t)nslots * lanes_stride * n_q_heads;
     p.epoch = epoch;
     return run_decode(slots, nslots, lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim, scale,
-                      nullptr, stream, kvk, FAM_AUTO, &p);
+                      nullptr, stream, kvk, FAM_AUTO, &p, wht);
+}
+
+int q27_attn_decode_partial_push(const q27_slot* slots, int nslots, int lanes_stride, int q_stride,
+                                 int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                                 void* const* mailboxes, int world, int rank, unsigned epoch,
+                                 void* stream, int kvk) {
+    return partial_push(slots, nslots, lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim,
+                        scale, mailboxes, world, rank, epoch, stream, kvk, 0);
+}
+
+int q27_attn_decode_partial_push_wht(const q27_slot* slots, int nslots, int lanes_stride,
+                                     int q_stride, int n_q_heads, int n_kv_heads, int head_dim,
+                                     float scale, void* const* mailboxes, int world, int rank,
+                                     unsigned epoch, void* stream, int kvk) {
+    return partial_push(slots, nslots, lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim,
+                        scale, mailboxes, world, rank, epoch, stream, kvk,
+                        wht_flags_for(kvk) & WHT_Q);
+}
+
+static int merge_pushed(void* mailbox, int world, int64_t npairs, unsigned epoch, float* out,
+                        void* stream, int wht) {
+    if (!mailbox || !out || world < 1 || world > Q27_MAX_RANKS || npairs < 1 || (npairs & 1))
+        return Q27_ERR_INVALID_ARG;
+    if (npairs > INT_MAX) return Q27_ERR_TOO_LARGE;
+    return launch_merge_pushed(mailbox, world, npairs, epoch, out, wht,
+                               static_cast<cudaStream_t>(stream));
 }
 
 int q27_attn_merge_pushed(void* mailbox, int world, int64_t npairs, unsigned epoch, float* out,
                           void* stream) {
-    if (!mailbox || !out || world < 1 || world > Q27_MAX_RANKS || npairs < 1 || (npairs & 1))
-        return Q27_ERR_INVALID_ARG;
-    if (npairs > INT_MAX) return Q27_ERR_TOO_LARGE;
-    return launch_merge_pushed(mailbox, world, npairs, epoch, out, static_cast<cudaStream_t>(stream));
+    return merge_pushed(mailbox, world, npairs, epoch, out, stream, 0);
+}
+
+int q27_attn_merge_pushed_wht(void* mailbox, int world, int64_t npairs, unsigned epoch, float* out,
+                              void* stream, int kvk) {
+    if (!kind_known(kvk)) return Q27_ERR_UNSUPPORTED_KIND;
+    return merge_pushed(mailbox, world, npairs, epoch, out, stream, wht_flags_for(kvk) & WHT_OUT);
 }
 
 int q27_kv_dequant_side(const void* const* tab, int kvk, int is_v, int row0, int nrows,

@@ -6,6 +6,7 @@
 // against them on the GPU and against the CPU oracle.
 #include "common.cuh"
 #include "p2p_exchange.cuh"
+#include "wht.cuh"
 
 namespace q27b {
 
@@ -79,6 +80,10 @@ k_exact_partial(const __grid_constant__ DevBatch b) {
     __shared__ float s_shrink[GQA];
     for (int i = tid; i < GQA * HD; i += EX_THREADS)
         s_q[i / HD][i % HD] = S.q[t][(size_t)(kvh * GQA + i / HD) * b.q_stride + (i % HD)];
+    if (b.wht & WHT_Q) {                          // the forward rotation of wht3, in place
+        __syncthreads();
+        for (int gi = warp; gi < GQA * 2; gi += EX_THREADS / 32) wht_group<false>(&s_q[0][0] + gi * 128, lane);
+    }
 
     float m_run = NEG_SENTINEL, l_run = 0.f;      // head `warp` (warps 0..5), same in every lane
     float acc[GQA];                               // dimension `tid` of every head
@@ -206,6 +211,18 @@ __device__ __forceinline__ float combine_core(const float* __restrict__ pp, int 
     return a;
 }
 
+// The inverse rotation of wht3 on one output head held one dim per thread (threads 0..255 of a
+// block, every thread of the block calls): through shared memory, two warps, one group each.
+__device__ __forceinline__ float unrotate_head(float v) {
+    __shared__ float s_o[HD];
+    const int tid = threadIdx.x;
+    if (tid < HD) s_o[tid] = v;
+    __syncthreads();
+    if (tid < 64) wht_group<true>(s_o + (tid >> 5) * 128, tid & 31);
+    __syncthreads();
+    return tid < HD ? s_o[tid] : 0.f;
+}
+
 // Merge the nsplit partials of one (slot, lane, head). NORMALISE: write out = acc / l to the
 // lane's output row; otherwise write the merged {m, l, acc} for a cross-GPU merge.
 template <bool NORMALISE>
@@ -224,9 +241,11 @@ k_combine(const __grid_constant__ DevBatch b, float* __restrict__ partial_out, i
     }
     float mg, lg;
     const float a = combine_core(S.scratch + ((size_t)t * b.n_q + h) * b.nsplit * PART, b.nsplit, mg, lg);
+    float o = a * (lg > 0.f ? 1.0f / lg : 0.f);
+    if (NORMALISE && (b.wht & WHT_OUT)) o = unrotate_head(o);
     if (threadIdx.x < HD) {
         if (NORMALISE) {
-            S.out[t][(size_t)h * HD + threadIdx.x] = a * (lg > 0.f ? 1.0f / lg : 0.f);
+            S.out[t][(size_t)h * HD + threadIdx.x] = o;
         } else {
             float* d = partial_out + (((size_t)slot * lanes_stride + t) * b.n_q + h) * PART;
             d[2 + threadIdx.x] = a;
@@ -269,7 +288,8 @@ k_combine_push(const __grid_constant__ DevBatch b, const __grid_constant__ Peers
 
 // parts: [nparts][npairs][258] -> out [npairs][256] normalised
 __global__ void __launch_bounds__(256)
-k_merge(const float* __restrict__ parts, int nparts, int64_t npairs, float* __restrict__ out) {
+k_merge(const float* __restrict__ parts, int nparts, int64_t npairs, float* __restrict__ out,
+        int wht) {
     const int64_t w = blockIdx.x;
     float mg = NEG_SENTINEL;
     for (int s = 0; s < nparts; s++) mg = fmaxf(mg, parts[((size_t)s * npairs + w) * PART]);
@@ -279,14 +299,15 @@ k_merge(const float* __restrict__ parts, int nparts, int64_t npairs, float* __re
         if (pp[0] != NEG_SENTINEL) lg += pp[1] * expf(pp[0] - mg);
     }
     const float inv = lg > 0.f ? 1.0f / lg : 0.f;
-    for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-        float a = 0.f;
-        for (int s = 0; s < nparts; s++) {
-            const float* pp = parts + ((size_t)s * npairs + w) * PART;
-            if (pp[0] != NEG_SENTINEL) a += pp[2 + d] * expf(pp[0] - mg);
-        }
-        out[(size_t)w * HD + d] = a * inv;
+    const int d = threadIdx.x;                    // blockDim.x == HD
+    float a = 0.f;
+    for (int s = 0; s < nparts; s++) {
+        const float* pp = parts + ((size_t)s * npairs + w) * PART;
+        if (pp[0] != NEG_SENTINEL) a += pp[2 + d] * expf(pp[0] - mg);
     }
+    float o = a * inv;
+    if (wht & WHT_OUT) o = unrotate_head(o);
+    out[(size_t)w * HD + d] = o;
 }
 
 // Scalar causal prefill: one warp per (token, kv head), six heads per warp, rows read
@@ -297,11 +318,23 @@ __global__ void __launch_bounds__(PFX_WARPS * 32)
 k_prefill_exact(const float* __restrict__ qT, int q_stride, int q_row,
                 const void* const* __restrict__ ktab, const void* const* __restrict__ vtab,
                 float* __restrict__ outT, int out_row, int base_pos, int t0, int t_end, int n_kv,
-                float scale) {
+                float scale, int wht) {
+    __shared__ float s_rot[PFX_WARPS][HD];        // one head at a time, for the folded rotations
     const int kvh = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = t0 + blockIdx.y * PFX_WARPS + warp;
     if (t >= t_end) return;
+    // a head's 256 values, 8 per lane, through the rotation of wht_T and back
+    auto rotate8 = [&](float (&x)[8], bool inv) {
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; i++) s_rot[warp][8 * lane + i] = x[i];
+        __syncwarp();
+        if (inv) { wht_group<true>(s_rot[warp], lane); wht_group<true>(s_rot[warp] + 128, lane); }
+        else { wht_group<false>(s_rot[warp], lane); wht_group<false>(s_rot[warp] + 128, lane); }
+#pragma unroll
+        for (int i = 0; i < 8; i++) x[i] = s_rot[warp][8 * lane + i];
+    };
     const int bound = base_pos + t + 1;
     float qr[GQA][8], m[GQA], l[GQA], acc[GQA][8];
 #pragma unroll
@@ -313,6 +346,7 @@ k_prefill_exact(const float* __restrict__ qT, int q_stride, int q_row,
             acc[j][i] = 0.f;
             qr[j][i] = qT[(size_t)t * q_row + (size_t)(kvh * GQA + j) * q_stride + 8 * lane + i];
         }
+        if (wht & WHT_Q) rotate8(qr[j], false);
     }
     for (int p = 0; p < bound;) {
         const int pg = p >> PAGE_SHIFT;
@@ -344,8 +378,11 @@ k_prefill_exact(const float* __restrict__ qT, int q_stride, int q_row,
     for (int j = 0; j < GQA; j++) {
         const float inv = 1.0f / l[j];
 #pragma unroll
+        for (int i = 0; i < 8; i++) acc[j][i] *= inv;
+        if (wht & WHT_OUT) rotate8(acc[j], true);
+#pragma unroll
         for (int i = 0; i < 8; i++)
-            outT[(size_t)t * out_row + (size_t)(kvh * GQA + j) * HD + 8 * lane + i] = acc[j][i] * inv;
+            outT[(size_t)t * out_row + (size_t)(kvh * GQA + j) * HD + 8 * lane + i] = acc[j][i];
     }
 }
 
@@ -380,8 +417,9 @@ int launch_combine_push(const DevBatch& b, const Peers& peers, int lanes_stride,
     return Q27_OK;
 }
 
-int launch_merge(const float* parts, int nparts, int64_t npairs, float* out, cudaStream_t st) {
-    k_merge<<<(unsigned)npairs, 256, 0, st>>>(parts, nparts, npairs, out);
+int launch_merge(const float* parts, int nparts, int64_t npairs, float* out, int wht,
+                 cudaStream_t st) {
+    k_merge<<<(unsigned)npairs, HD, 0, st>>>(parts, nparts, npairs, out, wht);
     Q27_CUDA_TRY(cudaGetLastError());
     Q27_COUNT_LAUNCH();
     return Q27_OK;
@@ -389,13 +427,13 @@ int launch_merge(const float* parts, int nparts, int64_t npairs, float* out, cud
 
 int launch_prefill_exact(const float* qT, int q_stride, int q_row, const void* const* ktab,
                          const void* const* vtab, float* outT, int out_row, int base_pos, int t0,
-                         int SB, int n_q, int n_kv, float scale, cudaStream_t st, int kvk) {
+                         int SB, int n_q, int n_kv, float scale, cudaStream_t st, int kvk, int wht) {
     (void)n_q;
     dim3 grid(n_kv, (SB + PFX_WARPS - 1) / PFX_WARPS);
     const int te = t0 + SB;
 #define Q27_LAUNCH(KF, VF)                                        \
     k_prefill_exact<KF, VF><<<grid, PFX_WARPS * 32, 0, st>>>(     \
-        qT, q_stride, q_row, ktab, vtab, outT, out_row, base_pos, t0, te, n_kv, scale)
+        qT, q_stride, q_row, ktab, vtab, outT, out_row, base_pos, t0, te, n_kv, scale, wht)
     Q27_FOR_KIND(kvk, Q27_LAUNCH, return Q27_ERR_UNSUPPORTED_KIND)
 #undef Q27_LAUNCH
     Q27_CUDA_TRY(cudaGetLastError());

@@ -22,6 +22,7 @@
 // Every mbarrier wait is bounded; a timeout sets the library's flag and the CTA drains.
 #include "attn_umma.cuh"
 #include "t3_lut.cuh"
+#include "wht.cuh"
 
 namespace q27b {
 
@@ -211,6 +212,7 @@ struct TileArgs {
     // to part[((head * part_rows + (t - t0)) * PF_SPLIT_MAX + piece) * 258] for the fix-up
     float* part;
     int part_rows, nx, n_full, pieces;
+    int wht;            // WHT_Q: rotate the Q rows as they are staged; WHT_OUT: un-rotate the output rows
 };
 constexpr int PF_SPLIT_MAX = 8;   // pieces a row's scratch has room for (src/prefill.cuh:88)
 
@@ -330,10 +332,11 @@ __device__ __forceinline__ void half_store(const RawHalf<KVK>& t, uint8_t* dst, 
 template <int KVK, int MODE>
 __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* const* ktab,
                                           const void* const* vtab, int n_kv, float scale,
-                                          uint8_t* smem_raw) {
+                                          int wht, uint8_t* smem_raw) {
     uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = reinterpret_cast<uint64_t*>(base);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + 512);
+    uint32_t* epi_bad = tmem_slot + 1;  // a softmax warp gave up waiting: no folded output rotation
     uint8_t* q_sm = base + SMEM_BAR;
     uint8_t* k_sm = q_sm + Q_BYTES;
     uint8_t* v_sm = k_sm + K_SLOTS * KT_BYTES;
@@ -353,6 +356,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     const int ntiles = (pb.hi - pb.lo + BN - 1) / BN;
 
     if (threadIdx.x == 0) {
+        *epi_bad = 0;
         for (int s = 0; s < KSL; s++) {
             bar_init(k_full + 8 * s, NPROD);
             bar_init(k_empty + 8 * s, 1);
@@ -384,6 +388,24 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         // of two [128][128 B] swizzled blocks; dims 0..127 wait in the (still idle) K ring
         // for the thread that owns TMEM lane r.
         constexpr int QT_PITCH = 264;                       // bytes per row of the waiting half
+        // Folded forward rotation (wht3 / wht_T on Q, src/spec3.cu:595-614,
+        // src/prefill.cu:2598-2618): the tile's rows first land as fp32 in the idle third K slot
+        // and V ring, every warp rotates its share of the 128-groups in place, and the loop
+        // below converts from there instead of from global memory.
+        const float4* q_rot4 = reinterpret_cast<const float4*>(k_sm + 2 * KT_BYTES);
+        static_assert((K_SLOTS - 2 + V_SLOTS) * KT_BYTES >= BM * HD * 4, "room for the fp32 Q tile");
+        static_assert(2 * KT_BYTES >= BM * QT_PITCH, "the waiting half stays clear of it");
+        if (wht & WHT_Q) {
+            float* q_rot = reinterpret_cast<float*>(k_sm + 2 * KT_BYTES);
+            for (int i = threadIdx.x; i < BM * (HD / 4); i += UMMA_THREADS) {
+                const RowInfo rq = pb.row(i >> 6);
+                if (rq.q) reinterpret_cast<float4*>(q_rot)[i] = __ldg(reinterpret_cast<const float4*>(rq.q) + (i & 63));
+            }
+            __syncthreads();
+            for (int gi = warp; gi < 2 * BM; gi += UMMA_THREADS / 32)
+                if (pb.row(gi >> 1).q) wht_group<false>(q_rot + gi * 128, lane);
+            __syncthreads();
+        }
         for (int base_i = 0; base_i < BM * (HD / 4); base_i += UMMA_THREADS * 4) {
             float4 v[4];
             int idx[4];
@@ -393,7 +415,9 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (idx[u] < BM * (HD / 4)) {
                     const RowInfo rq = pb.row(idx[u] >> 6);
-                    if (rq.q) v[u] = __ldg(reinterpret_cast<const float4*>(rq.q) + (idx[u] & 63));
+                    if (rq.q)
+                        v[u] = (wht & WHT_Q) ? q_rot4[idx[u]]
+                                             : __ldg(reinterpret_cast<const float4*>(rq.q) + (idx[u] & 63));
                 }
             }
 #pragma unroll
@@ -526,6 +550,14 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         if (ok) ok = bar_wait(pvb + 8 * ((ntiles - 1) % S_BUFS), (uint32_t)(((ntiles - 1) / S_BUFS) & 1));
         ok = __all_sync(0xffffffffu, ok);
         tc_fence_after();
+        // Folded inverse rotation (wht_T on the output rows): the normalised rows go to the idle
+        // rings instead of global memory, and after the closing barrier every warp rotates and
+        // writes its share. (Rows of a split item go to the fix-up kernel, which rotates.)
+        constexpr int OROT_PITCH = HD + 4;          // floats: float4-aligned, rows 4 banks apart
+        static_assert((K_SLOTS + V_SLOTS) * KT_BYTES >= BM * OROT_PITCH * 4, "room for the fp32 O tile");
+        float* o_rot = reinterpret_cast<float*>(k_sm);
+        const bool rot_out = MODE == 0 && (wht & WHT_OUT) && pb.piece < 0;
+        if (!ok && rot_out) *epi_bad = 1;
         if (ok) {
             const float inv = l > 0.f ? 1.f / l : 0.f;
             if (ri.part) {
@@ -547,10 +579,11 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                     auto reg = [](int n) {
                         return KVK == Q27_KV_T3 ? (n & 16) + ((n & 1) ? 8 + ((n & 15) >> 1) : ((n & 15) >> 1)) : n;
                     };
+                    float* dst = rot_out ? o_rot + (size_t)r * OROT_PITCH : ri.out;
                     if (ri.out) {
 #pragma unroll
                         for (int e = 0; e < 32; e += 4)
-                            *reinterpret_cast<float4*>(ri.out + c + e) =
+                            *reinterpret_cast<float4*>(dst + c + e) =
                                 make_float4(o[reg(e)] * inv, o[reg(e + 1)] * inv, o[reg(e + 2)] * inv,
                                             o[reg(e + 3)] * inv);
                     } else if (ri.part) {
@@ -801,6 +834,17 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "n"(TMEM_COLS) : "memory");
     }
+    if (MODE == 0 && (wht & WHT_OUT) && pb.piece < 0 && *epi_bad == 0) {
+        constexpr int OROT_PITCH = HD + 4;
+        float* o_rot = reinterpret_cast<float*>(k_sm);
+        for (int gi = warp; gi < 2 * BM; gi += UMMA_THREADS / 32) {
+            const RowInfo ri = pb.row(gi >> 1);
+            if (!ri.out) continue;
+            float* x = o_rot + (size_t)(gi >> 1) * OROT_PITCH + (gi & 1) * 128;
+            wht_group<true>(x, lane);
+            reinterpret_cast<float4*>(ri.out + (gi & 1) * 128)[lane] = reinterpret_cast<const float4*>(x)[lane];
+        }
+    }
 }
 
 template <int KVK>
@@ -837,12 +881,13 @@ k_prefill_umma(const __grid_constant__ TileArgs a) {
             return;
         }
     }
-    attn_tile<KVK, 0>(pb, a.ktab, a.vtab, a.n_kv, a.scale, smem_raw);
+    attn_tile<KVK, 0>(pb, a.ktab, a.vtab, a.n_kv, a.scale, a.wht, smem_raw);
 }
 
 // Merge the pieces of the split items: one block per (item, token), thread = dim, six heads.
 __global__ void __launch_bounds__(HD)
 k_prefill_fixup(const __grid_constant__ TileArgs a) {
+    __shared__ float s_o[HD];
     pdl_wait();
     const int item = a.n_full + blockIdx.y;
     const int kvh = item / a.nx;
@@ -862,7 +907,16 @@ k_prefill_fixup(const __grid_constant__ TileArgs a) {
             lg += pp[(size_t)p * PART + 1] * w;
             acc += pp[(size_t)p * PART + 2 + threadIdx.x] * w;
         }
-        a.outT[(size_t)t * a.out_row + (size_t)h * HD + threadIdx.x] = lg > 0.f ? acc / lg : 0.f;
+        float o = lg > 0.f ? acc / lg : 0.f;
+        if (a.wht & WHT_OUT) {                    // the folded inverse rotation of wht_T on this head
+            __syncthreads();
+            s_o[threadIdx.x] = o;
+            __syncthreads();
+            if (threadIdx.x < 64) wht_group<true>(s_o + (threadIdx.x >> 5) * 128, threadIdx.x & 31);
+            __syncthreads();
+            o = s_o[threadIdx.x];
+        }
+        a.outT[(size_t)t * a.out_row + (size_t)h * HD + threadIdx.x] = o;
     }
 }
 
@@ -893,7 +947,7 @@ k_verify_umma(const __grid_constant__ DevBatch b) {
         }
         return;
     }
-    attn_tile<KVK, 1>(pb, S.ktab, S.vtab, b.n_kv, b.scale, smem_raw);
+    attn_tile<KVK, 1>(pb, S.ktab, S.vtab, b.n_kv, b.scale, b.wht, smem_raw);
 }
 
 template <int KVK>
@@ -913,7 +967,7 @@ int set_attrs() {
 int launch_prefill_umma(const float* qT, int q_stride, int q_row, const void* const* ktab,
                         const void* const* vtab, float* outT, int out_row, float* part,
                         int base_pos, int t0, int SB, int n_q, int n_kv, float scale,
-                        int sm_count, cudaStream_t st, int kvk, bool* done) {
+                        int sm_count, cudaStream_t st, int kvk, int wht, bool* done) {
     *done = false;
     if (kind_known(kvk) && !kind_has_tensor_path(kvk)) return Q27_OK;   // served by the fp32 family
     (void)n_q;
@@ -921,7 +975,7 @@ int launch_prefill_umma(const float* qT, int q_stride, int q_row, const void* co
     if ((q_stride & 3) || (q_row & 3) || (out_row & 3) || ((uintptr_t)qT & 15) || ((uintptr_t)outT & 15))
         return Q27_OK;
     TileArgs a{qT, ktab, vtab, outT, q_stride, q_row, out_row, base_pos, t0, t0 + SB, n_kv, scale,
-               part, (SB + 15) / 16 * 16, (SB + TOK_PER_TILE - 1) / TOK_PER_TILE, 0, 1};
+               part, (SB + 15) / 16 * 16, (SB + TOK_PER_TILE - 1) / TOK_PER_TILE, 0, 1, wht};
     // One CTA per SM: the items beyond the last full wave would hold the machine for a whole
     // item time at partial occupancy. They are cut into P key ranges each when that pays: a
     // piece costs its share of the item's tiles plus a fixed ~32 tile-times (measured: pipeline

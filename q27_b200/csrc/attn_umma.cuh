@@ -9,7 +9,7 @@ namespace q27b {
 int launch_prefill_umma(const float* qT, int q_stride, int q_row, const void* const* ktab,
                         const void* const* vtab, float* outT, int out_row, float* part,
                         int base_pos, int t0, int SB, int n_q, int n_kv, float scale,
-                        int sm_count, cudaStream_t st, int kvk, bool* done);
+                        int sm_count, cudaStream_t st, int kvk, int wht, bool* done);
 
 // Writes split-KV partials for every lane of every slot in ONE pass over the cache per
 // (slot, kv head, split); fills b.nsplit / b.unit for the combine. force_nsplit > 0 fixes the

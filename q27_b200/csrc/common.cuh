@@ -96,6 +96,8 @@ struct DevBatch {
     float scale;
     int unit;       // split granularity in rows (chunk is a multiple of it)
     int fuse;       // the partial kernel also merges the splits and writes the output rows
+    int wht;        // rotation folded into the call (WHT_Q: Q heads as they are staged;
+                    // WHT_OUT: output heads before they are written); 0 = the plain entries
 };
 static_assert(sizeof(DevBatch) <= 4000, "DevBatch must fit the kernel parameter space");
 
@@ -253,18 +255,19 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 int launch_combine(const DevBatch& b, float* partial_out, int lanes_stride, cudaStream_t st);
-int launch_merge(const float* parts, int nparts, int64_t npairs, float* out, cudaStream_t st);
+int launch_merge(const float* parts, int nparts, int64_t npairs, float* out, int wht,
+                 cudaStream_t st);
 // peer-memory exchange of partials (p2p_exchange.cu)
 size_t xchg_mailbox_bytes(int world, int64_t npairs);
 struct Peers;
 int launch_combine_push(const DevBatch& b, const Peers& peers, int lanes_stride, cudaStream_t st);
 int launch_merge_pushed(void* box, int world, int64_t npairs, uint32_t epoch, float* out,
-                        cudaStream_t st);
+                        int wht, cudaStream_t st);
 int read_xchg_timeout_flag(int* out);
 int read_umma_timeout_flag(int* out);
 int launch_prefill_exact(const float* qT, int q_stride, int q_row, const void* const* ktab,
                          const void* const* vtab, float* outT, int out_row, int base_pos, int t0,
-                         int SB, int n_q, int n_kv, float scale, cudaStream_t st, int kvk);
+                         int SB, int n_q, int n_kv, float scale, cudaStream_t st, int kvk, int wht);
 int launch_kv_dequant(const void* const* tab, int fmt, int row0, int nrows, int n_kv, float* out,
                       cudaStream_t st);
 int launch_kv_store_T(const float* kT, const float* vT, void* const* ktab, void* const* vtab,

@@ -32,6 +32,7 @@
 
 #include "decode_mma.cuh"
 #include "t3_lut.cuh"
+#include "wht.cuh"
 
 namespace q27b {
 
@@ -733,6 +734,12 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
                 reinterpret_cast<float4*>(q_stage)[i] = __ldg(reinterpret_cast<const float4*>(
                     S.q[t] + (size_t)(kvh0 * GQA + h) * b.q_stride) + d4);
             }
+            if (b.wht & WHT_Q) {
+                // the forward rotation of wht3 (src/spec3.cu:595-614) on the staged heads, a
+                // 128-group per warp at a time, while the producer is already filling the ring
+                asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32));
+                for (int gi = warp; gi < NHEADS * 2; gi += NCW) wht_group<false>(q_stage + gi * 128, lane);
+            }
             // Rows past the end of a ragged last stage are never copied; their weights are exact
             // zeros, so what the ring holds there only has to decode to finite numbers. Any
             // turbo3 byte pattern decodes to a centroid (its norms are masked). fp16 / fp8
@@ -905,8 +912,11 @@ int launch_one(DevBatch& b, int sm_count, bool may_fuse, cudaStream_t st) {
     // Small launches finish in this kernel: the last CTA of a (slot, lane, kv group) merges
     // the group's partials, if they are few enough for one SM to pull through in about the
     // time a second launch would cost. The ticket words sit behind split 64 of the scratch.
+    // (A call that also un-rotates its output leaves the merge to the combine kernel, which
+    // holds that rotation; the turbo3 layout, 24 heads per CTA, is past the byte limit anyway.)
     b.fuse = 0;
-    if (may_fuse && ns <= FUSE_MAX_SPLITS && F::KVH * GQA * ns * PART * 4 <= FUSE_MAX_BYTES) {
+    if (may_fuse && !(b.wht & WHT_OUT) && ns <= FUSE_MAX_SPLITS &&
+        F::KVH * GQA * ns * PART * 4 <= FUSE_MAX_BYTES) {
         b.fuse = 1;
         for (int i = 0; i < b.nslots; i++)
             if ((uintptr_t)b.s[i].scratch & 15) b.fuse = 0;   // bulk copies out of the scratch

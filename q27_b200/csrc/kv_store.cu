@@ -16,58 +16,16 @@
 // of each 64 dims, rounds absmax/127 to fp16 and quantises with the reciprocal of the ROUNDED
 // scale (i8g64_quant_group, src/i8g64.cuh:48-64) -- order-independent, hence exact.
 #include "common.cuh"
+#include "wht.cuh"
 
 namespace q27b {
 namespace {
-
-constexpr float INV_SQRT_128 = 0.08838834764831845f;
-__device__ __forceinline__ float sgn(const uint32_t* m, int j) {
-    return (m[j >> 5] >> (j & 31)) & 1u ? -1.f : 1.f;
-}
 
 __device__ __forceinline__ int t3_nearest(float v) { // src/turbo3.cuh:57-66
     int idx = 0;
 #pragma unroll
     for (int i = 0; i < 7; i++) idx += v < kT3Midpoint[i] ? 0 : 1;   // thresholds ascend
     return idx;
-}
-
-// 128-point butterfly over a warp's shared buffer: element pairs (j, j^h), lo+hi / lo-hi.
-// Every output is one add or subtract of two fixed inputs, so the result does not depend
-// on how the work is distributed: bitwise equal to the serial loop.
-__device__ __forceinline__ void butterfly128(float* x, int lane) {
-#pragma unroll
-    for (int h = 1; h < 128; h <<= 1) {
-        __syncwarp();
-        float v[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int j = lane + 32 * i;
-            const float a = x[j], b = x[j ^ h];
-            v[i] = (j & h) ? __fsub_rn(b, a) : __fadd_rn(a, b);
-        }
-        __syncwarp();
-#pragma unroll
-        for (int i = 0; i < 4; i++) x[lane + 32 * i] = v[i];
-    }
-    __syncwarp();
-}
-
-// forward rotation of one group in place: x *= s1; butterfly; x *= inv_sqrt*s2 (t3_fwht)
-template <bool INV>
-__device__ __forceinline__ void wht_group(float* x, int lane) {
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int j = lane + 32 * i;
-        x[j] = __fmul_rn(x[j], sgn(INV ? kS2Neg : kS1Neg, j));
-    }
-    butterfly128(x, lane);
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int j = lane + 32 * i;
-        x[j] = __fmul_rn(x[j], __fmul_rn(INV_SQRT_128, sgn(INV ? kS1Neg : kS2Neg, j)));
-    }
-    __syncwarp();
 }
 
 constexpr int ST_WARPS = 8;

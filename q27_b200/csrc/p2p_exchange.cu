@@ -11,6 +11,7 @@
 // slow peer (it cannot be two ahead: its own merge of step e+1 needs the peer's push of e+1,
 // which the peer issues after its merge of step e).
 #include "p2p_exchange.cuh"
+#include "wht.cuh"
 
 namespace q27b {
 
@@ -21,7 +22,7 @@ __device__ int g_xchg_timeout_flag = 0;
 // box: this rank's own mailbox. out [npairs][256] normalised.
 __global__ void __launch_bounds__(256)
 k_merge_pushed(uint8_t* __restrict__ box, int world, int64_t npairs, uint32_t epoch_given,
-               float* __restrict__ out) {
+               float* __restrict__ out, int wht) {
     pdl_wait();                  // this rank's own rows come from the kernel before this one
     const uint32_t epoch = xchg_epoch(box, world, npairs, epoch_given);
     const int par = epoch & 1;
@@ -39,8 +40,9 @@ k_merge_pushed(uint8_t* __restrict__ box, int world, int64_t npairs, uint32_t ep
         if (!got) { s_ok = 0; atomicExch(&g_xchg_timeout_flag, 4); }
     }
     __syncthreads();
-    const bool ok = s_ok != 0;
+    const bool ok = s_ok != 0;                    // the same in every thread of the block
     const int64_t w = blockIdx.x;
+    __shared__ float s_o[HD];
     if (ok) {
         const float* parts = reinterpret_cast<const float*>(box) + (size_t)par * xchg_data_floats(world, npairs);
         float mg = NEG_SENTINEL;
@@ -52,15 +54,22 @@ k_merge_pushed(uint8_t* __restrict__ box, int world, int64_t npairs, uint32_t ep
             if (ms != NEG_SENTINEL) lg += __ldcg(pp + 1) * expf(ms - mg);
         }
         const float inv = lg > 0.f ? 1.0f / lg : 0.f;
-        for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-            float a = 0.f;
-            for (int s = 0; s < world; s++) {
-                const float* pp = parts + ((size_t)s * npairs + w) * PART;
-                const float ms = __ldcg(pp);
-                if (ms != NEG_SENTINEL) a += __ldcg(pp + 2 + d) * expf(ms - mg);
-            }
-            out[(size_t)w * HD + d] = a * inv;
+        const int d = threadIdx.x;                // blockDim.x == HD
+        float a = 0.f;
+        for (int s = 0; s < world; s++) {
+            const float* pp = parts + ((size_t)s * npairs + w) * PART;
+            const float ms = __ldcg(pp);
+            if (ms != NEG_SENTINEL) a += __ldcg(pp + 2 + d) * expf(ms - mg);
         }
+        float o = a * inv;
+        if (wht & WHT_OUT) {                      // the inverse rotation of wht3 on this head
+            s_o[d] = o;
+            __syncthreads();
+            if (d < 64) wht_group<true>(s_o + (d >> 5) * 128, d & 31);
+            __syncthreads();
+            o = s_o[d];
+        }
+        out[(size_t)w * HD + d] = o;
     }
     // Every block, timed out or not, counts itself (a block that gave up adds a mark in the
     // upper half), so the counter always returns to zero. The last block records the exchange
@@ -86,10 +95,10 @@ size_t xchg_mailbox_bytes(int world, int64_t npairs) {
 }
 
 int launch_merge_pushed(void* box, int world, int64_t npairs, uint32_t epoch, float* out,
-                        cudaStream_t st) {
+                        int wht, cudaStream_t st) {
     if (npairs > 0xffff) return Q27_ERR_TOO_LARGE;   // the block counter keeps 16 bits
-    Q27_CUDA_TRY(launch_pdl(k_merge_pushed, dim3((unsigned)npairs), dim3(256), 0, st,
-                            static_cast<uint8_t*>(box), world, npairs, epoch, out));
+    Q27_CUDA_TRY(launch_pdl(k_merge_pushed, dim3((unsigned)npairs), dim3(HD), 0, st,
+                            static_cast<uint8_t*>(box), world, npairs, epoch, out, wht));
     return Q27_OK;
 }
 
