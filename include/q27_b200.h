@@ -352,6 +352,18 @@ int q27_kv_store_t3(const q27_CP3* k, const q27_CP3* v, void* const* ktab, void*
 int q27_wht3(const q27_P3* x, int n_heads, int head_dim, int stride, int inv, void* stream,
              int ntok);
 
+/* The stores above on a cache split by rows over several GPUs (any kind): every GPU runs the
+ * same call on the same lanes / chunk rows with its own tables and its own range of logical
+ * rows [row_base, row_base + row_count); a row is encoded and written by the GPU that owns it
+ * (at row - row_base of its tables) and skipped by the others, the decision taken on the
+ * device from the positions the lanes point at. No row crosses a link. */
+int q27_kv_store_lanes_shard(const q27_CP3* k, const q27_CP3* v, void* const* ktab,
+                             void* const* vtab, const q27_IP3* pos, int n_kv_heads, int head_dim,
+                             void* stream, int ntok, int kvk, int row_base, int row_count);
+int q27_kv_store_rows_shard(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
+                            int base_pos, int n_kv_heads, int head_dim, int T, void* stream,
+                            int kvk, int row_base, int row_count);
+
 /* mk_tab (src/test_kernels.cu:27-36): fill a DEVICE table of ceil(rows/64) entries with
  * identity page pointers over a contiguous buffer. d_tab is caller-allocated. */
 int q27_mk_tab(const void* base, size_t row_bytes, int rows, void** d_tab, void* stream);
@@ -371,6 +383,66 @@ void* q27_kvpool_page_ptr(const q27_kvpool* pool, int side, int idx);
 /* pops n page indices into out_idx; returns 0 (and pops nothing) if fewer are free */
 int q27_kvpool_reserve(q27_kvpool* pool, int side, int n, int* out_idx);
 void q27_kvpool_release(q27_kvpool* pool, int side, const int* idx, int n);
+
+/* ---- lineages: pooled pages of one conversation (src/engine.cuh:781-845) ---------------
+ * A lineage owns pool pages per side and per cache pair (one pair per attention layer plus
+ * any extra pair of the caller's, e.g. the draft head's) and keeps the device page tables
+ * [2][pairs][ceil(max_rows/64)] the attention and store entries read. On a cache sharded by
+ * rows over several GPUs each GPU runs one lineage over its own rows. Allocation happens at
+ * creation only; entitle / release just move page indices and rewrite table entries (the
+ * table POINTERS stay fixed, so captured graphs that hold them stay valid). */
+typedef struct q27_kvlineage q27_kvlineage;
+q27_kvlineage* q27_kvlineage_create(q27_kvpool* pool, int pairs, int max_rows);
+void q27_kvlineage_destroy(q27_kvlineage* l);          /* returns its pages to the pool */
+/* kv_entitle: make rows [0, rows + extra[pair]) of every pair addressable (extra may be NULL).
+ * All or nothing: 1 = mapped (table upload enqueued on `stream`), 0 = the pool lacks pages
+ * and nothing changed, -1 = invalid argument. Entries past the last owned page alias the
+ * pair's first page. Never shrinks. */
+int q27_kvlineage_entitle(q27_kvlineage* l, int rows, const int* extra, void* stream);
+/* kv_release_for_takeover: every page back to the pool; the tables keep stale but valid
+ * addresses until the next entitle. */
+void q27_kvlineage_release(q27_kvlineage* l);
+int q27_kvlineage_rows(const q27_kvlineage* l);
+int q27_kvlineage_npages(const q27_kvlineage* l);
+int q27_kvlineage_pages_of(const q27_kvlineage* l, int side, int pair);
+/* device page table of one (side, pair): what ktab / vtab of the attention entries take */
+const void* const* q27_kvlineage_tab(const q27_kvlineage* l, int side, int pair);
+/* kv_row_host (src/engine.cuh:840-845): device address of row r, from the host mirror */
+void* q27_kvlineage_row(const q27_kvlineage* l, int side, int pair, int r);
+
+/* ---- KV section of a prefix snapshot (pfx_export / pfx_import, src/engine.cuh:3786-3857) --
+ * Blob layout: for each pair in order, K rows [0, n) then V rows [0, n), n = nrows +
+ * extra[pair], rows in logical order whatever pages they live in -- so a blob is portable
+ * across pool geometries, page scatter and the number of GPUs a cache is sharded over. Export
+ * reads rows [row0, row0 + n) of this lineage (its local rows); `blob` is device-accessible
+ * memory, 16-byte aligned, q27_kv_snapshot_bytes long. One kernel per call. */
+#define Q27_SNAPSHOT_MAX_PAIRS 64
+int64_t q27_kv_snapshot_bytes(int pairs, int nrows, const int* extra, size_t k_row, size_t v_row);
+int q27_kv_snapshot_export(const q27_kvlineage* l, int row0, int nrows, const int* extra,
+                           void* blob, void* stream);
+int q27_kv_snapshot_import(q27_kvlineage* l, int row0, int nrows, const int* extra,
+                           const void* blob, void* stream);
+
+/* Identity of a snapshot (src/prefix_cache.h:44-82): FNV-1a over bytes (seed = the FNV offset
+ * basis for a fresh hash), the compatibility hash over model path / size / geometry / KV kind
+ * / format version, and the fixed 64-byte file header that precedes the L tokens and the
+ * state bytes. Host-only. */
+#define Q27_PFX_FNV_SEED 1469598103934665603ULL
+#define Q27_PFX_MAGIC 0x50373251u   /* 'Q27P' little-endian */
+#define Q27_PFX_VERSION 1u
+#pragma pack(push, 1)
+typedef struct {
+    uint32_t magic, version;
+    uint64_t compat, tok_hash;
+    int32_t L, pad;
+    uint64_t gdn_bytes, kv_bytes;
+    uint64_t reserved[2];
+} q27_pfx_hdr;
+#pragma pack(pop)
+uint64_t q27_pfx_fnv1a64(const void* p, size_t n, uint64_t seed);
+uint64_t q27_pfx_compat_hash(const char* model_path, uint64_t model_bytes, int n_layer, int n_kv,
+                             int head_dim, int gdn_heads, int gdn_dim, int gdn_ch, int kv_kind,
+                             int format_version);
 
 #ifdef __cplusplus
 }

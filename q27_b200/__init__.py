@@ -12,7 +12,8 @@ from .attn import (BatchedDecode, SlotArgs, marshal_slots, attn_decode, attn_dec
                    attn_decode_partial, attn_decode_partial_push, attn_merge_partials,
                    attn_merge_pushed, attn_prefill_T, attn_verify_partials, launch_count,
                    decode_scratch_floats, kv_dequant, kv_store3, kv_store_T, kv_store_T_t3,
-                   kv_store_t3, wht3,
+                   kv_store_t3, kv_store_lanes_shard, kv_store_rows_shard, wht3,
                    prefill_part_floats, wht_T)
+from .snapshot import KvLineage
 
 __all__ = [n for n in dir() if not n.startswith("_")]

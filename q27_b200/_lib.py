@@ -102,6 +102,9 @@ SIGNATURES = {
     "q27_kv_store_t3": (_i, [C.POINTER(P3), C.POINTER(P3), _vp, _vp, C.POINTER(P3), _i, _i, _vp, _i,
                              _i]),
     "q27_wht3": (_i, [C.POINTER(P3), _i, _i, _i, _i, _vp, _i]),
+    "q27_kv_store_lanes_shard": (_i, [C.POINTER(P3), C.POINTER(P3), _vp, _vp, C.POINTER(P3), _i, _i,
+                                      _vp, _i, _i, _i, _i]),
+    "q27_kv_store_rows_shard": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _i, _i, _i]),
     "q27_mk_tab": (_i, [_vp, _sz, _i, _vp, _vp]),
     "q27_kvpool_create": (_vp, [_sz, _sz, _sz, _sz]),
     "q27_kvpool_destroy": (None, [_vp]),
@@ -111,6 +114,20 @@ SIGNATURES = {
     "q27_kvpool_page_ptr": (_vp, [_vp, _i, _i]),
     "q27_kvpool_reserve": (_i, [_vp, _i, _i, C.POINTER(_i)]),
     "q27_kvpool_release": (None, [_vp, _i, C.POINTER(_i), _i]),
+    "q27_kvlineage_create": (_vp, [_vp, _i, _i]),
+    "q27_kvlineage_destroy": (None, [_vp]),
+    "q27_kvlineage_entitle": (_i, [_vp, _i, C.POINTER(_i), _vp]),
+    "q27_kvlineage_release": (None, [_vp]),
+    "q27_kvlineage_rows": (_i, [_vp]),
+    "q27_kvlineage_npages": (_i, [_vp]),
+    "q27_kvlineage_pages_of": (_i, [_vp, _i, _i]),
+    "q27_kvlineage_tab": (_vp, [_vp, _i, _i]),
+    "q27_kvlineage_row": (_vp, [_vp, _i, _i, _i]),
+    "q27_kv_snapshot_bytes": (_i64, [_i, _i, C.POINTER(_i), _sz, _sz]),
+    "q27_kv_snapshot_export": (_i, [_vp, _i, _i, C.POINTER(_i), _vp, _vp]),
+    "q27_kv_snapshot_import": (_i, [_vp, _i, _i, C.POINTER(_i), _vp, _vp]),
+    "q27_pfx_fnv1a64": (C.c_uint64, [_vp, _sz, C.c_uint64]),
+    "q27_pfx_compat_hash": (C.c_uint64, [C.c_char_p, C.c_uint64, _i, _i, _i, _i, _i, _i, _i, _i]),
 }
 
 _lib = None

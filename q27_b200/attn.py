@@ -271,6 +271,27 @@ def kv_store_t3(k_lanes, v_lanes, ktab, vtab, pos_lanes, n_kv_heads, head_dim, s
                                     len(k_lanes), kvk), "q27_kv_store_t3")
 
 
+def kv_store_lanes_shard(k_lanes, v_lanes, ktab, vtab, pos_lanes, n_kv_heads, head_dim, kvk,
+                         row_base, row_count, st=None):
+    """Lane-form store of any kind on a cache split by rows: only the lanes whose row falls in
+    [row_base, row_base + row_count) are written, at row - row_base of these tables."""
+    import ctypes as C
+    k, v, p = _p3(k_lanes), _p3(v_lanes), _p3(pos_lanes)
+    L.check(L.lib().q27_kv_store_lanes_shard(C.byref(k), C.byref(v), ktab.data_ptr(), vtab.data_ptr(),
+                                             C.byref(p), n_kv_heads, head_dim, stream_ptr(st),
+                                             len(k_lanes), kvk, row_base, row_count),
+            "q27_kv_store_lanes_shard")
+
+
+def kv_store_rows_shard(kT, vT, ktab, vtab, base_pos, n_kv_heads, head_dim, T, kvk, row_base,
+                        row_count, st=None):
+    """Chunk-form store (rows base_pos .. base_pos+T-1) of any kind on a cache split by rows."""
+    L.check(L.lib().q27_kv_store_rows_shard(kT.data_ptr(), vT.data_ptr(), ktab.data_ptr(),
+                                            vtab.data_ptr(), base_pos, n_kv_heads, head_dim, T,
+                                            stream_ptr(st), kvk, row_base, row_count),
+            "q27_kv_store_rows_shard")
+
+
 def wht3(x_lanes, n_heads, head_dim, stride, inv, st=None):
     """Lane form of wht_T: rotate each lane's heads in place."""
     import ctypes as C

@@ -571,6 +571,31 @@ int q27_kv_store_t3(const q27_CP3* k, const q27_CP3* v, void* const* ktab, void*
                             static_cast<cudaStream_t>(stream), kvk);
 }
 
+int q27_kv_store_lanes_shard(const q27_CP3* k, const q27_CP3* v, void* const* ktab,
+                             void* const* vtab, const q27_IP3* pos, int n_kv_heads, int head_dim,
+                             void* stream, int ntok, int kvk, int row_base, int row_count) {
+    if (!kind_known(kvk)) return Q27_ERR_UNSUPPORTED_KIND;
+    if (head_dim != HD || n_kv_heads < 1) return Q27_ERR_UNSUPPORTED_WIDTH;
+    if (!k || !v || !pos || !ktab || !vtab || ntok < 0 || ntok > Q27_MAX_LANES || row_base < 0 ||
+        row_count < 0)
+        return Q27_ERR_INVALID_ARG;
+    for (int t = 0; t < ntok; t++)
+        if (!k->p[t] || !v->p[t] || !pos->p[t]) return Q27_ERR_INVALID_ARG;
+    return launch_kv_store3(k->p, v->p, pos->p, ktab, vtab, n_kv_heads, ntok,
+                            static_cast<cudaStream_t>(stream), kvk, row_base, row_count);
+}
+
+int q27_kv_store_rows_shard(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
+                            int base_pos, int n_kv_heads, int head_dim, int T, void* stream,
+                            int kvk, int row_base, int row_count) {
+    if (!kind_known(kvk)) return Q27_ERR_UNSUPPORTED_KIND;
+    if (head_dim != HD || n_kv_heads < 1) return Q27_ERR_UNSUPPORTED_WIDTH;
+    if (!kT || !vT || !ktab || !vtab || base_pos < 0 || T < 0 || row_base < 0 || row_count < 0)
+        return Q27_ERR_INVALID_ARG;
+    return launch_kv_store_T(kT, vT, ktab, vtab, base_pos, n_kv_heads, T,
+                             static_cast<cudaStream_t>(stream), kvk, row_base, row_count);
+}
+
 int q27_wht3(const q27_P3* x, int n_heads, int head_dim, int stride, int inv, void* stream,
              int ntok) {
     if (head_dim != HD) return Q27_ERR_UNSUPPORTED_WIDTH;

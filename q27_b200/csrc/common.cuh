@@ -270,11 +270,13 @@ int launch_prefill_exact(const float* qT, int q_stride, int q_row, const void* c
                          int SB, int n_q, int n_kv, float scale, cudaStream_t st, int kvk, int wht);
 int launch_kv_dequant(const void* const* tab, int fmt, int row0, int nrows, int n_kv, float* out,
                       cudaStream_t st);
+// [row_base, row_base + row_count): the logical rows the tables hold (rows outside are skipped)
 int launch_kv_store_T(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
-                      int base_pos, int n_kv, int T, cudaStream_t st, int kvk);
+                      int base_pos, int n_kv, int T, cudaStream_t st, int kvk, int row_base = 0,
+                      int row_count = 0x7fffffff);
 int launch_kv_store3(const float* const* k, const float* const* v, const int* const* pos,
                      void* const* ktab, void* const* vtab, int n_kv, int ntok, cudaStream_t st,
-                     int kvk);
+                     int kvk, int row_base = 0, int row_count = 0x7fffffff);
 int launch_wht3(float* const* x, int n_heads, int stride, int ntok, bool inv, cudaStream_t st);
 int launch_wht_T(float* x, int n_heads, int head_stride, int row_stride, int T, bool inv,
                  cudaStream_t st);

@@ -184,7 +184,7 @@ __device__ __forceinline__ void encode_group(int fmt, const float* __restrict__ 
 // rows base_pos .. base_pos+T-1; kT/vT: [T][n_kv*256] fp32
 __global__ void __launch_bounds__(ST_WARPS * 32)
 k_kv_store_T_t3(const float* __restrict__ kT, const float* __restrict__ vT, void* const* ktab,
-                void* const* vtab, int base_pos, int n_kv, int T, int kfmt) {
+                void* const* vtab, int base_pos, int n_kv, int T, int kfmt, int row_base, int row_count) {
     __shared__ float xs[ST_WARPS][128];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gpr = n_kv * 2; // groups per row per side
@@ -194,7 +194,8 @@ k_kv_store_T_t3(const float* __restrict__ kT, const float* __restrict__ vT, void
         const int side = (int)(w & 1);
         const int64_t gidx = w >> 1;
         const int t = (int)(gidx / gpr), gi = (int)(gidx % gpr);
-        const int p = base_pos + t;
+        const int p = base_pos + t - row_base;     // row of this GPU's tables, if it owns the row
+        if (p < 0 || p >= row_count) continue;
         uint8_t* page = static_cast<uint8_t*>((side ? vtab : ktab)[p >> PAGE_SHIFT]);
         encode_group(side ? RF_T3 : kfmt, (side ? vT : kT) + (size_t)t * gpr * 128 + (size_t)gi * 128,
                      page, (size_t)(p & (PAGE - 1)) * gpr + gi, xs[warp], lane);
@@ -204,12 +205,13 @@ k_kv_store_T_t3(const float* __restrict__ kT, const float* __restrict__ vT, void
 template <bool FP8>
 __global__ void __launch_bounds__(256)
 k_kv_store_T(const float* __restrict__ kT, const float* __restrict__ vT, void* const* ktab,
-             void* const* vtab, int base_pos, int rowlen, int T) {
+             void* const* vtab, int base_pos, int rowlen, int T, int row_base, int row_count) {
     const int64_t total = (int64_t)T * rowlen;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int t = (int)(i / rowlen), e = (int)(i % rowlen);
-        const int p = base_pos + t;
+        const int p = base_pos + t - row_base;
+        if (p < 0 || p >= row_count) continue;
         const size_t off = (size_t)(p & (PAGE - 1)) * rowlen + e;
         if (FP8) {
             static_cast<__nv_fp8_e4m3*>(ktab[p >> PAGE_SHIFT])[off] = __nv_fp8_e4m3(kT[i]);
@@ -243,10 +245,14 @@ k_wht_T(float* __restrict__ x, int n_heads, int head_stride, int row_stride, int
 }
 
 // ---- lane forms: one row per draft lane, source rows and positions behind lane bundles ----
+// [row_base, row_base + row_count): the logical rows this GPU's tables hold (everything, or
+// its shard of a cache split by rows: a lane whose row lives elsewhere is skipped here and
+// stored by the GPU that owns it, every GPU running the same call on the same lanes).
 struct LaneRows {
     const float* k[Q27_MAX_LANES];
     const float* v[Q27_MAX_LANES];
     const int* pos[Q27_MAX_LANES];
+    int row_base, row_count;
 };
 struct LaneVecs {
     float* x[Q27_MAX_LANES];
@@ -262,7 +268,8 @@ k_kv_store3_t3(const __grid_constant__ LaneRows L, void* const* ktab, void* cons
     const int w = blockIdx.x * ST_WARPS + warp;          // (group, side)
     if (w >= gpr * 2) return;
     const int side = w & 1, gi = w >> 1;
-    const int p = __ldg(L.pos[t]);
+    const int p = __ldg(L.pos[t]) - L.row_base;
+    if (p < 0 || p >= L.row_count) return;
     uint8_t* page = static_cast<uint8_t*>((side ? vtab : ktab)[p >> PAGE_SHIFT]);
     encode_group(side ? RF_T3 : kfmt, (side ? L.v[t] : L.k[t]) + (size_t)gi * 128, page,
                  (size_t)(p & (PAGE - 1)) * gpr + gi, xs[warp], lane);
@@ -273,7 +280,8 @@ __global__ void __launch_bounds__(256)
 k_kv_store3(const __grid_constant__ LaneRows L, void* const* ktab, void* const* vtab, int rowlen) {
     const int e = blockIdx.x * blockDim.x + threadIdx.x, t = blockIdx.y;
     if (e >= rowlen) return;
-    const int p = __ldg(L.pos[t]);
+    const int p = __ldg(L.pos[t]) - L.row_base;
+    if (p < 0 || p >= L.row_count) return;
     const size_t off = (size_t)(p & (PAGE - 1)) * rowlen + e;
     if (FP8) {
         static_cast<__nv_fp8_e4m3*>(ktab[p >> PAGE_SHIFT])[off] = __nv_fp8_e4m3(L.k[t][e]);
@@ -309,17 +317,18 @@ unsigned blocks_for(int64_t units, int per_block) {
 } // namespace
 
 int launch_kv_store_T(const float* kT, const float* vT, void* const* ktab, void* const* vtab,
-                      int base_pos, int n_kv, int T, cudaStream_t st, int kvk) {
+                      int base_pos, int n_kv, int T, cudaStream_t st, int kvk, int row_base,
+                      int row_count) {
     if (T == 0) return Q27_OK;
     if (kvk >= Q27_KV_T3 && kind_known(kvk)) {
         k_kv_store_T_t3<<<blocks_for((int64_t)T * n_kv * 4, ST_WARPS), ST_WARPS * 32, 0, st>>>(
-            kT, vT, ktab, vtab, base_pos, n_kv, T, k_fmt(kvk));
+            kT, vT, ktab, vtab, base_pos, n_kv, T, k_fmt(kvk), row_base, row_count);
     } else if (kvk == Q27_KV_FP8) {
         k_kv_store_T<true><<<blocks_for((int64_t)T * n_kv * HD, 256), 256, 0, st>>>(
-            kT, vT, ktab, vtab, base_pos, n_kv * HD, T);
+            kT, vT, ktab, vtab, base_pos, n_kv * HD, T, row_base, row_count);
     } else if (kvk == Q27_KV_F16) {
         k_kv_store_T<false><<<blocks_for((int64_t)T * n_kv * HD, 256), 256, 0, st>>>(
-            kT, vT, ktab, vtab, base_pos, n_kv * HD, T);
+            kT, vT, ktab, vtab, base_pos, n_kv * HD, T, row_base, row_count);
     } else {
         return Q27_ERR_UNSUPPORTED_KIND;
     }
@@ -330,9 +339,11 @@ int launch_kv_store_T(const float* kT, const float* vT, void* const* ktab, void*
 
 int launch_kv_store3(const float* const* k, const float* const* v, const int* const* pos,
                      void* const* ktab, void* const* vtab, int n_kv, int ntok, cudaStream_t st,
-                     int kvk) {
+                     int kvk, int row_base, int row_count) {
     if (ntok == 0) return Q27_OK;
     LaneRows L{};
+    L.row_base = row_base;
+    L.row_count = row_count;
     for (int t = 0; t < ntok; t++) {
         L.k[t] = k[t];
         L.v[t] = v[t];

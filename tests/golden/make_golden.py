@@ -73,6 +73,28 @@ def main():
                         t5_serial=b5_serial, t5_dequant=d5, i8_blocks=b8, i8_dequant=d8)
     print("wrote k_codecs.npz", b5_tree.shape, b8.shape, int((b5_tree != b5_serial).sum()))
 
+    # identity of a prefix-snapshot entry (src/prefix_cache.h): hashes, compat hash, header bytes
+    L_ = ref.lib
+    L_.q27ref_pfx_fnv1a64.restype = C.c_uint64
+    L_.q27ref_pfx_fnv1a64.argtypes = [C.c_void_p, C.c_size_t]
+    L_.q27ref_pfx_compat_hash.restype = C.c_uint64
+    L_.q27ref_pfx_compat_hash.argtypes = [C.c_char_p, C.c_uint64] + [C.c_int] * 8
+    L_.q27ref_pfx_fill_hdr.argtypes = [C.c_void_p, C.c_uint64, C.c_void_p, C.c_int, C.c_uint64, C.c_uint64]
+    toks = (lcg_floats(5000, 77, 60000.0).astype(np.int32) % 151936).astype(np.int32)
+    lens = np.array([1, 2, 7, 64, 4096, 5000], np.int32)
+    keys = np.array([L_.q27ref_pfx_fnv1a64(toks.ctypes.data, int(n) * 4) for n in lens], np.uint64)
+    geoms = np.array([[15_000_000_000, 64, 4, 256, 32, 128, 8192, k, 1] for k in range(6)]
+                     + [[1, 2, 3, 4, 5, 6, 7, 2, 2]], np.int64)
+    path = b"/models/q27-q4.gguf"
+    compats = np.array([L_.q27ref_pfx_compat_hash(path, *[int(v) for v in g]) for g in geoms], np.uint64)
+    hdr = np.zeros(64, np.uint8)
+    L_.q27ref_pfx_fill_hdr(hdr.ctypes.data, int(compats[2]), toks.ctypes.data, 4096, 123456, 7890123)
+    np.savez_compressed(Path(__file__).parent / "pfx_identity.npz", tokens=toks, lens=lens, keys=keys,
+                        geoms=geoms, path=np.frombuffer(path, np.uint8), compats=compats, hdr=hdr,
+                        magic=np.uint32(L_.q27ref_pfx_magic()), version=np.uint32(L_.q27ref_pfx_version()),
+                        hdr_bytes=np.int32(L_.q27ref_pfx_hdr_bytes()))
+    print("wrote pfx_identity.npz", [hex(int(k)) for k in keys[:2]])
+
 
 if __name__ == "__main__":
     main()
