@@ -79,6 +79,8 @@ SIGNATURES = {
     "q27_attn_decode_partial_push": (_i, [C.POINTER(Slot), _i, _i, _i, _i, _i, _i, _f,
                                           C.POINTER(_vp), _i, _i, C.c_uint, _vp, _i]),
     "q27_attn_merge_pushed": (_i, [_vp, _i, _i64, C.c_uint, _vp, _vp]),
+    "q27_attn_decode_exchange": (_i, [C.POINTER(Slot), _i, _i, _i, _i, _i, _i, _f, C.POINTER(_vp), _i,
+                                      _i, C.c_uint, _vp, _vp, _i, _i]),
     "q27_attn_prefill_T": (_i, [_vp, _i, _i, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _f,
                                 _vp, _i]),
     "q27_attn_prefill_T_exact": (_i, [_vp, _i, _i, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _i,

@@ -190,6 +190,19 @@ def attn_decode_partial_push(slots, lanes_stride, q_stride, n_q_heads, n_kv_head
                len(mailboxes), rank, epoch, stream_ptr(st), kvk), "q27_attn_decode_partial_push")
 
 
+def attn_decode_exchange(slots, lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim, scale,
+                         mailboxes, rank, epoch, out, st=None, kvk=0, wht=False):
+    """One sharded decode / verify step: partials, then combine + peer stores + wait + merge
+    (one kernel when the rows fit the GPU at once); ``out`` [npairs][256] on every rank."""
+    import ctypes as C
+    arr = slots if isinstance(slots, C.Array) else _slots(slots)
+    boxes = (C.c_void_p * len(mailboxes))(*mailboxes)
+    L.check(L.lib().q27_attn_decode_exchange(arr, len(arr), lanes_stride, q_stride, n_q_heads,
+                                             n_kv_heads, head_dim, scale, boxes, len(mailboxes), rank,
+                                             epoch, out.data_ptr(), stream_ptr(st), kvk, int(wht)),
+            "q27_attn_decode_exchange")
+
+
 def attn_merge_pushed(mailbox, world, npairs, epoch, out, st=None, wht_kvk=None):
     """Device-side wait for every rank's push of ``epoch``, then the LSE merge into out.
     ``wht_kvk``: the cache kind, when the output rotation of that kind is to run here."""

@@ -92,7 +92,7 @@ thread_local cudaEvent_t g_ev_start = nullptr, g_ev_stop = nullptr;
 
 int run_decode(const q27_slot* slots, int nslots, int lanes_stride, int q_stride, int n_q, int n_kv,
                int head_dim, float scale, float* partial_out, void* stream, int kvk, Family fam,
-               const Peers* peers = nullptr, int wht = 0) {
+               const Peers* peers = nullptr, int wht = 0, float* xchg_out = nullptr) {
     DevBatch b;
     int rc = build_batch(slots, nslots, q_stride, n_q, n_kv, head_dim, scale, kvk,
                          partial_out == nullptr && peers == nullptr, b);
@@ -123,6 +123,17 @@ int run_decode(const q27_slot* slots, int nslots, int lanes_stride, int q_stride
         if (rc) return rc;
     }
     if (g_ev_stop) Q27_CUDA_TRY(cudaEventRecord(g_ev_stop, st));
+    if (peers && xchg_out) {
+        // the whole exchange in one kernel when its blocks are all resident at once, else the
+        // push kernel followed by the merge kernel
+        bool one = false;
+        rc = launch_combine_xchg(b, *peers, lanes_stride, xchg_out, sms, st, &one);
+        if (rc || one) return rc;
+        rc = launch_combine_push(b, *peers, lanes_stride, st);
+        if (rc) return rc;
+        return launch_merge_pushed(peers->box[peers->rank], peers->world, peers->npairs, peers->epoch,
+                                   xchg_out, wht & WHT_OUT, st);
+    }
     if (peers) return launch_combine_push(b, *peers, lanes_stride, st);
     if (b.fuse) return Q27_OK;       // the partial kernel has merged and normalised already
     return launch_combine(b, partial_out, partial_out ? lanes_stride : b.max_ntok, st);
@@ -398,11 +409,12 @@ int q27_set_kernel_events(void* ev_start, void* ev_stop) {
 
 int q27_wait_timeout_flag(int* out) {
     if (!out) return Q27_ERR_INVALID_ARG;
-    int a = 0, b = 0, c = 0, rc;
+    int a = 0, b = 0, c = 0, d = 0, rc;
     if ((rc = read_wait_timeout_flag(&a))) return rc;
     if ((rc = read_umma_timeout_flag(&b))) return rc;
     if ((rc = read_xchg_timeout_flag(&c))) return rc;
-    *out = a | b | c;
+    if ((rc = read_xchg1_timeout_flag(&d))) return rc;
+    *out = a | b | c | d;
     return Q27_OK;
 }
 
@@ -455,7 +467,7 @@ size_t q27_xchg_mailbox_bytes(int world, int64_t npairs) {
 static int partial_push(const q27_slot* slots, int nslots, int lanes_stride, int q_stride,
                         int n_q_heads, int n_kv_heads, int head_dim, float scale,
                         void* const* mailboxes, int world, int rank, unsigned epoch, void* stream,
-                        int kvk, int wht) {
+                        int kvk, int wht, float* xchg_out = nullptr) {
     if (!mailboxes || world < 1 || world > Q27_MAX_RANKS || rank < 0 || rank >= world)
         return Q27_ERR_INVALID_ARG;
     for (int r = 0; r < world; r++)
@@ -468,8 +480,19 @@ static int partial_push(const q27_slot* slots, int nslots, int lanes_stride, int
     p.rank = rank;
     p.npairs = (int64_t)nslots * lanes_stride * n_q_heads;
     p.epoch = epoch;
+    if (xchg_out && p.npairs > INT_MAX) return Q27_ERR_TOO_LARGE;
     return run_decode(slots, nslots, lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim, scale,
-                      nullptr, stream, kvk, FAM_AUTO, &p, wht);
+                      nullptr, stream, kvk, FAM_AUTO, &p, wht, xchg_out);
+}
+
+int q27_attn_decode_exchange(const q27_slot* slots, int nslots, int lanes_stride, int q_stride,
+                             int n_q_heads, int n_kv_heads, int head_dim, float scale,
+                             void* const* mailboxes, int world, int rank, unsigned epoch,
+                             float* out, void* stream, int kvk, int wht) {
+    if (!out) return Q27_ERR_INVALID_ARG;
+    return partial_push(slots, nslots, lanes_stride, q_stride, n_q_heads, n_kv_heads, head_dim,
+                        scale, mailboxes, world, rank, epoch, stream, kvk,
+                        wht ? wht_flags_for(kvk) : 0, out);
 }
 
 int q27_attn_decode_partial_push(const q27_slot* slots, int nslots, int lanes_stride, int q_stride,

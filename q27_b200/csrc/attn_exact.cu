@@ -12,6 +12,11 @@ namespace q27b {
 
 namespace {
 
+// without relocatable device code a __device__ variable is private to its translation unit:
+// the one-kernel exchange below keeps its own timeout flag, ORed into the library's by the reader
+__device__ int g_xchg1_timeout_flag = 0;
+__device__ __forceinline__ void xchg_note_timeout() { atomicExch(&g_xchg1_timeout_flag, 8); }
+
 // Split-KV partial of one (split, kv head, slot-lane), fp32 throughout, as a tiled two-phase
 // loop over blocks of 32 keys that lives in shared memory:
 //   phase 1  the block's K rows are decoded (bit-exact element decoders) into shared memory;
@@ -286,6 +291,94 @@ k_combine_push(const __grid_constant__ DevBatch b, const __grid_constant__ Peers
     xchg_publish(peers, gridDim.x * gridDim.y * gridDim.z);
 }
 
+// The whole exchange in ONE kernel, for launches whose blocks are all resident at once: block
+// (head, lane, slot) merges its splits, stores the row into slot `rank` of every rank's mailbox
+// and raises the row's own flag there; it then waits (bounded) for the same row from every other
+// rank in its own mailbox, merges the `world` rows and writes the output head -- un-rotated
+// if asked. A block waits only for rows that its peers store before they wait themselves, so
+// with all blocks resident nobody can be in anybody's way. Rows, flags, parities and the
+// step word are those of the two-kernel exchange (p2p_exchange.cu).
+__global__ void __launch_bounds__(COMBINE_THREADS, 2)
+k_combine_xchg(const __grid_constant__ DevBatch b, const __grid_constant__ Peers peers,
+               int lanes_stride, float* __restrict__ out) {
+    pdl_wait();                  // the partials come from the kernel before this one
+    uint8_t* own = peers.box[peers.rank];
+    const uint32_t epoch = xchg_epoch(own, peers.world, peers.npairs, peers.epoch);
+    const int par = epoch & 1;
+    const int h = blockIdx.x, t = blockIdx.y, slot = blockIdx.z, tid = threadIdx.x;
+    const DevSlot& S = b.s[slot];
+    const int64_t w = ((int64_t)slot * lanes_stride + t) * b.n_q + h;
+    const size_t row = (((size_t)par * peers.world + peers.rank) * (size_t)peers.npairs + (size_t)w) * PART;
+    __shared__ int s_ok;
+    __shared__ float s_m[Q27_MAX_RANKS], s_l[Q27_MAX_RANKS];
+    float a = 0.f, mg = NEG_SENTINEL, lg = 0.f;
+    if (t < S.ntok)
+        a = combine_core(S.scratch + ((size_t)t * b.n_q + h) * b.nsplit * PART, b.nsplit, mg, lg);
+    if (tid < HD)
+        for (int r = 0; r < peers.world; r++) {
+            float* d = reinterpret_cast<float*>(peers.box[r]) + row;
+            d[2 + tid] = a;
+            if (tid == 0) { d[0] = mg; d[1] = lg; }
+        }
+    if (tid == 0) s_ok = 1;
+    __syncthreads();             // every thread's stores, before the fence and the flags
+    if (tid == 0) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        for (int r = 0; r < peers.world; r++)
+            if (r != peers.rank)
+                asm volatile("st.relaxed.sys.global.u32 [%0], %1;"
+                             ::"l"(peers.box[r] + xchg_row_flag(peers.world, peers.npairs, par, peers.rank, w)),
+                               "r"(epoch) : "memory");
+    }
+    if (tid < peers.world && tid != peers.rank) {
+        const uint8_t* f = own + xchg_row_flag(peers.world, peers.npairs, par, tid, w);
+        bool got = false;
+        for (int i = 0; i < (1 << 22); i++) {          // about half a second, then give up
+            if (xchg_flag_acquire(f) == epoch) { got = true; break; }
+            if (i > 64) __nanosleep(100);
+        }
+        if (!got) { s_ok = 0; xchg_note_timeout(); }
+    }
+    __syncthreads();
+    const bool ok = s_ok != 0;                   // the same in every thread of the block
+    if (ok) {
+        const float* parts = reinterpret_cast<const float*>(own) + (size_t)par * xchg_data_floats(peers.world, peers.npairs);
+        if (tid < peers.world) {
+            const float* pp = parts + ((size_t)tid * peers.npairs + w) * PART;
+            s_m[tid] = tid == peers.rank ? mg : __ldcg(pp);
+            s_l[tid] = tid == peers.rank ? lg : __ldcg(pp + 1);
+        }
+        __syncthreads();
+        float m = NEG_SENTINEL;
+        for (int s = 0; s < peers.world; s++) m = fmaxf(m, s_m[s]);
+        float l = 0.f, o = 0.f;
+        for (int s = 0; s < peers.world; s++) {
+            if (s_m[s] == NEG_SENTINEL) continue;
+            const float e = expf(s_m[s] - m);
+            l += s_l[s] * e;
+            if (tid < HD)
+                o += (s == peers.rank ? a : __ldcg(parts + ((size_t)s * peers.npairs + w) * PART + 2 + tid)) * e;
+        }
+        o *= l > 0.f ? 1.0f / l : 0.f;
+        if (b.wht & WHT_OUT) o = unrotate_head(o);
+        if (tid < HD) out[(size_t)w * HD + tid] = o;
+    }
+    // completion, as in the two-kernel exchange: every block counts itself, the last one
+    // records the exchange as done only if nobody gave up
+    __syncthreads();
+    if (tid == 0) {
+        unsigned* ctr = reinterpret_cast<unsigned*>(own + xchg_counter_offset(peers.world, peers.npairs) + XCHG_MERGE_CTR);
+        __threadfence();
+        const unsigned nblocks = gridDim.x * gridDim.y * gridDim.z;
+        const unsigned seen = atomicAdd(ctr, ok ? 1u : 0x10001u) + (ok ? 1u : 0x10001u);
+        if ((seen & 0xffffu) == nblocks) {
+            *ctr = 0;
+            if ((seen >> 16) == 0)
+                *reinterpret_cast<volatile uint32_t*>(own + xchg_counter_offset(peers.world, peers.npairs) + XCHG_STEP) = epoch;
+        }
+    }
+}
+
 // parts: [nparts][npairs][258] -> out [npairs][256] normalised
 __global__ void __launch_bounds__(256)
 k_merge(const float* __restrict__ parts, int nparts, int64_t npairs, float* __restrict__ out,
@@ -414,6 +507,33 @@ int launch_combine_push(const DevBatch& b, const Peers& peers, int lanes_stride,
     dim3 grid(b.n_q, lanes_stride, b.nslots);
     Q27_CUDA_TRY(launch_pdl(k_combine_push, grid, dim3(COMBINE_THREADS), 0, st, b, peers, lanes_stride));
     Q27_CUDA_TRY(cudaGetLastError());
+    return Q27_OK;
+}
+
+// 0 = the launch does not fit the machine at once (the caller runs push + merge instead)
+int launch_combine_xchg(const DevBatch& b, const Peers& peers, int lanes_stride, float* out,
+                        int sm_count, cudaStream_t st, bool* done) {
+    *done = false;
+    static std::atomic<int> per_sm[MAX_DEVICES];
+    int dev = 0;
+    Q27_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= MAX_DEVICES) return Q27_ERR_INVALID_ARG;
+    int nb = per_sm[dev].load(std::memory_order_relaxed);
+    if (nb == 0) {
+        Q27_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_combine_xchg, COMBINE_THREADS, 0));
+        per_sm[dev].store(nb > 0 ? nb : -1, std::memory_order_relaxed);
+    }
+    const int64_t blocks = (int64_t)b.n_q * lanes_stride * b.nslots;
+    if (nb <= 0 || blocks > (int64_t)nb * sm_count || blocks > 0xffff) return Q27_OK;
+    dim3 grid(b.n_q, lanes_stride, b.nslots);
+    Q27_CUDA_TRY(launch_pdl(k_combine_xchg, grid, dim3(COMBINE_THREADS), 0, st, b, peers, lanes_stride, out));
+    Q27_CUDA_TRY(cudaGetLastError());
+    *done = true;
+    return Q27_OK;
+}
+
+int read_xchg1_timeout_flag(int* out) {
+    Q27_CUDA_TRY(cudaMemcpyFromSymbol(out, g_xchg1_timeout_flag, sizeof(int)));
     return Q27_OK;
 }
 

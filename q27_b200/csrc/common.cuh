@@ -263,7 +263,10 @@ struct Peers;
 int launch_combine_push(const DevBatch& b, const Peers& peers, int lanes_stride, cudaStream_t st);
 int launch_merge_pushed(void* box, int world, int64_t npairs, uint32_t epoch, float* out,
                         int wht, cudaStream_t st);
+int launch_combine_xchg(const DevBatch& b, const Peers& peers, int lanes_stride, float* out,
+                        int sm_count, cudaStream_t st, bool* done);
 int read_xchg_timeout_flag(int* out);
+int read_xchg1_timeout_flag(int* out);
 int read_umma_timeout_flag(int* out);
 int launch_prefill_exact(const float* qT, int q_stride, int q_row, const void* const* ktab,
                          const void* const* vtab, float* outT, int out_row, int base_pos, int t0,

@@ -23,6 +23,15 @@ __host__ __device__ inline size_t xchg_counter_offset(int world, int64_t npairs)
 
 // byte offsets from the first counter: push counter 0, merge counter 64, step word 128
 constexpr int XCHG_MERGE_CTR = 64, XCHG_STEP = 128;
+// behind the counters: one 4-byte flag per (parity, source rank, row), for the one-kernel
+// exchange in which every row travels and is waited for on its own
+__host__ __device__ inline size_t xchg_row_flags_offset(int world, int64_t npairs) {
+    return xchg_counter_offset(world, npairs) + 256;
+}
+__host__ __device__ inline size_t xchg_row_flag(int world, int64_t npairs, int parity, int src,
+                                                int64_t row) {
+    return xchg_row_flags_offset(world, npairs) + (((size_t)parity * world + src) * (size_t)npairs + row) * 4;
+}
 
 struct Peers {
     uint8_t* box[Q27_MAX_RANKS];   // every rank's mailbox as mapped in this process

@@ -15,8 +15,8 @@ import torch
 import torch.distributed as dist
 
 from . import _lib as L
-from .attn import (FD_ST, attn_decode_partial, attn_decode_partial_push, attn_merge_partials,
-                   attn_merge_pushed)
+from .attn import (FD_ST, attn_decode_exchange, attn_decode_partial, attn_decode_partial_push,
+                   attn_merge_partials, attn_merge_pushed)
 
 KV_PAGE = L.KV_PAGE
 
@@ -149,13 +149,20 @@ class PeerMailboxes:
         return self.npairs * FD_ST * 4
 
     def decode(self, slots, out: torch.Tensor, q_stride: int, n_kv_heads: int, scale: float,
-               kvk: int, st=None) -> torch.Tensor:
-        """One sharded decode / verify step; `out` [npairs][256] normalised on every rank."""
+               kvk: int, st=None, wht: bool = False, two_kernels: bool = False) -> torch.Tensor:
+        """One sharded decode / verify step; `out` [npairs][256] normalised on every rank.
+        ``two_kernels``: the push and the merge as separate calls (what the single call falls
+        back to when the rows of a step do not fit the GPU at once)."""
         self.epoch += 1
         epoch = 0 if self.device_epoch else self.epoch
-        attn_decode_partial_push(slots, self.lanes, q_stride, self.n_q, n_kv_heads, L.HEAD_DIM,
-                                 scale, self.boxes, self.rank, epoch, st=st, kvk=kvk)
-        attn_merge_pushed(self.own, self.world, self.npairs, epoch, out, st=st)
+        if two_kernels:
+            attn_decode_partial_push(slots, self.lanes, q_stride, self.n_q, n_kv_heads, L.HEAD_DIM,
+                                     scale, self.boxes, self.rank, epoch, st=st, kvk=kvk, wht=wht)
+            attn_merge_pushed(self.own, self.world, self.npairs, epoch, out, st=st,
+                              wht_kvk=kvk if wht else None)
+        else:
+            attn_decode_exchange(slots, self.lanes, q_stride, self.n_q, n_kv_heads, L.HEAD_DIM, scale,
+                                 self.boxes, self.rank, epoch, out, st=st, kvk=kvk, wht=wht)
         return out
 
     def close(self, group=None):

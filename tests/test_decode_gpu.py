@@ -198,6 +198,35 @@ def test_kv_split_through_mailboxes(oracle, cuda, kvk):
             Q._lib.check(lib.q27_xchg_free(b), "q27_xchg_free")
 
 
+def test_one_call_exchange_with_a_single_owner(oracle, cuda):
+    """q27_attn_decode_exchange with one rank: the combine, the (empty) exchange and the merge in
+    ONE kernel, device-counted epochs over several steps, equal to the plain decode. (With more
+    owners the kernel waits for its peers' rows, which only real ranks on their own GPUs can
+    provide: tests/test_multi_gpu.py.)"""
+    import ctypes as C
+    lib = Q._lib.lib()
+    c = synth.make_case(oracle, KV_T3, rows=3000, pos=[2999, 2000, 7], seed=66, outlier_frac=0.02)
+    ref = oracle.attn_decode(c.q, c.k, c.v, KV_T3, c.pos)
+    dc = DeviceCase(c, cuda)
+    npairs = 3 * 24
+    ptr = C.c_void_p()
+    Q._lib.check(lib.q27_xchg_alloc(lib.q27_xchg_mailbox_bytes(1, npairs), C.byref(ptr), None), "q27_xchg_alloc")
+    try:
+        out = torch.full((npairs, 256), float("nan"), device=cuda)
+        n0 = Q.launch_count()
+        for _ in range(3):                          # epoch 0: the mailbox counts the steps itself
+            Q.attn_decode_exchange([dc.slot()], 3, synth.Q_STRIDE, 24, 4, 256, SCALE, [ptr.value], 0, 0, out,
+                                   kvk=KV_T3)
+        torch.cuda.synchronize()
+        assert Q.launch_count() - n0 == 3 * 2       # partial kernel + one exchange kernel per step
+        assert synth.tolerance_ok(out.cpu().numpy().reshape(3, -1), ref)[0]
+        plain = dc.run3()
+        assert (out.cpu().numpy().reshape(3, -1).view(np.uint32) == plain.view(np.uint32)).all()
+    finally:
+        torch.cuda.synchronize()
+        Q._lib.check(lib.q27_xchg_free(ptr.value), "q27_xchg_free")
+
+
 @pytest.mark.skipif(not REF_GPU_SO.exists(), reason="oracle/_ref not built")
 @pytest.mark.parametrize("kvk", KINDS)
 def test_against_reference_kernels_on_this_gpu(oracle, cuda, kvk):
