@@ -47,14 +47,17 @@ ROW_BYTES = {KV_F16: 2048, KV_FP8: 1024, KV_T3: 400}
 KIND_NAME = {KV_F16: "fp16", KV_FP8: "fp8-e4m3", KV_T3: "turbo3"}
 # name -> (kvk, slots, lanes, context rows per slot, outlier fraction, rows split over ranks)
 DECODE = {"c1": (KV_F16, 1, 1, 4096, 0.0, False), "c2": (KV_FP8, 1, 6, 32768, 0.0, False),
-          "c3": (KV_T3, 2, 1, 131072, 0.02, False), "c5": (KV_T3, 8, 6, 262144, 0.02, True)}
+          "c3": (KV_T3, 2, 1, 131072, 0.02, False), "c5": (KV_T3, 8, 6, 262144, 0.02, True),
+          # c5's kernel at a size a profiler capture can hold (2 slots x 65536 rows): only ever
+          # run as `--workload c5s`, never part of the default line
+          "c5s": (KV_T3, 2, 6, 65536, 0.02, False)}
 PREFILL = {"prefix": 8192, "new": 16384, "chunk": 2048}
 METRIC = "decode/verify attn KV GB/s (frac of HBM peak) @131K ctx"
 PREFILL_METRIC = "prefill attn TFLOP/s"
 L2_BYTES = 126 * 2**20
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from the ncu
 # captures summarised under profiles/ (None where no capture exists for the workload)
-NCU_TRAFFIC = {"c3": 217.9e6, "c2": 68.9e6}
+NCU_TRAFFIC = {"c3": 214.3e6, "c2": 68.9e6}
 BAR = "|got - ref| <= 2e-3 + 1e-3*|ref|"
 
 
@@ -230,10 +233,19 @@ class DecodeRun:
         self.calls = [Q.BatchedDecode(sl, Q_STRIDE, N_Q, N_KV, HD, SCALE, kvk=kvk) for sl in self.slot_sets]
         self.marshalled = [Q.marshal_slots(sl) for sl in self.slot_sets]
         self.use_graph = not args.no_graph and (world == 1 or self.boxes is not None)
+        # Across ranks a step's merge waits (bounded, about half a second) for every rank's push:
+        # the ranks enter each group of steps together, whatever their host-side set-up took.
+        self.barrier()
         self.launches_per_step = self._count_launches()
+        self.barrier()
         self.round_graph = self._graph(lambda: [self.step(c) for c in range(copies)]) if self.use_graph else None
-        self.e2e_graphs = ([self._graph(lambda c=c: self._e2e_body(c)) for c in range(copies)]
-                           if self.use_graph else None)
+        self.e2e_graphs = None
+        if self.use_graph:
+            self.e2e_graphs = []
+            for c in range(copies):
+                self.barrier()
+                self.e2e_graphs.append(self._graph(lambda c=c: self._e2e_body(c)))
+        self.barrier()
 
     def _slots(self, c):
         Q = self.Q
@@ -284,6 +296,7 @@ class DecodeRun:
         with torch.cuda.stream(side):
             fn()
         torch.cuda.current_stream().wait_stream(side)
+        self.barrier()               # the warm-up steps have run on every rank before the capture
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             fn()
@@ -319,6 +332,49 @@ class DecodeRun:
             self.barrier()
             out.append(e0.elapsed_time(e1) / steps)
         return self._max_over_ranks(out)
+
+    def time_call_patterns(self, steps) -> dict:
+        """The step launched directly (no graph) in two ways: the batched entry with all slots
+        in one call, and the way the reference's engine would call a drop-in today -- one
+        single-slot `attn_decode3` per request, each on its own stream, running concurrently.
+        ms per step, single GPU."""
+        torch, Q = self.torch, self.Q
+        main = torch.cuda.current_stream()
+        streams = [torch.cuda.Stream() for _ in range(self.nslots)]
+        fork, joins = torch.cuda.Event(), [torch.cuda.Event() for _ in range(self.nslots)]
+
+        def batched(i):
+            self.calls[i % self.copies]()
+
+        def per_request(i):
+            sl = self.slot_sets[i % self.copies]
+            fork.record(main)
+            for s, st in enumerate(streams):
+                st.wait_event(fork)
+                with torch.cuda.stream(st):
+                    a = sl[s]
+                    Q.attn_decode3(a.q_lanes, Q_STRIDE, a.ktab, a.vtab, a.out_lanes, a.scratch, a.pos_lanes,
+                                   0, N_Q, N_KV, HD, SCALE, st=st, ntok=self.lanes, kvk=self.kvk)
+                joins[s].record(st)
+            for j in joins:
+                main.wait_event(j)
+
+        out = {}
+        for name, fn in (("batched_direct_ms", batched), ("one_call_per_request_on_own_streams_ms", per_request)):
+            for i in range(6):
+                fn(i)
+            torch.cuda.synchronize()
+            ms = []
+            for _ in range(15):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for i in range(steps):
+                    fn(i)
+                e1.record()
+                torch.cuda.synchronize()
+                ms.append(e0.elapsed_time(e1) / steps)
+            out[name] = round(statistics.median(ms), 5)
+        return out
 
     def time_kernel(self, steps):
         """Mean duration of the dominant (split-KV partial) kernel, bracketed by events that the
@@ -629,6 +685,7 @@ def run_ours(args):
         time.sleep(0.15)
     m = measure_decode(run, args, oracle, args.repeats)
     clocks = sampler.stop() if rank == 0 else None
+    patterns = run.time_call_patterns(args.steps) if world == 1 and run.nslots > 1 else None
     cpu_base = None
     if rank == 0 and world == 1 and oracle is not None and main_name == "c3":
         cpu_base = cpu_baseline(run, oracle)
@@ -657,7 +714,8 @@ def run_ours(args):
         "repeats": m["repeats"], "higher_is_better": True, "scaling": m["scaling"], "vs_baseline": None,
         "dtype": "u8" if kvk != KV_F16 else "f16", "data": "synthetic",
         "config": m["config"],
-        "run": {"launch": m["launch"], "exchange": m["exchange"], "checked": m["checked"]},
+        "run": {"launch": m["launch"], "exchange": m["exchange"], "checked": m["checked"],
+                **({"call_patterns": patterns} if patterns else {})},
         "e2e": dict(m["e2e"], note="Q lanes + positions in from pinned host memory, outputs back, one "
                                    "stream sync per step; the KV cache is engine state resident in HBM"),
         "gpu_launches": m["gpu_launches_per_step"] * args.steps,

@@ -132,7 +132,10 @@ def test_verify_partials_refuses_what_it_does_not_cover(cuda):
     one = torch.zeros(8, device=cuda)
     lanes = [one] * 17
     with pytest.raises(L.Q27Error):
-        Q.attn_verify_partials([one], 512, one, one, one, [one], 4, 6, 256, SCALE, 16, kvk=4)   # turbo5k
+        Q.attn_verify_partials([one], 512, one, one, one, [one], 4, 6, 256, SCALE, 16, kvk=6)   # outside KvKind
+    # a kind without a tensor-core verify (turbo5k): `false`, the caller falls through to the
+    # scalar entry as it does in the reference (src/spec3.cu:1118-1135)
+    assert Q.attn_verify_partials([one] * 4, 512, one, one, one, [one] * 4, 4, 6, 256, SCALE, 16, kvk=4) is False
     assert Q.attn_verify_partials([one] * 4, 512, one, one, one, [one] * 4, 4, 8, 256, SCALE, 16) is False
     assert Q.attn_verify_partials([one] * 4, 512, one, one, one, [one] * 4, 4, 6, 256, SCALE, 129) is False
     del lanes
