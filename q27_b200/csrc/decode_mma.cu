@@ -25,9 +25,10 @@
 // fragment registers come from contiguous packed bytes; Q^T fragments and the output rows
 // use the same maps (kdim_* / vdim_* below), so the permutation cancels.
 //
-// Small launches finish in the same kernel: when the partials of a (slot, lane, kv group)
-// fit one SM's appetite, the CTA that completes a group last merges its splits and writes the
-// normalised output rows, so a short decode is ONE launch (q27b::arrive_last).
+// Small launches finish in the same kernel: when a (slot, lane, kv group) has few splits, its
+// CTAs wait for one another once their partials are written (cooperative launch, bounded wait)
+// and each merges its share of the group's outputs and writes the normalised values, so a short
+// decode is ONE launch.
 #include <limits.h>
 
 #include "decode_mma.cuh"
@@ -44,8 +45,11 @@ constexpr int STAGE_ROWS = 32;    // rows per ring stage (= 2 key tiles; never c
 constexpr int TILE = 16;          // keys per MMA tile
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
-constexpr int FUSE_MAX_SPLITS = 64;               // the ticket words live behind split 64
-constexpr int FUSE_MAX_BYTES = 288 * 1024;        // partial bytes one finishing CTA may merge
+constexpr int FUSE_MAX_SPLITS = 127;              // the group counters live behind the last split
+// A launch finishes itself while its partials are few (measured: c1, 6 heads x 37 splits, 21.9 ->
+// 14.3 us per step); long launches are better off with the combine kernel, whose launch hides
+// behind the partial kernel's tail (c3, 24 heads x 74 splits: 94 us that way, 101 us fused).
+constexpr int FUSE_MAX_BYTES = 288 * 1024;
 
 template <int KVK> struct Fmt;
 template <> struct Fmt<Q27_KV_F16> {
@@ -505,94 +509,92 @@ __device__ __forceinline__ void stage_t3(WarpAcc& A, uint32_t ks, uint32_t vs, i
 }
 
 // ---- the finishing step of a fused launch -------------------------------------------------
-// Log-sum-exp merge (k_attn_fd_combine, src/spec3.cu:706-739) of the first `used` splits of NH
-// heads of one lane by the CTA that completed the group last. A head's partials are `used`
-// consecutive 258-float records; bulk copies bring them into the idle ring, up to NBUF heads
-// ahead (one SM pulls a few hundred KB out of L2 in a couple of microseconds this way; plain
-// loads would take several times longer). Sums run in split order with four interleaved
-// accumulators added in a fixed order: the result is the same every run.
-template <int NH, int WORK_BYTES>
-__device__ void finish_group(const float* __restrict__ base, int nsplit, int used,
-                             float* __restrict__ out, uint8_t* ring, uint64_t* bars) {
-    __shared__ float s_w[FUSE_MAX_SPLITS];
+// Log-sum-exp merge (k_attn_fd_combine, src/spec3.cu:706-739) of the first `used` splits of the
+// NH heads of one (slot, lane, kv group), shared out over the group's own CTAs: once every CTA
+// of the group has written its partial, CTA `me` of `n` merges the 128-output half heads me,
+// me + n, ... of the group's 2 NH. A CTA reads a few tens of KB straight out of L2 (the splits'
+// {m, l} of the head, then `used` values per output, two threads per output on alternate
+// splits, sixteen loads in flight each), so the merge takes a microsecond or two however many
+// heads the group has. Fixed summation order: the result is the same every run. With WHT_OUT
+// the half head -- one 128-group of the rotation -- is un-rotated before it is written.
+template <int NH>
+__device__ void finish_halves(const float* __restrict__ base, int nsplit, int used,
+                              float* __restrict__ out, int me, int n, int wht) {
+    __shared__ float s_w[128];
     __shared__ float s_inv;
+    __shared__ float s_part[128];
     const int tid = threadIdx.x, lane = tid & 31;
-    if (used == 0) {             // nothing attended (an empty shard): zeros, like the combine
-        for (int i = tid; i < NH * HD; i += blockDim.x) out[i] = 0.f;
-        return;
-    }
-    const uint32_t rec_bytes = (uint32_t)used * PART * 4;
-    const uint32_t buf_bytes = (rec_bytes + 16 + 15) & ~15u;        // slack for the alignment shift
-    const int nbuf = min(NH, (int)(WORK_BYTES / buf_bytes));
-    if (tid == 0) {
-        for (int i = 0; i < nbuf; i++) mbar_init(&bars[i], 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // ring: generic reads/writes -> bulk writes
-    __syncthreads();
-    auto issue = [&](int h) {
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(base + (size_t)h * nsplit * PART);
-        const uint32_t off = (uint32_t)((uintptr_t)src & 15);
-        const uint32_t bytes = (off + rec_bytes + 15) & ~15u;
-        mbar_expect_tx(&bars[h % nbuf], bytes);
-        bulk_g2s(ring + (size_t)(h % nbuf) * buf_bytes, src - off, bytes, &bars[h % nbuf]);
-    };
-    if (tid == 0)
-        for (int h = 0; h < nbuf; h++) issue(h);
-    bool ok = true;
-    for (int h = 0; h < NH; h++) {
-        ok = ok && mbar_wait(&bars[h % nbuf], (uint32_t)((h / nbuf) & 1));
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(base + (size_t)h * nsplit * PART);
-        const float* rec = reinterpret_cast<const float*>(ring + (size_t)(h % nbuf) * buf_bytes +
-                                                          ((uintptr_t)src & 15));
+    for (int g = me; g < 2 * NH; g += n) {
+        const int h = g >> 1, d = (g & 1) * 128 + (tid & 127), par = tid >> 7;   // par 0, 1: summing; 2: idle
+        float* dst = out + (size_t)h * HD + (g & 1) * 128;
+        if (used == 0) {         // nothing attended (an empty shard): zeros, like the combine
+            if (tid < 128) dst[tid] = 0.f;
+            continue;
+        }
+        const float* rec = base + (size_t)h * nsplit * PART;
+        __syncthreads();                                    // s_w / s_inv / s_part of the group before
         if (tid < 32) {
-            // used <= 64: lane owns splits lane and lane + 32 (clamped loads, masked weights)
-            const int s0 = min(lane, used - 1), s1 = min(lane + 32, used - 1);
-            const float m0 = rec[s0 * PART], m1 = rec[s1 * PART];
-            const float l0 = rec[s0 * PART + 1], l1 = rec[s1 * PART + 1];
-            const bool v0 = lane < used && m0 != NEG_SENTINEL, v1 = lane + 32 < used && m1 != NEG_SENTINEL;
-            float m = fmaxf(v0 ? m0 : NEG_SENTINEL, v1 ? m1 : NEG_SENTINEL);
+            // used <= 128: lane owns splits lane + 32 k (clamped loads, masked weights)
+            float2 ml[4];
+            bool live[4];
+            float m = NEG_SENTINEL;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int sp = lane + 32 * k;
+                ml[k] = __ldcg(reinterpret_cast<const float2*>(rec + (size_t)min(sp, used - 1) * PART));
+                live[k] = sp < used && ml[k].x != NEG_SENTINEL;
+                m = fmaxf(m, live[k] ? ml[k].x : NEG_SENTINEL);
+            }
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-            const float w0 = v0 ? expf(m0 - m) : 0.f, w1 = v1 ? expf(m1 - m) : 0.f;
-            s_w[lane] = w0;
-            s_w[lane + 32] = w1;
-            float l = (v0 ? l0 * w0 : 0.f) + (v1 ? l1 * w1 : 0.f);
+            float l = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float w = live[k] ? expf(ml[k].x - m) : 0.f;
+                s_w[lane + 32 * k] = w;
+                l += live[k] ? ml[k].y * w : 0.f;
+            }
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
             if (lane == 0) s_inv = l > 0.f ? 1.0f / l : 0.f;
         }
         __syncthreads();
-        if (tid < HD && ok) {
+        float sum = 0.f;
+        if (par < 2) {
             float a[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int s0 = 0; s0 < used; s0 += 8) {
-                float v[8], w[8];
+            for (int s0 = par; s0 < used; s0 += 32) {       // this thread's splits: s0, s0 + 2, ...
+                float v[16], w[16];
 #pragma unroll
-                for (int u = 0; u < 8; u++) {     // every load is issued before any is used
-                    const int sp = min(s0 + u, used - 1);
-                    v[u] = rec[sp * PART + 2 + tid];
-                    w[u] = s0 + u < used ? s_w[sp] : 0.f;
+                for (int u = 0; u < 16; u++) {              // every load is issued before any is used
+                    const int sp = min(s0 + 2 * u, used - 1);
+                    v[u] = __ldcg(rec + (size_t)sp * PART + 2 + d);
+                    w[u] = s0 + 2 * u < used ? s_w[sp] : 0.f;
                 }
 #pragma unroll
-                for (int u = 0; u < 8; u++) {
+                for (int u = 0; u < 16; u++) {
                     // sentinel splits hold undefined accumulators: selected, never added
                     const float x = v[u] * w[u];
                     a[u & 3] += w[u] != 0.f ? x : 0.f;
                 }
             }
-            out[(size_t)h * HD + tid] = ((a[0] + a[1]) + (a[2] + a[3])) * s_inv;
+            sum = (a[0] + a[1]) + (a[2] + a[3]);
+            if (par == 1) s_part[tid & 127] = sum;
         }
-        __syncthreads();         // every thread is done reading this buffer
-        if (tid == 0 && h + nbuf < NH && ok) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // reads before the overwrite
-            issue(h + nbuf);
+        __syncthreads();
+        if (tid < 128) s_part[tid] = (sum + s_part[tid]) * s_inv;    // even splits + odd splits
+        if (wht & WHT_OUT) {
+            __syncthreads();
+            if (tid < 32) wht_group<true>(s_part, lane);
         }
+        __syncthreads();
+        if (tid < 128) dst[tid] = s_part[tid];
     }
-    if (!ok) atomicExch(&g_wait_timeout_flag, 1);
 }
 
 // ---- the kernel -------------------------------------------------------------------------
-template <int KVK>
+// FUSE: the variant that also finishes the launch (b.fuse is set for it and only for it); the
+// plain variant does not carry that code.
+template <int KVK, bool FUSE>
 __global__ void __launch_bounds__(n_threads<KVK>(), 1)
 k_decode_mma(const __grid_constant__ DevBatch b) {
     using F = Fmt<KVK>;
@@ -604,7 +606,7 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
     uint64_t* empty = full + 16;
     uint8_t* ring = smem + HEADER_BYTES;
     float* q_stage = reinterpret_cast<float*>(ring + work_bytes<KVK>());
-    __shared__ int s_fail, s_last;
+    __shared__ int s_fail, s_grp_ok;
     __shared__ float s_wt[NHEADS][WAYS], s_mb[NHEADS], s_lb[NHEADS];
 
     pdl_trigger();               // a combine kernel may be scheduled; it waits for this grid
@@ -616,14 +618,16 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     unsigned long long* ticket = nullptr;
-    if (b.fuse) {
-        // the ticket word of this (lane, kv group), behind split 64 of the slot's scratch; a
-        // word that does not carry the tag yet (first use of this scratch) is armed here, long
-        // before anybody arrives on it
+    if (FUSE) {
+        // the two counters of this (lane, kv group) -- arrivals, departures -- behind the last
+        // split's partials in the slot's scratch (nsplit <= 127 of the 128 splits the scratch
+        // has room for); words that do not carry the tag yet (first use of this scratch, or
+        // partials of a call with more splits written over them) are armed here, long before
+        // anybody arrives on them
         ticket = reinterpret_cast<unsigned long long*>(
-                     S.scratch + (size_t)S.ntok * b.n_q * FUSE_MAX_SPLITS * PART) +
-                 (size_t)t * groups + kvg;
-        if (threadIdx.x == 0) ticket_arm(ticket);
+                     S.scratch + (size_t)S.ntok * b.n_q * b.nsplit * PART) +
+                 ((size_t)t * groups + kvg) * 2;
+        if (threadIdx.x == 0) { ticket_arm(ticket); ticket_arm(ticket + 1); }
     }
     int max_len = 0;
     for (int u = 0; u < S.ntok; u++)
@@ -880,16 +884,38 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
         __syncthreads();         // the producer has drained: shared memory is quiet from here on
     }
 
-    if (b.fuse) {
-        // the CTA that completes this (slot, lane, kv group) last merges its splits
+    if (FUSE) {
+        // Every CTA of this (slot, lane, kv group) waits for the group's partials (the launch is
+        // cooperative: all CTAs are resident), merges its share of the group's outputs and
+        // leaves; the last one to leave clears the counters for the next launch.
+        const unsigned n = (unsigned)b.nsplit;
+        __syncthreads();                          // this CTA's partial rows are written
+        if (threadIdx.x == 0) {
+            __threadfence();
+            atomicAdd(ticket, 1ull);
+            bool ok = false;
+            for (int i = 0; i < (1 << 20) && !ok; i++) {   // bounded: ~0.1 s, then the flag
+                unsigned long long v;
+                asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(ticket) : "memory");
+                ok = (unsigned)(v & 0xffffu) >= n;
+                if (!ok && i > 64) __nanosleep(64);
+            }
+            if (!ok) atomicExch(&g_wait_timeout_flag, 1);
+            s_grp_ok = ok ? 1 : 0;
+        }
         __syncthreads();
-        if (threadIdx.x == 0) s_last = ticket_take(ticket, (unsigned)b.nsplit) ? 1 : 0;
-        __syncthreads();
-        if (s_last) {
+        if (s_grp_ok) {
             const int used = min(b.nsplit, (max_len + chunk - 1) / chunk);
-            finish_group<NHEADS, work_bytes<KVK>()>(
-                S.scratch + ((size_t)t * b.n_q + kvh0 * GQA) * b.nsplit * PART, b.nsplit, used,
-                S.out[t] + (size_t)kvh0 * GQA * HD, ring, full);
+            finish_halves<NHEADS>(S.scratch + ((size_t)t * b.n_q + kvh0 * GQA) * b.nsplit * PART,
+                                  b.nsplit, used, S.out[t] + (size_t)kvh0 * GQA * HD, sp, (int)n, b.wht);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const unsigned long long prev = atomicAdd(ticket + 1, 1ull);
+            if ((unsigned)(prev & 0xffffu) + 1 == n) {
+                atomicExch(ticket, TICKET_TAG << 16);
+                atomicExch(ticket + 1, TICKET_TAG << 16);
+            }
         }
     }
 }
@@ -899,7 +925,10 @@ int launch_one(DevBatch& b, int sm_count, bool may_fuse, cudaStream_t st) {
     using F = Fmt<KVK>;
     static DeviceOnce once;      // the attribute belongs to a device, not to the process
     int rc = device_once(once, []() -> int {
-        Q27_CUDA_TRY(cudaFuncSetAttribute(k_decode_mma<KVK>,
+        Q27_CUDA_TRY(cudaFuncSetAttribute(k_decode_mma<KVK, false>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          smem_bytes<KVK>()));
+        Q27_CUDA_TRY(cudaFuncSetAttribute(k_decode_mma<KVK, true>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           smem_bytes<KVK>()));
         return Q27_OK;
@@ -909,22 +938,34 @@ int launch_one(DevBatch& b, int sm_count, bool may_fuse, cudaStream_t st) {
     const int per_split = b.nslots * b.max_ntok * groups;
     int ns = sm_count / per_split;
     ns = ns < 1 ? 1 : ns > Q27_MAX_SPLITS ? Q27_MAX_SPLITS : ns;
-    // Small launches finish in this kernel: the last CTA of a (slot, lane, kv group) merges
-    // the group's partials, if they are few enough for one SM to pull through in about the
-    // time a second launch would cost. The ticket words sit behind split 64 of the scratch.
-    // (A call that also un-rotates its output leaves the merge to the combine kernel, which
-    // holds that rotation; the turbo3 layout, 24 heads per CTA, is past the byte limit anyway.)
+    // The launch finishes in this kernel when nobody else wants the partials: the CTAs of a
+    // (slot, lane, kv group) wait for one another and share the merge of the group's outputs
+    // (and the un-rotation of the output, if asked). The counters sit behind the last split's
+    // partials in the scratch.
     b.fuse = 0;
-    if (may_fuse && !(b.wht & WHT_OUT) && ns <= FUSE_MAX_SPLITS &&
-        F::KVH * GQA * ns * PART * 4 <= FUSE_MAX_BYTES) {
+    if (may_fuse && ns <= FUSE_MAX_SPLITS && F::KVH * GQA * ns * PART * 4 <= FUSE_MAX_BYTES) {
         b.fuse = 1;
         for (int i = 0; i < b.nslots; i++)
-            if ((uintptr_t)b.s[i].scratch & 15) b.fuse = 0;   // bulk copies out of the scratch
+            if ((uintptr_t)b.s[i].scratch & 7) b.fuse = 0;    // 64-bit counters in the scratch
     }
     b.nsplit = ns;
     b.unit = STAGE_ROWS;
     dim3 grid(b.max_ntok, b.nsplit, b.nslots * groups);
-    k_decode_mma<KVK><<<grid, n_threads<KVK>(), smem_bytes<KVK>(), st>>>(b);
+    if (b.fuse) {
+        // the CTAs of a group wait for one another: a cooperative launch, which the runtime
+        // refuses unless every CTA can be resident at once
+        void* args[] = {const_cast<DevBatch*>(&b)};
+        const cudaError_t e = cudaLaunchCooperativeKernel(
+            reinterpret_cast<const void*>(&k_decode_mma<KVK, true>), grid, dim3(n_threads<KVK>()), args,
+            smem_bytes<KVK>(), st);
+        if (e == cudaSuccess) {
+            Q27_COUNT_LAUNCH();
+            return Q27_OK;
+        }
+        (void)cudaGetLastError();                 // not launchable that way here: two launches
+        b.fuse = 0;
+    }
+    k_decode_mma<KVK, false><<<grid, n_threads<KVK>(), smem_bytes<KVK>(), st>>>(b);
     Q27_CUDA_TRY(cudaGetLastError());
     Q27_COUNT_LAUNCH();
     return Q27_OK;
