@@ -239,8 +239,9 @@ int q27_attn_merge_pushed(void* mailbox, int world, int64_t npairs, unsigned epo
 /* One sharded decode / verify step in one call: q27_attn_decode_partial_push followed by
  * q27_attn_merge_pushed on this rank's own mailbox (mailboxes[rank]); `out` [npairs][256]
  * normalised on every rank. When all (slot, lane, head) rows of the call fit the GPU at once
- * the combine, the peer stores, the wait and the merge run as ONE kernel in which every row
- * travels and is waited for on its own (per-row flags); otherwise as the two kernels above.
+ * the combine, the peer stores, the wait and the merge run as ONE kernel in which every float
+ * travels in a 64-bit word together with the step's epoch and is polled for on its own (no
+ * fence, no flag); otherwise as the two kernels above.
  * wht != 0: the rotation of the kind folded in (see the _wht entries below). */
 int q27_attn_decode_exchange(const q27_slot* slots, int nslots, int lanes_stride, int q_stride,
                              int n_q_heads, int n_kv_heads, int head_dim, float scale,

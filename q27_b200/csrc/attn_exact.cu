@@ -292,12 +292,14 @@ k_combine_push(const __grid_constant__ DevBatch b, const __grid_constant__ Peers
 }
 
 // The whole exchange in ONE kernel, for launches whose blocks are all resident at once: block
-// (head, lane, slot) merges its splits, stores the row into slot `rank` of every rank's mailbox
-// and raises the row's own flag there; it then waits (bounded) for the same row from every other
-// rank in its own mailbox, merges the `world` rows and writes the output head -- un-rotated
-// if asked. A block waits only for rows that its peers store before they wait themselves, so
-// with all blocks resident nobody can be in anybody's way. Rows, flags, parities and the
-// step word are those of the two-kernel exchange (p2p_exchange.cu).
+// (head, lane, slot) merges its splits and stores the row into slot `rank` of every OTHER rank's
+// mailbox, each float in one 64-bit word together with the step's epoch; it then reads the same
+// row of every other rank from its own mailbox, polling (bounded) each word until it carries the
+// epoch, merges the `world` rows and writes the output head -- un-rotated if asked. No fence and
+// no flag: a word that shows the epoch is that step's value. A block waits only for words that
+// its peers store before they wait themselves, so with all blocks resident nobody can be in
+// anybody's way. Parities and the step word are those of the two-kernel exchange
+// (p2p_exchange.cu).
 __global__ void __launch_bounds__(COMBINE_THREADS, 2)
 k_combine_xchg(const __grid_constant__ DevBatch b, const __grid_constant__ Peers peers,
                int lanes_stride, float* __restrict__ out) {
@@ -308,61 +310,58 @@ k_combine_xchg(const __grid_constant__ DevBatch b, const __grid_constant__ Peers
     const int h = blockIdx.x, t = blockIdx.y, slot = blockIdx.z, tid = threadIdx.x;
     const DevSlot& S = b.s[slot];
     const int64_t w = ((int64_t)slot * lanes_stride + t) * b.n_q + h;
-    const size_t row = (((size_t)par * peers.world + peers.rank) * (size_t)peers.npairs + (size_t)w) * PART;
     __shared__ int s_ok;
     __shared__ float s_m[Q27_MAX_RANKS], s_l[Q27_MAX_RANKS];
     float a = 0.f, mg = NEG_SENTINEL, lg = 0.f;
     if (t < S.ntok)
         a = combine_core(S.scratch + ((size_t)t * b.n_q + h) * b.nsplit * PART, b.nsplit, mg, lg);
+    if (tid == 0) s_ok = 1;
+    // this rank's row into every other mailbox: word 0 = m, 1 = l, 2 + d = acc[d]
     if (tid < HD)
         for (int r = 0; r < peers.world; r++) {
-            float* d = reinterpret_cast<float*>(peers.box[r]) + row;
-            d[2 + tid] = a;
-            if (tid == 0) { d[0] = mg; d[1] = lg; }
+            if (r == peers.rank) continue;
+            uint8_t* d = peers.box[r] + xchg_ll_word(peers.world, peers.npairs, par, peers.rank, w);
+            xchg_ll_store(d + 8 * (2 + tid), a, epoch);
+            if (tid == 0) {
+                xchg_ll_store(d, mg, epoch);
+                xchg_ll_store(d + 8, lg, epoch);
+            }
         }
-    if (tid == 0) s_ok = 1;
-    __syncthreads();             // every thread's stores, before the fence and the flags
-    if (tid == 0) {
-        asm volatile("fence.acq_rel.sys;" ::: "memory");
-        for (int r = 0; r < peers.world; r++)
-            if (r != peers.rank)
-                asm volatile("st.relaxed.sys.global.u32 [%0], %1;"
-                             ::"l"(peers.box[r] + xchg_row_flag(peers.world, peers.npairs, par, peers.rank, w)),
-                               "r"(epoch) : "memory");
-    }
-    if (tid < peers.world && tid != peers.rank) {
-        const uint8_t* f = own + xchg_row_flag(peers.world, peers.npairs, par, tid, w);
-        bool got = false;
-        for (int i = 0; i < (1 << 22); i++) {          // about half a second, then give up
-            if (xchg_flag_acquire(f) == epoch) { got = true; break; }
-            if (i > 64) __nanosleep(100);
+    __syncthreads();             // s_ok
+    // {m, l} of every rank (two threads per rank), then every thread's own accumulator words
+    if (tid < 2 * peers.world) {
+        const int r = tid >> 1, which = tid & 1;
+        float v = which ? lg : mg;
+        if (r != peers.rank &&
+            !xchg_ll_load(own + xchg_ll_word(peers.world, peers.npairs, par, r, w) + 8 * which, epoch, v)) {
+            s_ok = 0;
+            xchg_note_timeout();
         }
-        if (!got) { s_ok = 0; xchg_note_timeout(); }
+        (which ? s_l : s_m)[r] = v;
     }
     __syncthreads();
-    const bool ok = s_ok != 0;                   // the same in every thread of the block
-    if (ok) {
-        const float* parts = reinterpret_cast<const float*>(own) + (size_t)par * xchg_data_floats(peers.world, peers.npairs);
-        if (tid < peers.world) {
-            const float* pp = parts + ((size_t)tid * peers.npairs + w) * PART;
-            s_m[tid] = tid == peers.rank ? mg : __ldcg(pp);
-            s_l[tid] = tid == peers.rank ? lg : __ldcg(pp + 1);
+    float m = NEG_SENTINEL;
+    for (int s = 0; s < peers.world; s++) m = fmaxf(m, s_m[s]);
+    float l = 0.f, o = 0.f;
+    bool mine_ok = true;
+    for (int s = 0; s < peers.world; s++) {
+        if (s_m[s] == NEG_SENTINEL) continue;       // an empty shard: its accumulator is never read
+        const float e = expf(s_m[s] - m);
+        l += s_l[s] * e;
+        if (tid < HD) {
+            float v = a;
+            if (s != peers.rank)
+                mine_ok = xchg_ll_load(own + xchg_ll_word(peers.world, peers.npairs, par, s, w) + 8 * (2 + tid),
+                                       epoch, v) && mine_ok;
+            o += v * e;
         }
-        __syncthreads();
-        float m = NEG_SENTINEL;
-        for (int s = 0; s < peers.world; s++) m = fmaxf(m, s_m[s]);
-        float l = 0.f, o = 0.f;
-        for (int s = 0; s < peers.world; s++) {
-            if (s_m[s] == NEG_SENTINEL) continue;
-            const float e = expf(s_m[s] - m);
-            l += s_l[s] * e;
-            if (tid < HD)
-                o += (s == peers.rank ? a : __ldcg(parts + ((size_t)s * peers.npairs + w) * PART + 2 + tid)) * e;
-        }
-        o *= l > 0.f ? 1.0f / l : 0.f;
-        if (b.wht & WHT_OUT) o = unrotate_head(o);
-        if (tid < HD) out[(size_t)w * HD + tid] = o;
     }
+    if (!mine_ok) { s_ok = 0; xchg_note_timeout(); }
+    __syncthreads();
+    const bool ok = s_ok != 0;                   // the same in every thread of the block
+    o *= l > 0.f ? 1.0f / l : 0.f;
+    if (b.wht & WHT_OUT) o = unrotate_head(o);
+    if (ok && tid < HD) out[(size_t)w * HD + tid] = o;
     // completion, as in the two-kernel exchange: every block counts itself, the last one
     // records the exchange as done only if nobody gave up
     __syncthreads();

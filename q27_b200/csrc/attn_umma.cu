@@ -49,7 +49,7 @@ constexpr int TMEM_COLS = 512;
 // off the shared-memory port, which the operand reads of the MMAs and the staging writes
 // otherwise saturate; all of Q does not fit beside three S buffers.
 constexpr int COL_S = 0, COL_O = S_BUFS * BN, COL_Q = COL_O + HD;
-static_assert(COL_Q + Q_TMEM_DIMS / 2 <= TMEM_COLS, "tensor memory budget");
+static_assert(COL_Q + Q_TMEM_DIMS / 2 <= TMEM_COLS, "tensor memory columns");
 constexpr float LOG2E_F = 1.4426950408889634f;
 constexpr float RESCALE_THRESHOLD = 8.0f;       // log2 units
 
@@ -716,34 +716,41 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             asm volatile("cp.async.wait_all;" ::: "memory");
         } else if constexpr (KVK == Q27_KV_T3) {
             // A tile's packed rows of this kv head (64 keys x 100 B, 400 B apart in the page)
-            // come in with 4-byte asynchronous copies, consecutive lanes on consecutive words
-            // (a block per thread straight from global memory costs one L1 wavefront per lane
-            // per load and bounded this path); two raw buffers per side, each with a "landed"
-            // and a "read" mbarrier. Each thread then decodes one 50-byte block from shared
-            // memory (lanes 25 words apart: conflict-free).
-            constexpr int RAW_BYTES = BN * 2 * T3_BLK;
+            // come in with 16-byte asynchronous copies of the aligned 112-byte window that
+            // holds them (a row starts on a 16-byte boundary and kv head h sits at byte 100 h,
+            // so the window [100 h rounded down, + 112) never leaves the row): 448 copies per
+            // tile and side instead of 1600 four-byte ones (a block per thread straight from
+            // global memory costs one L1 wavefront per lane per load and bounded this path);
+            // two raw buffers per side, each with a "landed" and a "read" mbarrier. Each thread
+            // then decodes one 50-byte block from shared memory.
+            constexpr int RAW_ROW = 112;
+            constexpr int RAW_BYTES = BN * RAW_ROW;
+            static_assert(4 * RAW_BYTES <= KT_BYTES, "the raw buffers live in the third V slot");
             uint8_t* raw = raw_sm + side * 2 * RAW_BYTES;
             const uint32_t rfull = raw_full + 8 * (2 * side), rempty = raw_empty + 8 * (2 * side);
-            // this thread's 13 words of a tile: source offset inside the page and key index are
-            // the same for every tile
-            uint32_t soff[13];
-            int wkey[13];
+            const int win0 = (pb.kvh * 2 * T3_BLK) & ~15;        // window start inside the row
+            const int blk_off = pb.kvh * 2 * T3_BLK - win0;      // 0, 4, 8 or 12
+            // this thread's (up to) 4 pieces of a tile: source offset inside the page and key
+            // index are the same for every tile
+            uint32_t soff[4], doff[4];
+            int wkey[4];
 #pragma unroll
-            for (int n = 0; n < 13; n++) {
-                const int w = p + NPROD * n;              // word 0..1599 of the tile's rows
-                const int key = w / 25, j = w - 25 * key;
-                wkey[n] = w < BN * 25 ? key : BN;         // BN: never below the tile's key count
-                soff[n] = (uint32_t)((key * n_kv + pb.kvh) * (2 * T3_BLK) + 4 * j);
+            for (int n = 0; n < 4; n++) {
+                const int c = p + NPROD * n;              // piece 0..447 of the tile's windows
+                const int key = c / 7, j = c - 7 * key;
+                wkey[n] = c < BN * 7 ? key : BN;          // BN: never below the tile's key count
+                soff[n] = (uint32_t)(key * n_kv * (2 * T3_BLK) + win0 + 16 * j);
+                doff[n] = (uint32_t)(key * RAW_ROW + 16 * j);
             }
             auto issue_raw = [&](int i) {
                 const int buf = i & 1, nk = nkeys_of(i);
                 const uint8_t* page = page_of(i);
-                const uint32_t dst = s32(raw + buf * RAW_BYTES) + 4 * p;
+                const uint32_t dst = s32(raw + buf * RAW_BYTES);
 #pragma unroll
-                for (int n = 0; n < 13; n++)
+                for (int n = 0; n < 4; n++)
                     if (wkey[n] < nk)
-                        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;"
-                                     ::"r"(dst + 4 * NPROD * n), "l"(page + soff[n]) : "memory");
+                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                                     ::"r"(dst + doff[n]), "l"(page + soff[n]) : "memory");
                 asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
                              ::"r"(rfull + 8 * buf) : "memory");
             };
@@ -757,7 +764,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 {
                     const int key = p & 63, blk = p >> 6;
                     const uint32_t* src = reinterpret_cast<const uint32_t*>(
-                        raw + buf * RAW_BYTES + key * (2 * T3_BLK) + 48 * blk);
+                        raw + buf * RAW_BYTES + key * RAW_ROW + blk_off + 48 * blk);
 #pragma unroll
                     for (int k = 0; k < 13; k++) rw.w[k] = src[k];
                     rw.w[13] = 0;
@@ -970,6 +977,7 @@ int launch_prefill_umma(const float* qT, int q_stride, int q_row, const void* co
                         int sm_count, cudaStream_t st, int kvk, int wht, bool* done) {
     *done = false;
     if (kind_known(kvk) && !kind_has_tensor_path(kvk)) return Q27_OK;   // served by the fp32 family
+    if (kvk == Q27_KV_T3 && (n_kv & 3)) return Q27_OK;   // turbo3 rows are copied in 16-byte pieces: 400 n_kv / 4 bytes per row
     (void)n_q;
     // float4 loads of Q rows and float4 stores of output rows
     if ((q_stride & 3) || (q_row & 3) || (out_row & 3) || ((uintptr_t)qT & 15) || ((uintptr_t)outT & 15))
@@ -1032,6 +1040,7 @@ int launch_verify_umma(DevBatch& b, int kvk, int sm_count, cudaStream_t st, bool
                        int force_nsplit) {
     *done = false;
     if (kind_known(kvk) && !kind_has_tensor_path(kvk)) return Q27_OK;   // served by the fp32 family
+    if (kvk == Q27_KV_T3 && (b.n_kv & 3)) return Q27_OK;   // turbo3 rows are copied in 16-byte pieces: 400 n_kv / 4 bytes per row
     if (b.q_stride & 3) return Q27_OK;
     for (int i = 0; i < b.nslots; i++)
         for (int t = 0; t < b.s[i].ntok; t++)

@@ -118,24 +118,14 @@ __host__ __device__ __forceinline__ int split_chunk(int max_len, int nsplit, int
     return c < unit ? unit : c;
 }
 
-// "Am I the last of n CTAs to get here?" on a 64-bit word of caller scratch that nobody has
-// to clear first: the word carries a 48-bit tag above a 16-bit count. ticket_arm (any time
-// before the first arrival, by every CTA that will arrive) gives a word without the tag a
-// zero count; ticket_take counts an arrival, and the n-th one re-arms the word for the next
-// launch. Call from ONE thread, ticket_take after a block barrier; its fences make every
-// earlier arrival's global writes visible to the last one.
+// Counters in caller scratch that nobody has to clear first: a 64-bit word carries a 48-bit
+// tag above a 16-bit count. ticket_arm (any time before the first arrival, by every CTA that
+// will use the word) gives a word without the tag a zero count; users count with atomicAdd and
+// put the word back to the armed value when they are done with it.
 constexpr unsigned long long TICKET_TAG = 0xD15C0A77E5B2ull;      // 48 bits
 __device__ __forceinline__ void ticket_arm(unsigned long long* word) {
     const unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(word);
     if ((old >> 16) != TICKET_TAG) atomicCAS(word, old, TICKET_TAG << 16);   // losers change nothing
-}
-__device__ __forceinline__ bool ticket_take(unsigned long long* word, unsigned n) {
-    __threadfence();
-    const unsigned long long prev = atomicAdd(word, 1ull);
-    const bool last = (unsigned)(prev & 0xffffu) + 1 >= n;
-    if (last) atomicExch(word, TICKET_TAG << 16);
-    __threadfence();
-    return last;
 }
 
 // ---- element decoders ---------------------------------------------------------------

@@ -91,7 +91,7 @@ k_merge_pushed(uint8_t* __restrict__ box, int world, int64_t npairs, uint32_t ep
 } // namespace
 
 size_t xchg_mailbox_bytes(int world, int64_t npairs) {
-    return xchg_row_flags_offset(world, npairs) + (size_t)2 * world * (size_t)npairs * 4 + 256;
+    return xchg_ll_offset(world, npairs) + (size_t)2 * world * (size_t)npairs * PART * 8 + 256;
 }
 
 int launch_merge_pushed(void* box, int world, int64_t npairs, uint32_t epoch, float* out,

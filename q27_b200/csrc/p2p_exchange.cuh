@@ -1,8 +1,8 @@
 // Layout of a partial-exchange mailbox and what a kernel needs to publish into every rank's:
-// [2 parities][world][npairs][258] floats, [2][world] release flags, two block counters and the
+// [2 parities][world][npairs][258] floats, [2][world] release flags, two block counters, the
 // step word (the number of exchanges completed on this rank, for callers that let the device
 // count the epochs so that a step's launches have constant arguments and can sit in a CUDA
-// graph).
+// graph) and the epoch-tagged copy of the rows that the one-kernel exchange uses.
 #pragma once
 #include "common.cuh"
 
@@ -23,14 +23,31 @@ __host__ __device__ inline size_t xchg_counter_offset(int world, int64_t npairs)
 
 // byte offsets from the first counter: push counter 0, merge counter 64, step word 128
 constexpr int XCHG_MERGE_CTR = 64, XCHG_STEP = 128;
-// behind the counters: one 4-byte flag per (parity, source rank, row), for the one-kernel
-// exchange in which every row travels and is waited for on its own
-__host__ __device__ inline size_t xchg_row_flags_offset(int world, int64_t npairs) {
+// Behind the counters: the rows once more for the one-kernel exchange, every float packed with
+// the step's epoch into ONE 64-bit word, [2 parities][world][npairs][258] words. A 64-bit store
+// is a single access, so a word whose upper half holds the epoch carries that step's value:
+// the receiver polls the words it needs and no fence orders anything (a system-scope fence
+// costs ~5 us on this part, measured).
+__host__ __device__ inline size_t xchg_ll_offset(int world, int64_t npairs) {
     return xchg_counter_offset(world, npairs) + 256;
 }
-__host__ __device__ inline size_t xchg_row_flag(int world, int64_t npairs, int parity, int src,
-                                                int64_t row) {
-    return xchg_row_flags_offset(world, npairs) + (((size_t)parity * world + src) * (size_t)npairs + row) * 4;
+__host__ __device__ inline size_t xchg_ll_word(int world, int64_t npairs, int parity, int src,
+                                               int64_t row) {
+    return xchg_ll_offset(world, npairs) + ((((size_t)parity * world + src) * (size_t)npairs + row) * PART) * 8;
+}
+__device__ __forceinline__ void xchg_ll_store(uint8_t* word, float v, uint32_t epoch) {
+    const unsigned long long x = ((unsigned long long)epoch << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(word), "l"(x) : "memory");
+}
+// bounded wait for the word to carry `epoch`; false = gave up
+__device__ __forceinline__ bool xchg_ll_load(const uint8_t* word, uint32_t epoch, float& v) {
+    for (int i = 0; i < (1 << 22); i++) {                  // about half a second, then give up
+        unsigned long long x;
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(x) : "l"(word) : "memory");
+        if ((uint32_t)(x >> 32) == epoch) { v = __uint_as_float((uint32_t)x); return true; }
+        if (i > 64) __nanosleep(100);
+    }
+    return false;
 }
 
 struct Peers {
