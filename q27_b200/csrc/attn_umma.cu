@@ -770,16 +770,19 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                     rw.w[13] = 0;
                 }
                 bar_arrive(rempty + 8 * buf);
-                if (i + 2 < ntiles) {
-                    if (!bar_wait(rempty + 8 * buf, par)) break;
-                    issue_raw(i + 2);
-                }
                 if (!wait_slot(i)) break;
                 const int st = i % nslots;
                 if (p >> 6) half_store<KVK, 1>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
                 else half_store<KVK, 0>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
                 fence_async_smem();
                 bar_arrive(full + 8 * st);
+                // the raw buffer is refilled only now: by this time every thread of the side has
+                // long read it, so nobody stalls on the barrier, and the copies still have more
+                // than a tile's time to land
+                if (i + 2 < ntiles) {
+                    if (!bar_wait(rempty + 8 * buf, par)) break;
+                    issue_raw(i + 2);
+                }
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
         } else {
@@ -822,15 +825,15 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 for (int n = 0; n < 16; n++)
                     rw.d[n] = *reinterpret_cast<const uint2*>(raw + buf * RAW_BYTES + (p + NPROD * n) * 8);
                 bar_arrive(rempty + 8 * buf);
-                if (i + 2 < ntiles) {
-                    if (!bar_wait(rempty + 8 * buf, par)) break;
-                    issue_raw(i + 2);
-                }
                 if (!wait_slot(i)) break;
                 const int st = i % nslots;
                 half_store<KVK>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
                 fence_async_smem();
                 bar_arrive(full + 8 * st);
+                if (i + 2 < ntiles) {                      // refill only now: nobody stalls on the barrier
+                    if (!bar_wait(rempty + 8 * buf, par)) break;
+                    issue_raw(i + 2);
+                }
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
         }
