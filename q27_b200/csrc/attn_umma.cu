@@ -232,6 +232,19 @@ struct Problem {
     int kvh, tile_t0, lo, hi, sp;
     int piece = -1;     // prefill: >= 0 when this CTA holds one key range of a split item
 
+    // the Q head of row r alone (nullptr for a padding row): what the staging loops need, without
+    // the bound (a load of the lane's position) and the output addresses of row()
+    __device__ __forceinline__ const float* q_of(int r) const {
+        const int tok = r / GQA, j = r % GQA;
+        if (MODE == 0) {
+            const int t = tile_t0 + tok;
+            if (tok >= TOK_PER_TILE || t >= ta->t_end) return nullptr;
+            return ta->qT + (size_t)t * ta->q_row + (size_t)(kvh * GQA + j) * ta->q_stride;
+        }
+        if (tok >= slot->ntok) return nullptr;
+        return slot->q[tok] + (size_t)(kvh * GQA + j) * vb->q_stride;
+    }
+
     __device__ __forceinline__ RowInfo row(int r) const {
         // a padding row (no q) sees everything: its lanes stay on the unmasked path of their
         // warp and what they compute from a zero Q row is dropped
@@ -398,30 +411,31 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         if (wht & WHT_Q) {
             float* q_rot = reinterpret_cast<float*>(k_sm + 2 * KT_BYTES);
             for (int i = threadIdx.x; i < BM * (HD / 4); i += UMMA_THREADS) {
-                const RowInfo rq = pb.row(i >> 6);
-                if (rq.q) reinterpret_cast<float4*>(q_rot)[i] = __ldg(reinterpret_cast<const float4*>(rq.q) + (i & 63));
+                const float* rq = pb.q_of(i >> 6);
+                if (rq) reinterpret_cast<float4*>(q_rot)[i] = __ldg(reinterpret_cast<const float4*>(rq) + (i & 63));
             }
             __syncthreads();
             for (int gi = warp; gi < 2 * BM; gi += UMMA_THREADS / 32)
-                if (pb.row(gi >> 1).q) wht_group<false>(q_rot + gi * 128, lane);
+                if (pb.q_of(gi >> 1)) wht_group<false>(q_rot + gi * 128, lane);
             __syncthreads();
         }
-        for (int base_i = 0; base_i < BM * (HD / 4); base_i += UMMA_THREADS * 4) {
-            float4 v[4];
-            int idx[4];
+        constexpr int QU = 4;                               // loads in flight per thread
+        for (int base_i = 0; base_i < BM * (HD / 4); base_i += UMMA_THREADS * QU) {
+            float4 v[QU];
+            int idx[QU];
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
+            for (int u = 0; u < QU; u++) {
                 idx[u] = base_i + u * UMMA_THREADS + threadIdx.x;
                 v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (idx[u] < BM * (HD / 4)) {
-                    const RowInfo rq = pb.row(idx[u] >> 6);
-                    if (rq.q)
+                    const float* rq = pb.q_of(idx[u] >> 6);
+                    if (rq)
                         v[u] = (wht & WHT_Q) ? q_rot4[idx[u]]
-                                             : __ldg(reinterpret_cast<const float4*>(rq.q) + (idx[u] & 63));
+                                             : __ldg(reinterpret_cast<const float4*>(rq) + (idx[u] & 63));
                 }
             }
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
+            for (int u = 0; u < QU; u++) {
                 if (idx[u] >= BM * (HD / 4)) continue;
                 const int row = idx[u] >> 6, d = (idx[u] & 63) * 4;
                 // where the 16-bit value of operand position X of this row lives

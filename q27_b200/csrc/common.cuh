@@ -27,7 +27,8 @@ constexpr int I8_BLK = Q27_I8_BLOCK_BYTES;
 // sides are stored alike; from turbo3 up the V side is always turbo3 and only the K side
 // varies (src/cuda_common.h:47-53).
 enum RowFmt : int { RF_F16 = 0, RF_FP8 = 1, RF_T3 = 2, RF_T5 = 3, RF_I8 = 4 };
-static_assert(RF_F16 == Q27_KV_F16 && RF_FP8 == Q27_KV_FP8 && RF_T3 == Q27_KV_T3, "formats 0..2 are kinds 0..2");
+static_assert((int)RF_F16 == (int)Q27_KV_F16 && (int)RF_FP8 == (int)Q27_KV_FP8 && (int)RF_T3 == (int)Q27_KV_T3,
+              "formats 0..2 are kinds 0..2");
 __host__ __device__ constexpr int k_fmt(int kvk) {
     return kvk == Q27_KV_T3V ? RF_F16 : kvk == Q27_KV_T5K ? RF_T5 : kvk == Q27_KV_I8G64 ? RF_I8 : kvk;
 }
