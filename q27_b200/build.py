@@ -72,11 +72,14 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         results = list(ex.map(lambda s: _compile(s, verbose), srcs))
     objs = [o for o, _ in results]
     if any(changed for _, changed in results) or not LIB.exists():
-        cmd = [_nvcc(), "-shared", "-o", str(LIB), *map(str, objs), "-lcudart"]
+        # link beside the target, then rename: a reader never sees a half-written library
+        tmp = LIB.with_name(LIB.name + ".linking")
+        cmd = [_nvcc(), "-shared", "-o", str(tmp), *map(str, objs), "-lcudart"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             sys.stderr.write(res.stdout + res.stderr)
             raise RuntimeError("link failed")
+        tmp.replace(LIB)
     return LIB
 
 

@@ -5,6 +5,7 @@
 // and k_attn_prefill_T, src/prefill.cu:2293-2388). The tensor-core kernels are checked
 // against them on the GPU and against the CPU oracle.
 #include "common.cuh"
+#include "finish.cuh"
 #include "p2p_exchange.cuh"
 #include "wht.cuh"
 
@@ -141,20 +142,21 @@ k_exact_partial(const __grid_constant__ DevBatch b) {
 
 // Log-sum-exp merge of the nsplit partials {m, l, acc[256]} at pp (stride PART) by a block of
 // COMBINE_THREADS threads. The kernel sits on the step's critical path behind the partial
-// kernel, so it is built around ONE round trip to L2: thread sp fetches {m, l} of split sp
+// kernel, so it is built around ONE round trip to L2: warp 0 fetches {m, l} of every split
 // and, in the same breath, every thread fetches the accumulator pieces it will weigh (four
 // groups of 128 threads each own every fourth split, two dims per thread; the first 80 splits
 // -- all of them in the usual one-CTA-per-SM launches -- are in flight together, which keeps the
 // block at 64 registers so that it fits beside a CTA of the partial kernel when it is launched
 // early); warp 0 then forms the global max, the weights
-// e^{m_s - M} and l; the groups' sums are added in a fixed order (same result every run).
+// e^{m_s - M} and l; the groups' sums are added in the order that csrc/finish.cuh lays down for
+// every merge of split records (same bits every run, and the same as a self-finished launch).
 // Splits with weight 0 (sentinels) hold undefined accumulators: selected, never added. On
 // return threads 0..255 hold the merged accumulator of dim threadIdx.x; mg / lg are valid in
 // every thread.
 constexpr int COMBINE_THREADS = 512;
 __device__ __forceinline__ float combine_core(const float* __restrict__ pp, int nsplit, float& mg,
                                               float& lg) {
-    __shared__ float s_mv[Q27_MAX_SPLITS], s_lv[Q27_MAX_SPLITS], s_w[Q27_MAX_SPLITS];
+    __shared__ float s_w[Q27_MAX_SPLITS];
     __shared__ float s_ml[2];
     __shared__ float s_red[4][HD];
     const int tid = threadIdx.x;
@@ -167,52 +169,33 @@ __device__ __forceinline__ float combine_core(const float* __restrict__ pp, int 
         v[k] = sp < nsplit ? *reinterpret_cast<const float2*>(pp + (size_t)sp * PART + 2 + 2 * c)
                            : make_float2(0.f, 0.f);
     }
-    if (tid < nsplit) {
-        const float2 ml = *reinterpret_cast<const float2*>(pp + (size_t)tid * PART);
-        s_mv[tid] = ml.x;
-        s_lv[tid] = ml.y;
-    }
-    __syncthreads();
     if (tid < 32) {
-        float m = NEG_SENTINEL;
-        for (int sp = tid; sp < nsplit; sp += 32) m = fmaxf(m, s_mv[sp]);
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-        float l = 0.f;
-        for (int sp = tid; sp < nsplit; sp += 32) {
-            const float ms = s_mv[sp];
-            const float w = ms == NEG_SENTINEL ? 0.f : expf(ms - m);
-            s_w[sp] = w;
-            l += s_lv[sp] * w;
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+        float m, l;
+        split_weights(pp, nsplit, tid, s_w, m, l);
         if (tid == 0) { s_ml[0] = m; s_ml[1] = l; }
     }
     __syncthreads();
     mg = s_ml[0];
     lg = s_ml[1];
-    float ax = 0.f, ay = 0.f;
+    float ax = 0.f, ay = 0.f;            // group grp is running sum grp of the merge order
 #pragma unroll
     for (int k = 0; k < EARLY; k++) {
         const int sp = grp + 4 * k;
         const float w = sp < nsplit ? s_w[sp] : 0.f;
-        const float px = v[k].x * w, py = v[k].y * w;
-        ax += w != 0.f ? px : 0.f;
-        ay += w != 0.f ? py : 0.f;
+        split_add(ax, v[k].x, w);
+        split_add(ay, v[k].y, w);
     }
     for (int sp = grp + 4 * EARLY; sp < nsplit; sp += 4) {
         const float w = s_w[sp];
         const float2 u = *reinterpret_cast<const float2*>(pp + (size_t)sp * PART + 2 + 2 * c);
-        const float px = u.x * w, py = u.y * w;
-        ax += w != 0.f ? px : 0.f;
-        ay += w != 0.f ? py : 0.f;
+        split_add(ax, u.x, w);
+        split_add(ay, u.y, w);
     }
     s_red[grp][2 * c] = ax;
     s_red[grp][2 * c + 1] = ay;
     __syncthreads();
     float a = 0.f;
-    if (tid < HD) a = ((s_red[0][tid] + s_red[1][tid]) + s_red[2][tid]) + s_red[3][tid];
+    if (tid < HD) a = split_total(s_red[0][tid], s_red[1][tid], s_red[2][tid], s_red[3][tid]);
     return a;
 }
 
@@ -246,7 +229,7 @@ k_combine(const __grid_constant__ DevBatch b, float* __restrict__ partial_out, i
     }
     float mg, lg;
     const float a = combine_core(S.scratch + ((size_t)t * b.n_q + h) * b.nsplit * PART, b.nsplit, mg, lg);
-    float o = a * (lg > 0.f ? 1.0f / lg : 0.f);
+    float o = __fmul_rn(a, split_inv(lg));
     if (NORMALISE && (b.wht & WHT_OUT)) o = unrotate_head(o);
     if (threadIdx.x < HD) {
         if (NORMALISE) {

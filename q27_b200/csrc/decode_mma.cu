@@ -34,6 +34,7 @@
 #include "decode_mma.cuh"
 #include "t3_lut.cuh"
 #include "wht.cuh"
+#include "finish.cuh"
 
 namespace q27b {
 
@@ -45,7 +46,7 @@ constexpr int STAGE_ROWS = 32;    // rows per ring stage (= 2 key tiles; never c
 constexpr int TILE = 16;          // keys per MMA tile
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
-constexpr int FUSE_MAX_SPLITS = 127;              // the group counters live behind the last split
+constexpr int FUSE_MAX_SPLITS = FINISH_MAX_SPLITS;
 // A launch finishes itself while its partials are few (measured: c1, 6 heads x 37 splits, 21.9 ->
 // 14.3 us per step); long launches are better off with the combine kernel, whose launch hides
 // behind the partial kernel's tail (c3, 24 heads x 74 splits: 94 us that way, 101 us fused).
@@ -508,89 +509,6 @@ __device__ __forceinline__ void stage_t3(WarpAcc& A, uint32_t ks, uint32_t vs, i
     }
 }
 
-// ---- the finishing step of a fused launch -------------------------------------------------
-// Log-sum-exp merge (k_attn_fd_combine, src/spec3.cu:706-739) of the first `used` splits of the
-// NH heads of one (slot, lane, kv group), shared out over the group's own CTAs: once every CTA
-// of the group has written its partial, CTA `me` of `n` merges the 128-output half heads me,
-// me + n, ... of the group's 2 NH. A CTA reads a few tens of KB straight out of L2 (the splits'
-// {m, l} of the head, then `used` values per output, two threads per output on alternate
-// splits, sixteen loads in flight each), so the merge takes a microsecond or two however many
-// heads the group has. Fixed summation order: the result is the same every run. With WHT_OUT
-// the half head -- one 128-group of the rotation -- is un-rotated before it is written.
-template <int NH>
-__device__ void finish_halves(const float* __restrict__ base, int nsplit, int used,
-                              float* __restrict__ out, int me, int n, int wht) {
-    __shared__ float s_w[128];
-    __shared__ float s_inv;
-    __shared__ float s_part[128];
-    const int tid = threadIdx.x, lane = tid & 31;
-    for (int g = me; g < 2 * NH; g += n) {
-        const int h = g >> 1, d = (g & 1) * 128 + (tid & 127), par = tid >> 7;   // par 0, 1: summing; 2: idle
-        float* dst = out + (size_t)h * HD + (g & 1) * 128;
-        if (used == 0) {         // nothing attended (an empty shard): zeros, like the combine
-            if (tid < 128) dst[tid] = 0.f;
-            continue;
-        }
-        const float* rec = base + (size_t)h * nsplit * PART;
-        __syncthreads();                                    // s_w / s_inv / s_part of the group before
-        if (tid < 32) {
-            // used <= 128: lane owns splits lane + 32 k (clamped loads, masked weights)
-            float2 ml[4];
-            bool live[4];
-            float m = NEG_SENTINEL;
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const int sp = lane + 32 * k;
-                ml[k] = __ldcg(reinterpret_cast<const float2*>(rec + (size_t)min(sp, used - 1) * PART));
-                live[k] = sp < used && ml[k].x != NEG_SENTINEL;
-                m = fmaxf(m, live[k] ? ml[k].x : NEG_SENTINEL);
-            }
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-            float l = 0.f;
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const float w = live[k] ? expf(ml[k].x - m) : 0.f;
-                s_w[lane + 32 * k] = w;
-                l += live[k] ? ml[k].y * w : 0.f;
-            }
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-            if (lane == 0) s_inv = l > 0.f ? 1.0f / l : 0.f;
-        }
-        __syncthreads();
-        float sum = 0.f;
-        if (par < 2) {
-            float a[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int s0 = par; s0 < used; s0 += 32) {       // this thread's splits: s0, s0 + 2, ...
-                float v[16], w[16];
-#pragma unroll
-                for (int u = 0; u < 16; u++) {              // every load is issued before any is used
-                    const int sp = min(s0 + 2 * u, used - 1);
-                    v[u] = __ldcg(rec + (size_t)sp * PART + 2 + d);
-                    w[u] = s0 + 2 * u < used ? s_w[sp] : 0.f;
-                }
-#pragma unroll
-                for (int u = 0; u < 16; u++) {
-                    // sentinel splits hold undefined accumulators: selected, never added
-                    const float x = v[u] * w[u];
-                    a[u & 3] += w[u] != 0.f ? x : 0.f;
-                }
-            }
-            sum = (a[0] + a[1]) + (a[2] + a[3]);
-            if (par == 1) s_part[tid & 127] = sum;
-        }
-        __syncthreads();
-        if (tid < 128) s_part[tid] = (sum + s_part[tid]) * s_inv;    // even splits + odd splits
-        if (wht & WHT_OUT) {
-            __syncthreads();
-            if (tid < 32) wht_group<true>(s_part, lane);
-        }
-        __syncthreads();
-        if (tid < 128) dst[tid] = s_part[tid];
-    }
-}
-
 // ---- the kernel -------------------------------------------------------------------------
 // FUSE: the variant that also finishes the launch (b.fuse is set for it and only for it); the
 // plain variant does not carry that code.
@@ -607,6 +525,7 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
     uint8_t* ring = smem + HEADER_BYTES;
     float* q_stage = reinterpret_cast<float*>(ring + work_bytes<KVK>());
     __shared__ int s_fail, s_grp_ok;
+    __shared__ float s_fin[FUSE ? FINISH_SMEM_FLOATS : 1];
     __shared__ float s_wt[NHEADS][WAYS], s_mb[NHEADS], s_lb[NHEADS];
 
     pdl_trigger();               // a combine kernel may be scheduled; it waits for this grid
@@ -624,10 +543,8 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
         // has room for); words that do not carry the tag yet (first use of this scratch, or
         // partials of a call with more splits written over them) are armed here, long before
         // anybody arrives on them
-        ticket = reinterpret_cast<unsigned long long*>(
-                     S.scratch + (size_t)S.ntok * b.n_q * b.nsplit * PART) +
-                 ((size_t)t * groups + kvg) * 2;
-        if (threadIdx.x == 0) { ticket_arm(ticket); ticket_arm(ticket + 1); }
+        ticket = group_counters(S.scratch, S.ntok, b.n_q, b.nsplit, t * groups + kvg);
+        if (threadIdx.x == 0) group_arm(ticket);
     }
     int max_len = 0;
     for (int u = 0; u < S.ntok; u++)
@@ -891,32 +808,21 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
         const unsigned n = (unsigned)b.nsplit;
         __syncthreads();                          // this CTA's partial rows are written
         if (threadIdx.x == 0) {
-            __threadfence();
-            atomicAdd(ticket, 1ull);
-            bool ok = false;
-            for (int i = 0; i < (1 << 20) && !ok; i++) {   // bounded: ~0.1 s, then the flag
-                unsigned long long v;
-                asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(ticket) : "memory");
-                ok = (unsigned)(v & 0xffffu) >= n;
-                if (!ok && i > 64) __nanosleep(64);
-            }
+            const bool ok = group_wait(ticket, n);
             if (!ok) atomicExch(&g_wait_timeout_flag, 1);
             s_grp_ok = ok ? 1 : 0;
         }
         __syncthreads();
         if (s_grp_ok) {
+            // CTA `sp` of `n` takes the half heads sp, sp + n, ... of the group's 2 NHEADS
             const int used = min(b.nsplit, (max_len + chunk - 1) / chunk);
-            finish_halves<NHEADS>(S.scratch + ((size_t)t * b.n_q + kvh0 * GQA) * b.nsplit * PART,
-                                  b.nsplit, used, S.out[t] + (size_t)kvh0 * GQA * HD, sp, (int)n, b.wht);
+            const float* base = S.scratch + ((size_t)t * b.n_q + kvh0 * GQA) * b.nsplit * PART;
+            for (int g = sp; g < 2 * NHEADS; g += (int)n)
+                merge_half_head(base + (size_t)(g >> 1) * b.nsplit * PART, used, g & 1,
+                                S.out[t] + (size_t)(kvh0 * GQA + (g >> 1)) * HD + (g & 1) * 128, b.wht, s_fin);
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            const unsigned long long prev = atomicAdd(ticket + 1, 1ull);
-            if ((unsigned)(prev & 0xffffu) + 1 == n) {
-                atomicExch(ticket, TICKET_TAG << 16);
-                atomicExch(ticket + 1, TICKET_TAG << 16);
-            }
-        }
+        if (threadIdx.x == 0) group_leave(ticket, n);
     }
 }
 

@@ -198,30 +198,38 @@ def test_kv_split_through_mailboxes(oracle, cuda, kvk):
             Q._lib.check(lib.q27_xchg_free(b), "q27_xchg_free")
 
 
-def test_one_call_exchange_with_a_single_owner(oracle, cuda):
+@pytest.mark.parametrize("kvk,pos", [(KV_T3, [2999, 2000, 7]), (KV_F16, [2999])],
+                         ids=["turbo3-three-lanes", "f16-one-lane"])
+def test_one_call_exchange_with_a_single_owner(oracle, cuda, kvk, pos):
     """q27_attn_decode_exchange with one rank: the combine, the (empty) exchange and the merge in
-    ONE kernel, device-counted epochs over several steps, equal to the plain decode. (With more
-    owners the kernel waits for its peers' rows, which only real ranks on their own GPUs can
-    provide: tests/test_multi_gpu.py.)"""
+    ONE kernel, device-counted epochs over several steps, equal to the plain decode bit for bit --
+    also where the plain decode is the single launch that merges its own splits (one lane, short
+    context): every merge of split records adds in one order. (With more owners the kernel waits
+    for its peers' rows, which only real ranks on their own GPUs can provide:
+    tests/test_multi_gpu.py.)"""
     import ctypes as C
     lib = Q._lib.lib()
-    c = synth.make_case(oracle, KV_T3, rows=3000, pos=[2999, 2000, 7], seed=66, outlier_frac=0.02)
-    ref = oracle.attn_decode(c.q, c.k, c.v, KV_T3, c.pos)
+    nl = len(pos)
+    c = synth.make_case(oracle, kvk, rows=3000, pos=pos, seed=66, outlier_frac=OUTLIERS[kvk])
+    ref = synth.scale_out(c, oracle.attn_decode(c.q, c.k, c.v, kvk, c.pos))
     dc = DeviceCase(c, cuda)
-    npairs = 3 * 24
+    npairs = nl * 24
     ptr = C.c_void_p()
     Q._lib.check(lib.q27_xchg_alloc(lib.q27_xchg_mailbox_bytes(1, npairs), C.byref(ptr), None), "q27_xchg_alloc")
     try:
         out = torch.full((npairs, 256), float("nan"), device=cuda)
         n0 = Q.launch_count()
         for _ in range(3):                          # epoch 0: the mailbox counts the steps itself
-            Q.attn_decode_exchange([dc.slot()], 3, synth.Q_STRIDE, 24, 4, 256, SCALE, [ptr.value], 0, 0, out,
-                                   kvk=KV_T3)
+            Q.attn_decode_exchange([dc.slot()], nl, synth.Q_STRIDE, 24, 4, 256, SCALE, [ptr.value], 0, 0, out,
+                                   kvk=kvk)
         torch.cuda.synchronize()
         assert Q.launch_count() - n0 == 3 * 2       # partial kernel + one exchange kernel per step
-        assert synth.tolerance_ok(out.cpu().numpy().reshape(3, -1), ref)[0]
+        assert synth.tolerance_ok(synth.scale_out(c, out.cpu().numpy().reshape(nl, -1)), ref)[0]
+        n1 = Q.launch_count()
         plain = dc.run3()
-        assert (out.cpu().numpy().reshape(3, -1).view(np.uint32) == plain.view(np.uint32)).all()
+        if nl == 1:
+            assert Q.launch_count() - n1 == 1       # the decode kernel finished the step itself
+        assert (out.cpu().numpy().reshape(nl, -1).view(np.uint32) == plain.view(np.uint32)).all()
     finally:
         torch.cuda.synchronize()
         Q._lib.check(lib.q27_xchg_free(ptr.value), "q27_xchg_free")
