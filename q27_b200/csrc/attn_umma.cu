@@ -245,6 +245,12 @@ struct Problem {
         return slot->q[tok] + (size_t)(kvh * GQA + j) * vb->q_stride;
     }
 
+    // rows [0, live_rows()) of the tile carry a Q head, the rest is padding
+    __device__ __forceinline__ int live_rows() const {
+        if (MODE == 0) return max(0, min(TOK_PER_TILE, ta->t_end - tile_t0)) * GQA;
+        return min(slot->ntok * GQA, BM);
+    }
+
     __device__ __forceinline__ RowInfo row(int r) const {
         // a padding row (no q) sees everything: its lanes stay on the unmasked path of their
         // warp and what they compute from a zero Q row is dropped
@@ -394,6 +400,89 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                      ::"r"(s32(tmem_slot)), "n"(TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
+    // ---- what the staging warps know about their side (K or V), before the roles part ways ----
+    // the first four staging warps feed the K ring, the other four the V ring; a tile is exactly
+    // one cache page
+    const bool is_load = warp >= FIRST_LOAD_WARP;
+    const int side = is_load ? (warp - FIRST_LOAD_WARP) >> 2 : 0;                  // 0 = K, 1 = V
+    const int p = is_load ? (int)threadIdx.x - (FIRST_LOAD_WARP + 4 * side) * 32 : 0;   // 0..127 within the side
+    const void* const* tab = side ? vtab : ktab;
+    auto page_of = [&](int i) {
+        return static_cast<const uint8_t*>(tab[(pb.lo + i * BN) >> PAGE_SHIFT]);
+    };
+    auto nkeys_of = [&](int i) { return min(BN, pb.hi - (pb.lo + i * BN)); };
+    // Packed rows (turbo3, fp8) come in with 16-byte asynchronous copies into two raw buffers
+    // per side, each with a "landed" and a "read" mbarrier.
+    //   turbo3: a tile's rows of this kv head are 64 keys x 100 B, 400 B apart in the page; what
+    //   is copied is the aligned 112-byte window that holds them (a row starts on a 16-byte
+    //   boundary and kv head h sits at byte 100 h, so the window [100 h rounded down, + 112)
+    //   never leaves the row): 448 copies per tile and side instead of 1600 four-byte ones (a
+    //   block per thread straight from global memory costs one L1 wavefront per lane per load
+    //   and bounded this path). The buffers live in the third V slot.
+    //   fp8: 64 keys x 256 B, coalesced; the third K slot and the third V slot each hold a
+    //   side's two buffers. (Holding two tiles of raw bytes in registers instead spilled and
+    //   made this path the bottleneck of the fp8 kernels.)
+    constexpr int RAW_ROW = 112;
+    constexpr int RAW_BYTES = KVK == Q27_KV_T3 ? BN * RAW_ROW : BN * HD;
+    static_assert(KVK != Q27_KV_T3 || 4 * RAW_BYTES <= KT_BYTES, "the raw buffers live in the third V slot");
+    uint8_t* raw = KVK == Q27_KV_T3 ? raw_sm + side * 2 * RAW_BYTES : (side ? v_sm : k_sm) + 2 * KT_BYTES;
+    const uint32_t rfull = raw_full + 8 * (2 * side), rempty = raw_empty + 8 * (2 * side);
+    const int win0 = (pb.kvh * 2 * T3_BLK) & ~15;        // turbo3: window start inside the row
+    const int blk_off = pb.kvh * 2 * T3_BLK - win0;      // 0, 4, 8 or 12
+    // turbo3: this thread's (up to) 4 pieces of a tile: source offset inside the page and key
+    // index are the same for every tile
+    uint32_t soff[4], doff[4];
+    int wkey[4];
+    if constexpr (KVK == Q27_KV_T3) {
+#pragma unroll
+        for (int n = 0; n < 4; n++) {
+            const int c = p + NPROD * n;              // piece 0..447 of the tile's windows
+            const int key = c / 7, j = c - 7 * key;
+            wkey[n] = c < BN * 7 ? key : BN;          // BN: never below the tile's key count
+            soff[n] = (uint32_t)(key * n_kv * (2 * T3_BLK) + win0 + 16 * j);
+            doff[n] = (uint32_t)(key * RAW_ROW + 16 * j);
+        }
+    }
+    auto issue_raw = [&](int i) {
+        const int buf = i & 1, nk = nkeys_of(i);
+        const uint8_t* page = page_of(i);
+        if constexpr (KVK == Q27_KV_T3) {
+            const uint32_t dst = s32(raw + buf * RAW_BYTES);
+#pragma unroll
+            for (int n = 0; n < 4; n++)
+                if (wkey[n] < nk)
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                                 ::"r"(dst + doff[n]), "l"(page + soff[n]) : "memory");
+        } else if constexpr (KVK == Q27_KV_FP8) {
+            uint8_t* dst = raw + buf * RAW_BYTES;
+#pragma unroll
+            for (int n = 0; n < 8; n++) {
+                const int q = p + NPROD * n;          // 16-byte chunk 0..1023
+                const int key = q >> 4, c16 = q & 15;
+                if (key < nk)
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                                 ::"r"(s32(dst + q * 16)),
+                                   "l"(page + ((size_t)key * n_kv + pb.kvh) * HD + c16 * 16)
+                                 : "memory");
+                else                                   // rows past the range: exact zeros
+                    *reinterpret_cast<uint4*>(dst + q * 16) = make_uint4(0, 0, 0, 0);
+            }
+            if (nk < BN) __threadfence_block();        // the zeros, before the arrival below
+        }
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
+                     ::"r"(rfull + 8 * buf) : "memory");
+    };
+    // The first two tiles' packed rows are asked for before the Q tile is staged (the table
+    // look-up and the trip to HBM overlap it) -- unless the folded rotation needs the buffers'
+    // room for the fp32 Q tile first.
+    const bool raw_early = KVK != Q27_KV_F16 && !(wht & WHT_Q);
+    if (raw_early) {
+        __syncthreads();                               // the barriers are initialised
+        if (is_load) {
+            if (ntiles > 0) issue_raw(0);
+            if (ntiles > 1) issue_raw(1);
+        }
+    }
     {
         // Q tile, fp32 -> fp16, by ALL threads with coalesced loads: consecutive threads take
         // consecutive 16-byte pieces of a row (a thread walking its own row costs a dependent
@@ -408,26 +497,31 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         const float4* q_rot4 = reinterpret_cast<const float4*>(k_sm + 2 * KT_BYTES);
         static_assert((K_SLOTS - 2 + V_SLOTS) * KT_BYTES >= BM * HD * 4, "room for the fp32 Q tile");
         static_assert(2 * KT_BYTES >= BM * QT_PITCH, "the waiting half stays clear of it");
+        // Only the tile's live rows (lanes x 6 heads of a verify step: 36 of 128) are fetched and
+        // converted; the rows behind them are zeroed without a trip to memory.
+        const int live = pb.live_rows();
+        const int pieces = live * (HD / 4);                 // 16-byte pieces of the live rows
         if (wht & WHT_Q) {
             float* q_rot = reinterpret_cast<float*>(k_sm + 2 * KT_BYTES);
-            for (int i = threadIdx.x; i < BM * (HD / 4); i += UMMA_THREADS) {
+            for (int i = threadIdx.x; i < pieces; i += UMMA_THREADS) {
                 const float* rq = pb.q_of(i >> 6);
                 if (rq) reinterpret_cast<float4*>(q_rot)[i] = __ldg(reinterpret_cast<const float4*>(rq) + (i & 63));
             }
             __syncthreads();
-            for (int gi = warp; gi < 2 * BM; gi += UMMA_THREADS / 32)
+            for (int gi = warp; gi < 2 * live; gi += UMMA_THREADS / 32)
                 if (pb.q_of(gi >> 1)) wht_group<false>(q_rot + gi * 128, lane);
             __syncthreads();
         }
-        constexpr int QU = 4;                               // loads in flight per thread
-        for (int base_i = 0; base_i < BM * (HD / 4); base_i += UMMA_THREADS * QU) {
+        // loads in flight per thread: a verify step's rows (up to 6 lanes) in one pass
+        constexpr int QU = MODE == 1 ? 5 : 4;
+        for (int base_i = 0; base_i < pieces; base_i += UMMA_THREADS * QU) {
             float4 v[QU];
             int idx[QU];
 #pragma unroll
             for (int u = 0; u < QU; u++) {
                 idx[u] = base_i + u * UMMA_THREADS + threadIdx.x;
                 v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (idx[u] < BM * (HD / 4)) {
+                if (idx[u] < pieces) {
                     const float* rq = pb.q_of(idx[u] >> 6);
                     if (rq)
                         v[u] = (wht & WHT_Q) ? q_rot4[idx[u]]
@@ -436,7 +530,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             }
 #pragma unroll
             for (int u = 0; u < QU; u++) {
-                if (idx[u] >= BM * (HD / 4)) continue;
+                if (idx[u] >= pieces) continue;
                 const int row = idx[u] >> 6, d = (idx[u] & 63) * 4;
                 // where the 16-bit value of operand position X of this row lives
                 auto q_loc = [&](int X) -> uint8_t* {
@@ -459,6 +553,13 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 }
             }
         }
+        // the padding rows of the shared-memory half: whole 128-byte rows of both blocks (the
+        // swizzle permutes 16-byte chunks inside a row); those of the tensor-memory half are
+        // zeroed by their owners below
+        for (int i = threadIdx.x; i < (BM - live) * 16; i += UMMA_THREADS) {
+            const int row = live + (i >> 4), blk = (i >> 3) & 1, ch = i & 7;
+            *reinterpret_cast<uint4*>(q_sm + blk * (BM * 128) + row * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+        }
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
@@ -471,7 +572,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             for (int c = 0; c < Q_TMEM_DIMS / 2; c += 32) {
                 float packed[32];
 #pragma unroll
-                for (int e = 0; e < 32; e++) packed[e] = __uint_as_float(src[c + e]);
+                for (int e = 0; e < 32; e++) packed[e] = (int)threadIdx.x < live ? __uint_as_float(src[c + e]) : 0.f;
                 tc_st32(qaddr + c, packed);
             }
             tc_wait_st();
@@ -571,17 +672,21 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         static_assert((K_SLOTS + V_SLOTS) * KT_BYTES >= BM * OROT_PITCH * 4, "room for the fp32 O tile");
         float* o_rot = reinterpret_cast<float*>(k_sm);
         const bool rot_out = MODE == 0 && (wht & WHT_OUT) && pb.piece < 0;
-        if (!ok && rot_out) *epi_bad = 1;
+        // Partial records {m, l, acc[256]} (verify; a key range of a split prefill item) take the
+        // same road: a thread owns a row, so storing it from here costs one 8-byte piece of 32
+        // different lines per instruction (2.7 us of a verify step). The rows go to the idle rings
+        // as {m, l, -, -, acc[256]} and every warp writes whole rows after the closing barrier.
+        const bool part_rows = MODE == 1 || pb.piece >= 0;
+        if (!ok && (rot_out || part_rows)) *epi_bad = 1;
         if (ok) {
             const float inv = l > 0.f ? 1.f / l : 0.f;
+            float* stage = o_rot + (size_t)r * OROT_PITCH;
             if (ri.part) {
-                ri.part[0] = m_ref == -INFINITY ? NEG_SENTINEL : m_ref * 0.6931471805599453f;
-                ri.part[1] = l;
+                stage[0] = m_ref == -INFINITY ? NEG_SENTINEL : m_ref * 0.6931471805599453f;
+                stage[1] = l;
             }
             // the TMEM loads are warp-collective: every lane runs them, padding rows just
-            // drop what they read (the stores are fire-and-forget: a row per thread is
-            // uncoalesced, but going through shared memory for whole-line stores measured
-            // slower -- it puts a dependent chain where the direct stores overlap)
+            // drop what they read
             if (warp_has_rows) {
 #pragma unroll 1
                 for (int c = 0; c < HD; c += 32) {
@@ -593,8 +698,8 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                     auto reg = [](int n) {
                         return KVK == Q27_KV_T3 ? (n & 16) + ((n & 1) ? 8 + ((n & 15) >> 1) : ((n & 15) >> 1)) : n;
                     };
-                    float* dst = rot_out ? o_rot + (size_t)r * OROT_PITCH : ri.out;
                     if (ri.out) {
+                        float* dst = rot_out ? stage : ri.out;
 #pragma unroll
                         for (int e = 0; e < 32; e += 4)
                             *reinterpret_cast<float4*>(dst + c + e) =
@@ -602,9 +707,9 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                                             o[reg(e + 3)] * inv);
                     } else if (ri.part) {
 #pragma unroll
-                        for (int e = 0; e < 32; e += 2)
-                            *reinterpret_cast<float2*>(ri.part + 2 + c + e) =
-                                make_float2(o[reg(e)], o[reg(e + 1)]);
+                        for (int e = 0; e < 32; e += 4)
+                            *reinterpret_cast<float4*>(stage + 4 + c + e) =
+                                make_float4(o[reg(e)], o[reg(e + 1)], o[reg(e + 2)], o[reg(e + 3)]);
                     }
                 }
             }
@@ -685,18 +790,9 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         }
     } else {
         // ------------------------------ K / V staging --------------------------------------
-        // the first four staging warps feed the K ring, the other four the V ring; a tile is
-        // exactly one cache page
-        const int side = (warp - FIRST_LOAD_WARP) >> 2;                 // 0 = K, 1 = V
-        const int p = threadIdx.x - (FIRST_LOAD_WARP + 4 * side) * 32;  // 0..127 within the side
         const int nslots = side ? VSL : KSL;
         const uint32_t full = side ? v_full : k_full, empty = side ? v_empty : k_empty;
         uint8_t* ring = side ? v_sm : k_sm;
-        const void* const* tab = side ? vtab : ktab;
-        auto page_of = [&](int i) {
-            return static_cast<const uint8_t*>(tab[(pb.lo + i * BN) >> PAGE_SHIFT]);
-        };
-        auto nkeys_of = [&](int i) { return min(BN, pb.hi - (pb.lo + i * BN)); };
         auto wait_slot = [&](int i) -> bool {
             bool okw = true;
             if (i >= nslots) okw = bar_wait(empty + 8 * (i % nslots), (uint32_t)(((i / nslots) - 1) & 1));
@@ -729,47 +825,11 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
         } else if constexpr (KVK == Q27_KV_T3) {
-            // A tile's packed rows of this kv head (64 keys x 100 B, 400 B apart in the page)
-            // come in with 16-byte asynchronous copies of the aligned 112-byte window that
-            // holds them (a row starts on a 16-byte boundary and kv head h sits at byte 100 h,
-            // so the window [100 h rounded down, + 112) never leaves the row): 448 copies per
-            // tile and side instead of 1600 four-byte ones (a block per thread straight from
-            // global memory costs one L1 wavefront per lane per load and bounded this path);
-            // two raw buffers per side, each with a "landed" and a "read" mbarrier. Each thread
-            // then decodes one 50-byte block from shared memory.
-            constexpr int RAW_ROW = 112;
-            constexpr int RAW_BYTES = BN * RAW_ROW;
-            static_assert(4 * RAW_BYTES <= KT_BYTES, "the raw buffers live in the third V slot");
-            uint8_t* raw = raw_sm + side * 2 * RAW_BYTES;
-            const uint32_t rfull = raw_full + 8 * (2 * side), rempty = raw_empty + 8 * (2 * side);
-            const int win0 = (pb.kvh * 2 * T3_BLK) & ~15;        // window start inside the row
-            const int blk_off = pb.kvh * 2 * T3_BLK - win0;      // 0, 4, 8 or 12
-            // this thread's (up to) 4 pieces of a tile: source offset inside the page and key
-            // index are the same for every tile
-            uint32_t soff[4], doff[4];
-            int wkey[4];
-#pragma unroll
-            for (int n = 0; n < 4; n++) {
-                const int c = p + NPROD * n;              // piece 0..447 of the tile's windows
-                const int key = c / 7, j = c - 7 * key;
-                wkey[n] = c < BN * 7 ? key : BN;          // BN: never below the tile's key count
-                soff[n] = (uint32_t)(key * n_kv * (2 * T3_BLK) + win0 + 16 * j);
-                doff[n] = (uint32_t)(key * RAW_ROW + 16 * j);
+            // each thread decodes one 50-byte block of the tile's packed rows from shared memory
+            if (!raw_early) {
+                if (ntiles > 0) issue_raw(0);
+                if (ntiles > 1) issue_raw(1);
             }
-            auto issue_raw = [&](int i) {
-                const int buf = i & 1, nk = nkeys_of(i);
-                const uint8_t* page = page_of(i);
-                const uint32_t dst = s32(raw + buf * RAW_BYTES);
-#pragma unroll
-                for (int n = 0; n < 4; n++)
-                    if (wkey[n] < nk)
-                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-                                     ::"r"(dst + doff[n]), "l"(page + soff[n]) : "memory");
-                asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
-                             ::"r"(rfull + 8 * buf) : "memory");
-            };
-            if (ntiles > 0) issue_raw(0);
-            if (ntiles > 1) issue_raw(1);
             for (int i = 0; i < ntiles; i++) {
                 const int buf = i & 1;
                 const uint32_t par = (uint32_t)((i >> 1) & 1);
@@ -800,36 +860,11 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
         } else {
-            // fp8: a tile's rows of this kv head (64 keys x 256 B) come in with coalesced
-            // 16-byte asynchronous copies into one of two raw buffers per side, and each
-            // thread converts its sixteen 8-byte pieces from shared memory. (Holding two
-            // tiles of raw bytes in registers instead spilled and made this path the
-            // bottleneck of the fp8 kernels.)
-            constexpr int RAW_BYTES = BN * HD;            // 16384
-            uint8_t* raw = (side ? v_sm : k_sm) + 2 * KT_BYTES;
-            const uint32_t rfull = raw_full + 8 * (2 * side), rempty = raw_empty + 8 * (2 * side);
-            auto issue_raw = [&](int i) {
-                const int buf = i & 1, nk = nkeys_of(i);
-                const uint8_t* page = page_of(i);
-                uint8_t* dst = raw + buf * RAW_BYTES;
-#pragma unroll
-                for (int n = 0; n < 8; n++) {
-                    const int q = p + NPROD * n;          // 16-byte chunk 0..1023
-                    const int key = q >> 4, c16 = q & 15;
-                    if (key < nk)
-                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-                                     ::"r"(s32(dst + q * 16)),
-                                       "l"(page + ((size_t)key * n_kv + pb.kvh) * HD + c16 * 16)
-                                     : "memory");
-                    else                                   // rows past the range: exact zeros
-                        *reinterpret_cast<uint4*>(dst + q * 16) = make_uint4(0, 0, 0, 0);
-                }
-                if (nk < BN) __threadfence_block();        // the zeros, before the arrival below
-                asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
-                             ::"r"(rfull + 8 * buf) : "memory");
-            };
-            if (ntiles > 0) issue_raw(0);
-            if (ntiles > 1) issue_raw(1);
+            // fp8: each thread converts its sixteen 8-byte pieces of the tile from shared memory
+            if (!raw_early) {
+                if (ntiles > 0) issue_raw(0);
+                if (ntiles > 1) issue_raw(1);
+            }
             for (int i = 0; i < ntiles; i++) {
                 const int buf = i & 1;
                 const uint32_t par = (uint32_t)((i >> 1) & 1);
@@ -857,6 +892,21 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "n"(TMEM_COLS) : "memory");
+    }
+    if ((MODE == 1 || pb.piece >= 0) && *epi_bad == 0) {
+        // the partial records of the live rows, a warp per row, 8-byte pieces (a record starts on
+        // an 8-byte boundary): whole lines
+        constexpr int OROT_PITCH = HD + 4;
+        const float* o_st = reinterpret_cast<const float*>(k_sm);
+        const int live = pb.live_rows();
+        for (int r = warp; r < live; r += UMMA_THREADS / 32) {
+            float* part = pb.row(r).part;
+            if (!part) continue;
+            const float* src = o_st + (size_t)r * OROT_PITCH;
+            for (int q = lane; q < PART / 2; q += 32)
+                reinterpret_cast<float2*>(part)[q] =
+                    q == 0 ? make_float2(src[0], src[1]) : *reinterpret_cast<const float2*>(src + 2 + 2 * q);
+        }
     }
     if (MODE == 0 && (wht & WHT_OUT) && pb.piece < 0 && *epi_bad == 0) {
         constexpr int OROT_PITCH = HD + 4;
