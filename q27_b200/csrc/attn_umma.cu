@@ -309,7 +309,6 @@ __device__ __forceinline__ void half_store(const RawHalf<KVK>& t, uint8_t* dst, 
     } else if constexpr (KVK == Q27_KV_T3) {
         const int key = p & 63;
         const uint32_t* w = t.w;
-        const T3Tab tab = t3_tables();
         // 32-bit little-endian word at byte `o` of the block (o even, compile time); block 1
         // sits 2 bytes into the loaded words, block 0 at byte 0
         auto word_at = [&](int o) {
@@ -319,6 +318,7 @@ __device__ __forceinline__ void half_store(const RawHalf<KVK>& t, uint8_t* dst, 
         constexpr int blk = BLK;
         const __half nh = __ushort_as_half((unsigned short)(word_at(0) & 0xffffu));
         const __half2 n2 = key < nkeys ? __half2half2(nh) : __float2half2_rn(0.f);
+        const T3Tab tab = t3_tables_scaled(n2);   // one block, one norm: the pools hold centroid x norm
 #pragma unroll
         for (int g8 = 0; g8 < 8; g8++) {         // 16 dims per group
             const uint32_t Qw = word_at(2 + 4 * g8);
@@ -332,13 +332,6 @@ __device__ __forceinline__ void half_store(const RawHalf<KVK>& t, uint8_t* dst, 
             // Q is staged with the same permutation (a dot product does not care) and the
             // output columns are put back in order in the epilogue, so the eight PRMTs per
             // group that would interleave them are never spent.
-#pragma unroll
-            for (int i = 0; i < 4; i++) {   // fp16 centroid x fp16 norm, rounded once
-                __half2 he = __hmul2(*reinterpret_cast<__half2*>(&e[i]), n2);
-                __half2 ho = __hmul2(*reinterpret_cast<__half2*>(&o[i]), n2);
-                e[i] = *reinterpret_cast<uint32_t*>(&he);
-                o[i] = *reinterpret_cast<uint32_t*>(&ho);
-            }
             const int ch = 16 * blk + 2 * g8;    // 8-position chunk index within the head
             *reinterpret_cast<uint4*>(dst + (ch >> 3) * (BN * 128) + sw128(key, ch & 7)) =
                 make_uint4(e[0], e[1], e[2], e[3]);
