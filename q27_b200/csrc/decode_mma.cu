@@ -83,7 +83,15 @@ template <int KVK> constexpr int merge_bytes() { return Fmt<KVK>::NCW * GQA * PA
 template <int KVK> constexpr int work_bytes() {
     return ring_bytes<KVK>() > merge_bytes<KVK>() ? ring_bytes<KVK>() : merge_bytes<KVK>();
 }
-template <int KVK> constexpr int qstage_bytes() { return Fmt<KVK>::KVH * GQA * HD * 4; }
+// The staged Q heads are read back as Q^T fragments by lanes that differ in head (g) and in
+// thread column (c). At a pitch of 256 floats every head starts on the same bank: 6 (fp16 /
+// fp8) or 24 (turbo3, where the columns are 32 floats apart as well) lanes of a load collide,
+// and the eight warps build their fragments through one shared-memory port (1.6 us of a short
+// decode). Padded pitches, in floats, multiples of 4 for the 16-byte staging stores: fp16 reads
+// 8-byte pairs at 8 g + 2 c, fp8 at 4 g + 16 c (two ways at best: its columns are 16 floats
+// apart), turbo3 single floats at 4 g (four ways: its columns stay 32 apart).
+template <int KVK> constexpr int q_pitch() { return KVK == Q27_KV_F16 ? HD + 8 : HD + 4; }
+template <int KVK> constexpr int qstage_bytes() { return Fmt<KVK>::KVH * GQA * q_pitch<KVK>() * 4; }
 template <int KVK> constexpr int smem_bytes() {
     return HEADER_BYTES + work_bytes<KVK>() + qstage_bytes<KVK>();
 }
@@ -524,6 +532,7 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
     uint64_t* empty = full + 16;
     uint8_t* ring = smem + HEADER_BYTES;
     float* q_stage = reinterpret_cast<float*>(ring + work_bytes<KVK>());
+    constexpr int QP = q_pitch<KVK>();
     __shared__ int s_fail, s_grp_ok;
     __shared__ float s_fin[FUSE ? FINISH_SMEM_FLOATS : 1];
     __shared__ float s_wt[NHEADS][WAYS], s_mb[NHEADS], s_lb[NHEADS];
@@ -649,17 +658,31 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
         } else {
             // ---------------- consumers ----------------
             const int ctid = threadIdx.x;         // 0 .. NCW*32-1
-            // the CTA's query heads, fp32, staged once with coalesced loads
-            for (int i = ctid; i < NHEADS * (HD / 4); i += NCW * 32) {
-                const int h = i / (HD / 4), d4 = i % (HD / 4);
-                reinterpret_cast<float4*>(q_stage)[i] = __ldg(reinterpret_cast<const float4*>(
-                    S.q[t] + (size_t)(kvh0 * GQA + h) * b.q_stride) + d4);
+            // the CTA's query heads, fp32, staged once with coalesced loads, all of a thread's
+            // loads in flight together (one after the other they cost a trip to L2 each: 4 us for
+            // the 24 heads of a turbo3 CTA)
+            {
+                constexpr int NQ4 = NHEADS * (HD / 4);
+                constexpr int QL = (NQ4 + NCW * 32 - 1) / (NCW * 32);
+                float4 qv[QL];
+#pragma unroll
+                for (int u = 0; u < QL; u++) {
+                    const int i = ctid + u * NCW * 32;
+                    const int h = min(i, NQ4 - 1) / (HD / 4), d4 = i % (HD / 4);
+                    qv[u] = __ldg(reinterpret_cast<const float4*>(S.q[t] + (size_t)(kvh0 * GQA + h) * b.q_stride) + d4);
+                }
+#pragma unroll
+                for (int u = 0; u < QL; u++) {
+                    const int i = ctid + u * NCW * 32;
+                    if (i < NQ4) reinterpret_cast<float4*>(q_stage + (i / (HD / 4)) * QP)[i % (HD / 4)] = qv[u];
+                }
             }
             if (b.wht & WHT_Q) {
                 // the forward rotation of wht3 (src/spec3.cu:595-614) on the staged heads, a
                 // 128-group per warp at a time, while the producer is already filling the ring
                 asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32));
-                for (int gi = warp; gi < NHEADS * 2; gi += NCW) wht_group<false>(q_stage + gi * 128, lane);
+                for (int gi = warp; gi < NHEADS * 2; gi += NCW)
+                    wht_group<false>(q_stage + (gi >> 1) * QP + (gi & 1) * 128, lane);
             }
             // Rows past the end of a ragged last stage are never copied; their weights are exact
             // zeros, so what the ring holds there only has to decode to finite numbers. Any
@@ -684,14 +707,22 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
             // Q^T fragments: column n = g is head (kvh0 + hq)*6 + g (columns 6, 7 are zero padding)
             uint32_t qf[16][2];
             {
-                const float* qh = q_stage + (size_t)(hq * GQA + (g < GQA ? g : 0)) * HD;
+                // padding columns read what a live lane of their half-warp reads (a broadcast)
+                const float* qh = q_stage + (size_t)(hq * GQA + (g < GQA ? g : g - 2)) * QP;
 #pragma unroll
                 for (int s = 0; s < 16; s++)
 #pragma unroll
                     for (int r = 0; r < 2; r++) {
-                        const float x0 = g < GQA ? qh[kdim<KVK>(s, c, r, 0)] : 0.f;
-                        const float x1 = g < GQA ? qh[kdim<KVK>(s, c, r, 1)] : 0.f;
-                        qf[s][r] = pack_h2(x0, x1);
+                        float x0, x1;
+                        if constexpr (KVK == Q27_KV_T3) {
+                            x0 = qh[kdim<KVK>(s, c, r, 0)];
+                            x1 = qh[kdim<KVK>(s, c, r, 1)];
+                        } else {            // the two elements of a register are neighbours
+                            const float2 x = *reinterpret_cast<const float2*>(qh + kdim<KVK>(s, c, r, 0));
+                            x0 = x.x;
+                            x1 = x.y;
+                        }
+                        qf[s][r] = g < GQA ? pack_h2(x0, x1) : 0u;
                     }
             }
             WarpAcc A;
