@@ -87,10 +87,16 @@ template <int KVK> constexpr int work_bytes() {
 // thread column (c). At a pitch of 256 floats every head starts on the same bank: 6 (fp16 /
 // fp8) or 24 (turbo3, where the columns are 32 floats apart as well) lanes of a load collide,
 // and the eight warps build their fragments through one shared-memory port (1.6 us of a short
-// decode). Padded pitches, in floats, multiples of 4 for the 16-byte staging stores: fp16 reads
-// 8-byte pairs at 8 g + 2 c, fp8 at 4 g + 16 c (two ways at best: its columns are 16 floats
-// apart), turbo3 single floats at 4 g (four ways: its columns stay 32 apart).
-template <int KVK> constexpr int q_pitch() { return KVK == Q27_KV_F16 ? HD + 8 : HD + 4; }
+// decode). So the pitch is padded -- fp16 reads 8-byte pairs at banks 8 g + 2 c, fp8 at 4 g +
+// 16 c (two ways at best: its columns are 16 floats apart) -- and turbo3 also skews the row:
+// every 32-float block sits one float further on and the second 128-group four more, which puts
+// lane (g, c) on bank 12 g + c: no two alike.
+template <int KVK> constexpr int q_pitch() { return KVK == Q27_KV_F16 ? HD + 8 : KVK == Q27_KV_T3 ? HD + 12 : HD + 4; }
+constexpr int Q_SKEW_T3 = 1;                 // floats between the 32-float blocks of a turbo3 Q row
+template <int KVK>
+__host__ __device__ __forceinline__ int q_at(int d) {     // where dim d of a staged head lives in its row
+    return KVK == Q27_KV_T3 ? d + Q_SKEW_T3 * ((d >> 5) & 3) + 4 * (d >> 7) : d;
+}
 template <int KVK> constexpr int qstage_bytes() { return Fmt<KVK>::KVH * GQA * q_pitch<KVK>() * 4; }
 template <int KVK> constexpr int smem_bytes() {
     return HEADER_BYTES + work_bytes<KVK>() + qstage_bytes<KVK>();
@@ -674,7 +680,14 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
 #pragma unroll
                 for (int u = 0; u < QL; u++) {
                     const int i = ctid + u * NCW * 32;
-                    if (i < NQ4) reinterpret_cast<float4*>(q_stage + (i / (HD / 4)) * QP)[i % (HD / 4)] = qv[u];
+                    if (i < NQ4) {
+                        float* dst = q_stage + (i / (HD / 4)) * QP + q_at<KVK>((i % (HD / 4)) * 4);
+                        if constexpr (KVK == Q27_KV_T3) {     // the skew leaves the row 4-byte aligned
+                            dst[0] = qv[u].x; dst[1] = qv[u].y; dst[2] = qv[u].z; dst[3] = qv[u].w;
+                        } else {
+                            *reinterpret_cast<float4*>(dst) = qv[u];
+                        }
+                    }
                 }
             }
             if (b.wht & WHT_Q) {
@@ -682,7 +695,7 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
                 // 128-group per warp at a time, while the producer is already filling the ring
                 asm volatile("bar.sync 1, %0;" ::"n"(NCW * 32));
                 for (int gi = warp; gi < NHEADS * 2; gi += NCW)
-                    wht_group<false>(q_stage + (gi >> 1) * QP + (gi & 1) * 128, lane);
+                    wht_group<false, KVK == Q27_KV_T3 ? Q_SKEW_T3 : 0>(q_stage + (gi >> 1) * QP + q_at<KVK>((gi & 1) * 128), lane);
             }
             // Rows past the end of a ragged last stage are never copied; their weights are exact
             // zeros, so what the ring holds there only has to decode to finite numbers. Any
@@ -715,8 +728,8 @@ k_decode_mma(const __grid_constant__ DevBatch b) {
                     for (int r = 0; r < 2; r++) {
                         float x0, x1;
                         if constexpr (KVK == Q27_KV_T3) {
-                            x0 = qh[kdim<KVK>(s, c, r, 0)];
-                            x1 = qh[kdim<KVK>(s, c, r, 1)];
+                            x0 = qh[q_at<KVK>(kdim<KVK>(s, c, r, 0))];
+                            x1 = qh[q_at<KVK>(kdim<KVK>(s, c, r, 1))];
                         } else {            // the two elements of a register are neighbours
                             const float2 x = *reinterpret_cast<const float2*>(qh + kdim<KVK>(s, c, r, 0));
                             x0 = x.x;

@@ -15,7 +15,13 @@ __device__ __forceinline__ float wht_sign(const uint32_t* m, int j) {
     return (m[j >> 5] >> (j & 31)) & 1u ? -1.f : 1.f;
 }
 
+// SKEW: element j of the group lives at x[j + SKEW * (j >> 5)] (a buffer whose 32-element
+// blocks are SKEW floats apart, for bank-conflict-free readers; 0 = contiguous).
+template <int SKEW>
+__device__ __forceinline__ int wht_at(int j) { return j + SKEW * (j >> 5); }
+
 // 128-point butterfly over a warp's shared buffer: element pairs (j, j^h), lo+hi / lo-hi.
+template <int SKEW = 0>
 __device__ __forceinline__ void butterfly128(float* x, int lane) {
 #pragma unroll
     for (int h = 1; h < 128; h <<= 1) {
@@ -24,30 +30,30 @@ __device__ __forceinline__ void butterfly128(float* x, int lane) {
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const int j = lane + 32 * i;
-            const float a = x[j], b = x[j ^ h];
+            const float a = x[wht_at<SKEW>(j)], b = x[wht_at<SKEW>(j ^ h)];
             v[i] = (j & h) ? __fsub_rn(b, a) : __fadd_rn(a, b);
         }
         __syncwarp();
 #pragma unroll
-        for (int i = 0; i < 4; i++) x[lane + 32 * i] = v[i];
+        for (int i = 0; i < 4; i++) x[wht_at<SKEW>(lane + 32 * i)] = v[i];
     }
     __syncwarp();
 }
 
 // rotation of one group in place by one warp (all 32 lanes; x visible to the warp on entry,
 // result visible to the warp on return)
-template <bool INV>
+template <bool INV, int SKEW = 0>
 __device__ __forceinline__ void wht_group(float* x, int lane) {
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         const int j = lane + 32 * i;
-        x[j] = __fmul_rn(x[j], wht_sign(INV ? kS2Neg : kS1Neg, j));
+        x[wht_at<SKEW>(j)] = __fmul_rn(x[wht_at<SKEW>(j)], wht_sign(INV ? kS2Neg : kS1Neg, j));
     }
-    butterfly128(x, lane);
+    butterfly128<SKEW>(x, lane);
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         const int j = lane + 32 * i;
-        x[j] = __fmul_rn(x[j], __fmul_rn(INV_SQRT_128, wht_sign(INV ? kS1Neg : kS2Neg, j)));
+        x[wht_at<SKEW>(j)] = __fmul_rn(x[wht_at<SKEW>(j)], __fmul_rn(INV_SQRT_128, wht_sign(INV ? kS1Neg : kS2Neg, j)));
     }
     __syncwarp();
 }
