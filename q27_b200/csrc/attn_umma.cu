@@ -57,6 +57,15 @@ constexpr int N_SOFTMAX_WARPS = 4, MMA_WARP = 4, N_S_WARPS = 2, PV_WARP = 6, FIR
               N_LOAD_WARPS = 8;
 constexpr int UMMA_THREADS = (FIRST_LOAD_WARP + N_LOAD_WARPS) * 32;   // 480
 constexpr int NPROD = N_LOAD_WARPS * 16;        // 128 staging threads per side (K or V)
+// turbo3: the 128 threads of a side work as two teams of 64 that take alternate tiles, each
+// with its own raw buffer. A tile costs a staging thread a fixed ~0.7 us of barrier round trips
+// and shared-memory latency around the decode itself (~0.6 us for a 128th of a tile): one team
+// of 128 on every tile published a tile every 1.45 us and set the pace of the whole loop; two
+// teams of 64 decode twice as much per thread and tile, pay the fixed part once per two tiles
+// and overlap each other (c5 -6 %). fp8 stays with one team of 128: its conversion runs on the
+// 16-lane convert pipe, which two teams only crowd (+20 % measured).
+constexpr int TEAM = NPROD / 2;
+template <int KVK> constexpr int stagers() { return KVK == Q27_KV_T3 ? TEAM : NPROD; }   // threads that stage one tile
 
 // ---- small PTX wrappers -------------------------------------------------------------------
 __device__ __forceinline__ uint32_t s32(const void* p) {
@@ -369,17 +378,18 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
 
     if (threadIdx.x == 0) {
         *epi_bad = 0;
+        constexpr int STAGERS = stagers<KVK>();
         for (int s = 0; s < KSL; s++) {
-            bar_init(k_full + 8 * s, NPROD);
+            bar_init(k_full + 8 * s, STAGERS);
             bar_init(k_empty + 8 * s, 1);
         }
         for (int s = 0; s < VSL; s++) {
-            bar_init(v_full + 8 * s, NPROD);
+            bar_init(v_full + 8 * s, STAGERS);
             bar_init(v_empty + 8 * s, 1);
         }
-        for (int s = 0; s < 4; s++) {
-            bar_init(raw_full + 8 * s, NPROD);
-            bar_init(raw_empty + 8 * s, NPROD);
+        for (int s = 0; s < 4; s++) {               // [side][tile parity]
+            bar_init(raw_full + 8 * s, STAGERS);
+            bar_init(raw_empty + 8 * s, STAGERS);
         }
         for (int s = 0; s < S_BUFS; s++) {
             bar_init(s_full + 8 * s, 1);
@@ -404,8 +414,9 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         return static_cast<const uint8_t*>(tab[(pb.lo + i * BN) >> PAGE_SHIFT]);
     };
     auto nkeys_of = [&](int i) { return min(BN, pb.hi - (pb.lo + i * BN)); };
-    // Packed rows (turbo3, fp8) come in with 16-byte asynchronous copies into two raw buffers
-    // per side, each with a "landed" and a "read" mbarrier.
+    // Packed rows (turbo3, fp8) come in with 16-byte asynchronous copies into two raw buffers per
+    // side (tile i: buffer i & 1 -- for turbo3 that is the buffer of the team that takes the
+    // tile), each with a "landed" and a "read" mbarrier.
     //   turbo3: a tile's rows of this kv head are 64 keys x 100 B, 400 B apart in the page; what
     //   is copied is the aligned 112-byte window that holds them (a row starts on a 16-byte
     //   boundary and kv head h sits at byte 100 h, so the window [100 h rounded down, + 112)
@@ -415,6 +426,8 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     //   fp8: 64 keys x 256 B, coalesced; the third K slot and the third V slot each hold a
     //   side's two buffers. (Holding two tiles of raw bytes in registers instead spilled and
     //   made this path the bottleneck of the fp8 kernels.)
+    constexpr bool TEAMS = KVK == Q27_KV_T3;
+    const int team = TEAMS ? p >> 6 : 0, q = TEAMS ? p & (TEAM - 1) : p;   // q: thread within the tile's stagers
     constexpr int RAW_ROW = 112;
     constexpr int RAW_BYTES = KVK == Q27_KV_T3 ? BN * RAW_ROW : BN * HD;
     static_assert(KVK != Q27_KV_T3 || 4 * RAW_BYTES <= KT_BYTES, "the raw buffers live in the third V slot");
@@ -422,48 +435,47 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     const uint32_t rfull = raw_full + 8 * (2 * side), rempty = raw_empty + 8 * (2 * side);
     const int win0 = (pb.kvh * 2 * T3_BLK) & ~15;        // turbo3: window start inside the row
     const int blk_off = pb.kvh * 2 * T3_BLK - win0;      // 0, 4, 8 or 12
-    // turbo3: this thread's (up to) 4 pieces of a tile: source offset inside the page and key
-    // index are the same for every tile
-    uint32_t soff[4], doff[4];
-    int wkey[4];
+    // turbo3: this thread's 7 pieces of a tile's 448 (piece c = key 7 + 16-byte chunk): key and
+    // chunk are the same for every tile
+    int t3_key[7], t3_j[7];
     if constexpr (KVK == Q27_KV_T3) {
 #pragma unroll
-        for (int n = 0; n < 4; n++) {
-            const int c = p + NPROD * n;              // piece 0..447 of the tile's windows
-            const int key = c / 7, j = c - 7 * key;
-            wkey[n] = c < BN * 7 ? key : BN;          // BN: never below the tile's key count
-            soff[n] = (uint32_t)(key * n_kv * (2 * T3_BLK) + win0 + 16 * j);
-            doff[n] = (uint32_t)(key * RAW_ROW + 16 * j);
+        for (int n = 0; n < 7; n++) {
+            const int c = q + TEAM * n;
+            t3_key[n] = c / 7;
+            t3_j[n] = c - 7 * t3_key[n];
         }
     }
+    // by the threads that stage tile i
     auto issue_raw = [&](int i) {
         const int buf = i & 1, nk = nkeys_of(i);
         const uint8_t* page = page_of(i);
         if constexpr (KVK == Q27_KV_T3) {
             const uint32_t dst = s32(raw + buf * RAW_BYTES);
 #pragma unroll
-            for (int n = 0; n < 4; n++)
-                if (wkey[n] < nk)
+            for (int n = 0; n < 7; n++)
+                if (t3_key[n] < nk)
                     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-                                 ::"r"(dst + doff[n]), "l"(page + soff[n]) : "memory");
+                                 ::"r"(dst + (uint32_t)(t3_key[n] * RAW_ROW + 16 * t3_j[n])),
+                                   "l"(page + (size_t)(t3_key[n] * n_kv * (2 * T3_BLK) + win0 + 16 * t3_j[n]))
+                                 : "memory");
         } else if constexpr (KVK == Q27_KV_FP8) {
             uint8_t* dst = raw + buf * RAW_BYTES;
 #pragma unroll
             for (int n = 0; n < 8; n++) {
-                const int q = p + NPROD * n;          // 16-byte chunk 0..1023
-                const int key = q >> 4, c16 = q & 15;
+                const int c = p + NPROD * n;          // 16-byte chunk 0..1023
+                const int key = c >> 4, c16 = c & 15;
                 if (key < nk)
                     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-                                 ::"r"(s32(dst + q * 16)),
+                                 ::"r"(s32(dst + c * 16)),
                                    "l"(page + ((size_t)key * n_kv + pb.kvh) * HD + c16 * 16)
                                  : "memory");
                 else                                   // rows past the range: exact zeros
-                    *reinterpret_cast<uint4*>(dst + q * 16) = make_uint4(0, 0, 0, 0);
+                    *reinterpret_cast<uint4*>(dst + c * 16) = make_uint4(0, 0, 0, 0);
             }
             if (nk < BN) __threadfence_block();        // the zeros, before the arrival below
         }
-        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];"
-                     ::"r"(rfull + 8 * buf) : "memory");
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(rfull + 8 * buf) : "memory");
     };
     // The first two tiles' packed rows are asked for before the Q tile is staged (the table
     // look-up and the trip to HBM overlap it) -- unless the folded rotation needs the buffers'
@@ -472,8 +484,12 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     if (raw_early) {
         __syncthreads();                               // the barriers are initialised
         if (is_load) {
-            if (ntiles > 0) issue_raw(0);
-            if (ntiles > 1) issue_raw(1);
+            if (TEAMS) {
+                if (team < ntiles) issue_raw(team);
+            } else {
+                if (ntiles > 0) issue_raw(0);
+                if (ntiles > 1) issue_raw(1);
+            }
         }
     }
     {
@@ -818,36 +834,34 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
         } else if constexpr (KVK == Q27_KV_T3) {
-            // each thread decodes one 50-byte block of the tile's packed rows from shared memory
-            if (!raw_early) {
-                if (ntiles > 0) issue_raw(0);
-                if (ntiles > 1) issue_raw(1);
-            }
-            for (int i = 0; i < ntiles; i++) {
-                const int buf = i & 1;
+            // each thread decodes the two 50-byte blocks of one key of its team's tiles from
+            // shared memory
+            if (!raw_early && team < ntiles) issue_raw(team);
+            for (int i = team; i < ntiles; i += 2) {
                 const uint32_t par = (uint32_t)((i >> 1) & 1);
-                if (!bar_wait(rfull + 8 * buf, par)) break;
-                RawHalf<KVK> rw;
+                if (!bar_wait(rfull + 8 * team, par)) break;
+                RawHalf<KVK> rw0, rw1;
                 {
-                    const int key = p & 63, blk = p >> 6;
-                    const uint32_t* src = reinterpret_cast<const uint32_t*>(
-                        raw + buf * RAW_BYTES + key * RAW_ROW + blk_off + 48 * blk);
+                    const uint32_t* src = reinterpret_cast<const uint32_t*>(raw + team * RAW_BYTES + q * RAW_ROW + blk_off);
 #pragma unroll
-                    for (int k = 0; k < 13; k++) rw.w[k] = src[k];
-                    rw.w[13] = 0;
+                    for (int k = 0; k < 13; k++) {
+                        rw0.w[k] = src[k];
+                        rw1.w[k] = src[12 + k];            // block 1 starts 2 bytes into word 12
+                    }
+                    rw0.w[13] = rw1.w[13] = 0;
                 }
-                bar_arrive(rempty + 8 * buf);
+                bar_arrive(rempty + 8 * team);
                 if (!wait_slot(i)) break;
                 const int st = i % nslots;
-                if (p >> 6) half_store<KVK, 1>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
-                else half_store<KVK, 0>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
+                half_store<KVK, 0>(rw0, ring + st * KT_BYTES, nkeys_of(i), q);
+                half_store<KVK, 1>(rw1, ring + st * KT_BYTES, nkeys_of(i), q);
                 fence_async_smem();
                 bar_arrive(full + 8 * st);
-                // the raw buffer is refilled only now: by this time every thread of the side has
-                // long read it, so nobody stalls on the barrier, and the copies still have more
-                // than a tile's time to land
+                // the raw buffer is refilled only now: by this time every thread of the team has
+                // long read it, so nobody stalls on the barrier, and the copies have the other
+                // team's tile time to land
                 if (i + 2 < ntiles) {
-                    if (!bar_wait(rempty + 8 * buf, par)) break;
+                    if (!bar_wait(rempty + 8 * team, par)) break;
                     issue_raw(i + 2);
                 }
             }
