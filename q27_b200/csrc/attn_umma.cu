@@ -435,21 +435,24 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     const uint32_t rfull = raw_full + 8 * (2 * side), rempty = raw_empty + 8 * (2 * side);
     const int win0 = (pb.kvh * 2 * T3_BLK) & ~15;        // turbo3: window start inside the row
     const int blk_off = pb.kvh * 2 * T3_BLK - win0;      // 0, 4, 8 or 12
-    // turbo3: this thread's 7 pieces of a tile's 448 (piece c = key 7 + 16-byte chunk): key and
-    // chunk are the same for every tile
+    // turbo3: a warp copies the windows of the 32 keys it decodes itself (224 pieces, 7 per lane;
+    // piece c = key 7 + 16-byte chunk; key and chunk are the same for every tile), so its raw
+    // rows need no barrier: the lanes wait for their own copies (cp.async groups) and meet in a
+    // __syncwarp. (With the team's two warps sharing the buffer through a pair of mbarriers, a
+    // staging thread spent 0.3-0.9 us per tile between reading its rows and having the next
+    // ones on their way.)
     int t3_key[7], t3_j[7];
     if constexpr (KVK == Q27_KV_T3) {
 #pragma unroll
         for (int n = 0; n < 7; n++) {
-            const int c = q + TEAM * n;
-            t3_key[n] = c / 7;
-            t3_j[n] = c - 7 * t3_key[n];
+            const int c = lane + 32 * n;
+            t3_key[n] = (q & 32) + c / 7;
+            t3_j[n] = c % 7;
         }
     }
     // by the threads that stage tile i
-    auto issue_raw = [&](int i) {
+    auto issue_raw = [&](int i, const uint8_t* page) {
         const int buf = i & 1, nk = nkeys_of(i);
-        const uint8_t* page = page_of(i);
         if constexpr (KVK == Q27_KV_T3) {
             const uint32_t dst = s32(raw + buf * RAW_BYTES);
 #pragma unroll
@@ -475,7 +478,10 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             }
             if (nk < BN) __threadfence_block();        // the zeros, before the arrival below
         }
-        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(rfull + 8 * buf) : "memory");
+        if constexpr (KVK == Q27_KV_T3)
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        else
+            asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(rfull + 8 * buf) : "memory");
     };
     // The first two tiles' packed rows are asked for before the Q tile is staged (the table
     // look-up and the trip to HBM overlap it) -- unless the folded rotation needs the buffers'
@@ -485,10 +491,10 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         __syncthreads();                               // the barriers are initialised
         if (is_load) {
             if (TEAMS) {
-                if (team < ntiles) issue_raw(team);
+                if (team < ntiles) issue_raw(team, page_of(team));
             } else {
-                if (ntiles > 0) issue_raw(0);
-                if (ntiles > 1) issue_raw(1);
+                if (ntiles > 0) issue_raw(0, page_of(0));
+                if (ntiles > 1) issue_raw(1, page_of(1));
             }
         }
     }
@@ -836,10 +842,13 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         } else if constexpr (KVK == Q27_KV_T3) {
             // each thread decodes the two 50-byte blocks of one key of its team's tiles from
             // shared memory
-            if (!raw_early && team < ntiles) issue_raw(team);
+            if (!raw_early && team < ntiles) issue_raw(team, page_of(team));
             for (int i = team; i < ntiles; i += 2) {
-                const uint32_t par = (uint32_t)((i >> 1) & 1);
-                if (!bar_wait(rfull + 8 * team, par)) break;
+                // the page of the tile after this one, looked up now: the refill below must not
+                // wait for the table
+                const uint8_t* next_page = i + 2 < ntiles ? page_of(i + 2) : nullptr;
+                asm volatile("cp.async.wait_group 0;" ::: "memory");
+                __syncwarp();                              // the warp's rows of tile i have landed
                 RawHalf<KVK> rw0, rw1;
                 {
                     const uint32_t* src = reinterpret_cast<const uint32_t*>(raw + team * RAW_BYTES + q * RAW_ROW + blk_off);
@@ -850,27 +859,24 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                     }
                     rw0.w[13] = rw1.w[13] = 0;
                 }
-                bar_arrive(rempty + 8 * team);
+                // The warp's raw rows are refilled as soon as its lanes have read them: the copies
+                // then have the decode below to land in. (Asked for after the decode, they cost
+                // a trip to memory per tile, 0.4-0.8 us.)
+                __syncwarp();
+                if (i + 2 < ntiles) issue_raw(i + 2, next_page);
                 if (!wait_slot(i)) break;
                 const int st = i % nslots;
                 half_store<KVK, 0>(rw0, ring + st * KT_BYTES, nkeys_of(i), q);
                 half_store<KVK, 1>(rw1, ring + st * KT_BYTES, nkeys_of(i), q);
                 fence_async_smem();
                 bar_arrive(full + 8 * st);
-                // the raw buffer is refilled only now: by this time every thread of the team has
-                // long read it, so nobody stalls on the barrier, and the copies have the other
-                // team's tile time to land
-                if (i + 2 < ntiles) {
-                    if (!bar_wait(rempty + 8 * team, par)) break;
-                    issue_raw(i + 2);
-                }
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
         } else {
             // fp8: each thread converts its sixteen 8-byte pieces of the tile from shared memory
             if (!raw_early) {
-                if (ntiles > 0) issue_raw(0);
-                if (ntiles > 1) issue_raw(1);
+                if (ntiles > 0) issue_raw(0, page_of(0));
+                if (ntiles > 1) issue_raw(1, page_of(1));
             }
             for (int i = 0; i < ntiles; i++) {
                 const int buf = i & 1;
@@ -888,7 +894,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                 bar_arrive(full + 8 * st);
                 if (i + 2 < ntiles) {                      // refill only now: nobody stalls on the barrier
                     if (!bar_wait(rempty + 8 * buf, par)) break;
-                    issue_raw(i + 2);
+                    issue_raw(i + 2, page_of(i + 2));
                 }
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
