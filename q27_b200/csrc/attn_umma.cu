@@ -463,25 +463,25 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                                    "l"(page + (size_t)(t3_key[n] * n_kv * (2 * T3_BLK) + win0 + 16 * t3_j[n]))
                                  : "memory");
         } else if constexpr (KVK == Q27_KV_FP8) {
+            // a warp copies the 16 rows it converts itself (keys 4 k + its index in the side):
+            // 256 16-byte chunks, 8 per lane
             uint8_t* dst = raw + buf * RAW_BYTES;
+            const int wq = p >> 5;
 #pragma unroll
             for (int n = 0; n < 8; n++) {
-                const int c = p + NPROD * n;          // 16-byte chunk 0..1023
-                const int key = c >> 4, c16 = c & 15;
+                const int c = lane + 32 * n;
+                const int key = 4 * (c >> 4) + wq, c16 = c & 15;
                 if (key < nk)
                     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-                                 ::"r"(s32(dst + c * 16)),
+                                 ::"r"(s32(dst + key * HD + c16 * 16)),
                                    "l"(page + ((size_t)key * n_kv + pb.kvh) * HD + c16 * 16)
                                  : "memory");
                 else                                   // rows past the range: exact zeros
-                    *reinterpret_cast<uint4*>(dst + c * 16) = make_uint4(0, 0, 0, 0);
+                    *reinterpret_cast<uint4*>(dst + key * HD + c16 * 16) = make_uint4(0, 0, 0, 0);
             }
-            if (nk < BN) __threadfence_block();        // the zeros, before the arrival below
         }
-        if constexpr (KVK == Q27_KV_T3)
-            asm volatile("cp.async.commit_group;" ::: "memory");
-        else
-            asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(rfull + 8 * buf) : "memory");
+        // the lanes wait for their own copies (cp.async groups) and meet in a __syncwarp
+        asm volatile("cp.async.commit_group;" ::: "memory");
     };
     // The first two tiles' packed rows are asked for before the Q tile is staged (the table
     // look-up and the trip to HBM overlap it) -- unless the folded rotation needs the buffers'
@@ -873,29 +873,29 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
         } else {
-            // fp8: each thread converts its sixteen 8-byte pieces of the tile from shared memory
+            // fp8: each thread converts its sixteen 8-byte pieces of the tile (they lie in the 16
+            // rows its warp copied) from shared memory
             if (!raw_early) {
                 if (ntiles > 0) issue_raw(0, page_of(0));
                 if (ntiles > 1) issue_raw(1, page_of(1));
             }
             for (int i = 0; i < ntiles; i++) {
                 const int buf = i & 1;
-                const uint32_t par = (uint32_t)((i >> 1) & 1);
-                if (!bar_wait(rfull + 8 * buf, par)) break;
+                // the copies of tile i have landed; those of tile i + 1 may still be on their way
+                if (i + 1 < ntiles) asm volatile("cp.async.wait_group 1;" ::: "memory");
+                else asm volatile("cp.async.wait_group 0;" ::: "memory");
+                __syncwarp();
                 RawHalf<KVK> rw;
 #pragma unroll
                 for (int n = 0; n < 16; n++)
                     rw.d[n] = *reinterpret_cast<const uint2*>(raw + buf * RAW_BYTES + (p + NPROD * n) * 8);
-                bar_arrive(rempty + 8 * buf);
+                __syncwarp();                              // the warp's rows are read: refill them
+                if (i + 2 < ntiles) issue_raw(i + 2, page_of(i + 2));
                 if (!wait_slot(i)) break;
                 const int st = i % nslots;
                 half_store<KVK>(rw, ring + st * KT_BYTES, nkeys_of(i), p);
                 fence_async_smem();
                 bar_arrive(full + 8 * st);
-                if (i + 2 < ntiles) {                      // refill only now: nobody stalls on the barrier
-                    if (!bar_wait(rempty + 8 * buf, par)) break;
-                    issue_raw(i + 2, page_of(i + 2));
-                }
             }
             asm volatile("cp.async.wait_all;" ::: "memory");
         }
