@@ -85,8 +85,10 @@ __device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity) {
         : "=r"(ok) : "r"(bar), "r"(parity), "r"(4000u) : "memory");   // suspend-time hint, ns
     return ok != 0;
 }
+// Bounded: ~2 s of polling, then the flag. (A tenth of that expired inside a profiler's
+// instrumented replay pass, which slows the kernel a thousandfold.)
 __device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
-    for (int i = 0; i < (1 << 20); i++) {
+    for (int i = 0; i < (1 << 24); i++) {
         if (bar_try(bar, parity)) return true;
         if (i > 2048) __nanosleep(64);
     }
