@@ -530,7 +530,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
             __syncthreads();
         }
         // loads in flight per thread: a verify step's rows (up to 6 lanes) in one pass
-        constexpr int QU = MODE == 1 ? 5 : 4;
+        constexpr int QU = MODE == 1 ? 5 : 9;              // prefill: 126 rows in two passes
         for (int base_i = 0; base_i < pieces; base_i += UMMA_THREADS * QU) {
             float4 v[QU];
             int idx[QU];
@@ -682,13 +682,17 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         if (ok) ok = bar_wait(pvb + 8 * ((ntiles - 1) % S_BUFS), (uint32_t)(((ntiles - 1) / S_BUFS) & 1));
         ok = __all_sync(0xffffffffu, ok);
         tc_fence_after();
-        // Folded inverse rotation (wht_T on the output rows): the normalised rows go to the idle
-        // rings instead of global memory, and after the closing barrier every warp rotates and
-        // writes its share. (Rows of a split item go to the fix-up kernel, which rotates.)
+        // The normalised rows of a prefill tile go to the idle rings instead of global memory, and
+        // after the closing barrier every warp writes its share -- un-rotated first where the
+        // inverse rotation is folded in (wht_T on the output rows). (Rows of a split item go to
+        // the fix-up kernel, which rotates.)
         constexpr int OROT_PITCH = HD + 4;          // floats: float4-aligned, rows 4 banks apart
         static_assert((K_SLOTS + V_SLOTS) * KT_BYTES >= BM * OROT_PITCH * 4, "room for the fp32 O tile");
         float* o_rot = reinterpret_cast<float*>(k_sm);
-        const bool rot_out = MODE == 0 && (wht & WHT_OUT) && pb.piece < 0;
+        // Output rows of a prefill tile take the same road whether or not they are rotated on the
+        // way: a row per thread straight to global memory is one 16-byte piece of 32 different
+        // lines per store instruction (5.6 us of a prefill CTA's ~150).
+        const bool rot_out = MODE == 0 && pb.piece < 0;
         // Partial records {m, l, acc[256]} (verify; a key range of a split prefill item) take the
         // same road: a thread owns a row, so storing it from here costs one 8-byte piece of 32
         // different lines per instruction (2.7 us of a verify step). The rows go to the idle rings
@@ -923,14 +927,16 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
                     q == 0 ? make_float2(src[0], src[1]) : *reinterpret_cast<const float2*>(src + 2 + 2 * q);
         }
     }
-    if (MODE == 0 && (wht & WHT_OUT) && pb.piece < 0 && *epi_bad == 0) {
+    if (MODE == 0 && pb.piece < 0 && *epi_bad == 0) {
+        // the normalised rows, half a row (one 128-group of the rotation) per warp at a time:
+        // un-rotated if asked, then 512 contiguous bytes per store instruction
         constexpr int OROT_PITCH = HD + 4;
         float* o_rot = reinterpret_cast<float*>(k_sm);
         for (int gi = warp; gi < 2 * BM; gi += UMMA_THREADS / 32) {
             const RowInfo ri = pb.row(gi >> 1);
             if (!ri.out) continue;
             float* x = o_rot + (size_t)(gi >> 1) * OROT_PITCH + (gi & 1) * 128;
-            wht_group<true>(x, lane);
+            if (wht & WHT_OUT) wht_group<true>(x, lane);
             reinterpret_cast<float4*>(ri.out + (gi & 1) * 128)[lane] = reinterpret_cast<const float4*>(x)[lane];
         }
     }

@@ -102,10 +102,13 @@ def test_decode_and_prefill_over_pool_pages_with_aliased_tail(oracle, cuda, kvk)
 
 
 @pytest.mark.parametrize("kvk", [KV_F16, KV_FP8, KV_T3])
-@pytest.mark.parametrize("ns", [128, 85, 42, 7])
+@pytest.mark.parametrize("ns", [128, 85, 42, 15, 10, 7, 3, 2, 1])
 def test_verify_partials_with_the_callers_split_count(oracle, cuda, kvk, ns):
     """The reference's tools/fdmma_test.cu pattern: NaN-poisoned scratch, partials for W lanes
-    with ns splits, every cell the combine will read is written, merged result == oracle."""
+    with ns splits, every cell the combine will read is written, merged result == oracle. The
+    split counts leave a CTA 1, 2, 3, 5, 10, 15 or all 29 tiles (the last one 8 rows): the
+    staging teams of the packed formats take alternate tiles, so even, odd and single-tile
+    ranges are all walked."""
     rows, W = 1800, 6
     pos = [rows - W + t for t in range(W)]
     c = synth.make_case(oracle, kvk, rows=rows, pos=pos, seed=7 + ns, outlier_frac=0.02 if kvk == KV_T3 else 0.0)
