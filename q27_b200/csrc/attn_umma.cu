@@ -328,8 +328,8 @@ __device__ __forceinline__ void half_store(const RawHalf<KVK>& t, uint8_t* dst, 
         };
         constexpr int blk = BLK;
         const __half nh = __ushort_as_half((unsigned short)(word_at(0) & 0xffffu));
-        const __half2 n2 = key < nkeys ? __half2half2(nh) : __float2half2_rn(0.f);
-        const T3Tab tab = t3_tables_scaled(n2);   // one block, one norm: the pools hold centroid x norm
+        // one block, one norm: the pools hold centroid x norm (rows past the range: zeros)
+        const T3Tab tab = t3_tables_scaled(key < nkeys ? __half2float(nh) : 0.f);
 #pragma unroll
         for (int g8 = 0; g8 < 8; g8++) {         // 16 dims per group
             const uint32_t Qw = word_at(2 + 4 * g8);

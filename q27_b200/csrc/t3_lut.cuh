@@ -30,15 +30,16 @@ __device__ __forceinline__ T3Tab t3_tables() {
     }
     return T3Tab{lo[0], lo[1], hi[0], hi[1]};
 }
-// The same pools for the centroids times one block norm: fp16 centroid x fp16 norm, rounded
-// once (what a multiplication after the lookup gives, element for element), at 4 HMUL2 + 4 PRMT
-// per block instead of one HMUL2 per two elements.
-__device__ __forceinline__ T3Tab t3_tables_scaled(__half2 norm2) {
+// The same pools for the centroids times one block norm: the fp32 centroid times the norm,
+// rounded ONCE to fp16 -- the nearest fp16 to the dequantised value (turbo3_deq_elem,
+// src/turbo3.cuh:134, is that fp32 product); an fp16 centroid times the fp16 norm would round
+// twice. 8 FMUL + 4 packs + 4 PRMT per block instead of one HMUL2 per two elements.
+__device__ __forceinline__ T3Tab t3_tables_scaled(float norm) {
     const float c[8] = {Q27_T3_CENTROID_LIST};
     uint32_t p[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const __half2 v = __hmul2(__floats2half2_rn(c[2 * i], c[2 * i + 1]), norm2);
+        const __half2 v = __floats2half2_rn(c[2 * i] * norm, c[2 * i + 1] * norm);
         p[i] = *reinterpret_cast<const uint32_t*>(&v);
     }
     return T3Tab{prmt(p[0], p[1], 0x6420u), prmt(p[2], p[3], 0x6420u), prmt(p[0], p[1], 0x7531u),
