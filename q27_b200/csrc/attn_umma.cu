@@ -108,22 +108,8 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                  ::"r"(bar) : "memory");
 }
-// A operand taken from tensor memory (row = lane, 16 fp16 of K per 8 columns)
-__device__ __forceinline__ void tc_mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                              uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
-        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
-}
-__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                           uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
-        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
-}
-// the same two with the accumulate flag known at compile time (no predicate set-up per MMA)
+// tcgen05.mma kind::f16 with the accumulate flag known at compile time (no predicate set-up per
+// MMA); _ta: the A operand taken from tensor memory (row = lane, 16 fp16 of K per 8 columns)
 template <int ACC>
 __device__ __forceinline__ void tc_mma_f16_ta_c(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
                                                 uint32_t idesc) {
@@ -374,7 +360,7 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     // the buffer for the S MMAs four tiles on and tells the softmax warps that O may be touched.
     const uint32_t k_full = s32(&bars[0]), k_empty = s32(&bars[4]), v_full = s32(&bars[8]),
                    v_empty = s32(&bars[12]), s_full = s32(&bars[16]), pvb = s32(&bars[20]),
-                   p_full = s32(&bars[24]), raw_full = s32(&bars[28]), raw_empty = s32(&bars[32]);
+                   p_full = s32(&bars[24]);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = (pb.hi - pb.lo + BN - 1) / BN;
 
@@ -388,10 +374,6 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
         for (int s = 0; s < VSL; s++) {
             bar_init(v_full + 8 * s, STAGERS);
             bar_init(v_empty + 8 * s, 1);
-        }
-        for (int s = 0; s < 4; s++) {               // [side][tile parity]
-            bar_init(raw_full + 8 * s, STAGERS);
-            bar_init(raw_empty + 8 * s, STAGERS);
         }
         for (int s = 0; s < S_BUFS; s++) {
             bar_init(s_full + 8 * s, 1);
@@ -418,7 +400,8 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     auto nkeys_of = [&](int i) { return min(BN, pb.hi - (pb.lo + i * BN)); };
     // Packed rows (turbo3, fp8) come in with 16-byte asynchronous copies into two raw buffers per
     // side (tile i: buffer i & 1 -- for turbo3 that is the buffer of the team that takes the
-    // tile), each with a "landed" and a "read" mbarrier.
+    // tile). A warp copies exactly the rows it converts, so the buffers need no barrier: the
+    // lanes wait for their own copies (cp.async groups) and meet in a __syncwarp.
     //   turbo3: a tile's rows of this kv head are 64 keys x 100 B, 400 B apart in the page; what
     //   is copied is the aligned 112-byte window that holds them (a row starts on a 16-byte
     //   boundary and kv head h sits at byte 100 h, so the window [100 h rounded down, + 112)
@@ -434,7 +417,6 @@ __device__ __forceinline__ void attn_tile(const Problem<MODE>& pb, const void* c
     constexpr int RAW_BYTES = KVK == Q27_KV_T3 ? BN * RAW_ROW : BN * HD;
     static_assert(KVK != Q27_KV_T3 || 4 * RAW_BYTES <= KT_BYTES, "the raw buffers live in the third V slot");
     uint8_t* raw = KVK == Q27_KV_T3 ? raw_sm + side * 2 * RAW_BYTES : (side ? v_sm : k_sm) + 2 * KT_BYTES;
-    const uint32_t rfull = raw_full + 8 * (2 * side), rempty = raw_empty + 8 * (2 * side);
     const int win0 = (pb.kvh * 2 * T3_BLK) & ~15;        // turbo3: window start inside the row
     const int blk_off = pb.kvh * 2 * T3_BLK - win0;      // 0, 4, 8 or 12
     // turbo3: a warp copies the windows of the 32 keys it decodes itself (224 pieces, 7 per lane;
